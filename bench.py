@@ -1,0 +1,477 @@
+#!/usr/bin/env python
+"""Benchmark of the dyn-quant fused split GEMV on B200.
+
+Metric: microseconds per GEMV and achieved HBM GB/s (fraction of the measured
+B200 copy bandwidth) at Llama-2 7B/70B dimensions, batch 1, INT4 group 128,
+k = 3.0.  A "step" is one batch-1 pass through the GEMVs of one workload:
+
+  llama2_7b_mlp  (default) gate 4096->11008, up 4096->11008, down 11008->4096, 1 % outliers
+  llama2_7b_q    q_proj 4096->4096, 2 % outliers
+  llama2_70b_mlp gate/up 8192->28672, down 28672->8192, 3 % outliers
+  llama2_70b_q   q_proj 8192->8192, 3 % outliers
+
+value = whole-job algorithmic bytes / time (GB/s, inputs resident in HBM,
+each step a CUDA graph of that step's launches; weights rotate over enough
+copies that every step reads them from HBM, not L2).  Algorithmic bytes per
+GEMV = d_out*d_in/2 (INT4) + 4*d_out*d_in/128 (FP16 scale + zero)
++ 2*d_out*n_o (FP16 outlier columns, n_o = detected outliers) + 2*d_in (x) + 2*d_out (y).
+
+One process per GPU; under torchrun every rank runs its own copy of the
+workload (independent weights and activations, no exchange: "scaling": "weak"),
+the time is the max over ranks, value sums all ranks' bytes.
+
+--impl reference times the reference's split GEMV restated on the CPU (the
+reference has no CPU GEMV of its own; this is the oracle port, OpenMP over
+rows) on the host cores, same workload and metric; under torchrun only rank 0
+runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(ROOT, "dyn-quant_b200")
+for _p in (ROOT, PKG_DIR):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+
+METRIC = "µs per GEMV and achieved HBM GB/s (% of B200 peak) at Llama-2 7B/70B dims"
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_HBM_GBS = 6650.0
+K_OUTLIER = 3.0
+
+# name -> list of (gemv name, d_out, d_in, outlier fraction, activation key)
+WORKLOADS = {
+    "llama2_7b_mlp": [("gate", 11008, 4096, 0.01, "h"), ("up", 11008, 4096, 0.01, "h"),
+                      ("down", 4096, 11008, 0.01, "ff")],
+    "llama2_7b_q": [("q", 4096, 4096, 0.02, "h")],
+    "llama2_70b_mlp": [("gate", 28672, 8192, 0.03, "h"), ("up", 28672, 8192, 0.03, "h"),
+                       ("down", 8192, 28672, 0.03, "ff")],
+    "llama2_70b_q": [("q", 8192, 8192, 0.03, "h")],
+}
+
+
+def gemv_bytes(d_out: int, d_in: int, n_o: int) -> int:
+    return d_out * d_in // 2 + 4 * d_out * (d_in // 128) + 2 * d_out * n_o + 2 * d_in + 2 * d_out
+
+
+def activations(workload: str, seed_base: int):
+    """Seeded activation vectors per key (numpy f16)."""
+    from dyn_quant import synth
+    acts = {}
+    for name, d_out, d_in, frac, key in WORKLOADS[workload]:
+        if key not in acts:
+            acts[key] = synth.activation(d_in, frac, seed=seed_base + (1 if key == "h" else 2))
+    return acts
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+            return
+        self._t = threading.Thread(target=self._read, daemon=True)
+        self._t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self._t:
+            self._t.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [v.strip() for v in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def measured_peak_gbs():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "of measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "of fallback"
+
+
+def ncu_traffic(workload: str):
+    """Per-launch DRAM bytes of the split GEMV from the committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f).get(workload)
+    except (OSError, ValueError):
+        return None
+
+
+# ---------------------------------------------------------------------------
+# CPU legs (oracle port of the reference's split GEMV)
+# ---------------------------------------------------------------------------
+def cpu_prepare(workload: str):
+    import oracle as O
+    from dyn_quant import synth
+    acts = activations(workload, 0)
+    mats = []
+    for i, (name, d_out, d_in, frac, key) in enumerate(WORKLOADS[workload]):
+        w = synth.weights(d_out, d_in, seed=100 + i)
+        mats.append((name, w, *O.quantize(w), acts[key]))
+    return mats
+
+
+def cpu_step(mats):
+    import oracle as O
+    total = 0
+    for name, w, packed, scales, zeros, x in mats:
+        _, _, mask = O.split_gemv(packed, scales, zeros, w, x, K_OUTLIER)
+        total += gemv_bytes(w.shape[0], w.shape[1], int(mask.sum()))
+    return total
+
+
+def cpu_baseline(workload: str, budget_s: float = 10.0) -> dict:
+    import oracle as O
+    cores = os.cpu_count() or 1
+    O.set_num_threads(cores)
+    mats = cpu_prepare(workload)
+    cpu_step(mats)  # warm
+    t0 = time.perf_counter()
+    nbytes, n = 0, 0
+    while True:
+        nbytes += cpu_step(mats)
+        n += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    gb_s = nbytes / dt / 1e9
+    return {"value": round(gb_s, 3), "unit": "GB/s", "cores": O.num_threads(), "kind": "port",
+            "sample": f"{n} full {workload} steps (split GEMV incl. detection) in {dt:.1f} s, "
+                      f"OpenMP over rows, oracle/dq_oracle.c -O3",
+            "us_per_gemv": round(dt / (n * len(mats)) * 1e6, 1)}
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    import oracle as O
+    cores = os.cpu_count() or 1
+    O.set_num_threads(cores)
+    mats = cpu_prepare(args.workload)
+    for _ in range(args.warmup):
+        cpu_step(mats)
+    t0 = time.perf_counter()
+    nbytes = 0
+    for _ in range(args.steps):
+        nbytes += cpu_step(mats)
+    dt = time.perf_counter() - t0
+    value = nbytes / dt / 1e9
+    ngemv = len(mats)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "w4a16 (fp32 accumulate)", "data": "synthetic",
+        "config": {"workload": args.workload, "gemvs": [[n, o, i] for n, o, i, *_ in WORKLOADS[args.workload]],
+                   "batch": 1, "group": 128, "outlier_k": K_OUTLIER},
+        "us_per_gemv": round(dt / (args.steps * ngemv) * 1e6, 2),
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": O.num_threads(), "kind": "port",
+                         "sample": f"{args.steps} full {args.workload} steps on the host cores (the reference "
+                                   f"ships no CPU split GEMV; this is its kernel restated in C, OpenMP over rows)"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU leg
+# ---------------------------------------------------------------------------
+def run_ours(args, rank: int, world: int, local_rank: int) -> None:
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    import dyn_quant
+    from dyn_quant import _lib
+
+    L = _lib.lib()
+    spec = WORKLOADS[args.workload]
+    acts_np = activations(args.workload, 1000 * rank)
+    acts = {k: torch.from_numpy(v).to(dev) for k, v in acts_np.items()}
+
+    # detected outliers per activation (the mask the kernel applies)
+    n_o = {}
+    for key, x in acts.items():
+        n_o[key] = int(dyn_quant.detect_outliers(x, K_OUTLIER)[0].sum().item())
+    step_bytes = sum(gemv_bytes(o, i, n_o[key]) for _, o, i, _, key in spec)
+    n_gemv = len(spec)
+
+    # weight sets, rotated so each step reads its weights from HBM
+    n_sets = max(2, math.ceil(3 * L2_BYTES / step_bytes))
+    gen = torch.Generator(device=dev)
+    sets = []
+    for s in range(n_sets):
+        mods = []
+        for gi, (name, d_out, d_in, frac, key) in enumerate(spec):
+            gen.manual_seed(10_000 * rank + 100 * s + gi)
+            w = (torch.randn(d_out, d_in, generator=gen, device=dev, dtype=torch.float32) / math.sqrt(d_in)).half()
+            lin = dyn_quant.DynQuantLinear(d_in, d_out, K_OUTLIER)
+            lin.load_weight(w)
+            del w
+            mods.append(lin)
+        sets.append(mods)
+    torch.cuda.synchronize()
+
+    outs = [torch.empty(o, dtype=torch.float16, device=dev) for _, o, _, _, _ in spec]
+    structs = []
+    for mods in sets:
+        row = []
+        for lin in mods:
+            row.append(_lib.weights(lin.packed.data_ptr(), lin.scales.data_ptr(), lin.zeros.data_ptr(), None,
+                                    lin.fp16_w.data_ptr(), lin.d_out, lin.d_in))
+        structs.append(row)
+
+    def launch_step(s: int, stream, events=None):
+        for gi, (name, d_out, d_in, frac, key) in enumerate(spec):
+            if events is not None:
+                events[gi].record(stream)
+            st = L.dq_split_gemv(C.byref(structs[s][gi]), C.c_void_p(acts[key].data_ptr()),
+                                 C.c_void_p(outs[gi].data_ptr()), K_OUTLIER, C.c_void_p(stream.cuda_stream))
+            if st != 0:
+                raise RuntimeError(f"dq_split_gemv: {_lib.status_string(st)}")
+        if events is not None:
+            events[n_gemv].record(stream)
+
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        launch_step(0, stream)  # first call: kernel attributes, module load
+    stream.synchronize()
+
+    # one graph per rotation slot (soak / warm-up) and one per timed step (with timing events)
+    def capture(s: int, events=None):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            launch_step(s, torch.cuda.current_stream(), events)
+        return g
+
+    slot_graphs = [capture(s) for s in range(n_sets)]
+    step_events = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(n_gemv + 1)]
+                   for _ in range(args.steps)]
+    step_graphs = [capture(i % n_sets, step_events[i]) for i in range(args.steps)]
+    torch.cuda.synchronize()
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            slot_graphs[i % n_sets].replay()
+    stream.synchronize()
+
+    # clocks: sample across a soak window that contains the timed region
+    sampler = ClockSampler(local_rank) if not args.no_clocks else None
+    if sampler:
+        sampler.start()
+
+    def soak(seconds: float):
+        t_end = time.perf_counter() + seconds
+        i = 0
+        with torch.cuda.stream(stream):
+            while time.perf_counter() < t_end:
+                for _ in range(50):
+                    slot_graphs[i % n_sets].replay()
+                    i += 1
+                stream.synchronize()
+
+    soak(args.soak)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        t_start.record(stream)
+        for g in step_graphs:
+            g.replay()
+        t_end.record(stream)
+    stream.synchronize()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    soak(args.soak)
+    clocks = sampler.stop() if sampler else None
+
+    elapsed_ms = t_start.elapsed_time(t_end)
+    if world > 1:
+        t = torch.tensor([elapsed_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    launch_ms = [[step_events[i][j].elapsed_time(step_events[i][j + 1]) for j in range(n_gemv)]
+                 for i in range(args.steps)]
+    kern_ms = sum(sum(r) for r in launch_ms)
+    per_gemv_bytes = [gemv_bytes(o, i, n_o[key]) for _, o, i, _, key in spec]
+    achieved = sum(per_gemv_bytes) * args.steps / (kern_ms * 1e-3) / 1e9
+    peak, peak_note = measured_peak_gbs()
+
+    value = world * step_bytes * args.steps / (elapsed_ms * 1e-3) / 1e9
+    us_per_gemv = elapsed_ms * 1e3 / (args.steps * n_gemv)
+
+    # end to end through the public API: pinned host x in, host y out, every step
+    e2e = run_e2e(args, spec, sets, acts_np, dev, step_bytes, world)
+
+    # CPU baseline on rank 0 at N = 1
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args.workload, args.cpu_budget)
+
+    if rank == 0:
+        per_name = {}
+        for j, (name, d_out, d_in, _, key) in enumerate(spec):
+            us = statistics.mean(r[j] for r in launch_ms) * 1e3
+            per_name[name] = {"shape": [d_out, d_in], "n_outliers": n_o[key], "bytes": per_gemv_bytes[j],
+                              "us": round(us, 3), "gb_s": round(per_gemv_bytes[j] / (us * 1e-6) / 1e9, 1)}
+        traffic = ncu_traffic(args.workload)
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(elapsed_ms / args.steps, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "w4a16 (fp32 accumulate)", "data": "synthetic (seeded N(0,1/d_in) weights, N(0,1) "
+                                                        "activations with U[10,100] outliers)",
+            "config": {"workload": args.workload, "gemvs": [[n, o, i] for n, o, i, *_ in spec], "batch": 1,
+                       "group": 128, "outlier_k": K_OUTLIER, "outlier_frac": spec[0][3],
+                       "l2": f"inputs larger than L2: {n_sets} rotating weight sets "
+                             f"({n_sets * step_bytes / 1e6:.0f} MB streamed per cycle)",
+                       "graphs": "one CUDA graph per step"},
+            "us_per_gemv": round(us_per_gemv, 3),
+            "gemvs": per_name,
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_note": peak_note,
+                         "kernel": "gemv_m1_kernel<split, colmajor>",
+                         "traffic": traffic},
+            "gpu_launches": args.steps * n_gemv,
+            "e2e": e2e,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+
+    for g in step_graphs + slot_graphs:
+        del g
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_e2e(args, spec, sets, acts_np, dev, step_bytes, world):
+    import torch
+    xh = {k: torch.from_numpy(v).pin_memory() for k, v in acts_np.items()}
+    xd = {k: torch.empty(v.shape, dtype=torch.float16, device=dev) for k, v in acts_np.items()}
+    yh = [torch.empty(o, dtype=torch.float16).pin_memory() for _, o, _, _, _ in spec]
+    h2d = sum(v.numel() * 2 for v in xh.values())
+    d2h = sum(v.numel() * 2 for v in yh)
+    stream = torch.cuda.current_stream(dev)
+    times = []
+
+    def step(s):
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for k in xh:
+            xd[k].copy_(xh[k], non_blocking=True)
+        for gi, (name, d_out, d_in, frac, key) in enumerate(spec):
+            y = sets[s][gi](xd[key])
+            yh[gi].copy_(y, non_blocking=True)
+        end.record(stream)
+        end.synchronize()
+        return start.elapsed_time(end)
+
+    n_sets = len(sets)
+    for i in range(max(3, args.warmup)):
+        step(i % n_sets)
+    for i in range(args.steps):
+        times.append(step(i % n_sets))
+    ms = max(statistics.mean(times), 1e-9)
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return {"value": round(world * step_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 4),
+            "api": "DynQuantLinear.forward, pinned host buffers, synchronised every step"}
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="llama2_7b_mlp")
+    ap.add_argument("--soak", type=float, default=0.6, help="seconds of replays before/after the timed region")
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-clocks", action="store_true")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,154 @@
+// dq_abi.cu -- the extern "C" entry points of include/dq_abi.h: argument
+// validation, error reporting, then the kernel launchers.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "dq_internal.h"
+
+namespace dq {
+
+namespace {
+thread_local int t_last_cuda_error = 0;
+
+constexpr int kMaxDev = 64;
+int g_sm_count[kMaxDev];
+int g_smem_optin[kMaxDev];
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline bool aligned2(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 1u) == 0; }
+
+dq_status_t check_dims(int32_t d_out, int32_t d_in) {
+    if (d_out < 0 || d_in <= 0 || d_in % 128 != 0) return DQ_ERR_SHAPE;
+    return DQ_OK;
+}
+}  // namespace
+
+void set_cuda_error(cudaError_t e) { t_last_cuda_error = static_cast<int>(e); }
+
+dq_status_t device_info(DeviceInfo* out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) { set_cuda_error(e); return DQ_ERR_CUDA; }
+    if (dev >= 0 && dev < kMaxDev) {
+        int sm = __atomic_load_n(&g_sm_count[dev], __ATOMIC_ACQUIRE);
+        if (sm > 0) {
+            out->sm_count = sm;
+            out->smem_optin = __atomic_load_n(&g_smem_optin[dev], __ATOMIC_ACQUIRE);
+            return DQ_OK;
+        }
+    }
+    int sm = 0, optin = 0;
+    if ((e = cudaDeviceGetAttribute(&sm, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess) {
+        set_cuda_error(e);
+        return DQ_ERR_CUDA;
+    }
+    if (dev >= 0 && dev < kMaxDev) {
+        __atomic_store_n(&g_smem_optin[dev], optin, __ATOMIC_RELEASE);
+        __atomic_store_n(&g_sm_count[dev], sm, __ATOMIC_RELEASE);
+    }
+    out->sm_count = sm;
+    out->smem_optin = optin;
+    return DQ_OK;
+}
+
+}  // namespace dq
+
+using namespace dq;
+
+extern "C" {
+
+const char* dq_status_string(dq_status_t s) {
+    switch (s) {
+        case DQ_OK: return "DQ_OK";
+        case DQ_ERR_INVALID_ARGUMENT: return "DQ_ERR_INVALID_ARGUMENT";
+        case DQ_ERR_SHAPE: return "DQ_ERR_SHAPE";
+        case DQ_ERR_ALIGNMENT: return "DQ_ERR_ALIGNMENT";
+        case DQ_ERR_UNSUPPORTED: return "DQ_ERR_UNSUPPORTED";
+        case DQ_ERR_CUDA: return "DQ_ERR_CUDA";
+        case DQ_ERR_WORKSPACE: return "DQ_ERR_WORKSPACE";
+    }
+    return "DQ_ERR_UNKNOWN";
+}
+
+int dq_last_cuda_error(void) { return t_last_cuda_error; }
+
+int dq_version(void) { return 100; }  // 0.1.0
+
+int32_t dq_max_d_in(void) { return kMaxDIn; }
+
+dq_status_t dq_quantize(const uint16_t* w16, int32_t d_out, int32_t d_in, uint8_t* packed,
+                        uint16_t* scales, uint16_t* zeros, void* stream) {
+    dq_status_t st = check_dims(d_out, d_in);
+    if (st != DQ_OK) return st;
+    if (d_out == 0) return DQ_OK;
+    if (!w16 || !packed || !scales || !zeros) return DQ_ERR_INVALID_ARGUMENT;
+    if (!aligned16(w16) || !aligned16(packed) || !aligned2(scales) || !aligned2(zeros))
+        return DQ_ERR_ALIGNMENT;
+    return launch_quantize(w16, d_out, d_in, packed, scales, zeros, static_cast<cudaStream_t>(stream));
+}
+
+dq_status_t dq_build_colmajor(const uint16_t* w16, int32_t d_out, int32_t d_in, uint16_t* fp16_cm,
+                              void* stream) {
+    dq_status_t st = check_dims(d_out, d_in);
+    if (st != DQ_OK) return st;
+    if (d_out == 0) return DQ_OK;
+    if (!w16 || !fp16_cm) return DQ_ERR_INVALID_ARGUMENT;
+    if (!aligned16(w16) || !aligned2(fp16_cm)) return DQ_ERR_ALIGNMENT;
+    return launch_colmajor(w16, d_out, d_in, fp16_cm, static_cast<cudaStream_t>(stream));
+}
+
+static dq_status_t check_weights(const dq_weights_t* w, const uint16_t* x, const uint16_t* y,
+                                 bool need_fp16) {
+    if (!w || !x || !y) return DQ_ERR_INVALID_ARGUMENT;
+    dq_status_t st = check_dims(w->d_out, w->d_in);
+    if (st != DQ_OK) return st;
+    if (w->d_in > kMaxDIn) return DQ_ERR_UNSUPPORTED;
+    if (w->d_out == 0) return DQ_OK;
+    if (!w->packed || !w->scales || !w->zeros) return DQ_ERR_INVALID_ARGUMENT;
+    if (need_fp16 && !w->fp16 && !w->fp16_cm) return DQ_ERR_INVALID_ARGUMENT;
+    if (!aligned16(w->packed) || !aligned16(x) || !aligned2(y) || !aligned2(w->scales) ||
+        !aligned2(w->zeros))
+        return DQ_ERR_ALIGNMENT;
+    if (need_fp16 && ((w->fp16 && !aligned2(w->fp16)) || (w->fp16_cm && !aligned2(w->fp16_cm))))
+        return DQ_ERR_ALIGNMENT;
+    return DQ_OK;
+}
+
+dq_status_t dq_split_gemv(const dq_weights_t* w, const uint16_t* x, uint16_t* y, float outlier_k,
+                          void* stream) {
+    dq_status_t st = check_weights(w, x, y, true);
+    if (st != DQ_OK || w->d_out == 0) return st;
+    return launch_gemv_m1(*w, x, y, outlier_k, true, static_cast<cudaStream_t>(stream));
+}
+
+dq_status_t dq_int4_gemv(const dq_weights_t* w, const uint16_t* x, uint16_t* y, void* stream) {
+    dq_status_t st = check_weights(w, x, y, false);
+    if (st != DQ_OK || w->d_out == 0) return st;
+    return launch_gemv_m1(*w, x, y, 0.f, false, static_cast<cudaStream_t>(stream));
+}
+
+dq_status_t dq_reference_gemv(const uint16_t* w16, const uint16_t* x, uint16_t* y, int32_t d_out,
+                              int32_t d_in, void* stream) {
+    if (!w16 || !x || !y) return DQ_ERR_INVALID_ARGUMENT;
+    dq_status_t st = check_dims(d_out, d_in);
+    if (st != DQ_OK) return st;
+    if (d_in > kMaxDIn) return DQ_ERR_UNSUPPORTED;
+    if (d_out == 0) return DQ_OK;
+    if (!aligned16(w16) || !aligned16(x) || !aligned2(y)) return DQ_ERR_ALIGNMENT;
+    return launch_reference_gemv(w16, x, y, d_out, d_in, static_cast<cudaStream_t>(stream));
+}
+
+dq_status_t dq_detect_outliers(const uint16_t* x, int32_t d_in, float outlier_k,
+                               uint32_t* mask_words, int32_t* indices, int32_t* count,
+                               float* stats, void* stream) {
+    if (!x) return DQ_ERR_INVALID_ARGUMENT;
+    if (d_in <= 0 || d_in % 128 != 0) return DQ_ERR_SHAPE;
+    if (d_in > kMaxDIn) return DQ_ERR_UNSUPPORTED;
+    if (!aligned16(x)) return DQ_ERR_ALIGNMENT;
+    return launch_detect(x, d_in, outlier_k, mask_words, indices, count, stats,
+                         static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,143 @@
+// dq_common.cuh -- shared device helpers for the dyn-quant sm_100a kernels.
+//
+// Everything here is plain inline PTX or CUDA intrinsics; the kernels are
+// compiled for sm_100a only (-gencode arch=compute_100a,code=sm_100a).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace dq {
+
+// Group size of the INT4 format: one FP16 scale and zero-point per 128
+// consecutive input columns of a row (src/quant_format.cuh:10).
+constexpr int kGroup = 128;
+// Rows per MMA row-block (the M of mma.m16n8k16).
+constexpr int kRowBlock = 16;
+
+// ---------------------------------------------------------------------------
+// Global loads
+// ---------------------------------------------------------------------------
+
+// Streaming 16-byte load of read-only data that is used once (packed weights):
+// bypasses L1 allocation.
+__device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ uint4 ldg_v4(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ uint16_t ldg_u16(const void* p) {
+    uint16_t r;
+    asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(r) : "l"(p));
+    return r;
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-core MMA: D(16x8,f32) += A(16x16,f16,row) * B(16x8,f16,col)
+// Fragment ownership (lane = 4*g + t):
+//   a0 = A[g][2t..2t+1]   a1 = A[g+8][2t..2t+1]   a2 = A[g][2t+8..+9]   a3 = A[g+8][2t+8..+9]
+//   b0 = B[2t..2t+1][g]   b1 = B[2t+8..+9][g]
+//   d0 = D[g][2t] d1 = D[g][2t+1] d2 = D[g+8][2t] d3 = D[g+8][2t+1]
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// ---------------------------------------------------------------------------
+// INT4 -> FP16 dequantisation of one 32-bit word of the packed format.
+//
+// The packed format (src/quant_format.cuh:25-38) stores column 2j in the low
+// nibble and column 2j+1 in the high nibble of byte j, so nibble n of a
+// little-endian 32-bit word is column n of that word's 8 columns.
+//
+// (w & 0x000F000F) | 0x6400_6400 is the f16 pair (1024 + q0, 1024 + q4);
+// (w & 0x00F000F0) | 0x6400_6400 is (1024 + 16 q1, 1024 + 16 q5).  Removing
+// the bias is exact in f16: (1024+q) - 1024 = q and (1024+16q)/16 - 64 = q, both
+// single-rounding operations whose exact result is a small integer.
+// Output pairs: p04 = (q0,q4), p15 = (q1,q5), p26 = (q2,q6), p37 = (q3,q7).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t mask, uint32_t orv) {
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(mask), "r"(orv));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t r;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+
+struct Deq4 {
+    uint32_t p04, p15, p26, p37;
+};
+
+__device__ __forceinline__ Deq4 dequant_word(uint32_t w) {
+    constexpr uint32_t kMagic = 0x64006400u;     // f16 pair (1024, 1024)
+    constexpr uint32_t kSixteenth = 0x2C002C00u; // f16 pair (1/16, 1/16)
+    constexpr uint32_t kMinus64 = 0xD400D400u;   // f16 pair (-64, -64)
+    const uint32_t w2 = w >> 8;
+    Deq4 r;
+    r.p04 = hsub2_u32(lop3_and_or(w, 0x000F000Fu, kMagic), kMagic);
+    r.p15 = hfma2_u32(lop3_and_or(w, 0x00F000F0u, kMagic), kSixteenth, kMinus64);
+    r.p26 = hsub2_u32(lop3_and_or(w2, 0x000F000Fu, kMagic), kMagic);
+    r.p37 = hfma2_u32(lop3_and_or(w2, 0x00F000F0u, kMagic), kSixteenth, kMinus64);
+    return r;
+}
+
+__device__ __forceinline__ uint32_t pack_h2(uint16_t lo, uint16_t hi) {
+    return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+}
+
+__device__ __forceinline__ float h2f_bits(uint16_t h) {
+    return __half2float(__ushort_as_half(h));
+}
+
+// ---------------------------------------------------------------------------
+// Deterministic block reductions (fixed xor-butterfly + warp-order tree).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// All threads of the block get the same sum.  red must hold >= NW floats and
+// is reused (a barrier guards it on entry and exit).
+template <int NT>
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    constexpr int NW = NT / 32;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_sum(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float s = (lane < NW) ? red[lane] : 0.f;
+    s = warp_sum(s);
+    return s;
+}
+
+}  // namespace dq

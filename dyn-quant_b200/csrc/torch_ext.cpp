@@ -1,0 +1,198 @@
+// torch_ext.cpp -- the dyn_quant._C torch extension: the reference's four
+// bindings (csrc/bindings.cpp:184-193 of dyn-quant) with the same names,
+// argument meaning and RuntimeError behaviour, implemented over the C ABI of
+// libdq_b200.so.  Extra functions: build_colmajor, detect_outliers.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include <tuple>
+
+#include "../../include/dq_abi.h"
+
+namespace {
+
+void check_status(dq_status_t s, const char* what) {
+    if (s == DQ_OK) return;
+    if (s == DQ_ERR_CUDA)
+        TORCH_CHECK(false, what, " failed: ", dq_status_string(s), " (cudaError ", dq_last_cuda_error(), ")");
+    TORCH_CHECK(false, what, " failed: ", dq_status_string(s));
+}
+
+// csrc/bindings.cpp:14-18
+void check_fp16_contiguous(const torch::Tensor& t, const char* name) {
+    TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+    TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+    TORCH_CHECK(t.scalar_type() == at::kHalf, name, " must be float16");
+}
+
+void* stream_of(const torch::Tensor&) { return at::cuda::getCurrentCUDAStream().stream(); }
+
+const uint16_t* h16(const torch::Tensor& t) { return reinterpret_cast<const uint16_t*>(t.data_ptr()); }
+uint16_t* h16m(torch::Tensor& t) { return reinterpret_cast<uint16_t*>(t.data_ptr()); }
+
+// The FP16 weights may be the row-major [d_out, d_in] copy the reference keeps,
+// or the transposed view of the column-major mirror (stride (1, d_out)) that
+// DynQuantLinear keeps; both are [d_out, d_in] tensors with the same values.
+struct Fp16View {
+    const uint16_t* rm = nullptr;
+    const uint16_t* cm = nullptr;
+};
+
+Fp16View fp16_view(const torch::Tensor& w) {
+    TORCH_CHECK(w.dim() == 2, "fp16_weights must be 2D");
+    TORCH_CHECK(w.is_cuda(), "fp16_weights must be a CUDA tensor");
+    TORCH_CHECK(w.scalar_type() == at::kHalf, "fp16_weights must be float16");
+    Fp16View v;
+    if (w.is_contiguous()) {
+        v.rm = h16(w);
+    } else if (w.t().is_contiguous()) {
+        v.cm = h16(w);
+    } else {
+        TORCH_CHECK(false, "fp16_weights must be contiguous (row-major) or the transpose of a contiguous column-major mirror");
+    }
+    return v;
+}
+
+// csrc/bindings.cpp:94-111 plus the shape checks the reference leaves implicit.
+dq_weights_t make_weights(const torch::Tensor& packed, const torch::Tensor& scales,
+                          const torch::Tensor& zeros, const torch::Tensor& fp16_w,
+                          const torch::Tensor& x, bool need_fp16) {
+    TORCH_CHECK(fp16_w.dim() == 2, "fp16_weights must be 2D");
+    check_fp16_contiguous(scales, "scales");
+    check_fp16_contiguous(zeros, "zeros");
+    check_fp16_contiguous(x, "x");
+    TORCH_CHECK(packed.is_cuda() && packed.is_contiguous() && packed.scalar_type() == at::kByte,
+                "packed must be a contiguous CUDA uint8 tensor");
+    const int64_t d_out = fp16_w.size(0), d_in = fp16_w.size(1);
+    TORCH_CHECK(d_in % 128 == 0, "d_in must be divisible by GROUP_SIZE=128");
+    TORCH_CHECK(x.numel() == d_in, "x length must equal d_in=", d_in);
+    TORCH_CHECK(packed.dim() == 2 && packed.size(0) == d_out && packed.size(1) == d_in / 2,
+                "packed column mismatch");
+    TORCH_CHECK(scales.numel() == d_out * (d_in / 128) && zeros.numel() == d_out * (d_in / 128),
+                "scales/zeros must hold d_out * d_in/128 values");
+    TORCH_CHECK(x.device() == packed.device() && x.device() == fp16_w.device() &&
+                    x.device() == scales.device() && x.device() == zeros.device(),
+                "all tensors must be on the same device");
+    dq_weights_t w{};
+    w.packed = reinterpret_cast<const uint8_t*>(packed.data_ptr());
+    w.scales = h16(scales);
+    w.zeros = h16(zeros);
+    if (need_fp16) {
+        Fp16View v = fp16_view(fp16_w);
+        w.fp16 = v.rm;
+        w.fp16_cm = v.cm;
+    }
+    w.d_out = static_cast<int32_t>(d_out);
+    w.d_in = static_cast<int32_t>(d_in);
+    return w;
+}
+
+// quantize_weights(weight [d_out, d_in] f16) -> (packed, scales, zeros, fp16_copy)
+// (csrc/bindings.cpp:25-75; quantized on the device, bit-exact with the host loop)
+std::tuple<torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor>
+quantize_weights(const torch::Tensor& weight) {
+    check_fp16_contiguous(weight, "weight");
+    TORCH_CHECK(weight.dim() == 2, "weight must be 2D [d_out, d_in]");
+    const int64_t d_out = weight.size(0), d_in = weight.size(1);
+    TORCH_CHECK(d_in % 128 == 0, "d_in must be divisible by GROUP_SIZE=", 128);
+    const at::cuda::CUDAGuard guard(weight.device());
+    auto u8 = torch::TensorOptions().dtype(torch::kUInt8).device(weight.device());
+    auto f16 = torch::TensorOptions().dtype(torch::kHalf).device(weight.device());
+    auto packed = torch::empty({d_out, d_in / 2}, u8);
+    auto scales = torch::empty({d_out, d_in / 128}, f16);
+    auto zeros = torch::empty({d_out, d_in / 128}, f16);
+    auto copy = weight.clone();
+    check_status(dq_quantize(h16(weight), static_cast<int32_t>(d_out), static_cast<int32_t>(d_in),
+                             reinterpret_cast<uint8_t*>(packed.data_ptr()), h16m(scales), h16m(zeros),
+                             stream_of(weight)),
+                 "quantize_weights");
+    return {packed, scales, zeros, copy};
+}
+
+// build_colmajor(weight [d_out, d_in] f16) -> mirror [d_in, d_out] f16 (contiguous)
+torch::Tensor build_colmajor(const torch::Tensor& weight) {
+    check_fp16_contiguous(weight, "weight");
+    TORCH_CHECK(weight.dim() == 2, "weight must be 2D [d_out, d_in]");
+    const int64_t d_out = weight.size(0), d_in = weight.size(1);
+    TORCH_CHECK(d_in % 128 == 0, "d_in must be divisible by GROUP_SIZE=", 128);
+    const at::cuda::CUDAGuard guard(weight.device());
+    auto cm = torch::empty({d_in, d_out}, weight.options());
+    check_status(dq_build_colmajor(h16(weight), static_cast<int32_t>(d_out),
+                                   static_cast<int32_t>(d_in), h16m(cm), stream_of(weight)),
+                 "build_colmajor");
+    return cm;
+}
+
+// split_gemv(packed, scales, zeros, fp16_weights, x, outlier_k) -> y [d_out] f16
+torch::Tensor split_gemv(const torch::Tensor& packed, const torch::Tensor& scales,
+                         const torch::Tensor& zeros, const torch::Tensor& fp16_w,
+                         const torch::Tensor& x, double outlier_k) {
+    dq_weights_t w = make_weights(packed, scales, zeros, fp16_w, x, true);
+    const at::cuda::CUDAGuard guard(x.device());
+    auto y = torch::empty({w.d_out}, x.options());
+    check_status(dq_split_gemv(&w, h16(x), h16m(y), static_cast<float>(outlier_k), stream_of(x)),
+                 "split_gemv");
+    return y;
+}
+
+// int4_gemv(packed, scales, zeros, fp16_weights, x) -> y [d_out] f16
+torch::Tensor int4_gemv(const torch::Tensor& packed, const torch::Tensor& scales,
+                        const torch::Tensor& zeros, const torch::Tensor& fp16_w,
+                        const torch::Tensor& x) {
+    dq_weights_t w = make_weights(packed, scales, zeros, fp16_w, x, false);
+    const at::cuda::CUDAGuard guard(x.device());
+    auto y = torch::empty({w.d_out}, x.options());
+    check_status(dq_int4_gemv(&w, h16(x), h16m(y), stream_of(x)), "int4_gemv");
+    return y;
+}
+
+// reference_gemv(fp16_weights, x) -> y [d_out] f16   (csrc/bindings.cpp:162-182)
+torch::Tensor reference_gemv(const torch::Tensor& fp16_w, const torch::Tensor& x) {
+    TORCH_CHECK(fp16_w.dim() == 2, "fp16_weights must be 2D");
+    check_fp16_contiguous(fp16_w, "fp16_weights");
+    check_fp16_contiguous(x, "x");
+    const int64_t d_out = fp16_w.size(0), d_in = fp16_w.size(1);
+    TORCH_CHECK(x.numel() == d_in, "x length must equal d_in");
+    TORCH_CHECK(d_in % 128 == 0, "d_in must be divisible by 128");
+    const at::cuda::CUDAGuard guard(x.device());
+    auto y = torch::empty({d_out}, x.options());
+    check_status(dq_reference_gemv(h16(fp16_w), h16(x), h16m(y), static_cast<int32_t>(d_out),
+                                   static_cast<int32_t>(d_in), stream_of(x)),
+                 "reference_gemv");
+    return y;
+}
+
+// detect_outliers(x, k) -> (mask_words int32 [d_in/32], indices int32 [d_in/4],
+//                           count int32 [1], stats f32 [4]); no host synchronisation.
+std::tuple<torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor>
+detect_outliers(const torch::Tensor& x, double outlier_k) {
+    check_fp16_contiguous(x, "x");
+    const int64_t d_in = x.numel();
+    TORCH_CHECK(d_in > 0 && d_in % 128 == 0, "x length must be a positive multiple of 128");
+    const at::cuda::CUDAGuard guard(x.device());
+    auto i32 = torch::TensorOptions().dtype(torch::kInt32).device(x.device());
+    auto mask = torch::empty({d_in / 32}, i32);
+    auto idx = torch::empty({d_in / 4}, i32);
+    auto cnt = torch::empty({1}, i32);
+    auto stats = torch::empty({4}, torch::TensorOptions().dtype(torch::kFloat32).device(x.device()));
+    check_status(dq_detect_outliers(h16(x), static_cast<int32_t>(d_in), static_cast<float>(outlier_k),
+                                    reinterpret_cast<uint32_t*>(mask.data_ptr()),
+                                    reinterpret_cast<int32_t*>(idx.data_ptr()),
+                                    reinterpret_cast<int32_t*>(cnt.data_ptr()),
+                                    reinterpret_cast<float*>(stats.data_ptr()), stream_of(x)),
+                 "detect_outliers");
+    return {mask, idx, cnt, stats};
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+    m.def("quantize_weights", &quantize_weights, "Quantize FP16 weight matrix to INT4 packed format");
+    m.def("split_gemv", &split_gemv, "Fused dynamic-precision GEMV with runtime outlier detection");
+    m.def("int4_gemv", &int4_gemv, "Dense INT4 GEMV baseline");
+    m.def("reference_gemv", &reference_gemv, "FP16 dense reference GEMV");
+    m.def("build_colmajor", &build_colmajor, "Column-major FP16 mirror of a weight matrix");
+    m.def("detect_outliers", &detect_outliers, "Standalone outlier detector");
+    m.def("version", []() { return dq_version(); });
+}

@@ -1,0 +1,247 @@
+"""dyn_quant: fused dynamic-precision W4A16 GEMV for NVIDIA B200 (sm_100a).
+
+Drop-in for the reference package of the same name (dyn-quant,
+dyn_quant/__init__.py:1-179): the same functions, the same DynQuantLinear
+module, the same argument meaning and the same RuntimeError behaviour, over
+hand-written sm_100a kernels (libdq_b200.so, C ABI in include/dq_abi.h).
+
+Exports:
+  DynQuantLinear   nn.Module: load_weight() quantizes on the GPU; forward()
+                   runs the fused split-precision GEMV.
+  quantize()       FP16 weight -> (packed INT4, scales, zeros, fp16 copy).
+  split_gemv()     fused dynamic-precision GEMV (functional API).
+  int4_gemv()      dense INT4 GEMV baseline.
+  reference_gemv() FP16 dense GEMV.
+  detect_outliers() the detector the split GEMV applies, standalone.
+
+There is no CPU path: every function raises if the extension is not built.
+"""
+from __future__ import annotations
+
+from typing import Tuple
+
+import torch
+import torch.nn as nn
+
+try:
+    from dyn_quant import _C  # noqa: F401
+
+    _EXTENSION_LOADED = True
+    _IMPORT_ERROR: Exception | None = None
+except ImportError as e:  # pragma: no cover - exercised only without a build
+    _EXTENSION_LOADED = False
+    _IMPORT_ERROR = e
+
+__all__ = [
+    "DynQuantLinear",
+    "quantize",
+    "split_gemv",
+    "int4_gemv",
+    "reference_gemv",
+    "detect_outliers",
+    "build_colmajor",
+]
+
+GROUP_SIZE = 128
+
+
+def _require_extension() -> None:
+    """dyn_quant/__init__.py:26-31 of the reference: fail loudly without the extension."""
+    if not _EXTENSION_LOADED:
+        raise RuntimeError(
+            "dyn_quant C extension not found. Build it with: python dyn-quant_b200/build.py"
+            + (f" ({_IMPORT_ERROR})" if _IMPORT_ERROR else ""))
+
+
+def _aligned(t: torch.Tensor) -> torch.Tensor:
+    """The kernels read x with 16-byte loads; re-home a misaligned view."""
+    if t.data_ptr() % 16:
+        t = t.clone()
+    return t
+
+
+def quantize(weight: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Quantize an FP16 weight matrix to packed INT4 format (on the GPU, bit-exact
+    with the reference's host quantizer, src/quant_format.cuh:58-97).
+
+    Args:
+        weight: [d_out, d_in] float16 tensor on CUDA.
+
+    Returns:
+        (packed, scales, zeros, fp16_copy):
+          packed    [d_out, d_in//2] uint8, two INT4 values per byte (even column low nibble)
+          scales    [d_out, d_in//128] float16, per-group scale
+          zeros     [d_out, d_in//128] float16, per-group zero-point
+          fp16_copy [d_out, d_in] float16, original weights for outlier columns
+    """
+    _require_extension()
+    if weight.dtype != torch.float16:
+        weight = weight.to(torch.float16)
+    if not weight.is_contiguous():
+        weight = weight.contiguous()
+    return _C.quantize_weights(_aligned(weight))
+
+
+def build_colmajor(weight: torch.Tensor) -> torch.Tensor:
+    """Column-major FP16 mirror [d_in, d_out] of a [d_out, d_in] weight.
+
+    Its transpose (``mirror.t()``) is a [d_out, d_in] view that split_gemv accepts
+    as ``fp16_w`` and uses for coalesced outlier-column reads."""
+    _require_extension()
+    if weight.dtype != torch.float16:
+        weight = weight.to(torch.float16)
+    if not weight.is_contiguous():
+        weight = weight.contiguous()
+    return _C.build_colmajor(_aligned(weight))
+
+
+def split_gemv(
+    packed: torch.Tensor,
+    scales: torch.Tensor,
+    zeros: torch.Tensor,
+    fp16_w: torch.Tensor,
+    x: torch.Tensor,
+    outlier_k: float = 3.0,
+) -> torch.Tensor:
+    """Fused dynamic-precision GEMV with runtime outlier detection.
+
+    Outlier channels (|x_i - mean| > outlier_k * std) use the FP16 weight
+    columns; the rest use INT4 dequantization; one FP32 accumulation, one FP16
+    write, one kernel launch.
+
+    Args:
+        packed:    [d_out, d_in//2] uint8 packed INT4 weights.
+        scales:    [d_out, d_in//128] float16 per-group scales.
+        zeros:     [d_out, d_in//128] float16 per-group zero-points.
+        fp16_w:    [d_out, d_in] float16 original weights: contiguous, or the
+                   transpose of a column-major mirror (see build_colmajor).
+        x:         [d_in] float16 activation vector.
+        outlier_k: sigma threshold for outlier detection (default 3.0).
+
+    Returns:
+        y: [d_out] float16 output vector.
+    """
+    _require_extension()
+    return _C.split_gemv(packed, scales, zeros, fp16_w, _aligned(x), float(outlier_k))
+
+
+def int4_gemv(
+    packed: torch.Tensor,
+    scales: torch.Tensor,
+    zeros: torch.Tensor,
+    fp16_w: torch.Tensor,
+    x: torch.Tensor,
+) -> torch.Tensor:
+    """Dense INT4 GEMV without outlier handling (fp16_w used only for shape)."""
+    _require_extension()
+    return _C.int4_gemv(packed, scales, zeros, fp16_w, _aligned(x))
+
+
+def reference_gemv(fp16_w: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    """FP16 dense GEMV with FP32 accumulation: y = fp16_w @ x."""
+    _require_extension()
+    return _C.reference_gemv(_aligned(fp16_w), _aligned(x))
+
+
+def detect_outliers(x: torch.Tensor, outlier_k: float = 3.0):
+    """The outlier detector the split GEMV applies, standalone.
+
+    Returns (mask, indices, stats): mask [d_in] bool, indices int32 in the
+    reference's list order (stripe class (c//32)%4 == 0 ascending, then 1, 2, 3),
+    stats float32 [mean, threshold, unbiased variance, M2].  Synchronises to
+    read the count."""
+    _require_extension()
+    if x.dtype != torch.float16:
+        x = x.to(torch.float16)
+    x = _aligned(x.contiguous().reshape(-1))
+    words, idx, cnt, stats = _C.detect_outliers(x, float(outlier_k))
+    n = int(cnt.item())
+    bits = (words.view(-1, 1) >> torch.arange(32, device=x.device, dtype=torch.int32)) & 1
+    return bits.reshape(-1).bool(), idx[:n], stats
+
+
+class DynQuantLinear(nn.Module):
+    """Linear layer using the fused INT4/FP16 split-precision GEMV.
+
+    load_weight() quantizes the weights on the GPU and builds the column-major
+    FP16 mirror used for outlier columns; forward() detects outlier channels of
+    x at run time (no calibration) and runs one fused kernel.
+
+    ``fp16_w`` is the [d_out, d_in] transpose view of the column-major mirror:
+    same shape and values as the reference's row-major copy, one copy in memory.
+
+    Args:
+        d_in:      Input feature dimension.
+        d_out:     Output feature dimension.
+        outlier_k: Sigma threshold for outlier detection (default 3.0).
+    """
+
+    def __init__(self, d_in: int, d_out: int, outlier_k: float = 3.0) -> None:
+        super().__init__()
+        self.d_in = d_in
+        self.d_out = d_out
+        self.outlier_k = outlier_k
+        self._quantized = False
+        self.register_buffer("packed", None)
+        self.register_buffer("scales", None)
+        self.register_buffer("zeros", None)
+        self.register_buffer("fp16_w", None)
+
+    def load_weight(self, weight: torch.Tensor) -> None:
+        """Quantize and store an FP16 weight matrix.
+
+        Args:
+            weight: [d_out, d_in] float16 CUDA tensor.
+        """
+        assert weight.shape == (self.d_out, self.d_in), (
+            f"Expected weight shape ({self.d_out}, {self.d_in}), got {tuple(weight.shape)}")
+        _require_extension()
+        if weight.dtype != torch.float16:
+            weight = weight.to(torch.float16)
+        weight = _aligned(weight.contiguous())
+        packed, scales, zeros, _copy = _C.quantize_weights(weight)
+        del _copy
+        self.packed = packed
+        self.scales = scales
+        self.zeros = zeros
+        self.fp16_w = _C.build_colmajor(weight).t()
+        self._quantized = True
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        """y = W_split x for one activation vector.
+
+        Args:
+            x: [d_in] float16 activation vector.
+
+        Returns:
+            y: [d_out] float16.
+        """
+        if not self._quantized:
+            raise RuntimeError("Call load_weight() before forward()")
+        if x.dtype != torch.float16:
+            x = x.to(torch.float16)
+        if not x.is_contiguous():
+            x = x.contiguous()
+        return split_gemv(self.packed, self.scales, self.zeros, self.fp16_w, x, self.outlier_k)
+
+    def _load_from_state_dict(self, state_dict, prefix, local_metadata, strict, missing_keys,
+                              unexpected_keys, error_msgs):
+        # A fresh module holds None buffers; materialise them from the checkpoint
+        # (rebuilding the column-major mirror) so load_state_dict round-trips.
+        names = ("packed", "scales", "zeros", "fp16_w")
+        if not self._quantized and all(prefix + n in state_dict for n in names):
+            _require_extension()
+            dev = state_dict[prefix + "packed"].device
+            if dev.type != "cuda":
+                dev = torch.device("cuda", torch.cuda.current_device())
+            self.packed = state_dict[prefix + "packed"].to(dev).contiguous()
+            self.scales = state_dict[prefix + "scales"].to(dev, torch.float16).contiguous()
+            self.zeros = state_dict[prefix + "zeros"].to(dev, torch.float16).contiguous()
+            w = state_dict[prefix + "fp16_w"].to(dev, torch.float16).contiguous()
+            self.fp16_w = _C.build_colmajor(_aligned(w)).t()
+            self._quantized = True
+        super()._load_from_state_dict(state_dict, prefix, local_metadata, strict, missing_keys,
+                                      unexpected_keys, error_msgs)
+
+    def extra_repr(self) -> str:
+        return f"d_in={self.d_in}, d_out={self.d_out}, outlier_k={self.outlier_k}"

@@ -1,0 +1,109 @@
+"""ctypes binding of the C ABI in include/dq_abi.h (libdq_b200.so).
+
+This is the language-neutral boundary: plain pointers, sizes, a status code.
+It is what a non-Python caller binds (cgo, JNI, N-API, ...); the Python API in
+dyn_quant/__init__.py goes through the torch extension dyn_quant._C, which
+calls the same library.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libdq_b200.so")
+
+DQ_OK = 0
+DQ_ERR_INVALID_ARGUMENT = 1
+DQ_ERR_SHAPE = 2
+DQ_ERR_ALIGNMENT = 3
+DQ_ERR_UNSUPPORTED = 4
+DQ_ERR_CUDA = 5
+DQ_ERR_WORKSPACE = 6
+
+# Every symbol include/dq_abi.h declares (checked by the CPU test suite).
+EXPORTED_SYMBOLS = (
+    "dq_status_string",
+    "dq_last_cuda_error",
+    "dq_version",
+    "dq_max_d_in",
+    "dq_quantize",
+    "dq_build_colmajor",
+    "dq_split_gemv",
+    "dq_int4_gemv",
+    "dq_reference_gemv",
+    "dq_detect_outliers",
+)
+
+
+class DqWeights(C.Structure):
+    """dq_weights_t (include/dq_abi.h)."""
+
+    _fields_ = [
+        ("packed", C.c_void_p),
+        ("scales", C.c_void_p),
+        ("zeros", C.c_void_p),
+        ("fp16", C.c_void_p),
+        ("fp16_cm", C.c_void_p),
+        ("d_out", C.c_int32),
+        ("d_in", C.c_int32),
+    ]
+
+
+class DqError(RuntimeError):
+    def __init__(self, status: int, what: str, cuda_error: int = 0):
+        self.status = status
+        self.cuda_error = cuda_error
+        msg = f"{what} failed: {status_string(status)}"
+        if status == DQ_ERR_CUDA:
+            msg += f" (cudaError {cuda_error})"
+        super().__init__(msg)
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """Load libdq_b200.so; raises if it has not been built (there is no fallback)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"{LIB_PATH} not found: build it with `python dyn-quant_b200/build.py` "
+                "(the dyn-quant kernels have no CPU fallback)")
+        L = C.CDLL(LIB_PATH)
+        P, i32, f32, st = C.c_void_p, C.c_int32, C.c_float, C.c_int
+        L.dq_status_string.restype = C.c_char_p
+        L.dq_status_string.argtypes = [st]
+        L.dq_last_cuda_error.restype = C.c_int
+        L.dq_version.restype = C.c_int
+        L.dq_max_d_in.restype = i32
+        L.dq_quantize.restype = st
+        L.dq_quantize.argtypes = [P, i32, i32, P, P, P, P]
+        L.dq_build_colmajor.restype = st
+        L.dq_build_colmajor.argtypes = [P, i32, i32, P, P]
+        L.dq_split_gemv.restype = st
+        L.dq_split_gemv.argtypes = [C.POINTER(DqWeights), P, P, f32, P]
+        L.dq_int4_gemv.restype = st
+        L.dq_int4_gemv.argtypes = [C.POINTER(DqWeights), P, P, P]
+        L.dq_reference_gemv.restype = st
+        L.dq_reference_gemv.argtypes = [P, P, P, i32, i32, P]
+        L.dq_detect_outliers.restype = st
+        L.dq_detect_outliers.argtypes = [P, i32, f32, P, P, P, P, P]
+        _lib = L
+    return _lib
+
+
+def status_string(status: int) -> str:
+    return lib().dq_status_string(int(status)).decode()
+
+
+def check(status: int, what: str) -> None:
+    if status != DQ_OK:
+        raise DqError(status, what, lib().dq_last_cuda_error() if status == DQ_ERR_CUDA else 0)
+
+
+def weights(packed: int, scales: int, zeros: int, fp16: int | None, fp16_cm: int | None,
+            d_out: int, d_in: int) -> DqWeights:
+    """Build a dq_weights_t from raw device addresses."""
+    return DqWeights(packed, scales, zeros, fp16 or None, fp16_cm or None, d_out, d_in)

@@ -1,0 +1,147 @@
+/*
+ * dq_abi.h -- C ABI of the dyn-quant B200 library (libdq_b200.so).
+ *
+ * Plain C: pointers, sizes and a status code; no CUDA or torch types.  Device
+ * buffers are raw device pointers; FP16 values are IEEE binary16 bit patterns
+ * (uint16_t); `stream` is a cudaStream_t passed as void* (NULL = legacy
+ * default stream).  Every call is stream-ordered and asynchronous: it enqueues
+ * work and returns; nothing allocates device memory and nothing synchronises.
+ *
+ * Each entry point names the reference interface it replaces (paths inside the
+ * dyn-quant project).  The reference's launchers return void and check no CUDA
+ * error (src/split_gemv.cu:160-198); here every call validates its arguments
+ * and returns a dq_status_t, with the CUDA error of a failed launch available
+ * from dq_last_cuda_error().
+ *
+ * Formats (bit-compatible with the reference, src/quant_format.cuh:12-38):
+ *   packed   uint8  [d_out][d_in/2]   column 2j in bits 3:0 of byte j, 2j+1 in bits 7:4
+ *   scales   f16    [d_out][d_in/128] per-group scale
+ *   zeros    f16    [d_out][d_in/128] per-group zero-point; w = scale * (code - zero)
+ *   fp16     f16    [d_out][d_in]     original weights, row-major (as the reference keeps them)
+ *   fp16_cm  f16    [d_in][d_out]     the same weights column-major (the outlier-column
+ *                                     mirror: one outlier column is d_out contiguous halves)
+ * Alignment: packed, x, fp16, fp16_cm and w16 need 16-byte aligned pointers;
+ * scales and zeros 2-byte.  d_in must be a positive multiple of 128.
+ */
+#ifndef DQ_ABI_H_
+#define DQ_ABI_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DQ_API __attribute__((visibility("default")))
+#else
+#define DQ_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum dq_status_t {
+    DQ_OK = 0,
+    DQ_ERR_INVALID_ARGUMENT = 1, /* null pointer where one is required, bad k */
+    DQ_ERR_SHAPE = 2,            /* d_in not a positive multiple of 128, negative d_out, ... */
+    DQ_ERR_ALIGNMENT = 3,        /* a pointer misses its required alignment */
+    DQ_ERR_UNSUPPORTED = 4,      /* shape beyond what the kernel supports (see dq_max_d_in) */
+    DQ_ERR_CUDA = 5,             /* a CUDA call failed: see dq_last_cuda_error() */
+    DQ_ERR_WORKSPACE = 6         /* workspace missing or too small */
+} dq_status_t;
+
+/* Non-owning view of one quantized weight matrix (the reference's
+ * QuantizedWeights, src/quant_format.cuh:12-23, plus the optional mirror).
+ * At least one of fp16 / fp16_cm must be set for the split GEMV; the
+ * column-major mirror is the fast path for outlier columns. */
+typedef struct dq_weights_t {
+    const uint8_t* packed;
+    const uint16_t* scales;
+    const uint16_t* zeros;
+    const uint16_t* fp16;    /* row-major [d_out][d_in], may be NULL if fp16_cm is set */
+    const uint16_t* fp16_cm; /* column-major [d_in][d_out], may be NULL */
+    int32_t d_out;
+    int32_t d_in;
+} dq_weights_t;
+
+/* Human-readable name of a status code (static string). */
+DQ_API const char* dq_status_string(dq_status_t s);
+
+/* The cudaError_t (as int) of the last call on this thread that returned
+ * DQ_ERR_CUDA, or 0. */
+DQ_API int dq_last_cuda_error(void);
+
+/* Library version as 10000*major + 100*minor + patch. */
+DQ_API int dq_version(void);
+
+/* Largest d_in the single-pass GEMV kernels accept on this build (the
+ * activation vector and its per-group tables live in shared memory). */
+DQ_API int32_t dq_max_d_in(void);
+
+/*
+ * Quantize an FP16 weight matrix on the device, bit-exactly as
+ * quantize_weights_host does on the host (src/quant_format.cuh:58-97):
+ * per row and 128-column group, min/max -> scale = range/15 (1 if range <
+ * 1e-8), zero = -min/scale, codes = clamp(trunc((v-min)/scale + 0.5), 0, 15).
+ * Replaces: quantize_weights_host (src/quant_format.cuh:58), and the host
+ * round trip of the torch binding (csrc/bindings.cpp:26-75).
+ * w16: device [d_out][d_in] f16.  Outputs are caller-allocated device buffers.
+ */
+DQ_API dq_status_t dq_quantize(const uint16_t* w16, int32_t d_out, int32_t d_in, uint8_t* packed,
+                        uint16_t* scales, uint16_t* zeros, void* stream);
+
+/*
+ * Build the column-major FP16 mirror fp16_cm[d_in][d_out] of w16[d_out][d_in].
+ * No reference counterpart: the reference gathers outlier columns from the
+ * row-major copy (src/split_gemv.cu:125,131).  Used by DynQuantLinear.load_weight.
+ */
+DQ_API dq_status_t dq_build_colmajor(const uint16_t* w16, int32_t d_out, int32_t d_in, uint16_t* fp16_cm,
+                              void* stream);
+
+/*
+ * Fused dynamic-precision GEMV, batch 1: y = W_split x.
+ * Channel c is an outlier when |x_c - mean(x)| > outlier_k * std(x) (unbiased
+ * variance floored at 1e-8, strict >), keeping at most d_in/16 outliers per
+ * 32-column stripe class as the reference's warp capacity does
+ * (src/outlier_detect.cuh:160-178).  Outlier columns use the FP16 weights, the
+ * rest the INT4 codes; FP32 accumulation; y is rounded to FP16 once.
+ * Replaces: launch_split_gemv (src/split_gemv.cu:160-198, src/split_gemv.cuh:10).
+ * x: device [d_in] f16, y: device [d_out] f16.
+ */
+DQ_API dq_status_t dq_split_gemv(const dq_weights_t* w, const uint16_t* x, uint16_t* y, float outlier_k,
+                          void* stream);
+
+/*
+ * Dense INT4 GEMV (no outlier handling): y = dequant(W) x.
+ * Replaces: launch_int4_gemv (src/int4_gemv.cu:80-100, src/int4_gemv.cuh:9).
+ * Only packed/scales/zeros of *w are read.
+ */
+DQ_API dq_status_t dq_int4_gemv(const dq_weights_t* w, const uint16_t* x, uint16_t* y, void* stream);
+
+/*
+ * FP16 dense GEMV with FP32 accumulation: y = W16 x.
+ * Replaces: launch_reference_gemv (src/reference_gemv.cu:60-78, src/reference_gemv.cuh:10).
+ */
+DQ_API dq_status_t dq_reference_gemv(const uint16_t* w16, const uint16_t* x, uint16_t* y, int32_t d_out,
+                              int32_t d_in, void* stream);
+
+/*
+ * Standalone outlier detector over x[d_in] with the statistics, threshold and
+ * capacity rule the split GEMV uses (bit-identical to the mask the GEMV
+ * applies).  Replaces: scan_outliers_block (src/outlier_detect.cuh:104-205),
+ * which in the reference exists only inside the GEMV kernel.
+ * Outputs (device, caller-allocated; any may be NULL):
+ *   mask_words [d_in/32] uint32  bit (c % 32) of word c/32 set for outlier c
+ *   indices    [d_in/4]  int32   outlier indices in the reference's list order
+ *                                (stripe class 0 ascending, then 1, 2, 3)
+ *   count      [1]       int32   number of outliers (<= d_in/4)
+ *   stats      [4]       float   mean, threshold, unbiased variance, M2
+ */
+DQ_API dq_status_t dq_detect_outliers(const uint16_t* x, int32_t d_in, float outlier_k,
+                               uint32_t* mask_words, int32_t* indices, int32_t* count,
+                               float* stats, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DQ_ABI_H_ */

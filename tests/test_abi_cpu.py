@@ -1,0 +1,76 @@
+"""The C-ABI library on a host without a GPU: it loads, exports every symbol
+include/dq_abi.h declares, and validates arguments before touching CUDA."""
+import ctypes as C
+import os
+import re
+import subprocess
+
+import pytest
+
+from dyn_quant import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "dq_abi.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"DQ_API\s+[\w\s\*]+?\b(dq_\w+)\s*\(", text)))
+
+
+def test_header_declares_the_exported_list():
+    assert declared_functions() == sorted(_lib.EXPORTED_SYMBOLS)
+
+
+def test_library_exports_every_declared_symbol():
+    L = _lib.lib()
+    for name in declared_functions():
+        assert hasattr(L, name), name
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True, text=True,
+                         check=True).stdout
+    exported = set(re.findall(r"\bT (dq_\w+)", out))
+    assert set(declared_functions()) <= exported
+    # nothing else leaks: the kernels' C++ symbols stay hidden
+    assert exported == set(declared_functions())
+
+
+def test_status_strings_and_version():
+    assert _lib.status_string(0) == "DQ_OK"
+    assert _lib.status_string(_lib.DQ_ERR_CUDA) == "DQ_ERR_CUDA"
+    assert _lib.status_string(99) == "DQ_ERR_UNKNOWN"
+    L = _lib.lib()
+    assert L.dq_version() >= 100
+    assert L.dq_max_d_in() >= 28672  # the Llama-2-70B down-projection width
+
+
+def test_validation_happens_before_any_cuda_call():
+    L = _lib.lib()
+    w = _lib.weights(16, 16, 16, 16, None, 16, 100)
+    assert L.dq_split_gemv(C.byref(w), C.c_void_p(16), C.c_void_p(16), 3.0, None) == _lib.DQ_ERR_SHAPE
+    w = _lib.weights(16, 16, 16, None, None, 16, 128)
+    assert L.dq_split_gemv(C.byref(w), C.c_void_p(16), C.c_void_p(16), 3.0, None) == _lib.DQ_ERR_INVALID_ARGUMENT
+    w = _lib.weights(17, 16, 16, 16, None, 16, 128)
+    assert L.dq_split_gemv(C.byref(w), C.c_void_p(16), C.c_void_p(16), 3.0, None) == _lib.DQ_ERR_ALIGNMENT
+    w = _lib.weights(16, 16, 16, 16, None, 16, 1 << 20)
+    assert L.dq_split_gemv(C.byref(w), C.c_void_p(16), C.c_void_p(16), 3.0, None) == _lib.DQ_ERR_UNSUPPORTED
+    assert L.dq_split_gemv(None, C.c_void_p(16), C.c_void_p(16), 3.0, None) == _lib.DQ_ERR_INVALID_ARGUMENT
+    w = _lib.weights(16, 16, 16, 16, None, -1, 128)
+    assert L.dq_split_gemv(C.byref(w), C.c_void_p(16), C.c_void_p(16), 3.0, None) == _lib.DQ_ERR_SHAPE
+    # d_out == 0 is an empty GEMV: nothing to launch
+    w = _lib.weights(16, 16, 16, 16, None, 0, 128)
+    assert L.dq_split_gemv(C.byref(w), C.c_void_p(16), C.c_void_p(16), 3.0, None) == _lib.DQ_OK
+    assert L.dq_int4_gemv(C.byref(w), C.c_void_p(16), C.c_void_p(16), None) == _lib.DQ_OK
+    assert L.dq_reference_gemv(C.c_void_p(16), C.c_void_p(16), C.c_void_p(16), 0, 128, None) == _lib.DQ_OK
+    assert L.dq_reference_gemv(C.c_void_p(16), C.c_void_p(16), C.c_void_p(16), 4, 100, None) == _lib.DQ_ERR_SHAPE
+    assert L.dq_quantize(C.c_void_p(16), 4, 100, C.c_void_p(16), C.c_void_p(16), C.c_void_p(16), None) == _lib.DQ_ERR_SHAPE
+    assert L.dq_quantize(C.c_void_p(18), 4, 128, C.c_void_p(16), C.c_void_p(16), C.c_void_p(16), None) == _lib.DQ_ERR_ALIGNMENT
+    assert L.dq_quantize(None, 4, 128, C.c_void_p(16), C.c_void_p(16), C.c_void_p(16), None) == _lib.DQ_ERR_INVALID_ARGUMENT
+    assert L.dq_detect_outliers(None, 128, 3.0, None, None, None, None, None) == _lib.DQ_ERR_INVALID_ARGUMENT
+    assert L.dq_detect_outliers(C.c_void_p(16), 100, 3.0, None, None, None, None, None) == _lib.DQ_ERR_SHAPE
+    assert L.dq_build_colmajor(C.c_void_p(16), 4, 100, C.c_void_p(16), None) == _lib.DQ_ERR_SHAPE
+
+
+def test_check_raises_dqerror():
+    with pytest.raises(_lib.DqError) as e:
+        _lib.check(_lib.DQ_ERR_SHAPE, "dq_split_gemv")
+    assert "DQ_ERR_SHAPE" in str(e.value)

@@ -1,0 +1,146 @@
+"""The Python API (dyn_quant.*, DynQuantLinear) on the GPU, mirroring the
+reference's tests/test_python.py (its three tests, with the FP32 reference
+computed in one dtype -- the reference's own version mixes fp16 and fp32 in
+torch.matmul and raises before asserting) plus parity against the oracle."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+import dyn_quant  # noqa: E402
+from dyn_quant import DynQuantLinear, quantize, split_gemv  # noqa: E402
+import oracle as O  # noqa: E402
+from dyn_quant import synth  # noqa: E402
+from dq_testutil import check_y, host  # noqa: E402
+
+D_IN = 4096
+D_OUT = 4096
+OUTLIER_FRAC = 0.05
+OUTLIER_MAG = 20.0
+OUTLIER_K = 3.0
+COSINE_THRESHOLD = 0.9999
+
+
+def generate_outlier_activation(d_in, frac, mag):
+    x = torch.randn(d_in, dtype=torch.float16, device="cuda")
+    n_out = int(frac * d_in)
+    x[:n_out] = (torch.randn(n_out, device="cuda") * mag).half()
+    return x
+
+
+def cosine_sim(a, b):
+    return float(torch.nn.functional.cosine_similarity(a.float().unsqueeze(0), b.float().unsqueeze(0)).item())
+
+
+def fp32_ref(weight, x):
+    return (weight.float() @ x.float()).half()
+
+
+def test_dyn_quant_linear():
+    torch.manual_seed(0)
+    weight = torch.randn(D_OUT, D_IN, dtype=torch.float16, device="cuda") * 0.02
+    x = generate_outlier_activation(D_IN, OUTLIER_FRAC, OUTLIER_MAG)
+    linear = DynQuantLinear(D_IN, D_OUT, outlier_k=OUTLIER_K)
+    linear.load_weight(weight)
+    linear.cuda()
+    y = linear(x)
+    assert y.shape == (D_OUT,) and y.dtype == torch.float16
+    assert cosine_sim(y, fp32_ref(weight, x)) >= COSINE_THRESHOLD
+
+
+def test_functional_api():
+    torch.manual_seed(1)
+    weight = torch.randn(D_OUT, D_IN, dtype=torch.float16, device="cuda") * 0.02
+    x = generate_outlier_activation(D_IN, OUTLIER_FRAC, OUTLIER_MAG)
+    packed, scales, zeros, fp16_copy = quantize(weight)
+    assert packed.shape == (D_OUT, D_IN // 2) and packed.dtype == torch.uint8
+    assert scales.shape == (D_OUT, D_IN // 128) and zeros.dtype == torch.float16
+    assert torch.equal(fp16_copy, weight)
+    y = split_gemv(packed, scales, zeros, fp16_copy, x, OUTLIER_K)
+    assert cosine_sim(y, fp32_ref(weight, x)) >= COSINE_THRESHOLD
+
+
+def test_int4_vs_split_with_outliers():
+    torch.manual_seed(2)
+    weight = torch.randn(D_OUT, D_IN, dtype=torch.float16, device="cuda") * 0.02
+    x = generate_outlier_activation(D_IN, OUTLIER_FRAC, OUTLIER_MAG)
+    packed, scales, zeros, fp16_copy = quantize(weight)
+    y_ref = fp32_ref(weight, x)
+    y_int4 = dyn_quant.int4_gemv(packed, scales, zeros, fp16_copy, x)
+    y_split = dyn_quant.split_gemv(packed, scales, zeros, fp16_copy, x, OUTLIER_K)
+    assert cosine_sim(y_split, y_ref) >= COSINE_THRESHOLD
+    assert cosine_sim(y_split, y_ref) > cosine_sim(y_int4, y_ref)
+
+
+@pytest.mark.parametrize("d_out,d_in,frac", [(4096, 4096, 0.02), (11008, 4096, 0.01), (4096, 11008, 0.01)])
+def test_module_matches_oracle(d_out, d_in, frac):
+    w = synth.weights(d_out, d_in, seed=0)
+    x = synth.activation(d_in, frac, seed=1)
+    lin = DynQuantLinear(d_in, d_out, 3.0)
+    lin.load_weight(torch.from_numpy(w).cuda())
+    y = host(lin(torch.from_numpy(x).cuda()))
+    packed, scales, zeros = O.quantize(w)
+    assert np.array_equal(host(lin.packed), packed)
+    assert np.array_equal(host(lin.scales).view(np.uint16), scales.view(np.uint16))
+    mask = host(dyn_quant.detect_outliers(torch.from_numpy(x).cuda(), 3.0)[0])
+    y16, y32 = O.split_gemv_masked(packed, scales, zeros, w, x, mask.astype(np.uint8))
+    check_y(y, y16, y32, what="DynQuantLinear")
+    y16o, _, _ = O.split_gemv(packed, scales, zeros, w, x, 3.0)
+    check_y(y, y16o, what="DynQuantLinear vs oracle detection")
+
+
+def test_fp16_w_is_a_view_of_the_mirror():
+    w = synth.weights(256, 512, seed=4)
+    lin = DynQuantLinear(512, 256)
+    lin.load_weight(torch.from_numpy(w).cuda())
+    assert lin.fp16_w.shape == (256, 512)
+    assert not lin.fp16_w.is_contiguous() and lin.fp16_w.t().is_contiguous()
+    assert np.array_equal(host(lin.fp16_w).view(np.uint16), w.view(np.uint16))
+    # the functional API takes either layout and gives the same bits
+    x = torch.from_numpy(synth.activation(512, 0.03, seed=5)).cuda()
+    a = split_gemv(lin.packed, lin.scales, lin.zeros, lin.fp16_w, x, 3.0)
+    b = split_gemv(lin.packed, lin.scales, lin.zeros, lin.fp16_w.contiguous(), x, 3.0)
+    assert torch.equal(a, b)
+
+
+def test_state_dict_round_trip():
+    w = torch.from_numpy(synth.weights(512, 1024, seed=6)).cuda()
+    x = torch.from_numpy(synth.activation(1024, 0.02, seed=7)).cuda()
+    a = DynQuantLinear(1024, 512, 2.5)
+    a.load_weight(w)
+    sd = a.state_dict()
+    b = DynQuantLinear(1024, 512, 2.5)
+    b.load_state_dict(sd)
+    assert torch.equal(a(x), b(x))
+    c = DynQuantLinear(1024, 512, 2.5)
+    c.load_state_dict({k: v.cpu() for k, v in sd.items()})
+    assert torch.equal(a(x), c(x))
+
+
+def test_errors_raise_runtime_error():
+    lin = DynQuantLinear(256, 16)
+    with pytest.raises(RuntimeError):
+        lin(torch.zeros(256, dtype=torch.float16, device="cuda"))
+    w = torch.zeros(16, 256, dtype=torch.float16, device="cuda")
+    p, s, z, f = quantize(w)
+    with pytest.raises(RuntimeError):
+        split_gemv(p, s, z, f, torch.zeros(128, dtype=torch.float16, device="cuda"))
+    with pytest.raises(RuntimeError):
+        split_gemv(p, s, z, f, torch.zeros(256, dtype=torch.float32, device="cuda"))
+    with pytest.raises(RuntimeError):
+        split_gemv(p.cpu(), s, z, f, torch.zeros(256, dtype=torch.float16, device="cuda"))
+    with pytest.raises(RuntimeError):
+        quantize(torch.zeros(16, 100, dtype=torch.float16, device="cuda"))
+
+
+def test_misaligned_activation_view_is_rehomed():
+    w = synth.weights(64, 256, seed=8)
+    p, s, z, f = quantize(torch.from_numpy(w).cuda())
+    buf = torch.from_numpy(synth.activation(257, 0.0, seed=9)).cuda()
+    x = buf[1:]  # 2-byte offset view
+    assert x.data_ptr() % 16 != 0
+    y1 = split_gemv(p, s, z, f, x, 3.0)
+    y2 = split_gemv(p, s, z, f, x.clone(), 3.0)
+    assert torch.equal(y1, y2)
