@@ -100,7 +100,7 @@ dq_status_t dq_build_colmajor(const uint16_t* w16, int32_t d_out, int32_t d_in, 
 }
 
 static dq_status_t check_weights(const dq_weights_t* w, const uint16_t* x, const uint16_t* y,
-                                 bool need_fp16) {
+                                 bool need_fp16, const void* workspace, size_t workspace_bytes) {
     if (!w || !x || !y) return DQ_ERR_INVALID_ARGUMENT;
     dq_status_t st = check_dims(w->d_out, w->d_in);
     if (st != DQ_OK) return st;
@@ -111,22 +111,54 @@ static dq_status_t check_weights(const dq_weights_t* w, const uint16_t* x, const
     if (!aligned16(w->packed) || !aligned16(x) || !aligned2(y) || !aligned2(w->scales) ||
         !aligned2(w->zeros))
         return DQ_ERR_ALIGNMENT;
-    if (need_fp16 && ((w->fp16 && !aligned2(w->fp16)) || (w->fp16_cm && !aligned2(w->fp16_cm))))
+    if (need_fp16 && ((w->fp16 && !aligned16(w->fp16)) || (w->fp16_cm && !aligned16(w->fp16_cm))))
         return DQ_ERR_ALIGNMENT;
+    if (w->native && !aligned16(w->native)) return DQ_ERR_ALIGNMENT;
+    if (!workspace || workspace_bytes < ws_layout(w->d_out, w->d_in).total) return DQ_ERR_WORKSPACE;
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return DQ_ERR_ALIGNMENT;
     return DQ_OK;
 }
 
-dq_status_t dq_split_gemv(const dq_weights_t* w, const uint16_t* x, uint16_t* y, float outlier_k,
-                          void* stream) {
-    dq_status_t st = check_weights(w, x, y, true);
-    if (st != DQ_OK || w->d_out == 0) return st;
-    return launch_gemv_m1(*w, x, y, outlier_k, true, static_cast<cudaStream_t>(stream));
+size_t dq_native_bytes(int32_t d_out, int32_t d_in) {
+    if (check_dims(d_out, d_in) != DQ_OK) return 0;
+    return native_bytes(d_out, d_in);
 }
 
-dq_status_t dq_int4_gemv(const dq_weights_t* w, const uint16_t* x, uint16_t* y, void* stream) {
-    dq_status_t st = check_weights(w, x, y, false);
-    if (st != DQ_OK || w->d_out == 0) return st;
-    return launch_gemv_m1(*w, x, y, 0.f, false, static_cast<cudaStream_t>(stream));
+dq_status_t dq_build_native(const uint8_t* packed, const uint16_t* scales, const uint16_t* zeros,
+                            int32_t d_out, int32_t d_in, uint8_t* native, void* stream) {
+    dq_status_t st = check_dims(d_out, d_in);
+    if (st != DQ_OK) return st;
+    if (d_out == 0) return DQ_OK;
+    if (!packed || !scales || !zeros || !native) return DQ_ERR_INVALID_ARGUMENT;
+    if (!aligned16(packed) || !aligned2(scales) || !aligned2(zeros) || !aligned16(native))
+        return DQ_ERR_ALIGNMENT;
+    return launch_build_native(packed, scales, zeros, d_out, d_in, native, static_cast<cudaStream_t>(stream));
+}
+
+dq_status_t dq_read_device_error(uint32_t* word, int clear) {
+    if (!word) return DQ_ERR_INVALID_ARGUMENT;
+    return read_device_error(word, clear != 0);
+}
+
+size_t dq_workspace_bytes(int32_t d_out, int32_t d_in) {
+    if (check_dims(d_out, d_in) != DQ_OK) return 0;
+    return ws_layout(d_out, d_in).total;
+}
+
+dq_status_t dq_split_gemv(const dq_weights_t* w, const uint16_t* x, uint16_t* y, float outlier_k,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+    if (w && w->d_out == 0 && check_dims(w->d_out, w->d_in) == DQ_OK) return DQ_OK;
+    dq_status_t st = check_weights(w, x, y, true, workspace, workspace_bytes);
+    if (st != DQ_OK) return st;
+    return launch_gemv_b1(*w, x, y, outlier_k, true, workspace, static_cast<cudaStream_t>(stream));
+}
+
+dq_status_t dq_int4_gemv(const dq_weights_t* w, const uint16_t* x, uint16_t* y, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+    if (w && w->d_out == 0 && check_dims(w->d_out, w->d_in) == DQ_OK) return DQ_OK;
+    dq_status_t st = check_weights(w, x, y, false, workspace, workspace_bytes);
+    if (st != DQ_OK) return st;
+    return launch_gemv_b1(*w, x, y, 0.f, false, workspace, static_cast<cudaStream_t>(stream));
 }
 
 dq_status_t dq_reference_gemv(const uint16_t* w16, const uint16_t* x, uint16_t* y, int32_t d_out,

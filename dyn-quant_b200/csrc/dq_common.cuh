@@ -141,3 +141,123 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 }
 
 }  // namespace dq
+
+// ---------------------------------------------------------------------------
+// Bulk async copies (TMA, non-tensor form) and mbarriers
+// ---------------------------------------------------------------------------
+namespace dq {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+// Makes the initialised barriers visible to the async (TMA) proxy.
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: gives up after ~2^31 SM cycles (about a second) and returns false.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - t0 > (1ll << 31)) return false;
+    }
+    return true;
+}
+
+// Global -> shared bulk copy completing on an mbarrier (16-byte aligned
+// addresses, size a multiple of 16).
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
+
+}  // namespace dq
+
+namespace dq {
+
+// Biased INT4 -> FP16 dequantisation for the batch-1 kernel: one shift and
+// four lop3 per packed word, keeping the f16 exponent bias (removed per group
+// in FP32 by the caller):
+//   lo0 = (1024 + q0, 1024 + q4)        lo1 = (1024 + q2, 1024 + q6)
+//   hi0 = (1024 + 16 q1, 1024 + 16 q5)  hi1 = (1024 + 16 q3, 1024 + 16 q7)
+// All values are exact in f16, so the MMA products with x are exact.
+struct Biased4 {
+    uint32_t lo0, lo1, hi0, hi1;
+};
+
+__device__ __forceinline__ Biased4 biased_word(uint32_t w) {
+    constexpr uint32_t kMagic = 0x64006400u;
+    const uint32_t w8 = w >> 8;
+    Biased4 r;
+    r.lo0 = lop3_and_or(w, 0x000F000Fu, kMagic);
+    r.lo1 = lop3_and_or(w8, 0x000F000Fu, kMagic);
+    r.hi0 = lop3_and_or(w, 0x00F000F0u, kMagic);
+    r.hi1 = lop3_and_or(w8, 0x00F000F0u, kMagic);
+    return r;
+}
+
+}  // namespace dq
+
+namespace dq {
+
+// Adds expected transaction bytes to the barrier's current phase without arriving.
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// 16-byte asynchronous global -> shared copy (L2 only), tracked by the
+// thread's cp.async group.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+// Makes the barrier's current phase also wait for this thread's prior
+// cp.async copies (pending count +1 now, arrive when they complete).
+__device__ __forceinline__ void cp_async_mbar_arrive(uint32_t bar) {
+    asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// Programmatic dependent launch: let the next kernel in the stream start its
+// prologue / wait until the preceding kernel's results are visible.
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ float ldcg_f32(const float* p) {
+    float v;
+    asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
+
+}  // namespace dq

@@ -1,16 +1,37 @@
 // torch_ext.cpp -- the dyn_quant._C torch extension: the reference's four
 // bindings (csrc/bindings.cpp:184-193 of dyn-quant) with the same names,
 // argument meaning and RuntimeError behaviour, implemented over the C ABI of
-// libdq_b200.so.  Extra functions: build_colmajor, detect_outliers.
+// libdq_b200.so.  Extra functions: build_colmajor, build_native, detect_outliers.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <map>
+#include <mutex>
 #include <tuple>
+#include <utility>
 
 #include "../../include/dq_abi.h"
 
 namespace {
+
+// Zero-filled GEMV workspace per (device, stream), grown on demand.  The
+// kernels leave it zeroed after every call, so it is reused as is; calls on one
+// stream are ordered, and each stream has its own.  Kept for the life of the
+// process (never destroyed: no CUDA calls during static destruction).
+torch::Tensor& workspace_for(const torch::Device& dev, void* stream, size_t bytes) {
+    static std::mutex mu;
+    static auto* cache = new std::map<std::pair<int, void*>, torch::Tensor>();
+    std::lock_guard<std::mutex> lock(mu);
+    const auto key = std::make_pair(static_cast<int>(dev.index()), stream);
+    auto it = cache->find(key);
+    if (it == cache->end() || static_cast<size_t>(it->second.numel()) < bytes) {
+        const int64_t n = static_cast<int64_t>((bytes + 4095) / 4096 * 4096);
+        (*cache)[key] = torch::zeros({n}, torch::TensorOptions().dtype(torch::kUInt8).device(dev));
+        it = cache->find(key);
+    }
+    return it->second;
+}
 
 void check_status(dq_status_t s, const char* what) {
     if (s == DQ_OK) return;
@@ -57,7 +78,8 @@ Fp16View fp16_view(const torch::Tensor& w) {
 // csrc/bindings.cpp:94-111 plus the shape checks the reference leaves implicit.
 dq_weights_t make_weights(const torch::Tensor& packed, const torch::Tensor& scales,
                           const torch::Tensor& zeros, const torch::Tensor& fp16_w,
-                          const torch::Tensor& x, bool need_fp16) {
+                          const torch::Tensor& x, bool need_fp16,
+                          const c10::optional<torch::Tensor>& native) {
     TORCH_CHECK(fp16_w.dim() == 2, "fp16_weights must be 2D");
     check_fp16_contiguous(scales, "scales");
     check_fp16_contiguous(zeros, "zeros");
@@ -82,6 +104,15 @@ dq_weights_t make_weights(const torch::Tensor& packed, const torch::Tensor& scal
         Fp16View v = fp16_view(fp16_w);
         w.fp16 = v.rm;
         w.fp16_cm = v.cm;
+    }
+    if (native.has_value() && native->defined()) {
+        const auto& nv = *native;
+        TORCH_CHECK(nv.is_cuda() && nv.is_contiguous() && nv.device() == x.device(),
+                    "native must be a contiguous CUDA tensor on x's device");
+        TORCH_CHECK(static_cast<size_t>(nv.numel() * nv.element_size()) ==
+                        dq_native_bytes(static_cast<int32_t>(d_out), static_cast<int32_t>(d_in)),
+                    "native layout size does not match the weight shape");
+        w.native = reinterpret_cast<const uint8_t*>(nv.data_ptr());
     }
     w.d_out = static_cast<int32_t>(d_out);
     w.d_in = static_cast<int32_t>(d_in);
@@ -127,11 +158,16 @@ torch::Tensor build_colmajor(const torch::Tensor& weight) {
 // split_gemv(packed, scales, zeros, fp16_weights, x, outlier_k) -> y [d_out] f16
 torch::Tensor split_gemv(const torch::Tensor& packed, const torch::Tensor& scales,
                          const torch::Tensor& zeros, const torch::Tensor& fp16_w,
-                         const torch::Tensor& x, double outlier_k) {
-    dq_weights_t w = make_weights(packed, scales, zeros, fp16_w, x, true);
+                         const torch::Tensor& x, double outlier_k,
+                         const c10::optional<torch::Tensor>& native) {
+    dq_weights_t w = make_weights(packed, scales, zeros, fp16_w, x, true, native);
     const at::cuda::CUDAGuard guard(x.device());
     auto y = torch::empty({w.d_out}, x.options());
-    check_status(dq_split_gemv(&w, h16(x), h16m(y), static_cast<float>(outlier_k), stream_of(x)),
+    void* stream = stream_of(x);
+    const size_t wsb = dq_workspace_bytes(w.d_out, w.d_in);
+    auto& ws = workspace_for(x.device(), stream, wsb);
+    check_status(dq_split_gemv(&w, h16(x), h16m(y), static_cast<float>(outlier_k), ws.data_ptr(),
+                               static_cast<size_t>(ws.numel()), stream),
                  "split_gemv");
     return y;
 }
@@ -139,12 +175,36 @@ torch::Tensor split_gemv(const torch::Tensor& packed, const torch::Tensor& scale
 // int4_gemv(packed, scales, zeros, fp16_weights, x) -> y [d_out] f16
 torch::Tensor int4_gemv(const torch::Tensor& packed, const torch::Tensor& scales,
                         const torch::Tensor& zeros, const torch::Tensor& fp16_w,
-                        const torch::Tensor& x) {
-    dq_weights_t w = make_weights(packed, scales, zeros, fp16_w, x, false);
+                        const torch::Tensor& x, const c10::optional<torch::Tensor>& native) {
+    dq_weights_t w = make_weights(packed, scales, zeros, fp16_w, x, false, native);
     const at::cuda::CUDAGuard guard(x.device());
     auto y = torch::empty({w.d_out}, x.options());
-    check_status(dq_int4_gemv(&w, h16(x), h16m(y), stream_of(x)), "int4_gemv");
+    void* stream = stream_of(x);
+    const size_t wsb = dq_workspace_bytes(w.d_out, w.d_in);
+    auto& ws = workspace_for(x.device(), stream, wsb);
+    check_status(dq_int4_gemv(&w, h16(x), h16m(y), ws.data_ptr(), static_cast<size_t>(ws.numel()), stream),
+                 "int4_gemv");
     return y;
+}
+
+// build_native(packed, scales, zeros) -> the unit layout the GEMV kernels stream (uint8 tensor)
+torch::Tensor build_native(const torch::Tensor& packed, const torch::Tensor& scales, const torch::Tensor& zeros) {
+    check_fp16_contiguous(scales, "scales");
+    check_fp16_contiguous(zeros, "zeros");
+    TORCH_CHECK(packed.is_cuda() && packed.is_contiguous() && packed.scalar_type() == at::kByte && packed.dim() == 2,
+                "packed must be a contiguous 2D CUDA uint8 tensor");
+    const int64_t d_out = packed.size(0), d_in = packed.size(1) * 2;
+    TORCH_CHECK(d_in % 128 == 0, "d_in must be divisible by 128");
+    TORCH_CHECK(scales.numel() == d_out * (d_in / 128) && zeros.numel() == scales.numel(),
+                "scales/zeros must hold d_out * d_in/128 values");
+    const at::cuda::CUDAGuard guard(packed.device());
+    const size_t bytes = dq_native_bytes(static_cast<int32_t>(d_out), static_cast<int32_t>(d_in));
+    auto out = torch::empty({static_cast<int64_t>(bytes)}, packed.options());
+    check_status(dq_build_native(reinterpret_cast<const uint8_t*>(packed.data_ptr()), h16(scales), h16(zeros),
+                                 static_cast<int32_t>(d_out), static_cast<int32_t>(d_in),
+                                 reinterpret_cast<uint8_t*>(out.data_ptr()), stream_of(packed)),
+                 "build_native");
+    return out;
 }
 
 // reference_gemv(fp16_weights, x) -> y [d_out] f16   (csrc/bindings.cpp:162-182)
@@ -189,8 +249,12 @@ detect_outliers(const torch::Tensor& x, double outlier_k) {
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("quantize_weights", &quantize_weights, "Quantize FP16 weight matrix to INT4 packed format");
-    m.def("split_gemv", &split_gemv, "Fused dynamic-precision GEMV with runtime outlier detection");
-    m.def("int4_gemv", &int4_gemv, "Dense INT4 GEMV baseline");
+    m.def("split_gemv", &split_gemv, "Fused dynamic-precision GEMV with runtime outlier detection",
+          py::arg("packed"), py::arg("scales"), py::arg("zeros"), py::arg("fp16_weights"), py::arg("x"),
+          py::arg("outlier_k"), py::arg("native") = py::none());
+    m.def("int4_gemv", &int4_gemv, "Dense INT4 GEMV baseline", py::arg("packed"), py::arg("scales"),
+          py::arg("zeros"), py::arg("fp16_weights"), py::arg("x"), py::arg("native") = py::none());
+    m.def("build_native", &build_native, "Unit layout streamed by the GEMV kernels");
     m.def("reference_gemv", &reference_gemv, "FP16 dense reference GEMV");
     m.def("build_colmajor", &build_colmajor, "Column-major FP16 mirror of a weight matrix");
     m.def("detect_outliers", &detect_outliers, "Standalone outlier detector");

@@ -40,6 +40,7 @@ __all__ = [
     "reference_gemv",
     "detect_outliers",
     "build_colmajor",
+    "build_native",
 ]
 
 GROUP_SIZE = 128
@@ -102,6 +103,7 @@ def split_gemv(
     fp16_w: torch.Tensor,
     x: torch.Tensor,
     outlier_k: float = 3.0,
+    native: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Fused dynamic-precision GEMV with runtime outlier detection.
 
@@ -117,12 +119,14 @@ def split_gemv(
                    transpose of a column-major mirror (see build_colmajor).
         x:         [d_in] float16 activation vector.
         outlier_k: sigma threshold for outlier detection (default 3.0).
+        native:    optional unit layout from build_native(packed, scales,
+                   zeros) -- the fast path (one bulk copy per unit).
 
     Returns:
         y: [d_out] float16 output vector.
     """
     _require_extension()
-    return _C.split_gemv(packed, scales, zeros, fp16_w, _aligned(x), float(outlier_k))
+    return _C.split_gemv(packed, scales, zeros, fp16_w, _aligned(x), float(outlier_k), native)
 
 
 def int4_gemv(
@@ -131,10 +135,19 @@ def int4_gemv(
     zeros: torch.Tensor,
     fp16_w: torch.Tensor,
     x: torch.Tensor,
+    native: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Dense INT4 GEMV without outlier handling (fp16_w used only for shape)."""
     _require_extension()
-    return _C.int4_gemv(packed, scales, zeros, fp16_w, _aligned(x))
+    return _C.int4_gemv(packed, scales, zeros, fp16_w, _aligned(x), native)
+
+
+def build_native(packed: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor) -> torch.Tensor:
+    """The unit layout the GEMV kernels stream with one bulk copy per 16-row x
+    512-column unit: packed codes in lane order plus interleaved (scale, zero),
+    a reordering of (packed, scales, zeros) (a uint8 tensor)."""
+    _require_extension()
+    return _C.build_native(packed, scales, zeros)
 
 
 def reference_gemv(fp16_w: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
@@ -186,6 +199,8 @@ class DynQuantLinear(nn.Module):
         self.register_buffer("scales", None)
         self.register_buffer("zeros", None)
         self.register_buffer("fp16_w", None)
+        # load-time unit layout the kernels stream (rebuilt from packed/scales/zeros, not saved)
+        self.register_buffer("_native", None, persistent=False)
 
     def load_weight(self, weight: torch.Tensor) -> None:
         """Quantize and store an FP16 weight matrix.
@@ -205,6 +220,7 @@ class DynQuantLinear(nn.Module):
         self.scales = scales
         self.zeros = zeros
         self.fp16_w = _C.build_colmajor(weight).t()
+        self._native = _C.build_native(packed, scales, zeros)
         self._quantized = True
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
@@ -222,7 +238,8 @@ class DynQuantLinear(nn.Module):
             x = x.to(torch.float16)
         if not x.is_contiguous():
             x = x.contiguous()
-        return split_gemv(self.packed, self.scales, self.zeros, self.fp16_w, x, self.outlier_k)
+        return split_gemv(self.packed, self.scales, self.zeros, self.fp16_w, x, self.outlier_k,
+                          self._native)
 
     def _load_from_state_dict(self, state_dict, prefix, local_metadata, strict, missing_keys,
                               unexpected_keys, error_msgs):
@@ -239,6 +256,7 @@ class DynQuantLinear(nn.Module):
             self.zeros = state_dict[prefix + "zeros"].to(dev, torch.float16).contiguous()
             w = state_dict[prefix + "fp16_w"].to(dev, torch.float16).contiguous()
             self.fp16_w = _C.build_colmajor(_aligned(w)).t()
+            self._native = _C.build_native(self.packed, self.scales, self.zeros)
             self._quantized = True
         super()._load_from_state_dict(state_dict, prefix, local_metadata, strict, missing_keys,
                                       unexpected_keys, error_msgs)

@@ -33,6 +33,10 @@ EXPORTED_SYMBOLS = (
     "dq_int4_gemv",
     "dq_reference_gemv",
     "dq_detect_outliers",
+    "dq_native_bytes",
+    "dq_build_native",
+    "dq_read_device_error",
+    "dq_workspace_bytes",
 )
 
 
@@ -45,6 +49,7 @@ class DqWeights(C.Structure):
         ("zeros", C.c_void_p),
         ("fp16", C.c_void_p),
         ("fp16_cm", C.c_void_p),
+        ("native", C.c_void_p),
         ("d_out", C.c_int32),
         ("d_in", C.c_int32),
     ]
@@ -83,13 +88,21 @@ def lib() -> C.CDLL:
         L.dq_build_colmajor.restype = st
         L.dq_build_colmajor.argtypes = [P, i32, i32, P, P]
         L.dq_split_gemv.restype = st
-        L.dq_split_gemv.argtypes = [C.POINTER(DqWeights), P, P, f32, P]
+        L.dq_split_gemv.argtypes = [C.POINTER(DqWeights), P, P, f32, P, C.c_size_t, P]
         L.dq_int4_gemv.restype = st
-        L.dq_int4_gemv.argtypes = [C.POINTER(DqWeights), P, P, P]
+        L.dq_int4_gemv.argtypes = [C.POINTER(DqWeights), P, P, P, C.c_size_t, P]
+        L.dq_workspace_bytes.restype = C.c_size_t
+        L.dq_workspace_bytes.argtypes = [i32, i32]
         L.dq_reference_gemv.restype = st
         L.dq_reference_gemv.argtypes = [P, P, P, i32, i32, P]
         L.dq_detect_outliers.restype = st
         L.dq_detect_outliers.argtypes = [P, i32, f32, P, P, P, P, P]
+        L.dq_native_bytes.restype = C.c_size_t
+        L.dq_native_bytes.argtypes = [i32, i32]
+        L.dq_build_native.restype = st
+        L.dq_build_native.argtypes = [P, P, P, i32, i32, P, P]
+        L.dq_read_device_error.restype = st
+        L.dq_read_device_error.argtypes = [C.POINTER(C.c_uint32), C.c_int]
         _lib = L
     return _lib
 
@@ -104,6 +117,6 @@ def check(status: int, what: str) -> None:
 
 
 def weights(packed: int, scales: int, zeros: int, fp16: int | None, fp16_cm: int | None,
-            d_out: int, d_in: int) -> DqWeights:
+            d_out: int, d_in: int, native: int | None = None) -> DqWeights:
     """Build a dq_weights_t from raw device addresses."""
-    return DqWeights(packed, scales, zeros, fp16 or None, fp16_cm or None, d_out, d_in)
+    return DqWeights(packed, scales, zeros, fp16 or None, fp16_cm or None, native or None, d_out, d_in)

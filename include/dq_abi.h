@@ -50,15 +50,18 @@ typedef enum dq_status_t {
 } dq_status_t;
 
 /* Non-owning view of one quantized weight matrix (the reference's
- * QuantizedWeights, src/quant_format.cuh:12-23, plus the optional mirror).
- * At least one of fp16 / fp16_cm must be set for the split GEMV; the
- * column-major mirror is the fast path for outlier columns. */
+ * QuantizedWeights, src/quant_format.cuh:12-23, plus two optional load-time
+ * layouts).  At least one of fp16 / fp16_cm must be set for the split GEMV;
+ * the column-major mirror is the fast path for outlier columns.  native, when
+ * set (dq_build_native), is what the kernels stream instead of packed /
+ * scales / zeros (which must still be valid and describe the same weights). */
 typedef struct dq_weights_t {
     const uint8_t* packed;
     const uint16_t* scales;
     const uint16_t* zeros;
-    const uint16_t* fp16;    /* row-major [d_out][d_in], may be NULL if fp16_cm is set */
-    const uint16_t* fp16_cm; /* column-major [d_in][d_out], may be NULL */
+    const uint16_t* fp16;       /* row-major [d_out][d_in], may be NULL if fp16_cm is set */
+    const uint16_t* fp16_cm;    /* column-major [d_in][d_out], may be NULL */
+    const uint8_t* native;      /* unit layout from dq_build_native, 16-byte aligned, may be NULL */
     int32_t d_out;
     int32_t d_in;
 } dq_weights_t;
@@ -98,24 +101,51 @@ DQ_API dq_status_t dq_build_colmajor(const uint16_t* w16, int32_t d_out, int32_t
                               void* stream);
 
 /*
+ * Native unit layout streamed by the batch-1 GEMV kernels with one bulk copy
+ * per 16-row x 512-column unit: for each (16-row block, 4-group chunk), 4096
+ * bytes of packed codes in the order the kernel's lanes read them, then 256
+ * bytes of (scale bits | zero bits << 16) for 16 rows x 4 groups; zero-padded
+ * past d_out and past the last group.  A reordering of the reference format
+ * (src/quant_format.cuh:12-23), built once at load time; no reference
+ * counterpart.  dq_native_bytes gives the size (0 for a bad shape).
+ */
+DQ_API size_t dq_native_bytes(int32_t d_out, int32_t d_in);
+DQ_API dq_status_t dq_build_native(const uint8_t* packed, const uint16_t* scales, const uint16_t* zeros,
+                                   int32_t d_out, int32_t d_in, uint8_t* native, void* stream);
+
+/*
+ * Workspace of the batch-1 GEMVs: device memory of at least
+ * dq_workspace_bytes(d_out, d_in) bytes, 256-byte aligned, ZERO-FILLED before
+ * its first use.  It holds the activation plan of the call (statistics,
+ * outlier list, MMA fragments of x) and per-row-block arrival counters; every
+ * call leaves the counters at zero again, so one zero-filled workspace serves
+ * any number of stream-ordered calls of any shape it is large enough for.
+ * Calls that share a workspace must not overlap on the GPU.
+ */
+DQ_API size_t dq_workspace_bytes(int32_t d_out, int32_t d_in);
+
+/*
  * Fused dynamic-precision GEMV, batch 1: y = W_split x.
  * Channel c is an outlier when |x_c - mean(x)| > outlier_k * std(x) (unbiased
  * variance floored at 1e-8, strict >), keeping at most d_in/16 outliers per
  * 32-column stripe class as the reference's warp capacity does
  * (src/outlier_detect.cuh:160-178).  Outlier columns use the FP16 weights, the
  * rest the INT4 codes; FP32 accumulation; y is rounded to FP16 once.
+ * Enqueues two kernels (the activation plan, then the GEMV as its programmatic
+ * dependent).
  * Replaces: launch_split_gemv (src/split_gemv.cu:160-198, src/split_gemv.cuh:10).
  * x: device [d_in] f16, y: device [d_out] f16.
  */
 DQ_API dq_status_t dq_split_gemv(const dq_weights_t* w, const uint16_t* x, uint16_t* y, float outlier_k,
-                          void* stream);
+                                 void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Dense INT4 GEMV (no outlier handling): y = dequant(W) x.
  * Replaces: launch_int4_gemv (src/int4_gemv.cu:80-100, src/int4_gemv.cuh:9).
- * Only packed/scales/zeros of *w are read.
+ * Only packed/scales/zeros (or native) of *w are read.
  */
-DQ_API dq_status_t dq_int4_gemv(const dq_weights_t* w, const uint16_t* x, uint16_t* y, void* stream);
+DQ_API dq_status_t dq_int4_gemv(const dq_weights_t* w, const uint16_t* x, uint16_t* y, void* workspace,
+                                size_t workspace_bytes, void* stream);
 
 /*
  * FP16 dense GEMV with FP32 accumulation: y = W16 x.
@@ -139,6 +169,14 @@ DQ_API dq_status_t dq_reference_gemv(const uint16_t* w16, const uint16_t* x, uin
 DQ_API dq_status_t dq_detect_outliers(const uint16_t* x, int32_t d_in, float outlier_k,
                                uint32_t* mask_words, int32_t* indices, int32_t* count,
                                float* stats, void* stream);
+
+/*
+ * Device error word of this library on the current device: bit 0 is set by a
+ * kernel whose bounded wait for its own bulk copies gave up (the kernel then
+ * drains its copies, skips the remaining work and returns; its output is not
+ * valid).  Synchronous; clear != 0 resets the word.  No reference counterpart.
+ */
+DQ_API dq_status_t dq_read_device_error(uint32_t* word, int clear);
 
 #ifdef __cplusplus
 }

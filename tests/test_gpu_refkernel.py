@@ -23,7 +23,7 @@ torch = pytest.importorskip("torch")
 import oracle as O  # noqa: E402
 from dyn_quant import synth  # noqa: E402
 from dq_testutil import (  # noqa: E402
-    abi_colmajor, abi_detect, abi_int4_gemv, abi_quantize, abi_reference_gemv, abi_split_gemv, abi_weights,
+    abi_build_native, abi_colmajor, abi_detect, abi_int4_gemv, abi_quantize, abi_reference_gemv, abi_split_gemv, abi_weights,
     check_mask, check_y, dev, host, stream_ptr,
 )
 
@@ -85,7 +85,7 @@ def test_against_reference_kernels(d_out, d_in, frac):
     check_mask(mask, r_mask, x.astype(np.float32), float(r_stats[0]), float(r_stats[1]), "vs reference detector")
     if np.array_equal(mask, r_mask):
         assert np.array_equal(o_idx, r_idx)  # same list order
-    wts = abi_weights(p_t, s_t, z_t, w_cm=abi_colmajor(w_t))
+    wts = abi_weights(p_t, s_t, z_t, w_cm=abi_colmajor(w_t), native=abi_build_native(p_t, s_t, z_t))
     y = host(abi_split_gemv(wts, x_t, k))
     rows = np.nonzero(np.arange(d_out) % 4 < 2)[0]
     check_y(y, host(y_rs), rows=rows, what="split vs reference kernel (rows%4<2)")
