@@ -1,36 +1,44 @@
 // dq_gemv.cu -- batch-1 GEMV kernels for sm_100a: fused split (INT4 + FP16
-// outlier columns), dense INT4, dense FP16, the activation plan / standalone
-// detector, the bit-exact quantizer and the layout builders.
+// outlier columns), dense INT4, dense FP16, the standalone outlier detector,
+// the bit-exact quantizer and the layout builders.
 //
 // Reference path (dyn-quant): src/split_gemv.cu:25-198, src/int4_gemv.cu:12-100,
 // src/reference_gemv.cu:9-78, src/outlier_detect.cuh:104-205,
 // src/quant_format.cuh:48-97.
 //
-// One split GEMV call = two kernels on the stream:
-//   1. plan_kernel (one 1024-thread CTA): statistics of x, the outlier mask
-//      (with the reference's capacity rule), the outlier list, the MMA B
-//      fragments of the masked activation and per-group sums -- computed once
-//      into the workspace.  It triggers the dependent launch at its start.
-//   2. gemv_kernel (persistent, one 256-thread CTA per SM, launched as a
-//      programmatic dependent of the plan): each warp starts streaming its
-//      weight units through a 3-stage shared-memory ring (cp.async.bulk, the
-//      non-tensor TMA form, completing on per-stage mbarriers) BEFORE it waits
-//      for the plan (griddepcontrol.wait); then one bulk copy brings the plan
-//      into shared memory and the warps run the dequant + tensor-core loop.
-//   * A unit is 16 rows x 4 groups of 128 columns (4 KB of packed INT4).  The
-//     units are split evenly across CTAs (and across the 8 warps of a CTA) in
-//     (row-block, column-chunk) order; a 16-row block that straddles two CTAs
-//     is finished by whichever of them arrives last, summing the partial row
-//     sums in CTA order (fixed order: results are bit-reproducible).
-//   * The contraction runs on the tensor cores: mma.sync.m16n8k16 with the
-//     packed codes as A (f16 1024+q or 1024+16q, exact) and the masked
-//     activation x' as column 0 of B, FP32 accumulate; the exponent bias is
-//     removed per group in FP32 from the plan's per-group sums.  Per
-//     (row, group): y += s * (sum_c q_c x'_c - z * sum_c x'_c), the value of
-//     the reference's sum of s*(q-z)*x over the non-outlier channels.
-//   * Outlier channels add W16[r][c] * x[c]: with the column-major mirror the
-//     16 rows of one outlier column (32 bytes) are fetched by cp.async into the
-//     unit's stage and complete on the same mbarrier as the weights.
+// One split / INT4 GEMV call is ONE kernel (b1_kernel): a persistent grid of
+// one 256-thread CTA per SM, launched as a programmatic dependent of whatever
+// precedes it on the stream.
+//   1. Each warp starts streaming its first weight units into a 3-stage
+//      shared-memory ring (cp.async.bulk, the non-tensor TMA form, completing
+//      on per-stage mbarriers) before griddepcontrol.wait, so the weight
+//      stream overlaps the tail of the previous kernel.
+//   2. Each CTA derives the activation plan itself from x (<= 60 KB, an L2
+//      hit after the first CTA): the statistics, the outlier mask with the
+//      reference's capacity rule, the ascending outlier list, and the MMA B
+//      fragments of the masked activation x' with per-group sums.
+//   3. The warps run dequant + tensor-core MMAs over their units.  A unit is
+//      16 rows x 4 groups of 128 columns; the units are split evenly across
+//      CTAs (and across the 8 warps of a CTA) in (row block, column chunk)
+//      order.  A 16-row block that straddles two CTAs is finished by whichever
+//      of them arrives last, summing the partial row sums in CTA order (fixed
+//      order: results are bit-reproducible).
+//   4. Outlier columns add W16[r][c] * x[c]: the CTA's row segment of each
+//      outlier column of the column-major FP16 mirror (contiguous, 32 bytes per
+//      row block) is brought into shared memory by one bulk copy per column,
+//      issued right after the list is known, and summed after the unit loop.
+//
+// Tensor-core formulation (mma.sync.m16n8k16, f16 x f16 -> f32).  Lane
+// (g, t) of a warp holds group t of the unit's 4-group chunk: A comes from the
+// packed codes with the exponent bias kept (f16 1024 + q for the even columns
+// of a word, 1024 + 16 q for the odd ones: one shift and four lop3 per word,
+// all exact).  B holds x' of group t in MMA columns 2t (even columns of the
+// words) and 2t + 1 (odd columns); every other lane supplies zeros.  The "lo"
+// MMA accumulates D_lo[:, 2t] = 1024 Xe + S_even, the "hi" MMA accumulates
+// D_hi[:, 2t + 1] = 1024 Xo + 16 S_odd (the other column of each is not read),
+// so lane (g, t) ends with the two sums of group t for rows g and g + 8 and
+// removes the bias in FP32 from the per-group sums of x':
+//   y += s * ((S_even + S_odd) - z * X),   the reference's sum of s (q - z) x.
 #include <cfloat>
 #include <climits>
 
@@ -51,247 +59,253 @@ constexpr int kStageBytes = kB1StageBytes;
 __device__ unsigned int g_error_word;
 
 // ---------------------------------------------------------------------------
-// Activation plan
+// Block-wide helpers (NT threads)
 // ---------------------------------------------------------------------------
 
-// Computes the plan of x into shared memory laid out by plan_layout, with NT
-// threads.  The outlier mask follows the reference's detector definition
-// (src/outlier_detect.cuh): mean and unbiased variance of x (two-pass, FP32,
-// fixed reduction order), thresh = k * sqrt(max(var, 1e-8)), outlier iff
-// |x - mean| > thresh, and at most (d_in/4)/4 outliers kept per stripe class
-// (columns c with (c/32) % 4 == w, the first ones in ascending order), as the
-// reference's per-warp capacity does (src/outlier_detect.cuh:160-178).
-// red: >= 64 floats of scratch.
-template <int NT, bool kSplit>
-__device__ void build_plan(const uint16_t* __restrict__ x, int d_in, float k, char* smem, float* red) {
+// Exclusive prefix sums over the threads (in thread order) of NV ints per
+// thread, plus the totals.  scratch: >= NW * NV ints; barrier on entry.
+template <int NT, int NV>
+__device__ __forceinline__ void block_scan(const int (&v)[NV], int (&pre)[NV], int (&tot)[NV], int* scratch) {
     constexpr int NW = NT / 32;
-    const PlanLayout P = plan_layout(d_in);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int G = d_in / kGroup;
-    const int n8 = d_in >> 3;
-    uint4* xb = reinterpret_cast<uint4*>(smem + P.bsm);  // natural order, then B fragments
-    uint8_t* smask = reinterpret_cast<uint8_t*>(smem + P.mask);
-    float* stat = reinterpret_cast<float*>(smem + P.stats);
-    int* stripe = reinterpret_cast<int*>(red + 40);
-    float4* xp4 = reinterpret_cast<float4*>(smem + P.xp);
-    int* goff = reinterpret_cast<int*>(smem + P.goff);
-    uint32_t* list = reinterpret_cast<uint32_t*>(smem + P.list);
-
-    if (tid < 4) stripe[tid] = 0;
-    float sum = 0.f;
-    for (int ch = tid; ch < n8; ch += NT) {
-        const uint4 v = ldg_v4(x + 8 * static_cast<size_t>(ch));
-        xb[ch] = v;
-        if (kSplit) {
-            const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int incl[NV];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                sum += h2f_bits(static_cast<uint16_t>(wv[i] & 0xFFFFu));
-                sum += h2f_bits(static_cast<uint16_t>(wv[i] >> 16));
-            }
-        }
-    }
-
-    if (kSplit) {
-        const float total = block_sum<NT>(sum, red);
-        const float mean = __fdiv_rn(total, static_cast<float>(d_in));
-        float m2 = 0.f;
-        for (int ch = tid; ch < n8; ch += NT) {
-            const uint4 v = xb[ch];
-            const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+    for (int i = 0; i < NV; ++i) incl[i] = v[i];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float d0 = __fsub_rn(h2f_bits(static_cast<uint16_t>(wv[i] & 0xFFFFu)), mean);
-                const float d1 = __fsub_rn(h2f_bits(static_cast<uint16_t>(wv[i] >> 16)), mean);
-                m2 = __fmaf_rn(d0, d0, m2);
-                m2 = __fmaf_rn(d1, d1, m2);
-            }
-        }
-        const float M2 = block_sum<NT>(m2, red);
-        const float var = (d_in > 1) ? __fdiv_rn(M2, static_cast<float>(d_in - 1)) : 0.f;
-        const float thresh = __fmul_rn(k, __fsqrt_rn(fmaxf(var, 1e-8f)));
-        if (tid == 0) {
-            stat[0] = mean;
-            stat[1] = thresh;
-            stat[2] = var;
-            stat[3] = M2;
-        }
-        for (int ch = tid; ch < n8; ch += NT) {
-            const uint4 v = xb[ch];
-            const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
-            uint32_t byte = 0;
+    for (int o = 1; o < 32; o <<= 1) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float a = h2f_bits(static_cast<uint16_t>(wv[i] & 0xFFFFu));
-                const float b = h2f_bits(static_cast<uint16_t>(wv[i] >> 16));
-                byte |= (fabsf(__fsub_rn(a, mean)) > thresh ? 1u : 0u) << (2 * i);
-                byte |= (fabsf(__fsub_rn(b, mean)) > thresh ? 1u : 0u) << (2 * i + 1);
-            }
-            smask[ch] = static_cast<uint8_t>(byte);
-            if (byte) atomicAdd(&stripe[(ch >> 2) & 3], __popc(byte));
+        for (int i = 0; i < NV; ++i) {
+            const int n = __shfl_up_sync(0xffffffffu, incl[i], o);
+            if (lane >= o) incl[i] += n;
         }
-        __syncthreads();
-        // Capacity rule (rare): keep the first warp_cap outliers of each stripe class.
-        const int warp_cap = (d_in / 4) / 4;
-        if (stripe[0] > warp_cap || stripe[1] > warp_cap || stripe[2] > warp_cap || stripe[3] > warp_cap) {
-            if (warp == 0 && lane < 4) {
-                uint32_t* words = reinterpret_cast<uint32_t*>(smask);
-                int kept = 0;
-                for (int wj = lane; wj < d_in / 32; wj += 4) {
-                    uint32_t m = words[wj];
-                    int c = __popc(m);
-                    if (kept + c > warp_cap) {
-                        int keep = warp_cap - kept;
-                        uint32_t out = 0;
-                        for (int b = 0; b < 32 && keep > 0; ++b)
-                            if (m & (1u << b)) { out |= 1u << b; --keep; }
-                        m = out;
-                        c = __popc(m);
-                    }
-                    words[wj] = m;
-                    kept += c;
-                }
-            }
-            __syncthreads();
-        }
-        // Per-group outlier counts (4 mask words per group).
-        const uint32_t* words = reinterpret_cast<const uint32_t*>(smask);
-        for (int j = warp; j < G; j += NW) {
-            int c = (lane < 4) ? __popc(words[4 * j + lane]) : 0;
-            c += __shfl_xor_sync(0xffffffffu, c, 1);
-            c += __shfl_xor_sync(0xffffffffu, c, 2);
-            if (lane == 0) goff[j] = c;
-        }
-        __syncthreads();
-        // Exclusive scan of the counts (one warp).
-        if (warp == 0) {
-            const int per = (G + 31) / 32;
-            const int b = lane * per;
-            int local = 0;
-            for (int i = 0; i < per; ++i)
-                if (b + i < G) local += goff[b + i];
-            int incl = local;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int n = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += n;
-            }
-            int run = incl - local;
-            for (int i = 0; i < per; ++i)
-                if (b + i < G) {
-                    const int c = goff[b + i];
-                    goff[b + i] = run;
-                    run += c;
-                }
-            if (lane == 31) {
-                goff[G] = incl;
-                reinterpret_cast<int*>(stat)[4] = incl;
-            }
-        }
-        __syncthreads();
-        // Ascending outlier list per group, with the activation value of each.
-        const uint16_t* xh = reinterpret_cast<const uint16_t*>(xb);
-        for (int j = warp; j < G; j += NW) {
-            const int c0 = kGroup * j + 4 * lane;
-            const uint32_t bits = (smask[c0 >> 3] >> (c0 & 7)) & 0xFu;
-            const int n = __popc(bits);
-            int incl = n;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int v = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += v;
-            }
-            int pos = goff[j] + incl - n;
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-                if (bits & (1u << i))
-                    list[pos++] = static_cast<uint32_t>(c0 + i) | (static_cast<uint32_t>(xh[c0 + i]) << 16);
-        }
-    } else {
-        for (int j = tid; j <= G; j += NT) goff[j] = 0;
-        if (tid == 0) reinterpret_cast<int*>(stat)[4] = 0;
     }
     __syncthreads();
-
-    // In place: natural chunk (j, t, wi) -> fragment slot (j, wi, t), outliers
-    // zeroed.  Word wi of chunk t feeds two MMAs: the "low" one takes columns
-    // (0,4) and (2,6) of the word, the "high" one (1,5) and (3,7) -- the
-    // pairs the dequantisation extracts without a shift.  Per group, xp holds
-    // (1024 * sum x' over even columns, 1024 * sum over odd columns, sum x', 0).
-    for (int j = warp; j < G; j += NW) {
-        uint4 out = make_uint4(0, 0, 0, 0);
-        float pe = 0.f, po = 0.f;
-        const int t = lane >> 2, wi = lane & 3;
-        if (lane < 16) {
-            const int ch = 16 * j + 4 * t + wi;
-            const uint4 v = xb[ch];
-            const uint32_t mb = kSplit ? smask[ch] : 0u;
-            uint16_t h[8];
-            h[0] = v.x & 0xFFFFu; h[1] = v.x >> 16; h[2] = v.y & 0xFFFFu; h[3] = v.y >> 16;
-            h[4] = v.z & 0xFFFFu; h[5] = v.z >> 16; h[6] = v.w & 0xFFFFu; h[7] = v.w >> 16;
+    if (lane == 31)
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-                if (mb & (1u << i)) h[i] = 0;
-            pe = (h2f_bits(h[0]) + h2f_bits(h[2])) + (h2f_bits(h[4]) + h2f_bits(h[6]));
-            po = (h2f_bits(h[1]) + h2f_bits(h[3])) + (h2f_bits(h[5]) + h2f_bits(h[7]));
-            out = make_uint4(pack_h2(h[0], h[4]), pack_h2(h[2], h[6]), pack_h2(h[1], h[5]), pack_h2(h[3], h[7]));
-        }
-        __syncwarp();
-        if (lane < 16) xb[16 * j + 4 * wi + t] = out;
-        pe = warp_sum(pe);
-        po = warp_sum(po);
-        if (lane == 0) xp4[j] = make_float4(1024.f * pe, 1024.f * po, pe + po, 0.f);
-    }
+        for (int i = 0; i < NV; ++i) scratch[warp * NV + i] = incl[i];
     __syncthreads();
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        int before = 0, all = 0;
+        for (int w = 0; w < NW; ++w) {
+            const int s = scratch[w * NV + i];
+            before += (w < warp) ? s : 0;
+            all += s;
+        }
+        pre[i] = before + incl[i] - v[i];
+        tot[i] = all;
+    }
 }
 
-// One CTA builds the plan of x.  Writes it to `plan` (the workspace) when
-// non-null, and the detector outputs when requested.  Lets the dependent GEMV
-// launch immediately: the GEMV only reads the plan after griddepcontrol.wait.
-template <bool kSplit>
-__global__ void __launch_bounds__(kPlanThreads, 1)
-    plan_kernel(const uint16_t* __restrict__ x, int d_in, float k, uint8_t* __restrict__ plan,
-                uint32_t* mask_words, int32_t* indices, int32_t* count, float* stats) {
-    pdl_launch_dependents();
-    extern __shared__ __align__(128) char smem[];
-    const PlanLayout P = plan_layout(d_in);
-    float* red = reinterpret_cast<float*>(smem + P.total);
-    build_plan<kPlanThreads, kSplit>(x, d_in, k, smem, red);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    if (plan) {
-        const uint4* src = reinterpret_cast<const uint4*>(smem);
-        uint4* dst = reinterpret_cast<uint4*>(plan);
-        for (int i = tid; i < P.total / 16; i += kPlanThreads) dst[i] = src[i];
-    }
-    if (!kSplit) return;
-    const int G = d_in / kGroup;
-    const uint32_t* words = reinterpret_cast<const uint32_t*>(smem + P.mask);
-    const int* goff = reinterpret_cast<const int*>(smem + P.goff);
-    const uint32_t* list = reinterpret_cast<const uint32_t*>(smem + P.list);
-    const float* stat = reinterpret_cast<const float*>(smem + P.stats);
-    if (mask_words)
-        for (int i = tid; i < d_in / 32; i += kPlanThreads) mask_words[i] = words[i];
-    const int total = goff[G];
-    if (tid == 0) {
-        if (count) *count = total;
-        if (stats)
-            for (int i = 0; i < 4; ++i) stats[i] = stat[i];
-    }
-    if (indices && warp < 4) {
-        // The reference's list order: stripe class 0 ascending, then 1, 2, 3.
-        int before = 0;
-        for (int i = lane; i < total; i += 32)
-            before += ((static_cast<int>(list[i] & 0xFFFFu) >> 5) & 3) < warp ? 1 : 0;
+__device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
+    return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
+}
+
+// ---------------------------------------------------------------------------
+// Activation plan (per CTA, NT threads)
+//
+// The outlier mask follows the reference's detector definition
+// (src/outlier_detect.cuh:104-205): mean and unbiased variance of x in FP32,
+// thresh = k * sqrt(max(var, 1e-8)), outlier iff |x - mean| > thresh, and at
+// most (d_in/4)/4 outliers kept per stripe class (columns c with
+// (c/32) % 4 == w, the first ones in ascending order), as the reference's
+// per-warp capacity does (src/outlier_detect.cuh:160-178).  Mean and variance
+// are computed two-pass with a fixed reduction order, so every CTA (and the
+// standalone detector) derives the same mask.
+// ---------------------------------------------------------------------------
+
+// x (d_in = 8 * n8 halves) from global memory into xs, natural order, as
+// 16-byte cp.async copies (completed by cp_async_wait_all + a barrier).
+template <int NT>
+__device__ __forceinline__ void load_x_async(const uint16_t* __restrict__ x, int n8, uint4* xs) {
+    for (int ch = threadIdx.x; ch < n8; ch += NT) cp_async16(smem_u32(xs + ch), x + 8 * static_cast<size_t>(ch));
+    cp_async_commit();
+}
+
+// Block-wide FP32 sum of x (barrier inside).
+template <int NT>
+__device__ __forceinline__ float x_sum(const uint4* xs, int n8, float* red) {
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+    for (int ch = threadIdx.x; ch < n8; ch += NT) {
+        const uint4 v = xs[ch];
 #pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) before += __shfl_xor_sync(0xffffffffu, before, o);
-        int pos = before;
-        for (int base = 0; base < total; base += 32) {
-            const int i = base + lane;
-            const int c = (i < total) ? static_cast<int>(list[i] & 0xFFFFu) : 0;
-            const bool mine = i < total && ((c >> 5) & 3) == warp;
-            const unsigned bal = __ballot_sync(0xffffffffu, mine);
-            if (mine) indices[pos + __popc(bal & ((1u << lane) - 1u))] = c;
-            pos += __popc(bal);
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t w = word_of(v, i);
+            s[i] = add_f16_f32(hi16(w), add_f16_f32(lo16(w), s[i]));
+        }
+    }
+    return block_sum<NT>((s[0] + s[1]) + (s[2] + s[3]), red);
+}
+
+struct XStats {
+    float mean, thresh, var, m2;
+};
+
+template <int NT>
+__device__ __forceinline__ XStats x_stats(const uint4* xs, int n8, int d_in, float k, float total, float* red) {
+    XStats r;
+    r.mean = __fdiv_rn(total, static_cast<float>(d_in));
+    float m[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+    for (int ch = threadIdx.x; ch < n8; ch += NT) {
+        const uint4 v = xs[ch];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t w = word_of(v, i);
+            const float d0 = sub_f16_f32(lo16(w), r.mean);
+            const float d1 = sub_f16_f32(hi16(w), r.mean);
+            m[i] = __fmaf_rn(d1, d1, __fmaf_rn(d0, d0, m[i]));
+        }
+    }
+    r.m2 = block_sum<NT>((m[0] + m[1]) + (m[2] + m[3]), red);
+    r.var = (d_in > 1) ? __fdiv_rn(r.m2, static_cast<float>(d_in - 1)) : 0.f;
+    r.thresh = __fmul_rn(k, __fsqrt_rn(fmaxf(r.var, 1e-8f)));
+    return r;
+}
+
+// One mask byte per 8 columns (bit i = column 8 ch + i).
+template <int NT>
+__device__ __forceinline__ void x_mask(const uint4* xs, int n8, float mean, float thresh, uint8_t* mask) {
+#pragma unroll 4
+    for (int ch = threadIdx.x; ch < n8; ch += NT) {
+        const uint4 v = xs[ch];
+        uint32_t byte = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t w = word_of(v, i);
+            byte |= (fabsf(sub_f16_f32(lo16(w), mean)) > thresh ? 1u : 0u) << (2 * i);
+            byte |= (fabsf(sub_f16_f32(hi16(w), mean)) > thresh ? 1u : 0u) << (2 * i + 1);
+        }
+        mask[ch] = static_cast<uint8_t>(byte);
+    }
+}
+
+// Applies the per-stripe-class capacity to the mask (32-bit word wj = columns
+// 32 wj .. 32 wj + 31, stripe class wj % 4) and writes the ascending outlier
+// list (column | FP16 bits of x << 16).  Returns the number of outliers; the
+// list is complete after the caller's next barrier.
+template <int NT>
+__device__ int x_list(const uint16_t* xh, int d_in, uint32_t* mask32, uint32_t* list, int* scratch) {
+    __syncthreads();  // mask bytes of all threads
+    const int nw = d_in / 32;
+    const int tid = threadIdx.x;
+    const int w0 = static_cast<int>(static_cast<long long>(tid) * nw / NT);
+    const int w1 = static_cast<int>(static_cast<long long>(tid + 1) * nw / NT);
+    int cnt[4] = {0, 0, 0, 0};
+    for (int wj = w0; wj < w1; ++wj) {
+        const int n = __popc(mask32[wj]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) cnt[i] += (wj & 3) == i ? n : 0;
+    }
+    int pre[4], tot[4];
+    block_scan<NT, 4>(cnt, pre, tot, scratch);
+    const int cap = (d_in / 4) / 4;
+    int kept[1] = {cnt[0] + cnt[1] + cnt[2] + cnt[3]};
+    if (tot[0] > cap || tot[1] > cap || tot[2] > cap || tot[3] > cap) {
+        kept[0] = 0;
+        for (int wj = w0; wj < w1; ++wj) {
+            uint32_t m = mask32[wj];
+            const int c = __popc(m);
+            const int w = wj & 3;
+            const int before = w == 0 ? pre[0] : (w == 1 ? pre[1] : (w == 2 ? pre[2] : pre[3]));
+            if (before + c > cap) {
+                int keep = cap - before;
+                uint32_t out = 0;
+                for (; keep > 0 && m; --keep) {
+                    out |= m & (~m + 1u);
+                    m &= m - 1u;
+                }
+                mask32[wj] = out;
+                kept[0] += __popc(out);
+            } else {
+                kept[0] += c;
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) pre[i] += w == i ? c : 0;
+        }
+    }
+    int pos[1], total[1];
+    block_scan<NT, 1>(kept, pos, total, scratch);
+    int p = pos[0];
+    for (int wj = w0; wj < w1; ++wj) {
+        uint32_t m = mask32[wj];
+        while (m) {
+            const int col = 32 * wj + (__ffs(m) - 1);
+            list[p++] = static_cast<uint32_t>(col) | (static_cast<uint32_t>(xh[col]) << 16);
+            m &= m - 1u;
+        }
+    }
+    return total[0];
+}
+
+// In place over xb: the 64 natural 8-column pieces of each 512-column chunk
+// -> MMA B order [word wi][slice sl][group jj] (16 bytes each: the f16 pairs
+// (x0,x4), (x2,x6), (x1,x5), (x3,x7) of the piece, outliers zeroed), and per
+// group xp = (1024 sum x' even columns, 1024 sum x' odd columns, sum x', 0).
+// Pieces past d_in are zero.  Each chunk is handled by one warp.
+template <int NT, bool kMask>
+__device__ __forceinline__ void x_fragments(uint4* xb, int n8, int NC, const uint8_t* mask, float4* xp4) {
+    constexpr int NW = NT / 32;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // Two chunks (c, c + NW) per iteration for instruction-level parallelism.
+    for (int cb = warp; cb < NC; cb += 2 * NW) {
+        uint4 v[2][2];
+        float pe[2][2], po[2][2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int c = cb + k * NW;
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                const int n = 64 * c + lane + 32 * q;
+                uint4 w = make_uint4(0, 0, 0, 0);
+                if (c < NC && n < n8) {
+                    w = xb[n];
+                    if (kMask) {
+                        const uint32_t mb = mask[n];
+                        if (mb) {
+                            uint32_t keep[4];
+#pragma unroll
+                            for (int i = 0; i < 4; ++i)
+                                keep[i] = ((mb >> (2 * i)) & 1u ? 0u : 0x0000FFFFu) |
+                                          ((mb >> (2 * i + 1)) & 1u ? 0u : 0xFFFF0000u);
+                            w.x &= keep[0];
+                            w.y &= keep[1];
+                            w.z &= keep[2];
+                            w.w &= keep[3];
+                        }
+                    }
+                }
+                pe[k][q] = add_f16_f32(lo16(w.w), add_f16_f32(lo16(w.z), add_f16_f32(lo16(w.y), add_f16_f32(lo16(w.x), 0.f))));
+                po[k][q] = add_f16_f32(hi16(w.w), add_f16_f32(hi16(w.z), add_f16_f32(hi16(w.y), add_f16_f32(hi16(w.x), 0.f))));
+                v[k][q] = make_uint4((w.x & 0xFFFFu) | (w.z << 16), (w.y & 0xFFFFu) | (w.w << 16),
+                                     (w.x >> 16) | (w.z & 0xFFFF0000u), (w.y >> 16) | (w.w & 0xFFFF0000u));
+            }
+        }
+        __syncwarp();
+#pragma unroll
+        for (int o = 8; o >= 1; o >>= 1) {
+#pragma unroll
+            for (int k = 0; k < 2; ++k)
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    pe[k][q] += __shfl_xor_sync(0xffffffffu, pe[k][q], o);
+                    po[k][q] += __shfl_xor_sync(0xffffffffu, po[k][q], o);
+                }
+        }
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int c = cb + k * NW;
+            if (c < NC) {
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    const int i = lane + 32 * q;
+                    const int jj = i >> 4, sl = (i >> 2) & 3, wi = i & 3;
+                    xb[64 * c + (wi * 4 + sl) * 4 + jj] = v[k][q];
+                    if ((lane & 15) == 0)
+                        xp4[kCG * c + jj] = make_float4(1024.f * pe[k][q], 1024.f * po[k][q], pe[k][q] + po[k][q], 0.f);
+                }
+            }
         }
     }
 }
@@ -299,44 +313,28 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
 // ---------------------------------------------------------------------------
 // Fused batch-1 GEMV
 // ---------------------------------------------------------------------------
-struct GemvArgs {
+struct B1Args {
     const uint8_t* packed;    // reference layout [d_out][d_in/2]
     const uint16_t* scales;   // reference layout [d_out][G]
     const uint16_t* zeros;
     const uint8_t* native;    // unit layout (native_bytes), or null
     const uint16_t* w16;      // row-major FP16 (split path without mirror)
     const uint16_t* w16_cm;   // column-major FP16 mirror
+    const uint16_t* x;
     uint16_t* y;
-    const uint8_t* plan;      // workspace: activation plan
-    float* fix;               // workspace: partial row sums of shared row blocks
-    unsigned int* cnt;        // workspace: arrival counters of shared row blocks
-    int d_out, d_in, n_rb, NC, U, nrb_max;
+    unsigned long long* fix;  // workspace: per CTA, the published partial sums of its first row block
+    float k;
+    int d_out, d_in, NC, U, nrb_max;
+    B1Smem S;
 };
 
-template <bool kCM>
-__device__ __forceinline__ uint32_t load_w16_pair(const GemvArgs& a, int r, int c) {
-    // (W16[r][c], W16[r+1][c]) as an f16 pair; rows past d_out read as 0.
-    if (kCM) {
-        const uint16_t* p = a.w16_cm + static_cast<size_t>(c) * a.d_out + r;
-        if (r + 1 < a.d_out) {
-            if ((a.d_out & 1) == 0) {
-                uint32_t v;
-                asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(v) : "l"(p));
-                return v;
-            }
-            return pack_h2(ldg_u16(p), ldg_u16(p + 1));
-        }
-        return (r < a.d_out) ? static_cast<uint32_t>(ldg_u16(p)) : 0u;
-    }
-    const uint16_t* p = a.w16 + static_cast<size_t>(r) * a.d_in + c;
-    const uint16_t lo = (r < a.d_out) ? ldg_u16(p) : static_cast<uint16_t>(0);
-    const uint16_t hi = (r + 1 < a.d_out) ? ldg_u16(p + a.d_in) : static_cast<uint16_t>(0);
-    return pack_h2(lo, hi);
-}
-
-__device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
-    return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
-}
+// How the split path reads the FP16 weights of outlier columns.
+enum : int {
+    kOutNone = 0,       // INT4 only
+    kOutStaged = 1,     // column-major mirror, d_out % 8 == 0: bulk copies of row segments
+    kOutColDirect = 2,  // column-major mirror, other d_out: plain loads
+    kOutRowDirect = 3,  // row-major FP16 only: plain loads
+};
 
 __host__ __device__ inline int unit_start(long long U, int c, int P) {
     return static_cast<int>(U * c / P);
@@ -347,60 +345,65 @@ __host__ __device__ inline int unit_owner(long long u, int P, long long U) {
 
 // kNative: weights in the unit layout (one bulk copy per unit, scale/zero
 // inside); otherwise the reference layout (one bulk copy per weight row of the
-// unit, scale/zero by plain loads).  kStage: outlier columns staged by cp.async
-// (column-major mirror with d_out % 8 == 0); otherwise loaded directly.
-template <bool kSplit, bool kCM, bool kNative, bool kStage>
-__global__ void __launch_bounds__(kT, 1) gemv_kernel(const GemvArgs a) {
+// unit, scale/zero by plain loads).
+template <bool kSplit, bool kNative, int kOut>
+__global__ void __launch_bounds__(kT, 1) b1_kernel(const B1Args a) {
     extern __shared__ __align__(128) char smem[];
-    const GemvSmem S = gemv_smem(a.d_in, a.nrb_max);
     const int G = a.d_in / kGroup;
     const int NC = a.NC;
+    const int n8 = a.d_in >> 3;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t = lane & 3;
-    const int p = lane & 7, q = lane >> 3;  // outlier lanes: rows 2p, 2p+1 of staged outlier q (+4i)
     const int P = gridDim.x, c = blockIdx.x;
     const long long U = a.U;
 
+    // This CTA's units [cu0, cu1) in (row block, chunk) order.  Warp w takes
+    // cu0 + w, cu0 + w + 8, ..., so all warps work through the first row block
+    // together at the start and through the last one at the end.
     const int cu0 = unit_start(U, c, P), cu1 = unit_start(U, c + 1, P);
     const int rbf = cu0 / NC;                 // first row block touched by this CTA
     const int rbz = (cu1 - 1) / NC;           // last
     const int nrb = rbz - rbf + 1;
-    const int wu0 = cu0 + static_cast<int>(static_cast<long long>(cu1 - cu0) * warp / kW);
-    const int wu1 = cu0 + static_cast<int>(static_cast<long long>(cu1 - cu0) * (warp + 1) / kW);
+    // A row block split between CTAs is finished by the CTA holding its chunk 0
+    // (the "finaliser", for which it is the last row block); every later CTA
+    // touching it (a "contributor", for which it is the first row block)
+    // publishes its partial row sums early, without the outlier columns, which
+    // the finaliser adds for the whole block.
+    const bool contrib = cu0 > rbf * NC;
+    const bool finaliser = cu1 < (rbz + 1) * NC && !(rbf == rbz && contrib);
+    const int n_pub = min(kW, min(cu1, (rbf + 1) * NC) - cu0);  // warps holding units of rbf
+    const int wn = (cu1 - cu0 > warp) ? (cu1 - cu0 - warp + kW - 1) / kW : 0;  // units of this warp
+    const int orb0 = contrib ? rbf + 1 : rbf;  // outlier rows of this CTA: row blocks orb0 .. rbz
     const size_t row_stride = static_cast<size_t>(a.d_in) / 2;
 
-    char* ring_p = smem + S.ring + warp * kStages * kStageBytes;
-    const uint32_t ring = smem_u32(ring_p);
-    const uint32_t bars = smem_u32(smem + S.bars) + warp * kStages * 8;
-    const uint32_t planbar = smem_u32(smem + S.bars) + kW * kStages * 8;
-    float* part = reinterpret_cast<float*>(smem + S.part);
-    const PlanLayout PL = plan_layout(a.d_in);
-    const char* plan_s = smem + S.plan;
-    const uint4* bsm = reinterpret_cast<const uint4*>(plan_s + PL.bsm);
-    const float4* xp4 = reinterpret_cast<const float4*>(plan_s + PL.xp);
-    const int* goff = reinterpret_cast<const int*>(plan_s + PL.goff);
-    const uint32_t* list = reinterpret_cast<const uint32_t*>(plan_s + PL.list);
-    int* flags = reinterpret_cast<int*>(smem + S.misc);
+    const uint32_t ring = smem_u32(smem + a.S.ring) + warp * kStages * kStageBytes;
+    const uint32_t bars = smem_u32(smem + a.S.bars) + warp * kStages * 8;
+    float* part = reinterpret_cast<float*>(smem + a.S.part);
+    uint4* xb = reinterpret_cast<uint4*>(smem + a.S.bsm);
+    float4* xp4 = reinterpret_cast<float4*>(smem + a.S.xp);
+    uint8_t* mask = reinterpret_cast<uint8_t*>(smem + a.S.mask);
+    float* red = reinterpret_cast<float*>(smem + a.S.red);
+    uint32_t* list = reinterpret_cast<uint32_t*>(smem + a.S.list);
+    const int ostride = a.nrb_max * 32;  // bytes per staged outlier column
 
     if (lane == 0) {
 #pragma unroll
         for (int s = 0; s < kStages; ++s) mbar_init(bars + 8 * s, 1);
-        if (warp == 0) mbar_init(planbar, 1);
         fence_mbar_init();
     }
-    for (int i = tid; i < nrb * kW * 16; i += kT) part[i] = 0.f;
+    for (int i = tid; i < nrb * (kW + 1) * 16; i += kT) part[i] = 0.f;
+    for (int i = tid; i < kB1ChunkB / 16; i += kT) reinterpret_cast<uint4*>(smem + a.S.zero)[i] = make_uint4(0, 0, 0, 0);
     __syncthreads();
 
-    uint32_t szr0[kStages], szr8[kStages];  // reference-layout (scale, zero): lane t's group
+    uint32_t szr0[kStages], szr8[kStages];  // reference layout: (scale, zero) of lane t's group, rows g, g+8
 
-    // Weight bytes of unit u into stage s (the stage's phase still needs the
-    // arrival of lane 0, after the outlier copies are registered).
-    auto issue_weights = [&](int s, int u) {
-        const int rb = u / NC, cc = u % NC;
+    // Weight bytes of unit u into stage s.
+    auto issue = [&](int s, int u) {
+        const int rb = u / NC, cc = u - rb * NC;
         const uint32_t bar = bars + 8 * s;
         if (kNative) {
             if (lane == 0) {
-                mbar_expect_tx(bar, kB1UnitBytes);
+                mbar_arrive_expect_tx(bar, kB1UnitBytes);
                 bulk_g2s(ring + s * kStageBytes, a.native + static_cast<size_t>(u) * kB1UnitBytes, kB1UnitBytes, bar);
             }
         } else {
@@ -408,7 +411,7 @@ __global__ void __launch_bounds__(kT, 1) gemv_kernel(const GemvArgs a) {
             const int ng = min(kCG, G - kCG * cc);
             const int vrows = min(kRowBlock, a.d_out - rbase);
             const uint32_t rbytes = static_cast<uint32_t>(ng) * 64u;
-            if (lane == 0) mbar_expect_tx(bar, vrows * rbytes);
+            if (lane == 0) mbar_arrive_expect_tx(bar, vrows * rbytes);
             __syncwarp();
             if (lane < vrows)
                 bulk_g2s(ring + s * kStageBytes + lane * kB1RowPitch,
@@ -427,167 +430,100 @@ __global__ void __launch_bounds__(kT, 1) gemv_kernel(const GemvArgs a) {
         }
     };
 
-    // Outlier columns of unit u into stage s (first 16: two 16-byte halves per
-    // column, one cp.async per lane), then lane 0's arrival closes the phase.
-    auto issue_outliers_and_arrive = [&](int s, int u) {
-        const uint32_t bar = bars + 8 * s;
-        if (kSplit && kStage) {
-            const int rb = u / NC, cc = u % NC;
-            const int j0 = kCG * cc, j1 = min(G, j0 + kCG);
-            const int ob = goff[j0], n = min(goff[j1] - ob, kB1OutlierSlots);
-            const int slot = lane >> 1, half = lane & 1;
-            const int r = rb * kRowBlock + 8 * half;
-            if (slot < n && r < a.d_out) {
-                const int col = static_cast<int>(list[ob + slot] & 0xFFFFu);
-                cp_async16(ring + s * kStageBytes + kB1StageOutliers + slot * 32 + half * 16,
-                           a.w16_cm + static_cast<size_t>(col) * a.d_out + r);
+    // FP16 rows orb0*16 .. rbz*16+15 of outlier columns list[b0 .. b0+nb) into
+    // obuf: 16-byte cp.async pieces spread over all threads (the load/store
+    // path, leaving the bulk-copy engine to the weight stream); completed by
+    // cp_async_wait_all.
+    auto issue_outliers = [&](int b0, int nb) {
+        const uint32_t ob = smem_u32(smem + a.S.obuf);
+        const int maxp = nrb * 2;  // 16-byte pieces per column slot
+        const int r_lo = orb0 * kRowBlock, r_hi = min((rbz + 1) * kRowBlock, a.d_out);
+        for (int it = tid; it < nb * maxp; it += kT) {
+            const int o = it / maxp, pc = it - o * maxp;
+            const int r0 = rbf * kRowBlock + 8 * pc;
+            if (r0 >= r_lo && r0 < r_hi) {
+                const int col = static_cast<int>(list[b0 + o] & 0xFFFFu);
+                cp_async16(ob + o * ostride + pc * 16, a.w16_cm + static_cast<size_t>(col) * a.d_out + r0);
             }
-            cp_async_mbar_arrive(bar);
-            __syncwarp();
         }
-        if (lane == 0) mbar_arrive(bar);
+        cp_async_commit();
     };
 
-    float acc0 = 0.f, acc8 = 0.f, cor0 = 0.f, cor1 = 0.f;
-
-    auto consume = [&](int s, int u, bool flush) {
-        const char* st = ring_p + s * kStageBytes;
-        const int rb = u / NC, cc = u % NC;
-        const int j0 = kCG * cc;
-        const int ng = min(kCG, G - j0);
-        // packed words of rows g and g+8 for the unit's groups
-        uint4 aw[kCG][2];
-#pragma unroll
-        for (int jj = 0; jj < kCG; ++jj)
-#pragma unroll
-            for (int h = 0; h < 2; ++h)
-                aw[jj][h] = kNative
-                                ? *reinterpret_cast<const uint4*>(st + ((jj * 2 + h) * 32 + lane) * 16)
-                                : *reinterpret_cast<const uint4*>(st + (g + 8 * h) * kB1RowPitch + 64 * jj + 16 * t);
-        // Two independent accumulators per group (even / odd columns): 8 chains of 4 MMAs.
-        float dl[kCG][4], dh[kCG][4];
-#pragma unroll
-        for (int jj = 0; jj < kCG; ++jj)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) dl[jj][i] = dh[jj][i] = 0.f;
-#pragma unroll
-        for (int wi = 0; wi < 4; ++wi) {
-#pragma unroll
-            for (int jj = 0; jj < kCG; ++jj) {
-                if (jj < ng) {
-                    const uint4 bq = (g == 0) ? bsm[((j0 + jj) * 4 + wi) * 4 + t] : make_uint4(0, 0, 0, 0);
-                    const Biased4 qa = biased_word(word_of(aw[jj][0], wi));
-                    const Biased4 qb = biased_word(word_of(aw[jj][1], wi));
-                    mma_16816(dl[jj], qa.lo0, qb.lo0, qa.lo1, qb.lo1, bq.x, bq.y);
-                    mma_16816(dh[jj], qa.hi0, qb.hi0, qa.hi1, qb.hi1, bq.z, bq.w);
-                }
-            }
-        }
-        uint32_t sz0[kCG], sz8[kCG];
-        if (kNative) {
-            const uint4 v0 = *reinterpret_cast<const uint4*>(st + kB1UnitPacked + 16 * g);
-            const uint4 v8 = *reinterpret_cast<const uint4*>(st + kB1UnitPacked + 16 * (g + 8));
-            sz0[0] = v0.x; sz0[1] = v0.y; sz0[2] = v0.z; sz0[3] = v0.w;
-            sz8[0] = v8.x; sz8[1] = v8.y; sz8[2] = v8.z; sz8[3] = v8.w;
-        } else {
-#pragma unroll
-            for (int jj = 0; jj < kCG; ++jj) {
-                sz0[jj] = __shfl_sync(0xffffffffu, szr0[s], (lane & ~3) + jj);
-                sz8[jj] = __shfl_sync(0xffffffffu, szr8[s], (lane & ~3) + jj);
-            }
-        }
-        if (t == 0) {
-            // D_lo = 1024*Xe + S_even, D_hi = 1024*Xo + 16*S_odd  ->  S = S_even + S_odd;
-            // y += s * (S - z * X) over the non-outlier columns of the group.
-#pragma unroll
-            for (int jj = 0; jj < kCG; ++jj) {
-                if (jj < ng) {
-                    const float4 xq = xp4[j0 + jj];
-                    const float s0 = h2f_bits(sz0[jj] & 0xFFFFu), z0 = h2f_bits(sz0[jj] >> 16);
-                    const float s8 = h2f_bits(sz8[jj] & 0xFFFFu), z8 = h2f_bits(sz8[jj] >> 16);
-                    const float S0 = fmaf(dh[jj][0] - xq.y, 0.0625f, dl[jj][0] - xq.x);
-                    const float S8 = fmaf(dh[jj][2] - xq.y, 0.0625f, dl[jj][2] - xq.x);
-                    acc0 = fmaf(s0, fmaf(-z0, xq.z, S0), acc0);
-                    acc8 = fmaf(s8, fmaf(-z8, xq.z, S8), acc8);
-                }
-            }
-        }
-        if (kSplit) {
-            const int ob = goff[j0], n = goff[j0 + ng] - ob;
-            const int r = rb * kRowBlock + 2 * p;
-            int first_direct = 0;
-            if (kStage) {
-                first_direct = kB1OutlierSlots;
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int o = q + 4 * i;
-                    if (o < n) {
-                        const uint32_t w = *reinterpret_cast<const uint32_t*>(st + kB1StageOutliers + o * 32 + 4 * p);
-                        const float xv = h2f_bits(static_cast<uint16_t>(list[ob + o] >> 16));
-                        cor0 = fmaf(h2f_bits(w & 0xFFFFu), xv, cor0);
-                        cor1 = fmaf(h2f_bits(w >> 16), xv, cor1);
-                    }
-                }
-            }
-            for (int o = first_direct + q; o < n; o += 4) {
-                const uint32_t e = list[ob + o];
-                const float xv = h2f_bits(static_cast<uint16_t>(e >> 16));
-                const uint32_t w = load_w16_pair<kCM>(a, r, static_cast<int>(e & 0xFFFFu));
-                cor0 = fmaf(h2f_bits(w & 0xFFFFu), xv, cor0);
-                cor1 = fmaf(h2f_bits(w >> 16), xv, cor1);
-            }
-        }
-        if (flush) {
-            // End of this warp's part of the row block: publish its row sums.
-            float* pp = part + ((rb - rbf) * kW + warp) * 16;
-            if (t == 0) {
-                pp[g] = acc0;
-                pp[g + 8] = acc8;
-            }
-            if (kSplit) {
-                cor0 += __shfl_xor_sync(0xffffffffu, cor0, 8);
-                cor0 += __shfl_xor_sync(0xffffffffu, cor0, 16);
-                cor1 += __shfl_xor_sync(0xffffffffu, cor1, 8);
-                cor1 += __shfl_xor_sync(0xffffffffu, cor1, 16);
-                __syncwarp();
-                if (lane < 8) {
-                    pp[2 * lane] += cor0;
-                    pp[2 * lane + 1] += cor1;
-                }
-            }
-            acc0 = acc8 = cor0 = cor1 = 0.f;
-        }
-    };
-
-    // Weights of the first units go out before the plan is ready.
+    // The first unit of each warp goes out before the previous kernel has
+    // finished; x is requested next, ahead of the other stages, because the
+    // plan (and so every MMA) waits for it.
     uint32_t armed = 0;
 #pragma unroll
-    for (int s = 0; s < kStages; ++s)
-        if (wu0 + s < wu1) {
-            issue_weights(s, wu0 + s);
+    for (int s = 0; s < kStages; ++s) {
+        if (s == 1) {
+            pdl_launch_dependents();
+            pdl_wait();  // x, y and the workspace may belong to the preceding kernel until here
+            load_x_async<kT>(a.x, n8, xb);
+        }
+        if (s < wn) {
+            issue(s, cu0 + warp + kW * s);
             armed |= 1u << s;
         }
-
-    // Wait for the plan kernel (programmatic dependent launch), then bring the plan in.
-    pdl_wait();
-    if (tid == 0) {
-        mbar_arrive_expect_tx(planbar, PL.copy_bytes);
-        bulk_g2s(smem_u32(smem + S.plan), a.plan, PL.copy_bytes, planbar);
     }
-    bool ok = mbar_wait_bounded(planbar, 0);
-    ok = __all_sync(0xffffffffu, ok);
-    if (!ok && lane == 0) atomicOr(&g_error_word, 1u);
+    cp_async_wait_all();
+    __syncthreads();
 
+    // ---- activation plan ----
+    int n_out = 0;
+    if (kSplit) {
+        const float total = x_sum<kT>(xb, n8, red);
+        const XStats st = x_stats<kT>(xb, n8, a.d_in, a.k, total, red);
+        x_mask<kT>(xb, n8, st.mean, st.thresh, mask);
+        n_out = x_list<kT>(reinterpret_cast<const uint16_t*>(xb), a.d_in, reinterpret_cast<uint32_t*>(mask), list,
+                           reinterpret_cast<int*>(red));
+    }
+    __syncthreads();  // list complete; x no longer read in natural order
+    const int ocap = (kOut == kOutStaged) ? a.S.obuf_bytes / ostride : n_out;
+    if (kSplit && kOut == kOutStaged && n_out > 0 && orb0 <= rbz) issue_outliers(0, min(ocap, n_out));
+    x_fragments<kT, kSplit>(xb, n8, NC, mask, xp4);
+    __syncthreads();
+
+    // Partial row sums of rbf (shared with earlier CTAs) go to the workspace as
+    // soon as the warps holding its units are done with it: those warps meet on
+    // named barrier 1 and the last of them publishes.  Each sum is one 64-bit
+    // word (1 << 32 | FP32 bits), written in one piece, so the finaliser needs
+    // no fence or flag: a nonzero high half marks a published value.  Called
+    // exactly once by each of warps 0 .. n_pub-1 (also on the error path, so
+    // that the barrier fills).
+    bool pub_pending = contrib && warp < n_pub;
+    auto publish_first = [&]() {
+        if (warp == n_pub - 1) {
+            if (n_pub > 1) named_bar_sync(1, n_pub * 32);
+            if (lane < 16) {
+                float v = 0.f;
 #pragma unroll
-    for (int s = 0; s < kStages; ++s)
-        if (wu0 + s < wu1) issue_outliers_and_arrive(s, wu0 + s);
+                for (int w = 0; w < kW; ++w) v += part[w * 16 + lane];
+                st_relaxed_gpu_u64(a.fix + c * 16 + lane, (1ull << 32) | __float_as_uint(v));
+            }
+        } else {
+            named_bar_arrive(1, n_pub * 32);
+        }
+    };
+    // The finaliser's warp 0 (lanes 0-15 = rows of rbz) adds the contributors'
+    // sums in CTA order.  With one contributor its word is loaded in the middle
+    // of the unit loop and only inspected at the end.
+    const int c_hi = finaliser ? unit_owner(static_cast<long long>(rbz + 1) * NC - 1, P, U) : c;
+    unsigned long long early = 0ull;
 
+    // ---- units ----
+    const uint32_t zero_a = smem_u32(smem + a.S.zero);
+    const uint32_t bsm_a = smem_u32(xb);
+    const uint32_t xp_a = smem_u32(xp4);
+    const bool b_owner = (g >> 1) == t;  // lane supplies B column 2t (g even) or 2t+1 (g odd)
+    const uint32_t b_lane = t * 16 + (g & 1) * 8;
+    float acc0 = 0.f, acc8 = 0.f;
+    bool ok = true;
     uint32_t phase = 0;
-    for (int ub = wu0; ub < wu1 && ok; ub += kStages) {
+    for (int ib = 0; ib < wn && ok; ib += kStages) {
 #pragma unroll
         for (int s = 0; s < kStages; ++s) {
-            const int u = ub + s;
-            if (u < wu1 && ok) {
+            const int i = ib + s;
+            if (i < wn && ok) {
                 const bool got = mbar_wait_bounded(bars + 8 * s, (phase >> s) & 1u);
                 if (!__all_sync(0xffffffffu, got)) {
                     ok = false;
@@ -595,13 +531,76 @@ __global__ void __launch_bounds__(kT, 1) gemv_kernel(const GemvArgs a) {
                 } else {
                     phase ^= 1u << s;
                     armed &= ~(1u << s);
-                    consume(s, u, (u % NC) == NC - 1 || u == wu1 - 1);
-                    __syncwarp();
-                    if (u + kStages < wu1) {
-                        issue_weights(s, u + kStages);
-                        armed |= 1u << s;
-                        issue_outliers_and_arrive(s, u + kStages);
+                    const int u = cu0 + warp + kW * i;
+                    const int rb = u / NC, cc = u - rb * NC;
+                    const uint32_t st = ring + s * kStageBytes;
+                    uint4 aw[4][2];  // [slice][row g / g+8]: 32 columns of group t
+#pragma unroll
+                    for (int sl = 0; sl < 4; ++sl)
+#pragma unroll
+                        for (int h = 0; h < 2; ++h)
+                            aw[sl][h] = kNative ? lds_v4(st + ((sl * 2 + h) * 32 + lane) * 16)
+                                                : lds_v4(st + (g + 8 * h) * kB1RowPitch + 64 * t + 16 * sl);
+                    const uint32_t bb = (b_owner ? bsm_a + cc * kB1ChunkB : zero_a) + b_lane;
+                    float dl[4][4], dh[4][4];
+#pragma unroll
+                    for (int sl = 0; sl < 4; ++sl)
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) dl[sl][q] = dh[sl][q] = 0.f;
+#pragma unroll
+                    for (int wi = 0; wi < 4; ++wi) {
+#pragma unroll
+                        for (int sl = 0; sl < 4; ++sl) {
+                            const Biased4 qa = biased_word(word_of(aw[sl][0], wi));
+                            const Biased4 qb = biased_word(word_of(aw[sl][1], wi));
+                            const uint2 b = lds_v2(bb + (wi * 4 + sl) * 64);
+                            mma_16816(dl[sl], qa.lo0, qb.lo0, qa.lo1, qb.lo1, b.x, b.y);
+                            mma_16816(dh[sl], qa.hi0, qb.hi0, qa.hi1, qb.hi1, b.x, b.y);
+                        }
                     }
+                    const float lo0 = (dl[0][0] + dl[1][0]) + (dl[2][0] + dl[3][0]);
+                    const float hi0 = (dh[0][1] + dh[1][1]) + (dh[2][1] + dh[3][1]);
+                    const float lo8 = (dl[0][2] + dl[1][2]) + (dl[2][2] + dl[3][2]);
+                    const float hi8 = (dh[0][3] + dh[1][3]) + (dh[2][3] + dh[3][3]);
+                    uint32_t sz0, sz8;
+                    if (kNative) {
+                        sz0 = lds_u32(st + kB1UnitPacked + 16 * g + 4 * t);
+                        sz8 = lds_u32(st + kB1UnitPacked + 16 * (g + 8) + 4 * t);
+                    } else {
+                        sz0 = szr0[s];
+                        sz8 = szr8[s];
+                    }
+                    const uint4 xqb = lds_v4(xp_a + (kCG * cc + t) * 16);
+                    const float xe = __uint_as_float(xqb.x), xo = __uint_as_float(xqb.y), xs = __uint_as_float(xqb.z);
+                    const float S0 = fmaf(hi0 - xo, 0.0625f, lo0 - xe);
+                    const float S8 = fmaf(hi8 - xo, 0.0625f, lo8 - xe);
+                    acc0 = fmaf(h2f_bits(lo16(sz0)), fmaf(-h2f_bits(hi16(sz0)), xs, S0), acc0);
+                    acc8 = fmaf(h2f_bits(lo16(sz8)), fmaf(-h2f_bits(hi16(sz8)), xs, S8), acc8);
+                    const bool last_in_rb = i == wn - 1 || u + kW >= (rb + 1) * NC;
+                    if (last_in_rb) {
+                        // This warp is done with row block rb: publish its row sums.
+                        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+                        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+                        acc8 += __shfl_xor_sync(0xffffffffu, acc8, 1);
+                        acc8 += __shfl_xor_sync(0xffffffffu, acc8, 2);
+                        if (t == 0) {
+                            float* pp = part + ((rb - rbf) * (kW + 1) + warp) * 16;
+                            pp[g] = acc0;
+                            pp[g + 8] = acc8;
+                        }
+                        acc0 = acc8 = 0.f;
+                    }
+                    __syncwarp();
+                    if (i + kStages < wn) {
+                        issue(s, u + kW * kStages);
+                        armed |= 1u << s;
+                    }
+                    if (last_in_rb && rb == rbf && pub_pending) {
+                        publish_first();
+                        pub_pending = false;
+                    }
+                    if (finaliser && c_hi == c + 1 && warp == 0 && i == wn / 2)
+                        early = ld_relaxed_gpu_u64(a.fix + (c + 1) * 16 + (lane & 15));
                 }
             }
         }
@@ -612,72 +611,142 @@ __global__ void __launch_bounds__(kT, 1) gemv_kernel(const GemvArgs a) {
         for (int s = 0; s < kStages; ++s)
             if (armed & (1u << s)) mbar_wait_bounded(bars + 8 * s, (phase >> s) & 1u);
     }
+    if (pub_pending) publish_first();  // error path: keep named barrier 1 balanced
+    const bool blk_ok = __syncthreads_and(ok) != 0;
+
+    // ---- outlier columns: y[r] += W16[r][c] * x[c] for rows of row blocks orb0 .. rbz ----
+    if (kSplit && kOut != kOutNone && n_out > 0 && orb0 <= rbz) {
+        if (!blk_ok) {
+            if (kOut == kOutStaged) cp_async_wait_all();
+        } else {
+            const int nq = (rbz - orb0 + 1) * 4;  // row quads
+            const int nsl = nq >= kT ? 1 : kT / nq;
+            const uint32_t ob = smem_u32(smem + a.S.obuf);
+            for (int b0 = 0; b0 < n_out; b0 += ocap) {
+                const int nb = min(ocap, n_out - b0);
+                if (kOut == kOutStaged) {
+                    if (b0 > 0) {
+                        __syncthreads();  // previous batch consumed
+                        issue_outliers(b0, nb);
+                    }
+                    cp_async_wait_all();
+                    __syncthreads();
+                }
+                for (int it = tid; it < nq * nsl; it += kT) {
+                    const int qd = it % nq, slice = it / nq;
+                    const int rb_rel = orb0 - rbf + (qd >> 2), rr = (qd & 3) * 4;
+                    const int row = (rbf + rb_rel) * kRowBlock + rr;
+                    float sr[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 2
+                    for (int o = slice; o < nb; o += nsl) {
+                        const uint32_t e = list[b0 + o];
+                        const int col = static_cast<int>(e & 0xFFFFu);
+                        const uint16_t xv = hi16(e);
+                        uint32_t w01, w23;
+                        if (kOut == kOutStaged) {
+                            const uint2 v = lds_v2(ob + o * ostride + (rb_rel * kRowBlock + rr) * 2);
+                            w01 = v.x;
+                            w23 = v.y;
+                        } else {
+                            uint16_t h[4];
+#pragma unroll
+                            for (int q = 0; q < 4; ++q)
+                                h[q] = row + q < a.d_out
+                                           ? (kOut == kOutColDirect
+                                                  ? ldg_u16(a.w16_cm + static_cast<size_t>(col) * a.d_out + row + q)
+                                                  : ldg_u16(a.w16 + static_cast<size_t>(row + q) * a.d_in + col))
+                                           : static_cast<uint16_t>(0);
+                            w01 = pack_h2(h[0], h[1]);
+                            w23 = pack_h2(h[2], h[3]);
+                        }
+                        sr[0] = fma_f16_f32(lo16(w01), xv, sr[0]);
+                        sr[1] = fma_f16_f32(hi16(w01), xv, sr[1]);
+                        sr[2] = fma_f16_f32(lo16(w23), xv, sr[2]);
+                        sr[3] = fma_f16_f32(hi16(w23), xv, sr[3]);
+                    }
+                    if (nsl == 1) {
+                        float* pp = part + (rb_rel * (kW + 1) + kW) * 16 + rr;
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) pp[q] += sr[q];
+                    } else {
+                        reinterpret_cast<float4*>(red)[slice * nq + qd] = make_float4(sr[0], sr[1], sr[2], sr[3]);
+                    }
+                }
+                if (nsl > 1) {
+                    __syncthreads();
+                    if (tid < nq) {
+                        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                        for (int sl = 0; sl < nsl; ++sl) {
+                            const float4 v = reinterpret_cast<const float4*>(red)[sl * nq + tid];
+                            acc.x += v.x;
+                            acc.y += v.y;
+                            acc.z += v.z;
+                            acc.w += v.w;
+                        }
+                        const int rb_rel = orb0 - rbf + (tid >> 2);
+                        float* pp = part + (rb_rel * (kW + 1) + kW) * 16 + (tid & 3) * 4;
+                        pp[0] += acc.x;
+                        pp[1] += acc.y;
+                        pp[2] += acc.z;
+                        pp[3] += acc.w;
+                    }
+                    __syncthreads();
+                }
+            }
+        }
+    }
     __syncthreads();
 
-    // Row sums: row blocks owned by this CTA alone are written directly; a row
-    // block shared with a neighbour goes through the workspace, and the CTA that
-    // arrives last sums the contributions in CTA order.
+    // Row sums: warps in order, then the outlier slot.  rbf of a contributor was
+    // published above; rbz of a finaliser adds the contributors' sums (in CTA order).
     for (int r = tid; r < nrb * 16; r += kT) {
         const int rbl = r >> 4, rr = r & 15;
         const int rb = rbf + rbl;
+        if ((rbl == 0 && contrib) || (rb == rbz && finaliser)) continue;
         float sum = 0.f;
 #pragma unroll
-        for (int w = 0; w < kW; ++w) sum += part[(rbl * kW + w) * 16 + rr];
-        const bool owned = rb * NC >= cu0 && (rb + 1) * NC <= cu1;
-        if (owned) {
-            const int row = rb * kRowBlock + rr;
-            if (row < a.d_out) a.y[row] = __half_as_ushort(__float2half_rn(sum));
-        } else {
-            a.fix[(c * 2 + (rb == rbf ? 0 : 1)) * 16 + rr] = sum;
-        }
+        for (int w = 0; w <= kW; ++w) sum += part[(rbl * (kW + 1) + w) * 16 + rr];
+        const int row = rb * kRowBlock + rr;
+        if (row < a.d_out) a.y[row] = __half_as_ushort(__float2half_rn(sum));
     }
-    __threadfence();
-    __syncthreads();
-    if (tid < 2) {
-        const int rb = tid == 0 ? rbf : rbz;
-        const bool shared = !(rb * NC >= cu0 && (rb + 1) * NC <= cu1) && (tid == 0 || rbz != rbf);
-        int last = 0;
-        if (shared) {
-            const int c_first = unit_owner(static_cast<long long>(rb) * NC, P, U);
-            const int c_last = unit_owner(static_cast<long long>(rb + 1) * NC - 1, P, U);
-            const unsigned int ticket = atomicAdd(&a.cnt[rb], 1u);
-            last = ticket == static_cast<unsigned int>(c_last - c_first) ? 1 : 0;
-        }
-        flags[tid] = last;
-    }
-    __syncthreads();
+    if (finaliser && warp == 0) {
+        const int rbl = rbz - rbf;
+        float sum = 0.f;
 #pragma unroll
-    for (int which = 0; which < 2; ++which) {
-        if (flags[which]) {
-            __threadfence();
-            const int rb = which == 0 ? rbf : rbz;
-            const int c_first = unit_owner(static_cast<long long>(rb) * NC, P, U);
-            const int c_last = unit_owner(static_cast<long long>(rb + 1) * NC - 1, P, U);
-            if (tid < 16) {
-                float sum = 0.f;
-                for (int cc = c_first; cc <= c_last; ++cc) {
-                    const int slot = (rb == unit_start(U, cc, P) / NC) ? 0 : 1;
-                    sum += ldcg_f32(a.fix + (cc * 2 + slot) * 16 + tid);
-                }
-                const int row = rb * kRowBlock + tid;
-                if (row < a.d_out) a.y[row] = __half_as_ushort(__float2half_rn(sum));
+        for (int w = 0; w <= kW; ++w) sum += part[(rbl * (kW + 1) + w) * 16 + (lane & 15)];
+        bool ok_all = true;
+        for (int cc = c + 1; cc <= c_hi; ++cc) {
+            unsigned long long* slot = a.fix + cc * 16 + (lane & 15);
+            unsigned long long v = (cc == c + 1) ? early : 0ull;
+            if ((v >> 32) == 0ull) {
+                v = ld_relaxed_gpu_u64(slot);
+                const long long t0 = clock64();
+                while ((v >> 32) == 0ull && clock64() - t0 < (1ll << 31)) v = ld_relaxed_gpu_u64(slot);
             }
-            if (tid == 0) a.cnt[rb] = 0;
+            ok_all = ok_all && (v >> 32) != 0ull;
+            sum += __uint_as_float(static_cast<uint32_t>(v));
         }
+        if (!__all_sync(0xffffffffu, ok_all) && lane == 0) atomicOr(&g_error_word, 2u);
+        const int row = rbz * kRowBlock + lane;
+        if (lane < 16 && row < a.d_out) a.y[row] = __half_as_ushort(__float2half_rn(sum));
+        __syncwarp();
+        // Leave the slots zero for the next call.
+        for (int i = lane; i < (c_hi - c) * 16; i += 32) st_relaxed_gpu_u64(a.fix + (c + 1) * 16 + i, 0ull);
     }
 }
 
 // Native unit layout: per (row-block rb, 4-group chunk c) one block of
-// kB1UnitBytes = 4096 bytes of packed codes ordered [group jj][half h][lane]
-// (16 bytes each: row rb*16 + g + 8h, columns 128(4c+jj) + 32t .. +31, with
-// lane = 4g + t) followed by 256 bytes of (scale | zero << 16) for
-// [16 rows][4 groups].  Rows past d_out and groups past G are zero.
+// kB1UnitBytes = 4096 bytes of packed codes ordered [slice sl][half h][lane]
+// (16 bytes each: row rb*16 + g + 8h, group 4c + t, columns 32 sl .. 32 sl + 31
+// of that group, with lane = 4g + t) followed by 256 bytes of
+// (scale | zero << 16) for [16 rows][4 groups].  Rows past d_out and groups
+// past G are zero.
 __global__ void build_native_kernel(const uint8_t* __restrict__ packed, const uint16_t* __restrict__ scales,
                                     const uint16_t* __restrict__ zeros, int d_out, int d_in,
                                     uint8_t* __restrict__ out, long long n_chunks) {
     const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (idx >= n_chunks) return;
-    constexpr int kChunks = kB1UnitBytes / 16;  // 272 sixteen-byte chunks per unit
+    constexpr int kChunks = kB1UnitBytes / 16;  // 272 sixteen-byte pieces per unit
     const int G = d_in / kGroup;
     const int NC = (G + kCG - 1) / kCG;
     const long long unit = idx / kChunks;
@@ -685,12 +754,11 @@ __global__ void build_native_kernel(const uint8_t* __restrict__ packed, const ui
     const int rb = static_cast<int>(unit / NC), c = static_cast<int>(unit % NC);
     uint4 v = make_uint4(0, 0, 0, 0);
     if (i < kB1UnitPacked / 16) {
-        const int jj = i >> 6, h = (i >> 5) & 1, ln = i & 31;
+        const int sl = i >> 6, h = (i >> 5) & 1, ln = i & 31;
         const int row = rb * kRowBlock + (ln >> 2) + 8 * h;
-        const int grp = kCG * c + jj;
+        const int grp = kCG * c + (ln & 3);
         if (row < d_out && grp < G)
-            v = *reinterpret_cast<const uint4*>(packed + static_cast<size_t>(row) * (d_in / 2) + 64 * grp +
-                                                16 * (ln & 3));
+            v = *reinterpret_cast<const uint4*>(packed + static_cast<size_t>(row) * (d_in / 2) + 64 * grp + 16 * sl);
     } else {
         const int row = rb * kRowBlock + (i - kB1UnitPacked / 16);
         uint32_t e[4];
@@ -706,6 +774,75 @@ __global__ void build_native_kernel(const uint8_t* __restrict__ packed, const ui
         v = make_uint4(e[0], e[1], e[2], e[3]);
     }
     *reinterpret_cast<uint4*>(out + 16 * idx) = v;
+}
+
+// ---------------------------------------------------------------------------
+// Standalone outlier detector (one 1024-thread CTA): the same mask, list and
+// statistics as the GEMV's plan, written out.
+// ---------------------------------------------------------------------------
+struct DetectSmem {
+    int xs, mask, list, red, total;
+};
+__host__ __device__ inline DetectSmem detect_smem(int d_in) {
+    DetectSmem S;
+    int off = 0;
+    S.xs = off;   off += 2 * d_in;
+    S.mask = off; off += align16(d_in / 8);
+    S.list = off; off += align16(d_in);
+    S.red = off;  off += 1024;
+    S.total = off;
+    return S;
+}
+
+__global__ void __launch_bounds__(kPlanThreads, 1)
+    detect_kernel(const uint16_t* __restrict__ x, int d_in, float k, uint32_t* mask_words, int32_t* indices,
+                  int32_t* count, float* stats) {
+    extern __shared__ __align__(128) char smem[];
+    const DetectSmem S = detect_smem(d_in);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int n8 = d_in / 8;
+    uint4* xs = reinterpret_cast<uint4*>(smem + S.xs);
+    uint8_t* mask = reinterpret_cast<uint8_t*>(smem + S.mask);
+    uint32_t* list = reinterpret_cast<uint32_t*>(smem + S.list);
+    float* red = reinterpret_cast<float*>(smem + S.red);
+    load_x_async<kPlanThreads>(x, n8, xs);
+    cp_async_wait_all();
+    __syncthreads();
+    const float total = x_sum<kPlanThreads>(xs, n8, red);
+    const XStats st = x_stats<kPlanThreads>(xs, n8, d_in, k, total, red);
+    x_mask<kPlanThreads>(xs, n8, st.mean, st.thresh, mask);
+    const int n = x_list<kPlanThreads>(reinterpret_cast<const uint16_t*>(xs), d_in,
+                                       reinterpret_cast<uint32_t*>(mask), list, reinterpret_cast<int*>(red));
+    __syncthreads();
+    const uint32_t* words = reinterpret_cast<const uint32_t*>(mask);
+    if (mask_words)
+        for (int i = tid; i < d_in / 32; i += kPlanThreads) mask_words[i] = words[i];
+    if (tid == 0) {
+        if (count) *count = n;
+        if (stats) {
+            stats[0] = st.mean;
+            stats[1] = st.thresh;
+            stats[2] = st.var;
+            stats[3] = st.m2;
+        }
+    }
+    if (indices && warp < 4) {
+        // The reference's list order: stripe class 0 ascending, then 1, 2, 3.
+        int before = 0;
+        for (int i = lane; i < n; i += 32)
+            before += ((static_cast<int>(list[i] & 0xFFFFu) >> 5) & 3) < warp ? 1 : 0;
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) before += __shfl_xor_sync(0xffffffffu, before, o);
+        int pos = before;
+        for (int base = 0; base < n; base += 32) {
+            const int i = base + lane;
+            const int c = (i < n) ? static_cast<int>(list[i] & 0xFFFFu) : 0;
+            const bool mine = i < n && ((c >> 5) & 3) == warp;
+            const unsigned bal = __ballot_sync(0xffffffffu, mine);
+            if (mine) indices[pos + __popc(bal & ((1u << lane) - 1u))] = c;
+            pos += __popc(bal);
+        }
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -919,36 +1056,30 @@ dq_status_t check_launch() {
     return DQ_OK;
 }
 
-int plan_smem_bytes(int d_in) { return plan_layout(d_in).total + 256; }
 
-template <bool kSplit>
-dq_status_t launch_plan(const uint16_t* x, int d_in, float k, uint8_t* plan, uint32_t* mask_words,
-                        int32_t* indices, int32_t* count, float* stats, cudaStream_t stream) {
-    const int smem = plan_smem_bytes(d_in);
-    const dq_status_t st = ensure_smem(plan_kernel<kSplit>, kSplit ? 1 : 2, smem);
-    if (st != DQ_OK) return st;
-    plan_kernel<kSplit><<<1, kPlanThreads, smem, stream>>>(x, d_in, k, plan, mask_words, indices, count, stats);
-    return check_launch();
-}
-
-template <bool kSplit, bool kCM, bool kNative, bool kStage>
-dq_status_t launch_gemv_pdl(const GemvArgs& a, int grid, int smem, cudaStream_t stream) {
-    constexpr int id = 4 + (kSplit ? 8 : 0) + (kCM ? 4 : 0) + (kNative ? 2 : 0) + (kStage ? 1 : 0);
-    const dq_status_t st = ensure_smem(gemv_kernel<kSplit, kCM, kNative, kStage>, id, smem);
+template <bool kSplit, bool kNative, int kOut>
+dq_status_t launch_b1(const B1Args& a, int grid, cudaStream_t stream) {
+    constexpr int id = 8 + (kSplit ? 8 : 0) + (kNative ? 4 : 0) + kOut;
+    const dq_status_t st = ensure_smem(b1_kernel<kSplit, kNative, kOut>, id, a.S.total);
     if (st != DQ_OK) return st;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kT);
-    cfg.dynamicSmemBytes = smem;
+    cfg.dynamicSmemBytes = a.S.total;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_kernel<kSplit, kCM, kNative, kStage>, a);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, b1_kernel<kSplit, kNative, kOut>, a);
     if (e != cudaSuccess) { set_cuda_error(e); return DQ_ERR_CUDA; }
     return check_launch();
+}
+
+template <bool kSplit, int kOut>
+dq_status_t launch_b1_layout(const B1Args& a, int grid, cudaStream_t stream) {
+    return a.native ? launch_b1<kSplit, true, kOut>(a, grid, stream) : launch_b1<kSplit, false, kOut>(a, grid, stream);
 }
 
 }  // namespace
@@ -956,57 +1087,54 @@ dq_status_t launch_gemv_pdl(const GemvArgs& a, int grid, int smem, cudaStream_t 
 dq_status_t launch_gemv_b1(const dq_weights_t& w, const uint16_t* x, uint16_t* y, float k,
                            bool split, void* workspace, cudaStream_t stream) {
     DeviceInfo di;
-    dq_status_t st = device_info(&di);
+    const dq_status_t st = device_info(&di);
     if (st != DQ_OK) return st;
     const int G = w.d_in / kGroup;
-    GemvArgs a;
+    const long long n_rb = (static_cast<long long>(w.d_out) + kRowBlock - 1) / kRowBlock;
+    const int NC = (G + kCG - 1) / kCG;
+    if (n_rb * NC > INT_MAX) return DQ_ERR_UNSUPPORTED;
+    B1Args a;
     a.packed = w.packed;
     a.scales = w.scales;
     a.zeros = w.zeros;
     a.native = w.native;
     a.w16 = w.fp16;
     a.w16_cm = w.fp16_cm;
+    a.x = x;
     a.y = y;
+    a.k = k;
     a.d_out = w.d_out;
     a.d_in = w.d_in;
-    a.n_rb = (w.d_out + kRowBlock - 1) / kRowBlock;
-    a.NC = (G + kCG - 1) / kCG;
-    a.U = a.n_rb * a.NC;
+    a.NC = NC;
+    a.U = static_cast<int>(n_rb * NC);
     const WsLayout W = ws_layout(w.d_out, w.d_in);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
-    a.plan = ws + W.plan;
-    a.fix = reinterpret_cast<float*>(ws + W.fix);
-    a.cnt = reinterpret_cast<unsigned int*>(ws + W.cnt);
+    a.fix = reinterpret_cast<unsigned long long*>(ws + W.fix);
     int grid = di.sm_count < a.U ? di.sm_count : a.U;
     if (grid > kMaxCtas) grid = kMaxCtas;
     int nrb_max = 1;
     for (int c = 0; c < grid; ++c) {
         const int u0 = unit_start(a.U, c, grid), u1 = unit_start(a.U, c + 1, grid);
-        const int n = (u1 - 1) / a.NC - u0 / a.NC + 1;
+        const int n = (u1 - 1) / NC - u0 / NC + 1;
         if (n > nrb_max) nrb_max = n;
     }
     a.nrb_max = nrb_max;
-    const GemvSmem S = gemv_smem(a.d_in, a.nrb_max);
-    if (S.total > di.smem_optin || plan_smem_bytes(a.d_in) > di.smem_optin) return DQ_ERR_UNSUPPORTED;
 
-    st = split ? launch_plan<true>(x, a.d_in, k, ws + W.plan, nullptr, nullptr, nullptr, nullptr, stream)
-               : launch_plan<false>(x, a.d_in, k, ws + W.plan, nullptr, nullptr, nullptr, nullptr, stream);
-    if (st != DQ_OK) return st;
-
-    const bool nat = w.native != nullptr;
-    if (!split)
-        return nat ? launch_gemv_pdl<false, false, true, false>(a, grid, S.total, stream)
-                   : launch_gemv_pdl<false, false, false, false>(a, grid, S.total, stream);
-    if (w.fp16_cm) {
-        const bool stage = (w.d_out % 8) == 0;
-        if (stage)
-            return nat ? launch_gemv_pdl<true, true, true, true>(a, grid, S.total, stream)
-                       : launch_gemv_pdl<true, true, false, true>(a, grid, S.total, stream);
-        return nat ? launch_gemv_pdl<true, true, true, false>(a, grid, S.total, stream)
-                   : launch_gemv_pdl<true, true, false, false>(a, grid, S.total, stream);
+    int out_mode = kOutNone;
+    if (split) out_mode = w.fp16_cm ? ((w.d_out % 8) == 0 ? kOutStaged : kOutColDirect) : kOutRowDirect;
+    a.S = b1_smem(w.d_in, nrb_max, split, out_mode == kOutStaged, di.smem_optin);
+    if (out_mode == kOutStaged && a.S.obuf_bytes < nrb_max * 32) {
+        out_mode = kOutColDirect;  // no room for even one staged column
+        a.S = b1_smem(w.d_in, nrb_max, split, false, di.smem_optin);
     }
-    return nat ? launch_gemv_pdl<true, false, true, false>(a, grid, S.total, stream)
-               : launch_gemv_pdl<true, false, false, false>(a, grid, S.total, stream);
+    if (a.S.total > di.smem_optin) return DQ_ERR_UNSUPPORTED;
+
+    switch (out_mode) {
+        case kOutStaged: return launch_b1_layout<true, kOutStaged>(a, grid, stream);
+        case kOutColDirect: return launch_b1_layout<true, kOutColDirect>(a, grid, stream);
+        case kOutRowDirect: return launch_b1_layout<true, kOutRowDirect>(a, grid, stream);
+        default: return launch_b1_layout<false, kOutNone>(a, grid, stream);
+    }
 }
 
 dq_status_t launch_build_native(const uint8_t* packed, const uint16_t* scales, const uint16_t* zeros,
@@ -1058,8 +1186,12 @@ dq_status_t launch_detect(const uint16_t* x, int d_in, float k, uint32_t* mask_w
     DeviceInfo di;
     const dq_status_t st = device_info(&di);
     if (st != DQ_OK) return st;
-    if (plan_smem_bytes(d_in) > di.smem_optin) return DQ_ERR_UNSUPPORTED;
-    return launch_plan<true>(x, d_in, k, nullptr, mask_words, indices, count, stats, stream);
+    const int smem = detect_smem(d_in).total;
+    if (smem > di.smem_optin) return DQ_ERR_UNSUPPORTED;
+    const dq_status_t s2 = ensure_smem(detect_kernel, 1, smem);
+    if (s2 != DQ_OK) return s2;
+    detect_kernel<<<1, kPlanThreads, smem, stream>>>(x, d_in, k, mask_words, indices, count, stats);
+    return check_launch();
 }
 
 dq_status_t launch_quantize(const uint16_t* w16, int d_out, int d_in, uint8_t* packed,

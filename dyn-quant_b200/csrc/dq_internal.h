@@ -19,77 +19,74 @@ constexpr int kB1UnitPacked = 4096;                  // packed INT4 of one unit 
 constexpr int kB1StageSZ = 256;                      // 16 rows x 4 groups x (scale, zero)
 constexpr int kB1UnitBytes = kB1UnitPacked + kB1StageSZ;  // one unit of the native layout
 constexpr int kB1RowPitch = 272;                     // reference layout: smem bytes per weight row
-constexpr int kB1OutlierSlots = 16;                  // FP16 outlier columns staged per unit
-constexpr int kB1StageOutliers = kB1UnitBytes;       // offset of the outlier slots in a stage
-constexpr int kB1StageBytes = kB1UnitBytes + kB1OutlierSlots * 32;
-constexpr int kPlanThreads = 1024;                   // threads of the activation-plan kernel
+constexpr int kB1StageBytes = kB1UnitBytes;          // 16 rows x 272 bytes is the same size
+constexpr int kB1ChunkB = 1024;                      // MMA B fragments of one 512-column chunk
+constexpr int kB1RedBytes = 4096;                    // reduction / scan scratch
+constexpr int kPlanThreads = 1024;                   // threads of the standalone detector
 constexpr int kMaxCtas = 1024;                       // bound on the GEMV grid (workspace sizing)
 
 __host__ __device__ inline int align16(int v) { return (v + 15) & ~15; }
 
-// Activation plan: everything the GEMV needs to know about x, computed once
-// per call by the plan kernel.  Same layout in the plan kernel's shared memory,
-// in the workspace, and (its first copy_bytes) in each GEMV CTA's shared memory.
-struct PlanLayout {
-    int bsm;    // MMA B fragments of x' (outliers zeroed): 2*d_in bytes
-    int xp;     // per group float4 (1024 * sum x' even cols, 1024 * sum odd cols, sum x', 0)
-    int goff;   // per-group outlier list offsets, G+1 ints
-    int list;   // outliers: column | FP16 bits of x << 16, capacity d_in/4
-    int copy_bytes;
-    int mask;   // outlier bitmask, d_in/8 bytes
-    int stats;  // mean, thresh, var, M2 (float), count (int)
-    int total;
+// Shared memory of one batch-1 GEMV CTA.  Every CTA derives the activation
+// plan itself (x is at most 60 KB and stays in L2):
+//   ring  per-warp stages of weight units
+//   bars  the stage barriers + the outlier-batch barrier
+//   zero  1 KB of zeros (B operand of lanes outside their column pair)
+//   bsm   x, then in place the MMA B fragments of x' (outliers zeroed), NC chunks
+//   xp    per group float4 (1024 sum x' even cols, 1024 sum x' odd cols, sum x', 0)
+//   mask  outlier bits (split only)
+//   red   reduction and scan scratch
+//   part  per row block: one partial row-sum slot per warp + one for the outliers
+//   list  outliers, column | FP16 bits of x << 16, capacity d_in/4 (split only)
+//   obuf  FP16 row segments of a batch of outlier columns (staged path only)
+struct B1Smem {
+    int ring, bars, zero, bsm, xp, mask, red, part, list, obuf, obuf_bytes, total;
 };
 
-__host__ __device__ inline PlanLayout plan_layout(int d_in) {
-    const int G = d_in / 128;
-    PlanLayout P;
+inline B1Smem b1_smem(int d_in, int nrb_max, bool split, bool staged, int smem_limit) {
+    const int NC = (d_in / 128 + kB1ChunkGroups - 1) / kB1ChunkGroups;
+    B1Smem S;
     int off = 0;
-    P.bsm = off;  off += 2 * d_in;
-    P.xp = off;   off += 16 * G;
-    P.goff = off; off += align16(4 * (G + 1));
-    P.list = off; off += align16(4 * (d_in / 4));
-    P.copy_bytes = off;
-    P.mask = off; off += align16(d_in / 8);
-    P.stats = off; off += 32;
-    P.total = off;
-    return P;
+    S.ring = off; off += kB1Warps * kB1Stages * kB1StageBytes;
+    S.bars = off; off += 256;
+    S.zero = off; off += kB1ChunkB;
+    S.bsm = off;  off += NC * kB1ChunkB;
+    S.xp = off;   off += NC * kB1ChunkGroups * 16;
+    S.mask = off; off += split ? NC * 64 : 0;
+    S.red = off;  off += kB1RedBytes;
+    S.part = off; off += nrb_max * (kB1Warps + 1) * 16 * 4;
+    S.list = off; off += split ? align16(d_in) : 0;
+    S.obuf = off;
+    S.obuf_bytes = 0;
+    if (staged) {
+        const int stride = nrb_max * 32;
+        const int want = (d_in / 4) * stride;
+        int room = (smem_limit - off) / stride * stride;
+        S.obuf_bytes = room < want ? room : want;
+        if (S.obuf_bytes < 0) S.obuf_bytes = 0;
+    }
+    off += S.obuf_bytes;
+    S.total = off;
+    return S;
 }
 
-// Workspace of a batch-1 GEMV call: the plan, two partial-row-sum slots per
-// CTA for row blocks shared with a neighbouring CTA, and one arrival counter
-// per row block (zero before first use; every call leaves them zero).
+// Workspace of a batch-1 GEMV call: per CTA, the 16 partial row sums of its
+// first row block when that block is shared with the preceding CTA, each a
+// 64-bit word (1 << 32 | FP32 bits; zero = not yet published).  Zero before
+// first use; every call leaves it zero.
 struct WsLayout {
-    size_t plan, fix, cnt, total;
+    size_t fix, total;
 };
 
 inline size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
 inline WsLayout ws_layout(int d_out, int d_in) {
+    (void)d_out;
+    (void)d_in;
     WsLayout W;
-    W.plan = 0;
-    W.fix = align256(static_cast<size_t>(plan_layout(d_in).total));
-    W.cnt = W.fix + align256(static_cast<size_t>(kMaxCtas) * 2 * 16 * sizeof(float));
-    const size_t n_rb = (static_cast<size_t>(d_out) + 15) / 16;
-    W.total = W.cnt + align256(n_rb * sizeof(unsigned int));
+    W.fix = 0;
+    W.total = align256(static_cast<size_t>(kMaxCtas) * 16 * sizeof(unsigned long long));
     return W;
-}
-
-// Shared-memory plan of the batch-1 GEMV kernel.
-struct GemvSmem {
-    int ring, bars, plan, part, misc, total;
-};
-
-__host__ __device__ inline GemvSmem gemv_smem(int d_in, int nrb_max) {
-    GemvSmem S;
-    int off = 0;
-    S.ring = off; off += kB1Warps * kB1Stages * kB1StageBytes;
-    S.bars = off; off += align16((kB1Warps * kB1Stages + 1) * 8);
-    S.plan = off; off += plan_layout(d_in).copy_bytes;
-    S.part = off; off += nrb_max * kB1Warps * 16 * 4;
-    S.misc = off; off += 64;
-    S.total = off;
-    return S;
 }
 
 // Bytes of the native unit layout the batch-1 kernel streams with one bulk

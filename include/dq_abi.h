@@ -116,11 +116,11 @@ DQ_API dq_status_t dq_build_native(const uint8_t* packed, const uint16_t* scales
 /*
  * Workspace of the batch-1 GEMVs: device memory of at least
  * dq_workspace_bytes(d_out, d_in) bytes, 256-byte aligned, ZERO-FILLED before
- * its first use.  It holds the activation plan of the call (statistics,
- * outlier list, MMA fragments of x) and per-row-block arrival counters; every
- * call leaves the counters at zero again, so one zero-filled workspace serves
- * any number of stream-ordered calls of any shape it is large enough for.
- * Calls that share a workspace must not overlap on the GPU.
+ * its first use.  It holds the partial row sums of the 16-row blocks that two
+ * CTAs share and one arrival counter per row block; every call leaves the
+ * counters at zero again, so one zero-filled workspace serves any number of
+ * stream-ordered calls of any shape it is large enough for.  Calls that share
+ * a workspace must not overlap on the GPU.
  */
 DQ_API size_t dq_workspace_bytes(int32_t d_out, int32_t d_in);
 
@@ -131,8 +131,9 @@ DQ_API size_t dq_workspace_bytes(int32_t d_out, int32_t d_in);
  * 32-column stripe class as the reference's warp capacity does
  * (src/outlier_detect.cuh:160-178).  Outlier columns use the FP16 weights, the
  * rest the INT4 codes; FP32 accumulation; y is rounded to FP16 once.
- * Enqueues two kernels (the activation plan, then the GEMV as its programmatic
- * dependent).
+ * Enqueues one kernel, launched as a programmatic dependent of the preceding
+ * work on the stream: it starts streaming weights early and reads x, y and
+ * the workspace only once that work has completed.
  * Replaces: launch_split_gemv (src/split_gemv.cu:160-198, src/split_gemv.cuh:10).
  * x: device [d_in] f16, y: device [d_out] f16.
  */

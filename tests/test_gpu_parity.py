@@ -195,14 +195,15 @@ def test_native_layout():
     for rb in range(n_rb):
         for c in range(NC):
             blk = ref[rb, c]
-            for jj in range(4):
-                grp = 4 * c + jj
+            # [slice sl][half h][lane = 4g + t]: row rb*16 + g + 8h, group 4c + t, columns 32 sl .. +31
+            for sl in range(4):
                 for h in range(2):
                     for ln in range(32):
                         row = rb * 16 + ln // 4 + 8 * h
+                        grp = 4 * c + ln % 4
                         if row < d_out and grp < G:
-                            o = ((jj * 2 + h) * 32 + ln) * 16
-                            blk[o:o + 16] = packed[row, 64 * grp + 16 * (ln % 4):64 * grp + 16 * (ln % 4) + 16]
+                            o = ((sl * 2 + h) * 32 + ln) * 16
+                            blk[o:o + 16] = packed[row, 64 * grp + 16 * sl:64 * grp + 16 * sl + 16]
             sz = np.zeros((16, 4), np.uint32)
             for r in range(16):
                 row = rb * 16 + r
