@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <mutex>
 
 #include "dq_internal.h"
 
@@ -184,3 +185,75 @@ dq_status_t dq_detect_outliers(const uint16_t* x, int32_t d_in, float outlier_k,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Split GEMV without a caller-provided workspace.
+//
+// Some callers cannot allocate device memory when they call the GEMV: plugin
+// interfaces of inference runtimes whose execute step must not allocate and
+// hands over no scratch buffer, hosts that reserve a fixed device-memory
+// budget at start-up and may not grow it afterwards, and C hosts that only
+// receive device pointers from another runtime and have no allocator of their
+// own.  For them the split GEMV's workspace is this file-scope device array.
+// It is static device memory of the library's module: every GPU that loads
+// the library holds these kStaticScratchBytes until the process exits.
+//
+// In host code g_dq_static_scratch is only a host-side stand-in for the
+// symbol, not a device address; the device address comes from
+// cudaGetSymbolAddress, looked up once per device (with that device current)
+// on the first call made there.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kStaticScratchBytes = 128 * 1024;  // workspace of grids up to kMaxCtas CTAs
+static_assert(kStaticScratchBytes >= sizeof(unsigned long long) * 16 * dq::kMaxCtas,
+              "static scratch smaller than the split GEMV workspace");
+
+static __device__ __align__(256) unsigned char g_dq_static_scratch[kStaticScratchBytes];
+
+void* g_static_scratch_ptr[kMaxDev];  // device address per ordinal, set once
+std::mutex g_static_scratch_mu;
+
+// Device address of the static scratch on the current device.  The first call
+// on a device looks it up and clears the array on `stream` (the kernel wants
+// it zero on entry and leaves it zero on exit).
+dq_status_t static_scratch(void** out, cudaStream_t stream) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) { set_cuda_error(e); return DQ_ERR_CUDA; }
+    if (dev < 0 || dev >= kMaxDev) return DQ_ERR_UNSUPPORTED;
+    void* p = __atomic_load_n(&g_static_scratch_ptr[dev], __ATOMIC_ACQUIRE);
+    if (!p) {
+        std::lock_guard<std::mutex> lock(g_static_scratch_mu);
+        p = g_static_scratch_ptr[dev];
+        if (!p) {
+            e = cudaGetSymbolAddress(&p, g_dq_static_scratch);
+            if (e != cudaSuccess) { set_cuda_error(e); return DQ_ERR_CUDA; }
+            e = cudaMemsetAsync(p, 0, kStaticScratchBytes, stream);
+            if (e != cudaSuccess) { set_cuda_error(e); return DQ_ERR_CUDA; }
+            __atomic_store_n(&g_static_scratch_ptr[dev], p, __ATOMIC_RELEASE);
+        }
+    }
+    *out = p;
+    return DQ_OK;
+}
+
+}  // namespace
+
+extern "C" dq_status_t dq_split_gemv_noalloc(const dq_weights_t* w, const uint16_t* x, uint16_t* y,
+                                             float outlier_k, void* stream) {
+    if (w && w->d_out == 0 && check_dims(w->d_out, w->d_in) == DQ_OK) return DQ_OK;
+    if (!w) return DQ_ERR_INVALID_ARGUMENT;
+    dq_status_t st = check_dims(w->d_out, w->d_in);
+    if (st != DQ_OK) return st;
+    if (ws_layout(w->d_out, w->d_in).total > kStaticScratchBytes) return DQ_ERR_WORKSPACE;
+    // Validate everything but the workspace before any CUDA call; a non-null,
+    // 256-byte aligned stand-in passes the workspace checks, which the static
+    // array meets by construction.
+    st = check_weights(w, x, y, true, reinterpret_cast<const void*>(uintptr_t{256}), kStaticScratchBytes);
+    if (st != DQ_OK) return st;
+    void* ws = nullptr;
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if ((st = static_scratch(&ws, s)) != DQ_OK) return st;
+    return launch_gemv_b1(*w, x, y, outlier_k, true, ws, s);
+}

@@ -30,6 +30,7 @@ EXPORTED_SYMBOLS = (
     "dq_quantize",
     "dq_build_colmajor",
     "dq_split_gemv",
+    "dq_split_gemv_noalloc",
     "dq_int4_gemv",
     "dq_reference_gemv",
     "dq_detect_outliers",
@@ -89,6 +90,8 @@ def lib() -> C.CDLL:
         L.dq_build_colmajor.argtypes = [P, i32, i32, P, P]
         L.dq_split_gemv.restype = st
         L.dq_split_gemv.argtypes = [C.POINTER(DqWeights), P, P, f32, P, C.c_size_t, P]
+        L.dq_split_gemv_noalloc.restype = st
+        L.dq_split_gemv_noalloc.argtypes = [C.POINTER(DqWeights), P, P, f32, P]
         L.dq_int4_gemv.restype = st
         L.dq_int4_gemv.argtypes = [C.POINTER(DqWeights), P, P, P, C.c_size_t, P]
         L.dq_workspace_bytes.restype = C.c_size_t

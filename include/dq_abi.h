@@ -141,6 +141,28 @@ DQ_API dq_status_t dq_split_gemv(const dq_weights_t* w, const uint16_t* x, uint1
                                  void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * The split GEMV of dq_split_gemv with no workspace argument.  No counterpart
+ * in the reference.
+ * For callers that cannot allocate device memory at call time: runtime plugin
+ * interfaces whose execute step must not allocate and pass no scratch buffer,
+ * hosts with a device-memory budget fixed at start-up, C hosts that receive
+ * device pointers from another runtime and have no allocator of their own.
+ * The workspace is a 128 KiB static device array inside the library; every GPU
+ * that loads the library holds it until the process exits.  A shape whose
+ * workspace (dq_workspace_bytes) would exceed 128 KiB is rejected with
+ * DQ_ERR_WORKSPACE.  Arguments, validation and results are otherwise those
+ * of dq_split_gemv.
+ * The first call on each device (with that device current) looks up the
+ * array's address and clears it on `stream`; make that first call before any
+ * stream capture.  All calls on a device share the array, and each call leaves
+ * it zero for the next: calls whose GPU work overlaps (unordered streams, or
+ * several host threads at once) race on it and give wrong results.
+ * Allocates nothing: no cudaMalloc, cudaFree or allocating library routine.
+ */
+DQ_API dq_status_t dq_split_gemv_noalloc(const dq_weights_t* w, const uint16_t* x, uint16_t* y,
+                                         float outlier_k, void* stream);
+
+/*
  * Dense INT4 GEMV (no outlier handling): y = dequant(W) x.
  * Replaces: launch_int4_gemv (src/int4_gemv.cu:80-100, src/int4_gemv.cuh:9).
  * Only packed/scales/zeros (or native) of *w are read.
