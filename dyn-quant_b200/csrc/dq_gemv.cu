@@ -63,7 +63,8 @@ __device__ unsigned int g_error_word;
 // ---------------------------------------------------------------------------
 
 // Exclusive prefix sums over the threads (in thread order) of NV ints per
-// thread, plus the totals.  scratch: >= NW * NV ints; barrier on entry.
+// thread, plus the totals.  scratch: NW * NV ints used by nothing else; one
+// barrier.
 template <int NT, int NV>
 __device__ __forceinline__ void block_scan(const int (&v)[NV], int (&pre)[NV], int (&tot)[NV], int* scratch) {
     constexpr int NW = NT / 32;
@@ -79,7 +80,6 @@ __device__ __forceinline__ void block_scan(const int (&v)[NV], int (&pre)[NV], i
             if (lane >= o) incl[i] += n;
         }
     }
-    __syncthreads();
     if (lane == 31)
 #pragma unroll
         for (int i = 0; i < NV; ++i) scratch[warp * NV + i] = incl[i];
@@ -87,6 +87,7 @@ __device__ __forceinline__ void block_scan(const int (&v)[NV], int (&pre)[NV], i
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
         int before = 0, all = 0;
+#pragma unroll
         for (int w = 0; w < NW; ++w) {
             const int s = scratch[w * NV + i];
             before += (w < warp) ? s : 0;
@@ -110,8 +111,9 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
 // most (d_in/4)/4 outliers kept per stripe class (columns c with
 // (c/32) % 4 == w, the first ones in ascending order), as the reference's
 // per-warp capacity does (src/outlier_detect.cuh:160-178).  Mean and variance
-// are computed two-pass with a fixed reduction order, so every CTA (and the
-// standalone detector) derives the same mask.
+// are merged from per-thread two-pass summaries in a fixed order, so every CTA
+// (and the standalone detector, which runs the same code with the same thread
+// count) derives the same mask.
 // ---------------------------------------------------------------------------
 
 // x (d_in = 8 * n8 halves) from global memory into xs, natural order, as
@@ -122,9 +124,21 @@ __device__ __forceinline__ void load_x_async(const uint16_t* __restrict__ x, int
     cp_async_commit();
 }
 
-// Block-wide FP32 sum of x (barrier inside).
+struct XStats {
+    float mean, thresh, var, m2;
+};
+
+// Mean and unbiased variance of x (in xs), threshold k * sqrt(max(var, 1e-8)).
+// Two passes (sum, then sum of squared deviations), each reduced in a fixed
+// order: xor butterfly within each warp, then the warp totals in warp order,
+// so every CTA of a launch and the standalone detector (same NT) get
+// bit-identical statistics.  inv_n = 1/d_in and inv_n1 = 1/(d_in - 1) are
+// computed once on the host.  red: >= 2 NW floats, not in use; two barriers.
 template <int NT>
-__device__ __forceinline__ float x_sum(const uint4* xs, int n8, float* red) {
+__device__ __forceinline__ XStats x_stats(const uint4* xs, int n8, int d_in, float k, float inv_n, float inv_n1,
+                                          float* red) {
+    constexpr int NW = NT / 32;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     float s[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4
     for (int ch = threadIdx.x; ch < n8; ch += NT) {
@@ -135,17 +149,14 @@ __device__ __forceinline__ float x_sum(const uint4* xs, int n8, float* red) {
             s[i] = add_f16_f32(hi16(w), add_f16_f32(lo16(w), s[i]));
         }
     }
-    return block_sum<NT>((s[0] + s[1]) + (s[2] + s[3]), red);
-}
-
-struct XStats {
-    float mean, thresh, var, m2;
-};
-
-template <int NT>
-__device__ __forceinline__ XStats x_stats(const uint4* xs, int n8, int d_in, float k, float total, float* red) {
+    const float ws = warp_sum((s[0] + s[1]) + (s[2] + s[3]));
+    if (lane == 0) red[warp] = ws;
+    __syncthreads();
+    float total = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) total += red[w];
     XStats r;
-    r.mean = __fdiv_rn(total, static_cast<float>(d_in));
+    r.mean = __fmul_rn(total, inv_n);
     float m[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4
     for (int ch = threadIdx.x; ch < n8; ch += NT) {
@@ -158,156 +169,178 @@ __device__ __forceinline__ XStats x_stats(const uint4* xs, int n8, int d_in, flo
             m[i] = __fmaf_rn(d1, d1, __fmaf_rn(d0, d0, m[i]));
         }
     }
-    r.m2 = block_sum<NT>((m[0] + m[1]) + (m[2] + m[3]), red);
-    r.var = (d_in > 1) ? __fdiv_rn(r.m2, static_cast<float>(d_in - 1)) : 0.f;
+    const float wq = warp_sum((m[0] + m[1]) + (m[2] + m[3]));
+    if (lane == 0) red[NW + warp] = wq;
+    __syncthreads();
+    float m2 = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) m2 += red[NW + w];
+    r.m2 = m2;
+    r.var = (d_in > 1) ? __fmul_rn(m2, inv_n1) : 0.f;
     r.thresh = __fmul_rn(k, __fsqrt_rn(fmaxf(r.var, 1e-8f)));
     return r;
 }
 
-// One mask byte per 8 columns (bit i = column 8 ch + i).
+// Outlier mask with the reference's capacity rule, and the ascending outlier
+// list (column | FP16 bits of x << 16).  Thread tid owns the 32-column stripe
+// words [w0, w1) (at most 4; word wj = columns 32 wj .. 32 wj + 31, stripe
+// class wj % 4): it computes their bits, the block scan of the per-class
+// counts gives each class's count before it, and the capacity keeps the first
+// (d_in/4)/4 of each class in column order.  Writes mask32 and list; returns
+// the outlier count.  Barrier-synchronised; the list and mask are complete
+// after the caller's next barrier.  scratch: >= NW * 5 ints used by nothing
+// else.
 template <int NT>
-__device__ __forceinline__ void x_mask(const uint4* xs, int n8, float mean, float thresh, uint8_t* mask) {
-#pragma unroll 4
-    for (int ch = threadIdx.x; ch < n8; ch += NT) {
-        const uint4 v = xs[ch];
-        uint32_t byte = 0;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const uint32_t w = word_of(v, i);
-            byte |= (fabsf(sub_f16_f32(lo16(w), mean)) > thresh ? 1u : 0u) << (2 * i);
-            byte |= (fabsf(sub_f16_f32(hi16(w), mean)) > thresh ? 1u : 0u) << (2 * i + 1);
-        }
-        mask[ch] = static_cast<uint8_t>(byte);
-    }
-}
-
-// Applies the per-stripe-class capacity to the mask (32-bit word wj = columns
-// 32 wj .. 32 wj + 31, stripe class wj % 4) and writes the ascending outlier
-// list (column | FP16 bits of x << 16).  Returns the number of outliers; the
-// list is complete after the caller's next barrier.
-template <int NT>
-__device__ int x_list(const uint16_t* xh, int d_in, uint32_t* mask32, uint32_t* list, int* scratch) {
-    __syncthreads();  // mask bytes of all threads
+__device__ int x_mask_list(const uint4* xs, int d_in, float mean, float thresh, uint32_t* mask32, uint32_t* list,
+                           int* scratch) {
+    constexpr int kMaxWords = 4;
+    static_assert(kMaxDIn / 32 <= kMaxWords * NT, "stripe words per thread");
     const int nw = d_in / 32;
     const int tid = threadIdx.x;
     const int w0 = static_cast<int>(static_cast<long long>(tid) * nw / NT);
     const int w1 = static_cast<int>(static_cast<long long>(tid + 1) * nw / NT);
+    uint32_t bits[kMaxWords];
     int cnt[4] = {0, 0, 0, 0};
-    for (int wj = w0; wj < w1; ++wj) {
-        const int n = __popc(mask32[wj]);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) cnt[i] += (wj & 3) == i ? n : 0;
+    for (int q = 0; q < kMaxWords; ++q) {
+        bits[q] = 0;
+        const int wj = w0 + q;
+        if (wj < w1) {
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+                const uint4 v = xs[4 * wj + p];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const uint32_t w = word_of(v, i);
+                    bits[q] |= (fabsf(sub_f16_f32(lo16(w), mean)) > thresh ? 1u : 0u) << (8 * p + 2 * i);
+                    bits[q] |= (fabsf(sub_f16_f32(hi16(w), mean)) > thresh ? 1u : 0u) << (8 * p + 2 * i + 1);
+                }
+            }
+            const int c = __popc(bits[q]);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) cnt[i] += (wj & 3) == i ? c : 0;
+        }
     }
     int pre[4], tot[4];
     block_scan<NT, 4>(cnt, pre, tot, scratch);
     const int cap = (d_in / 4) / 4;
-    int kept[1] = {cnt[0] + cnt[1] + cnt[2] + cnt[3]};
+    int pos;
     if (tot[0] > cap || tot[1] > cap || tot[2] > cap || tot[3] > cap) {
-        kept[0] = 0;
-        for (int wj = w0; wj < w1; ++wj) {
-            uint32_t m = mask32[wj];
-            const int c = __popc(m);
-            const int w = wj & 3;
-            const int before = w == 0 ? pre[0] : (w == 1 ? pre[1] : (w == 2 ? pre[2] : pre[3]));
-            if (before + c > cap) {
-                int keep = cap - before;
-                uint32_t out = 0;
-                for (; keep > 0 && m; --keep) {
-                    out |= m & (~m + 1u);
-                    m &= m - 1u;
-                }
-                mask32[wj] = out;
-                kept[0] += __popc(out);
-            } else {
-                kept[0] += c;
-            }
+        int kept[1] = {0};
 #pragma unroll
-            for (int i = 0; i < 4; ++i) pre[i] += w == i ? c : 0;
+        for (int q = 0; q < kMaxWords; ++q) {
+            const int wj = w0 + q;
+            if (wj < w1) {
+                uint32_t m = bits[q];
+                const int c = __popc(m);
+                const int w = wj & 3;
+                const int before = w == 0 ? pre[0] : (w == 1 ? pre[1] : (w == 2 ? pre[2] : pre[3]));
+                if (before + c > cap) {
+                    int keep = cap - before;
+                    uint32_t out = 0;
+                    for (; keep > 0 && m; --keep) {
+                        out |= m & (~m + 1u);
+                        m &= m - 1u;
+                    }
+                    bits[q] = out;
+                }
+                kept[0] += __popc(bits[q]);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) pre[i] += w == i ? c : 0;
+            }
+        }
+        int p1[1], t1[1];
+        block_scan<NT, 1>(kept, p1, t1, scratch + (NT / 32) * 4);
+        pos = p1[0];
+        tot[0] = t1[0];
+        tot[1] = tot[2] = tot[3] = 0;
+    } else {
+        pos = (pre[0] + pre[1]) + (pre[2] + pre[3]);
+    }
+    const uint16_t* xh = reinterpret_cast<const uint16_t*>(xs);
+#pragma unroll
+    for (int q = 0; q < kMaxWords; ++q) {
+        const int wj = w0 + q;
+        if (wj < w1) {
+            mask32[wj] = bits[q];
+            uint32_t m = bits[q];
+            while (m) {
+                const int col = 32 * wj + (__ffs(m) - 1);
+                list[pos++] = static_cast<uint32_t>(col) | (static_cast<uint32_t>(xh[col]) << 16);
+                m &= m - 1u;
+            }
         }
     }
-    int pos[1], total[1];
-    block_scan<NT, 1>(kept, pos, total, scratch);
-    int p = pos[0];
-    for (int wj = w0; wj < w1; ++wj) {
-        uint32_t m = mask32[wj];
-        while (m) {
-            const int col = 32 * wj + (__ffs(m) - 1);
-            list[p++] = static_cast<uint32_t>(col) | (static_cast<uint32_t>(xh[col]) << 16);
-            m &= m - 1u;
-        }
-    }
-    return total[0];
+    return (tot[0] + tot[1]) + (tot[2] + tot[3]);
 }
 
-// In place over xb: the 64 natural 8-column pieces of each 512-column chunk
-// -> MMA B order [word wi][slice sl][group jj] (16 bytes each: the f16 pairs
-// (x0,x4), (x2,x6), (x1,x5), (x3,x7) of the piece, outliers zeroed), and per
-// group xp = (1024 sum x' even columns, 1024 sum x' odd columns, sum x', 0).
-// Pieces past d_in are zero.  Each chunk is handled by one warp.
-template <int NT, bool kMask>
-__device__ __forceinline__ void x_fragments(uint4* xb, int n8, int NC, const uint8_t* mask, float4* xp4) {
-    constexpr int NW = NT / 32;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    // Two chunks (c, c + NW) per iteration for instruction-level parallelism.
-    for (int cb = warp; cb < NC; cb += 2 * NW) {
-        uint4 v[2][2];
-        float pe[2][2], po[2][2];
+// One warp, in place over xb: the 64 natural 8-column pieces of each of the
+// 512-column chunks ca and cb (cb < 0: none) -> MMA B order [word wi][slice
+// sl][group jj] (16 bytes each: the f16 pairs (x0,x4), (x2,x6), (x1,x5),
+// (x3,x7) of the piece, outliers zeroed), and per group xp = (1024 sum x' even
+// columns, 1024 sum x' odd columns, sum x', 0).  Pieces past d_in are zero.
+// Two chunks at a time keep two independent instruction streams in flight.
+template <bool kMask>
+__device__ __forceinline__ void build_chunks(uint4* xb, int n8, int ca, int cb, const uint8_t* mask, float4* xp4) {
+    const int lane = threadIdx.x & 31;
+    uint4 v[2][2];
+    float pe[2][2], po[2][2];
 #pragma unroll
-        for (int k = 0; k < 2; ++k) {
-            const int c = cb + k * NW;
+    for (int k = 0; k < 2; ++k) {
+        const int c = k == 0 ? ca : cb;
 #pragma unroll
-            for (int q = 0; q < 2; ++q) {
-                const int n = 64 * c + lane + 32 * q;
-                uint4 w = make_uint4(0, 0, 0, 0);
-                if (c < NC && n < n8) {
-                    w = xb[n];
-                    if (kMask) {
-                        const uint32_t mb = mask[n];
-                        if (mb) {
-                            uint32_t keep[4];
+        for (int q = 0; q < 2; ++q) {
+            const int n = 64 * c + lane + 32 * q;
+            uint4 w = make_uint4(0, 0, 0, 0);
+            if (c >= 0 && n < n8) {
+                w = xb[n];
+                if (kMask) {
+                    const uint32_t mb = mask[n];
+                    if (mb) {
+                        uint32_t keep[4];
 #pragma unroll
-                            for (int i = 0; i < 4; ++i)
-                                keep[i] = ((mb >> (2 * i)) & 1u ? 0u : 0x0000FFFFu) |
-                                          ((mb >> (2 * i + 1)) & 1u ? 0u : 0xFFFF0000u);
-                            w.x &= keep[0];
-                            w.y &= keep[1];
-                            w.z &= keep[2];
-                            w.w &= keep[3];
-                        }
+                        for (int i = 0; i < 4; ++i)
+                            keep[i] = ((mb >> (2 * i)) & 1u ? 0u : 0x0000FFFFu) |
+                                      ((mb >> (2 * i + 1)) & 1u ? 0u : 0xFFFF0000u);
+                        w.x &= keep[0];
+                        w.y &= keep[1];
+                        w.z &= keep[2];
+                        w.w &= keep[3];
                     }
                 }
-                pe[k][q] = add_f16_f32(lo16(w.w), add_f16_f32(lo16(w.z), add_f16_f32(lo16(w.y), add_f16_f32(lo16(w.x), 0.f))));
-                po[k][q] = add_f16_f32(hi16(w.w), add_f16_f32(hi16(w.z), add_f16_f32(hi16(w.y), add_f16_f32(hi16(w.x), 0.f))));
-                v[k][q] = make_uint4((w.x & 0xFFFFu) | (w.z << 16), (w.y & 0xFFFFu) | (w.w << 16),
-                                     (w.x >> 16) | (w.z & 0xFFFF0000u), (w.y >> 16) | (w.w & 0xFFFF0000u));
             }
+            pe[k][q] = add_f16_f32(lo16(w.w), add_f16_f32(lo16(w.z), add_f16_f32(lo16(w.y), add_f16_f32(lo16(w.x), 0.f))));
+            po[k][q] = add_f16_f32(hi16(w.w), add_f16_f32(hi16(w.z), add_f16_f32(hi16(w.y), add_f16_f32(hi16(w.x), 0.f))));
+            v[k][q] = make_uint4((w.x & 0xFFFFu) | (w.z << 16), (w.y & 0xFFFFu) | (w.w << 16),
+                                 (w.x >> 16) | (w.z & 0xFFFF0000u), (w.y >> 16) | (w.w & 0xFFFF0000u));
         }
-        __syncwarp();
+    }
+    __syncwarp();
 #pragma unroll
-        for (int o = 8; o >= 1; o >>= 1) {
+    for (int o = 8; o >= 1; o >>= 1) {
 #pragma unroll
-            for (int k = 0; k < 2; ++k)
+        for (int k = 0; k < 2; ++k)
 #pragma unroll
-                for (int q = 0; q < 2; ++q) {
-                    pe[k][q] += __shfl_xor_sync(0xffffffffu, pe[k][q], o);
-                    po[k][q] += __shfl_xor_sync(0xffffffffu, po[k][q], o);
-                }
-        }
+            for (int q = 0; q < 2; ++q) {
+                pe[k][q] += __shfl_xor_sync(0xffffffffu, pe[k][q], o);
+                po[k][q] += __shfl_xor_sync(0xffffffffu, po[k][q], o);
+            }
+    }
 #pragma unroll
-        for (int k = 0; k < 2; ++k) {
-            const int c = cb + k * NW;
-            if (c < NC) {
+    for (int k = 0; k < 2; ++k) {
+        const int c = k == 0 ? ca : cb;
+        if (c >= 0) {
 #pragma unroll
-                for (int q = 0; q < 2; ++q) {
-                    const int i = lane + 32 * q;
-                    const int jj = i >> 4, sl = (i >> 2) & 3, wi = i & 3;
-                    xb[64 * c + (wi * 4 + sl) * 4 + jj] = v[k][q];
-                    if ((lane & 15) == 0)
-                        xp4[kCG * c + jj] = make_float4(1024.f * pe[k][q], 1024.f * po[k][q], pe[k][q] + po[k][q], 0.f);
-                }
+            for (int q = 0; q < 2; ++q) {
+                const int i = lane + 32 * q;
+                const int jj = i >> 4, sl = (i >> 2) & 3, wi = i & 3;
+                xb[64 * c + (wi * 4 + sl) * 4 + jj] = v[k][q];
+                if ((lane & 15) == 0)
+                    xp4[kCG * c + jj] = make_float4(1024.f * pe[k][q], 1024.f * po[k][q], pe[k][q] + po[k][q], 0.f);
             }
         }
     }
+    __syncwarp();
 }
 
 // ---------------------------------------------------------------------------
@@ -324,6 +357,7 @@ struct B1Args {
     uint16_t* y;
     unsigned long long* fix;  // workspace: per CTA, the published partial sums of its first row block
     float k;
+    float inv_n, inv_n1;      // 1/d_in, 1/(d_in - 1) for the statistics of x
     int d_out, d_in, NC, U, nrb_max;
     B1Smem S;
 };
@@ -471,17 +505,28 @@ __global__ void __launch_bounds__(kT, 1) b1_kernel(const B1Args a) {
     // ---- activation plan ----
     int n_out = 0;
     if (kSplit) {
-        const float total = x_sum<kT>(xb, n8, red);
-        const XStats st = x_stats<kT>(xb, n8, a.d_in, a.k, total, red);
-        x_mask<kT>(xb, n8, st.mean, st.thresh, mask);
-        n_out = x_list<kT>(reinterpret_cast<const uint16_t*>(xb), a.d_in, reinterpret_cast<uint32_t*>(mask), list,
-                           reinterpret_cast<int*>(red));
+        const XStats st = x_stats<kT>(xb, n8, a.d_in, a.k, a.inv_n, a.inv_n1, red);
+        n_out = x_mask_list<kT>(xb, a.d_in, st.mean, st.thresh, reinterpret_cast<uint32_t*>(mask), list,
+                                reinterpret_cast<int*>(red) + 2 * kW);
+        __syncthreads();  // mask and list complete; x no longer read in natural order by other warps
     }
-    __syncthreads();  // list complete; x no longer read in natural order
     const int ocap = (kOut == kOutStaged) ? a.S.obuf_bytes / ostride : n_out;
-    if (kSplit && kOut == kOutStaged && n_out > 0 && orb0 <= rbz) issue_outliers(0, min(ocap, n_out));
-    x_fragments<kT, kSplit>(xb, n8, NC, mask, xp4);
-    __syncthreads();
+    const bool outl = kSplit && kOut == kOutStaged && n_out > 0 && orb0 <= rbz;
+    // MMA B fragments.  When NC is a multiple of the warp count, warp w only
+    // ever meets the chunks (cu0 + w + 8 i) mod NC, i < NC/8, and builds
+    // exactly those, in place, without waiting for the other warps; otherwise
+    // all warps build all chunks and meet on a barrier.
+    bool oc_issued = false;  // this thread's pieces of the first outlier batch are in flight
+    if ((NC % kW) == 0) {
+        const int nbw = min(wn, NC / kW);
+        for (int i = 0; i < nbw; i += 2)
+            build_chunks<kSplit>(xb, n8, (cu0 + warp + kW * i) % NC,
+                                 i + 1 < nbw ? (cu0 + warp + kW * (i + 1)) % NC : -1, mask, xp4);
+    } else {
+        for (int cb = warp; cb < NC; cb += 2 * kW)
+            build_chunks<kSplit>(xb, n8, cb, cb + kW < NC ? cb + kW : -1, mask, xp4);
+        __syncthreads();
+    }
 
     // Partial row sums of rbf (shared with earlier CTAs) go to the workspace as
     // soon as the warps holding its units are done with it: those warps meet on
@@ -599,6 +644,10 @@ __global__ void __launch_bounds__(kT, 1) b1_kernel(const B1Args a) {
                         publish_first();
                         pub_pending = false;
                     }
+                    if (outl && i == 0) {
+                        issue_outliers(0, min(ocap, n_out));
+                        oc_issued = true;
+                    }
                     if (finaliser && c_hi == c + 1 && warp == 0 && i == wn / 2)
                         early = ld_relaxed_gpu_u64(a.fix + (c + 1) * 16 + (lane & 15));
                 }
@@ -612,6 +661,7 @@ __global__ void __launch_bounds__(kT, 1) b1_kernel(const B1Args a) {
             if (armed & (1u << s)) mbar_wait_bounded(bars + 8 * s, (phase >> s) & 1u);
     }
     if (pub_pending) publish_first();  // error path: keep named barrier 1 balanced
+    if (outl && !oc_issued) issue_outliers(0, min(ocap, n_out));  // warps without units, error path
     const bool blk_ok = __syncthreads_and(ok) != 0;
 
     // ---- outlier columns: y[r] += W16[r][c] * x[c] for rows of row blocks orb0 .. rbz ----
@@ -777,8 +827,8 @@ __global__ void build_native_kernel(const uint8_t* __restrict__ packed, const ui
 }
 
 // ---------------------------------------------------------------------------
-// Standalone outlier detector (one 1024-thread CTA): the same mask, list and
-// statistics as the GEMV's plan, written out.
+// Standalone outlier detector (one CTA of the GEMV's thread count): the same
+// mask, list and statistics as the GEMV's plan, written out.
 // ---------------------------------------------------------------------------
 struct DetectSmem {
     int xs, mask, list, red, total;
@@ -794,9 +844,9 @@ __host__ __device__ inline DetectSmem detect_smem(int d_in) {
     return S;
 }
 
-__global__ void __launch_bounds__(kPlanThreads, 1)
-    detect_kernel(const uint16_t* __restrict__ x, int d_in, float k, uint32_t* mask_words, int32_t* indices,
-                  int32_t* count, float* stats) {
+__global__ void __launch_bounds__(kT, 1)
+    detect_kernel(const uint16_t* __restrict__ x, int d_in, float k, float inv_n, float inv_n1,
+                  uint32_t* mask_words, int32_t* indices, int32_t* count, float* stats) {
     extern __shared__ __align__(128) char smem[];
     const DetectSmem S = detect_smem(d_in);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -805,18 +855,16 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
     uint8_t* mask = reinterpret_cast<uint8_t*>(smem + S.mask);
     uint32_t* list = reinterpret_cast<uint32_t*>(smem + S.list);
     float* red = reinterpret_cast<float*>(smem + S.red);
-    load_x_async<kPlanThreads>(x, n8, xs);
+    load_x_async<kT>(x, n8, xs);
     cp_async_wait_all();
     __syncthreads();
-    const float total = x_sum<kPlanThreads>(xs, n8, red);
-    const XStats st = x_stats<kPlanThreads>(xs, n8, d_in, k, total, red);
-    x_mask<kPlanThreads>(xs, n8, st.mean, st.thresh, mask);
-    const int n = x_list<kPlanThreads>(reinterpret_cast<const uint16_t*>(xs), d_in,
-                                       reinterpret_cast<uint32_t*>(mask), list, reinterpret_cast<int*>(red));
+    const XStats st = x_stats<kT>(xs, n8, d_in, k, inv_n, inv_n1, red);
+    const int n = x_mask_list<kT>(xs, d_in, st.mean, st.thresh, reinterpret_cast<uint32_t*>(mask), list,
+                                  reinterpret_cast<int*>(red) + 2 * kW);
     __syncthreads();
     const uint32_t* words = reinterpret_cast<const uint32_t*>(mask);
     if (mask_words)
-        for (int i = tid; i < d_in / 32; i += kPlanThreads) mask_words[i] = words[i];
+        for (int i = tid; i < d_in / 32; i += kT) mask_words[i] = words[i];
     if (tid == 0) {
         if (count) *count = n;
         if (stats) {
@@ -1103,6 +1151,8 @@ dq_status_t launch_gemv_b1(const dq_weights_t& w, const uint16_t* x, uint16_t* y
     a.x = x;
     a.y = y;
     a.k = k;
+    a.inv_n = 1.0f / static_cast<float>(w.d_in);
+    a.inv_n1 = w.d_in > 1 ? 1.0f / static_cast<float>(w.d_in - 1) : 0.f;
     a.d_out = w.d_out;
     a.d_in = w.d_in;
     a.NC = NC;
@@ -1190,7 +1240,9 @@ dq_status_t launch_detect(const uint16_t* x, int d_in, float k, uint32_t* mask_w
     if (smem > di.smem_optin) return DQ_ERR_UNSUPPORTED;
     const dq_status_t s2 = ensure_smem(detect_kernel, 1, smem);
     if (s2 != DQ_OK) return s2;
-    detect_kernel<<<1, kPlanThreads, smem, stream>>>(x, d_in, k, mask_words, indices, count, stats);
+    detect_kernel<<<1, kT, smem, stream>>>(x, d_in, k, 1.0f / static_cast<float>(d_in),
+                                            d_in > 1 ? 1.0f / static_cast<float>(d_in - 1) : 0.f, mask_words,
+                                            indices, count, stats);
     return check_launch();
 }
 

@@ -22,7 +22,7 @@ constexpr int kB1RowPitch = 272;                     // reference layout: smem b
 constexpr int kB1StageBytes = kB1UnitBytes;          // 16 rows x 272 bytes is the same size
 constexpr int kB1ChunkB = 1024;                      // MMA B fragments of one 512-column chunk
 constexpr int kB1RedBytes = 4096;                    // reduction / scan scratch
-constexpr int kPlanThreads = 1024;                   // threads of the standalone detector
+constexpr int kB1BarBytes = (kB1Warps * kB1Stages * 8 + 127) / 128 * 128;  // one mbarrier per stage and warp
 constexpr int kMaxCtas = 1024;                       // bound on the GEMV grid (workspace sizing)
 
 __host__ __device__ inline int align16(int v) { return (v + 15) & ~15; }
@@ -48,7 +48,7 @@ inline B1Smem b1_smem(int d_in, int nrb_max, bool split, bool staged, int smem_l
     B1Smem S;
     int off = 0;
     S.ring = off; off += kB1Warps * kB1Stages * kB1StageBytes;
-    S.bars = off; off += 256;
+    S.bars = off; off += kB1BarBytes;
     S.zero = off; off += kB1ChunkB;
     S.bsm = off;  off += NC * kB1ChunkB;
     S.xp = off;   off += NC * kB1ChunkGroups * 16;
