@@ -49,8 +49,6 @@ namespace dq {
 
 namespace {
 
-constexpr int kW = kB1Warps;
-constexpr int kT = kB1Threads;
 constexpr int kStages = kB1Stages;
 constexpr int kCG = kB1ChunkGroups;
 constexpr int kStageBytes = kB1StageBytes;
@@ -129,52 +127,60 @@ struct XStats {
 };
 
 // Mean and unbiased variance of x (in xs), threshold k * sqrt(max(var, 1e-8)).
-// Two passes (sum, then sum of squared deviations), each reduced in a fixed
-// order: xor butterfly within each warp, then the warp totals in warp order,
-// so every CTA of a launch and the standalone detector (same NT) get
-// bit-identical statistics.  inv_n = 1/d_in and inv_n1 = 1/(d_in - 1) are
-// computed once on the host.  red: >= 2 NW floats, not in use; two barriers.
+// Two passes (sum, then sum of squared deviations) over a fixed partition of
+// kStatThreads virtual threads (virtual thread v: pieces v, v + 512, ...;
+// xor butterfly within each virtual warp; virtual-warp totals summed in
+// order), run by the NT real threads: every CTA of a launch, whatever its warp
+// count, and the standalone detector get bit-identical statistics.
+// inv_n = 1/d_in and inv_n1 = 1/(d_in - 1) come from the host.
+// red: >= 32 floats, not in use; two barriers.
 template <int NT>
 __device__ __forceinline__ XStats x_stats(const uint4* xs, int n8, int d_in, float k, float inv_n, float inv_n1,
                                           float* red) {
     constexpr int NW = NT / 32;
+    constexpr int NWV = kStatThreads / 32;
+    static_assert(NT <= kStatThreads && NT % 32 == 0, "statistics partition");
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    float s[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int vw = warp; vw < NWV; vw += NW) {
+        float s[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4
-    for (int ch = threadIdx.x; ch < n8; ch += NT) {
-        const uint4 v = xs[ch];
+        for (int ch = 32 * vw + lane; ch < n8; ch += kStatThreads) {
+            const uint4 v = xs[ch];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const uint32_t w = word_of(v, i);
-            s[i] = add_f16_f32(hi16(w), add_f16_f32(lo16(w), s[i]));
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t w = word_of(v, i);
+                s[i] = add_f16_f32(hi16(w), add_f16_f32(lo16(w), s[i]));
+            }
         }
+        const float ws = warp_sum((s[0] + s[1]) + (s[2] + s[3]));
+        if (lane == 0) red[vw] = ws;
     }
-    const float ws = warp_sum((s[0] + s[1]) + (s[2] + s[3]));
-    if (lane == 0) red[warp] = ws;
     __syncthreads();
     float total = 0.f;
 #pragma unroll
-    for (int w = 0; w < NW; ++w) total += red[w];
+    for (int w = 0; w < NWV; ++w) total += red[w];
     XStats r;
     r.mean = __fmul_rn(total, inv_n);
-    float m[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int vw = warp; vw < NWV; vw += NW) {
+        float m[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4
-    for (int ch = threadIdx.x; ch < n8; ch += NT) {
-        const uint4 v = xs[ch];
+        for (int ch = 32 * vw + lane; ch < n8; ch += kStatThreads) {
+            const uint4 v = xs[ch];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const uint32_t w = word_of(v, i);
-            const float d0 = sub_f16_f32(lo16(w), r.mean);
-            const float d1 = sub_f16_f32(hi16(w), r.mean);
-            m[i] = __fmaf_rn(d1, d1, __fmaf_rn(d0, d0, m[i]));
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t w = word_of(v, i);
+                const float d0 = sub_f16_f32(lo16(w), r.mean);
+                const float d1 = sub_f16_f32(hi16(w), r.mean);
+                m[i] = __fmaf_rn(d1, d1, __fmaf_rn(d0, d0, m[i]));
+            }
         }
+        const float wq = warp_sum((m[0] + m[1]) + (m[2] + m[3]));
+        if (lane == 0) red[NWV + vw] = wq;
     }
-    const float wq = warp_sum((m[0] + m[1]) + (m[2] + m[3]));
-    if (lane == 0) red[NW + warp] = wq;
     __syncthreads();
     float m2 = 0.f;
 #pragma unroll
-    for (int w = 0; w < NW; ++w) m2 += red[NW + w];
+    for (int w = 0; w < NWV; ++w) m2 += red[NWV + w];
     r.m2 = m2;
     r.var = (d_in > 1) ? __fmul_rn(m2, inv_n1) : 0.f;
     r.thresh = __fmul_rn(k, __fsqrt_rn(fmaxf(r.var, 1e-8f)));
@@ -380,8 +386,9 @@ __host__ __device__ inline int unit_owner(long long u, int P, long long U) {
 // kNative: weights in the unit layout (one bulk copy per unit, scale/zero
 // inside); otherwise the reference layout (one bulk copy per weight row of the
 // unit, scale/zero by plain loads).
-template <bool kSplit, bool kNative, int kOut>
-__global__ void __launch_bounds__(kT, 1) b1_kernel(const B1Args a) {
+template <bool kSplit, bool kNative, int kOut, int kW>
+__global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
+    constexpr int kT = kW * 32;
     extern __shared__ __align__(128) char smem[];
     const int G = a.d_in / kGroup;
     const int NC = a.NC;
@@ -392,7 +399,7 @@ __global__ void __launch_bounds__(kT, 1) b1_kernel(const B1Args a) {
     const long long U = a.U;
 
     // This CTA's units [cu0, cu1) in (row block, chunk) order.  Warp w takes
-    // cu0 + w, cu0 + w + 8, ..., so all warps work through the first row block
+    // cu0 + w, cu0 + w + kW, ..., so all warps work through the first row block
     // together at the start and through the last one at the end.
     const int cu0 = unit_start(U, c, P), cu1 = unit_start(U, c + 1, P);
     const int rbf = cu0 / NC;                 // first row block touched by this CTA
@@ -412,20 +419,22 @@ __global__ void __launch_bounds__(kT, 1) b1_kernel(const B1Args a) {
 
     const uint32_t ring = smem_u32(smem + a.S.ring) + warp * kStages * kStageBytes;
     const uint32_t bars = smem_u32(smem + a.S.bars) + warp * kStages * 8;
-    float* part = reinterpret_cast<float*>(smem + a.S.part);
+    float* part = reinterpret_cast<float*>(smem + a.S.part);    // [row block][warp][16]
+    float* opart = reinterpret_cast<float*>(smem + a.S.opart);  // [warp][row block][16]
     uint4* xb = reinterpret_cast<uint4*>(smem + a.S.bsm);
     float4* xp4 = reinterpret_cast<float4*>(smem + a.S.xp);
     uint8_t* mask = reinterpret_cast<uint8_t*>(smem + a.S.mask);
     float* red = reinterpret_cast<float*>(smem + a.S.red);
     uint32_t* list = reinterpret_cast<uint32_t*>(smem + a.S.list);
-    const int ostride = a.nrb_max * 32;  // bytes per staged outlier column
 
     if (lane == 0) {
 #pragma unroll
         for (int s = 0; s < kStages; ++s) mbar_init(bars + 8 * s, 1);
         fence_mbar_init();
     }
-    for (int i = tid; i < nrb * (kW + 1) * 16; i += kT) part[i] = 0.f;
+    for (int i = tid; i < nrb * kW * 16; i += kT) part[i] = 0.f;
+    if (kSplit && kOut != kOutNone)
+        for (int i = tid; i < kW * a.nrb_max * 16; i += kT) opart[i] = 0.f;
     for (int i = tid; i < kB1ChunkB / 16; i += kT) reinterpret_cast<uint4*>(smem + a.S.zero)[i] = make_uint4(0, 0, 0, 0);
     __syncthreads();
 
@@ -464,27 +473,8 @@ __global__ void __launch_bounds__(kT, 1) b1_kernel(const B1Args a) {
         }
     };
 
-    // FP16 rows orb0*16 .. rbz*16+15 of outlier columns list[b0 .. b0+nb) into
-    // obuf: 16-byte cp.async pieces spread over all threads (the load/store
-    // path, leaving the bulk-copy engine to the weight stream); completed by
-    // cp_async_wait_all.
-    auto issue_outliers = [&](int b0, int nb) {
-        const uint32_t ob = smem_u32(smem + a.S.obuf);
-        const int maxp = nrb * 2;  // 16-byte pieces per column slot
-        const int r_lo = orb0 * kRowBlock, r_hi = min((rbz + 1) * kRowBlock, a.d_out);
-        for (int it = tid; it < nb * maxp; it += kT) {
-            const int o = it / maxp, pc = it - o * maxp;
-            const int r0 = rbf * kRowBlock + 8 * pc;
-            if (r0 >= r_lo && r0 < r_hi) {
-                const int col = static_cast<int>(list[b0 + o] & 0xFFFFu);
-                cp_async16(ob + o * ostride + pc * 16, a.w16_cm + static_cast<size_t>(col) * a.d_out + r0);
-            }
-        }
-        cp_async_commit();
-    };
-
     // The first unit of each warp goes out before the previous kernel has
-    // finished; x is requested next, ahead of the other stages, because the
+    // finished; x is requested next, ahead of the second stage, because the
     // plan (and so every MMA) waits for it.
     uint32_t armed = 0;
 #pragma unroll
@@ -507,16 +497,13 @@ __global__ void __launch_bounds__(kT, 1) b1_kernel(const B1Args a) {
     if (kSplit) {
         const XStats st = x_stats<kT>(xb, n8, a.d_in, a.k, a.inv_n, a.inv_n1, red);
         n_out = x_mask_list<kT>(xb, a.d_in, st.mean, st.thresh, reinterpret_cast<uint32_t*>(mask), list,
-                                reinterpret_cast<int*>(red) + 2 * kW);
+                                reinterpret_cast<int*>(red) + 2 * (kStatThreads / 32));
         __syncthreads();  // mask and list complete; x no longer read in natural order by other warps
     }
-    const int ocap = (kOut == kOutStaged) ? a.S.obuf_bytes / ostride : n_out;
-    const bool outl = kSplit && kOut == kOutStaged && n_out > 0 && orb0 <= rbz;
     // MMA B fragments.  When NC is a multiple of the warp count, warp w only
-    // ever meets the chunks (cu0 + w + 8 i) mod NC, i < NC/8, and builds
+    // ever meets the chunks (cu0 + w + kW i) mod NC, i < NC/kW, and builds
     // exactly those, in place, without waiting for the other warps; otherwise
     // all warps build all chunks and meet on a barrier.
-    bool oc_issued = false;  // this thread's pieces of the first outlier batch are in flight
     if ((NC % kW) == 0) {
         const int nbw = min(wn, NC / kW);
         for (int i = 0; i < nbw; i += 2)
@@ -527,6 +514,80 @@ __global__ void __launch_bounds__(kT, 1) b1_kernel(const B1Args a) {
             build_chunks<kSplit>(xb, n8, cb, cb + kW < NC ? cb + kW : -1, mask, xp4);
         __syncthreads();
     }
+
+    // ---- outlier columns: y[r] += W16[r][c] * x[c] for the rows of row blocks orb0 .. rbz ----
+    // A small tensor-core GEMM.  Tasks (row block, 16 outlier columns), in
+    // row-block-major order, are split contiguously over the warps and run
+    // between the warps' units.  A task's 16 column segments (16 rows of FP16
+    // each, column-major) come into one of the warp's kB1OutBufs buffers, one
+    // 16-byte piece per lane; ldmatrix.trans turns them into the MMA A fragment
+    // (rows x outlier columns) and B holds the outliers' x.  A warp accumulates
+    // in registers while it stays in one row block and then writes its opart row.
+    constexpr bool kOutl = kSplit && kOut != kOutNone;
+    const int n_orb = (kOutl && n_out > 0 && orb0 <= rbz) ? rbz - orb0 + 1 : 0;
+    const int nbat = (n_out + kB1OutBatch - 1) / kB1OutBatch;
+    const int ntask = n_orb * nbat;
+    const int tk0 = static_cast<int>(static_cast<long long>(ntask) * warp / kW);
+    const int ntk = static_cast<int>(static_cast<long long>(ntask) * (warp + 1) / kW) - tk0;
+    const uint32_t wbuf = smem_u32(smem + a.S.obuf) + warp * kB1OutBufs * kB1OutBufBytes;
+    float od[4] = {0.f, 0.f, 0.f, 0.f};
+    auto o_issue = [&](int k) {  // task tk0 + k into buffer k % kB1OutBufs
+        const int task = tk0 + k;
+        const int rb = orb0 + task / nbat;
+        const int kc = (task % nbat) * kB1OutBatch + (lane >> 1);  // outlier (list index) of this lane's piece
+        const int row0 = rb * kRowBlock + 8 * (lane & 1);
+        const uint32_t dst = wbuf + (k % kB1OutBufs) * kB1OutBufBytes + 16 * lane;
+        const bool valid = kc < n_out && row0 < a.d_out;
+        const int col = valid ? static_cast<int>(list[kc] & 0xFFFFu) : 0;
+        if (kOut == kOutStaged) {
+            if (valid) cp_async16(dst, a.w16_cm + static_cast<size_t>(col) * a.d_out + row0);
+            else sts_v4(dst, make_uint4(0, 0, 0, 0));
+            cp_async_commit();
+        } else {
+            uint16_t h[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int r = row0 + i;
+                h[i] = (valid && r < a.d_out)
+                           ? (kOut == kOutColDirect ? ldg_u16(a.w16_cm + static_cast<size_t>(col) * a.d_out + r)
+                                                    : ldg_u16(a.w16 + static_cast<size_t>(r) * a.d_in + col))
+                           : static_cast<uint16_t>(0);
+            }
+            sts_v4(dst, make_uint4(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]), pack_h2(h[4], h[5]),
+                                   pack_h2(h[6], h[7])));
+        }
+    };
+    auto o_step = [&](int k) {  // run task tk0 + k
+        const int task = tk0 + k;
+        const int rb = orb0 + task / nbat;
+        const int k0 = (task % nbat) * kB1OutBatch;
+        if (kOut == kOutStaged) {
+            if (k + 2 < ntk) cp_async_wait_group<2>();
+            else if (k + 1 < ntk) cp_async_wait_group<1>();
+            else cp_async_wait_group<0>();
+        }
+        __syncwarp();
+        const uint32_t buf = wbuf + (k % kB1OutBufs) * kB1OutBufBytes;
+        uint32_t a0, a1, a2, a3;
+        // matrix j = (column half j >> 1, row half j & 1); lane 8j + i gives column (j >> 1) * 8 + i
+        ldmatrix_x4_trans(buf + (((lane >> 4) * 8 + (lane & 7)) * 32) + ((lane >> 3) & 1) * 16, a0, a1, a2, a3);
+        auto xo = [&](int kk) -> uint32_t { return kk < n_out ? (list[kk] >> 16) : 0u; };
+        const uint32_t b0 = xo(k0 + 2 * t) | (xo(k0 + 2 * t + 1) << 16);
+        const uint32_t b1 = xo(k0 + 2 * t + 8) | (xo(k0 + 2 * t + 9) << 16);
+        mma_16816(od, a0, a1, a2, a3, b0, b1);
+        __syncwarp();  // every lane is done with the buffer before it is refilled
+        if (k + kB1OutBufs < ntk) o_issue(k + kB1OutBufs);
+        if (k == ntk - 1 || (task + 1) % nbat == 0) {  // leaving row block rb
+            if (t == 0) {
+                float* op = opart + (warp * a.nrb_max + (rb - rbf)) * 16;
+                op[g] = od[0];
+                op[g + 8] = od[2];
+            }
+            od[0] = od[1] = od[2] = od[3] = 0.f;
+        }
+    };
+    int o_done = 0;  // outlier tasks run by this warp
+    for (int k = 0; k < kB1OutBufs && k < ntk; ++k) o_issue(k);
 
     // Partial row sums of rbf (shared with earlier CTAs) go to the workspace as
     // soon as the warps holding its units are done with it: those warps meet on
@@ -629,7 +690,7 @@ __global__ void __launch_bounds__(kT, 1) b1_kernel(const B1Args a) {
                         acc8 += __shfl_xor_sync(0xffffffffu, acc8, 1);
                         acc8 += __shfl_xor_sync(0xffffffffu, acc8, 2);
                         if (t == 0) {
-                            float* pp = part + ((rb - rbf) * (kW + 1) + warp) * 16;
+                            float* pp = part + ((rb - rbf) * kW + warp) * 16;
                             pp[g] = acc0;
                             pp[g + 8] = acc8;
                         }
@@ -644,12 +705,11 @@ __global__ void __launch_bounds__(kT, 1) b1_kernel(const B1Args a) {
                         publish_first();
                         pub_pending = false;
                     }
-                    if (outl && i == 0) {
-                        issue_outliers(0, min(ocap, n_out));
-                        oc_issued = true;
-                    }
                     if (finaliser && c_hi == c + 1 && warp == 0 && i == wn / 2)
                         early = ld_relaxed_gpu_u64(a.fix + (c + 1) * 16 + (lane & 15));
+                    // outlier tasks, spread evenly over this warp's units
+                    const int target = min(ntk, (ntk * (i + 1) + wn - 1) / wn);
+                    for (; o_done < target; ++o_done) o_step(o_done);
                 }
             }
         }
@@ -661,101 +721,23 @@ __global__ void __launch_bounds__(kT, 1) b1_kernel(const B1Args a) {
             if (armed & (1u << s)) mbar_wait_bounded(bars + 8 * s, (phase >> s) & 1u);
     }
     if (pub_pending) publish_first();  // error path: keep named barrier 1 balanced
-    if (outl && !oc_issued) issue_outliers(0, min(ocap, n_out));  // warps without units, error path
-    const bool blk_ok = __syncthreads_and(ok) != 0;
-
-    // ---- outlier columns: y[r] += W16[r][c] * x[c] for rows of row blocks orb0 .. rbz ----
-    if (kSplit && kOut != kOutNone && n_out > 0 && orb0 <= rbz) {
-        if (!blk_ok) {
-            if (kOut == kOutStaged) cp_async_wait_all();
-        } else {
-            const int nq = (rbz - orb0 + 1) * 4;  // row quads
-            const int nsl = nq >= kT ? 1 : kT / nq;
-            const uint32_t ob = smem_u32(smem + a.S.obuf);
-            for (int b0 = 0; b0 < n_out; b0 += ocap) {
-                const int nb = min(ocap, n_out - b0);
-                if (kOut == kOutStaged) {
-                    if (b0 > 0) {
-                        __syncthreads();  // previous batch consumed
-                        issue_outliers(b0, nb);
-                    }
-                    cp_async_wait_all();
-                    __syncthreads();
-                }
-                for (int it = tid; it < nq * nsl; it += kT) {
-                    const int qd = it % nq, slice = it / nq;
-                    const int rb_rel = orb0 - rbf + (qd >> 2), rr = (qd & 3) * 4;
-                    const int row = (rbf + rb_rel) * kRowBlock + rr;
-                    float sr[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 2
-                    for (int o = slice; o < nb; o += nsl) {
-                        const uint32_t e = list[b0 + o];
-                        const int col = static_cast<int>(e & 0xFFFFu);
-                        const uint16_t xv = hi16(e);
-                        uint32_t w01, w23;
-                        if (kOut == kOutStaged) {
-                            const uint2 v = lds_v2(ob + o * ostride + (rb_rel * kRowBlock + rr) * 2);
-                            w01 = v.x;
-                            w23 = v.y;
-                        } else {
-                            uint16_t h[4];
-#pragma unroll
-                            for (int q = 0; q < 4; ++q)
-                                h[q] = row + q < a.d_out
-                                           ? (kOut == kOutColDirect
-                                                  ? ldg_u16(a.w16_cm + static_cast<size_t>(col) * a.d_out + row + q)
-                                                  : ldg_u16(a.w16 + static_cast<size_t>(row + q) * a.d_in + col))
-                                           : static_cast<uint16_t>(0);
-                            w01 = pack_h2(h[0], h[1]);
-                            w23 = pack_h2(h[2], h[3]);
-                        }
-                        sr[0] = fma_f16_f32(lo16(w01), xv, sr[0]);
-                        sr[1] = fma_f16_f32(hi16(w01), xv, sr[1]);
-                        sr[2] = fma_f16_f32(lo16(w23), xv, sr[2]);
-                        sr[3] = fma_f16_f32(hi16(w23), xv, sr[3]);
-                    }
-                    if (nsl == 1) {
-                        float* pp = part + (rb_rel * (kW + 1) + kW) * 16 + rr;
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) pp[q] += sr[q];
-                    } else {
-                        reinterpret_cast<float4*>(red)[slice * nq + qd] = make_float4(sr[0], sr[1], sr[2], sr[3]);
-                    }
-                }
-                if (nsl > 1) {
-                    __syncthreads();
-                    if (tid < nq) {
-                        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-                        for (int sl = 0; sl < nsl; ++sl) {
-                            const float4 v = reinterpret_cast<const float4*>(red)[sl * nq + tid];
-                            acc.x += v.x;
-                            acc.y += v.y;
-                            acc.z += v.z;
-                            acc.w += v.w;
-                        }
-                        const int rb_rel = orb0 - rbf + (tid >> 2);
-                        float* pp = part + (rb_rel * (kW + 1) + kW) * 16 + (tid & 3) * 4;
-                        pp[0] += acc.x;
-                        pp[1] += acc.y;
-                        pp[2] += acc.z;
-                        pp[3] += acc.w;
-                    }
-                    __syncthreads();
-                }
-            }
-        }
-    }
+    for (; o_done < ntk; ++o_done) o_step(o_done);  // warps without units, error path
     __syncthreads();
 
-    // Row sums: warps in order, then the outlier slot.  rbf of a contributor was
-    // published above; rbz of a finaliser adds the contributors' sums (in CTA order).
+    // Row sums: the warps' INT4 sums in order, then the warps' outlier sums in
+    // order.  rbf of a contributor was published above; rbz of a finaliser adds
+    // the contributors' sums (in CTA order).
+    const bool with_out = kOutl && n_orb > 0;
     for (int r = tid; r < nrb * 16; r += kT) {
         const int rbl = r >> 4, rr = r & 15;
         const int rb = rbf + rbl;
         if ((rbl == 0 && contrib) || (rb == rbz && finaliser)) continue;
         float sum = 0.f;
 #pragma unroll
-        for (int w = 0; w <= kW; ++w) sum += part[(rbl * (kW + 1) + w) * 16 + rr];
+        for (int w = 0; w < kW; ++w) sum += part[(rbl * kW + w) * 16 + rr];
+        if (with_out && rb >= orb0)
+#pragma unroll
+            for (int w = 0; w < kW; ++w) sum += opart[(w * a.nrb_max + rbl) * 16 + rr];
         const int row = rb * kRowBlock + rr;
         if (row < a.d_out) a.y[row] = __half_as_ushort(__float2half_rn(sum));
     }
@@ -763,7 +745,11 @@ __global__ void __launch_bounds__(kT, 1) b1_kernel(const B1Args a) {
         const int rbl = rbz - rbf;
         float sum = 0.f;
 #pragma unroll
-        for (int w = 0; w <= kW; ++w) sum += part[(rbl * (kW + 1) + w) * 16 + (lane & 15)];
+        for (int w = 0; w < kW; ++w) sum += part[(rbl * kW + w) * 16 + (lane & 15)];
+        if (with_out)
+#pragma unroll
+            for (int w = 0; w < kW; ++w) sum += opart[(w * a.nrb_max + rbl) * 16 + (lane & 15)];
+        const int row = rbz * kRowBlock + (lane & 15);
         bool ok_all = true;
         for (int cc = c + 1; cc <= c_hi; ++cc) {
             unsigned long long* slot = a.fix + cc * 16 + (lane & 15);
@@ -777,7 +763,6 @@ __global__ void __launch_bounds__(kT, 1) b1_kernel(const B1Args a) {
             sum += __uint_as_float(static_cast<uint32_t>(v));
         }
         if (!__all_sync(0xffffffffu, ok_all) && lane == 0) atomicOr(&g_error_word, 2u);
-        const int row = rbz * kRowBlock + lane;
         if (lane < 16 && row < a.d_out) a.y[row] = __half_as_ushort(__float2half_rn(sum));
         __syncwarp();
         // Leave the slots zero for the next call.
@@ -844,7 +829,7 @@ __host__ __device__ inline DetectSmem detect_smem(int d_in) {
     return S;
 }
 
-__global__ void __launch_bounds__(kT, 1)
+__global__ void __launch_bounds__(kStatThreads, 1)
     detect_kernel(const uint16_t* __restrict__ x, int d_in, float k, float inv_n, float inv_n1,
                   uint32_t* mask_words, int32_t* indices, int32_t* count, float* stats) {
     extern __shared__ __align__(128) char smem[];
@@ -855,16 +840,16 @@ __global__ void __launch_bounds__(kT, 1)
     uint8_t* mask = reinterpret_cast<uint8_t*>(smem + S.mask);
     uint32_t* list = reinterpret_cast<uint32_t*>(smem + S.list);
     float* red = reinterpret_cast<float*>(smem + S.red);
-    load_x_async<kT>(x, n8, xs);
+    load_x_async<kStatThreads>(x, n8, xs);
     cp_async_wait_all();
     __syncthreads();
-    const XStats st = x_stats<kT>(xs, n8, d_in, k, inv_n, inv_n1, red);
-    const int n = x_mask_list<kT>(xs, d_in, st.mean, st.thresh, reinterpret_cast<uint32_t*>(mask), list,
-                                  reinterpret_cast<int*>(red) + 2 * kW);
+    const XStats st = x_stats<kStatThreads>(xs, n8, d_in, k, inv_n, inv_n1, red);
+    const int n = x_mask_list<kStatThreads>(xs, d_in, st.mean, st.thresh, reinterpret_cast<uint32_t*>(mask), list,
+                                            reinterpret_cast<int*>(red) + 2 * (kStatThreads / 32));
     __syncthreads();
     const uint32_t* words = reinterpret_cast<const uint32_t*>(mask);
     if (mask_words)
-        for (int i = tid; i < d_in / 32; i += kT) mask_words[i] = words[i];
+        for (int i = tid; i < d_in / 32; i += kStatThreads) mask_words[i] = words[i];
     if (tid == 0) {
         if (count) *count = n;
         if (stats) {
@@ -1076,7 +1061,7 @@ __global__ void colmajor_kernel(const uint16_t* __restrict__ w, int d_out, int d
 
 // Per-device, per-kernel "max dynamic shared memory" opt-in, done once.
 constexpr int kMaxDevices = 64;
-constexpr int kNumKernels = 32;
+constexpr int kNumKernels = 64;
 int g_smem_set[kMaxDevices][kNumKernels];  // bytes already opted in (0 = none)
 
 template <class K>
@@ -1105,14 +1090,14 @@ dq_status_t check_launch() {
 }
 
 
-template <bool kSplit, bool kNative, int kOut>
+template <bool kSplit, bool kNative, int kOut, int kW>
 dq_status_t launch_b1(const B1Args& a, int grid, cudaStream_t stream) {
-    constexpr int id = 8 + (kSplit ? 8 : 0) + (kNative ? 4 : 0) + kOut;
-    const dq_status_t st = ensure_smem(b1_kernel<kSplit, kNative, kOut>, id, a.S.total);
+    constexpr int id = 4 + (kW == kB1Warps ? 0 : 16) + (kSplit ? 8 : 0) + (kNative ? 4 : 0) + kOut;
+    const dq_status_t st = ensure_smem(b1_kernel<kSplit, kNative, kOut, kW>, id, a.S.total);
     if (st != DQ_OK) return st;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kT);
+    cfg.blockDim = dim3(kW * 32);
     cfg.dynamicSmemBytes = a.S.total;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -1120,14 +1105,25 @@ dq_status_t launch_b1(const B1Args& a, int grid, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, b1_kernel<kSplit, kNative, kOut>, a);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, b1_kernel<kSplit, kNative, kOut, kW>, a);
     if (e != cudaSuccess) { set_cuda_error(e); return DQ_ERR_CUDA; }
     return check_launch();
 }
 
-template <bool kSplit, int kOut>
+template <bool kSplit, int kOut, int kW>
 dq_status_t launch_b1_layout(const B1Args& a, int grid, cudaStream_t stream) {
-    return a.native ? launch_b1<kSplit, true, kOut>(a, grid, stream) : launch_b1<kSplit, false, kOut>(a, grid, stream);
+    return a.native ? launch_b1<kSplit, true, kOut, kW>(a, grid, stream)
+                    : launch_b1<kSplit, false, kOut, kW>(a, grid, stream);
+}
+
+template <int kW>
+dq_status_t launch_b1_warps(const B1Args& a, int out_mode, int grid, cudaStream_t stream) {
+    switch (out_mode) {
+        case kOutStaged: return launch_b1_layout<true, kOutStaged, kW>(a, grid, stream);
+        case kOutColDirect: return launch_b1_layout<true, kOutColDirect, kW>(a, grid, stream);
+        case kOutRowDirect: return launch_b1_layout<true, kOutRowDirect, kW>(a, grid, stream);
+        default: return launch_b1_layout<false, kOutNone, kW>(a, grid, stream);
+    }
 }
 
 }  // namespace
@@ -1172,19 +1168,16 @@ dq_status_t launch_gemv_b1(const dq_weights_t& w, const uint16_t* x, uint16_t* y
 
     int out_mode = kOutNone;
     if (split) out_mode = w.fp16_cm ? ((w.d_out % 8) == 0 ? kOutStaged : kOutColDirect) : kOutRowDirect;
-    a.S = b1_smem(w.d_in, nrb_max, split, out_mode == kOutStaged, di.smem_optin);
-    if (out_mode == kOutStaged && a.S.obuf_bytes < nrb_max * 32) {
-        out_mode = kOutColDirect;  // no room for even one staged column
-        a.S = b1_smem(w.d_in, nrb_max, split, false, di.smem_optin);
+    // 16 warps where their rings fit next to x and the plan, else 12.
+    int warps = kB1Warps;
+    a.S = b1_smem(w.d_in, nrb_max, split, warps);
+    if (a.S.total > di.smem_optin) {
+        warps = kB1WarpsSmall;
+        a.S = b1_smem(w.d_in, nrb_max, split, warps);
     }
     if (a.S.total > di.smem_optin) return DQ_ERR_UNSUPPORTED;
-
-    switch (out_mode) {
-        case kOutStaged: return launch_b1_layout<true, kOutStaged>(a, grid, stream);
-        case kOutColDirect: return launch_b1_layout<true, kOutColDirect>(a, grid, stream);
-        case kOutRowDirect: return launch_b1_layout<true, kOutRowDirect>(a, grid, stream);
-        default: return launch_b1_layout<false, kOutNone>(a, grid, stream);
-    }
+    return warps == kB1Warps ? launch_b1_warps<kB1Warps>(a, out_mode, grid, stream)
+                             : launch_b1_warps<kB1WarpsSmall>(a, out_mode, grid, stream);
 }
 
 dq_status_t launch_build_native(const uint8_t* packed, const uint16_t* scales, const uint16_t* zeros,
@@ -1240,7 +1233,7 @@ dq_status_t launch_detect(const uint16_t* x, int d_in, float k, uint32_t* mask_w
     if (smem > di.smem_optin) return DQ_ERR_UNSUPPORTED;
     const dq_status_t s2 = ensure_smem(detect_kernel, 1, smem);
     if (s2 != DQ_OK) return s2;
-    detect_kernel<<<1, kT, smem, stream>>>(x, d_in, k, 1.0f / static_cast<float>(d_in),
+    detect_kernel<<<1, kStatThreads, smem, stream>>>(x, d_in, k, 1.0f / static_cast<float>(d_in),
                                             d_in > 1 ? 1.0f / static_cast<float>(d_in - 1) : 0.f, mask_words,
                                             indices, count, stats);
     return check_launch();

@@ -11,9 +11,9 @@ namespace dq {
 
 // Geometry of the batch-1 split / INT4 kernel (shared by host sizing and
 // device carving).
-constexpr int kB1Warps = 8;                          // warps per CTA (one CTA per SM)
-constexpr int kB1Threads = kB1Warps * 32;
-constexpr int kB1Stages = 3;                         // bulk-copy ring stages per warp
+constexpr int kB1Warps = 16;                         // warps per CTA (one CTA per SM), at most
+constexpr int kB1WarpsSmall = 12;                    // when 16 warps' rings do not fit next to x
+constexpr int kB1Stages = 2;                         // bulk-copy ring stages per warp
 constexpr int kB1ChunkGroups = 4;                    // 128-column groups per unit
 constexpr int kB1UnitPacked = 4096;                  // packed INT4 of one unit (16 rows x 512 columns)
 constexpr int kB1StageSZ = 256;                      // 16 rows x 4 groups x (scale, zero)
@@ -21,51 +21,48 @@ constexpr int kB1UnitBytes = kB1UnitPacked + kB1StageSZ;  // one unit of the nat
 constexpr int kB1RowPitch = 272;                     // reference layout: smem bytes per weight row
 constexpr int kB1StageBytes = kB1UnitBytes;          // 16 rows x 272 bytes is the same size
 constexpr int kB1ChunkB = 1024;                      // MMA B fragments of one 512-column chunk
-constexpr int kB1RedBytes = 4096;                    // reduction / scan scratch
+constexpr int kB1RedBytes = 2048;                    // reduction / scan scratch
+constexpr int kB1OutBatch = 16;                      // outlier columns per tensor-core task
+constexpr int kB1OutBufs = 3;                        // per-warp task buffers in flight
+constexpr int kB1OutBufBytes = kB1OutBatch * 32;     // 16 columns x 16 rows of FP16
 constexpr int kB1BarBytes = (kB1Warps * kB1Stages * 8 + 127) / 128 * 128;  // one mbarrier per stage and warp
+constexpr int kStatThreads = 512;                    // fixed partition of the statistics of x
 constexpr int kMaxCtas = 1024;                       // bound on the GEMV grid (workspace sizing)
 
 __host__ __device__ inline int align16(int v) { return (v + 15) & ~15; }
 
-// Shared memory of one batch-1 GEMV CTA.  Every CTA derives the activation
-// plan itself (x is at most 60 KB and stays in L2):
+// Shared memory of one batch-1 GEMV CTA with `warps` warps.  Every CTA derives
+// the activation plan itself (x is at most 60 KB and stays in L2):
 //   ring  per-warp stages of weight units
-//   bars  the stage barriers + the outlier-batch barrier
+//   bars  the stage barriers
 //   zero  1 KB of zeros (B operand of lanes outside their column pair)
 //   bsm   x, then in place the MMA B fragments of x' (outliers zeroed), NC chunks
 //   xp    per group float4 (1024 sum x' even cols, 1024 sum x' odd cols, sum x', 0)
 //   mask  outlier bits (split only)
 //   red   reduction and scan scratch
-//   part  per row block: one partial row-sum slot per warp + one for the outliers
+//   part  per row block and warp: partial row sums of the INT4 part
+//   opart per warp and row block: partial row sums of the outlier columns (split only)
 //   list  outliers, column | FP16 bits of x << 16, capacity d_in/4 (split only)
-//   obuf  FP16 row segments of a batch of outlier columns (staged path only)
+//   obuf  per warp, kB1OutBufs buffers of 16 outlier columns x 16 rows (split only)
 struct B1Smem {
-    int ring, bars, zero, bsm, xp, mask, red, part, list, obuf, obuf_bytes, total;
+    int ring, bars, zero, bsm, xp, mask, red, part, opart, list, obuf, total;
 };
 
-inline B1Smem b1_smem(int d_in, int nrb_max, bool split, bool staged, int smem_limit) {
+inline B1Smem b1_smem(int d_in, int nrb_max, bool split, int warps) {
     const int NC = (d_in / 128 + kB1ChunkGroups - 1) / kB1ChunkGroups;
     B1Smem S;
     int off = 0;
-    S.ring = off; off += kB1Warps * kB1Stages * kB1StageBytes;
-    S.bars = off; off += kB1BarBytes;
-    S.zero = off; off += kB1ChunkB;
-    S.bsm = off;  off += NC * kB1ChunkB;
-    S.xp = off;   off += NC * kB1ChunkGroups * 16;
-    S.mask = off; off += split ? NC * 64 : 0;
-    S.red = off;  off += kB1RedBytes;
-    S.part = off; off += nrb_max * (kB1Warps + 1) * 16 * 4;
-    S.list = off; off += split ? align16(d_in) : 0;
-    S.obuf = off;
-    S.obuf_bytes = 0;
-    if (staged) {
-        const int stride = nrb_max * 32;
-        const int want = (d_in / 4) * stride;
-        int room = (smem_limit - off) / stride * stride;
-        S.obuf_bytes = room < want ? room : want;
-        if (S.obuf_bytes < 0) S.obuf_bytes = 0;
-    }
-    off += S.obuf_bytes;
+    S.ring = off;  off += warps * kB1Stages * kB1StageBytes;
+    S.bars = off;  off += kB1BarBytes;
+    S.zero = off;  off += kB1ChunkB;
+    S.bsm = off;   off += NC * kB1ChunkB;
+    S.xp = off;    off += NC * kB1ChunkGroups * 16;
+    S.mask = off;  off += split ? NC * 64 : 0;
+    S.red = off;   off += kB1RedBytes;
+    S.part = off;  off += nrb_max * warps * 16 * 4;
+    S.opart = off; off += split ? warps * nrb_max * 16 * 4 : 0;
+    S.list = off;  off += split ? align16(d_in) : 0;
+    S.obuf = off;  off += split ? warps * kB1OutBufs * kB1OutBufBytes : 0;
     S.total = off;
     return S;
 }
