@@ -16,9 +16,13 @@ copies that every step reads them from HBM, not L2).  Algorithmic bytes per
 GEMV = d_out*d_in/2 (INT4) + 4*d_out*d_in/128 (FP16 scale + zero)
 + 2*d_out*n_o (FP16 outlier columns, n_o = detected outliers) + 2*d_in (x) + 2*d_out (y).
 
-One process per GPU; under torchrun every rank runs its own copy of the
-workload (independent weights and activations, no exchange: "scaling": "weak"),
-the time is the max over ranks, value sums all ranks' bytes.
+One process per GPU.  Under torchrun (N > 1) every GEMV of the workload is
+row-sharded: each rank holds whole 16-row blocks of the weights, runs the
+split GEMV on its slice with the same x, and the output slices are
+all-gathered with NCCL after every GEMV ("scaling": "strong": the total work
+is the workload's, whatever N).  The time is the max over ranks; value is the
+full GEMVs' algorithmic bytes over that time.  The roofline line describes
+this rank's kernel alone (its slice's bytes over its launch time).
 
 --impl reference times the reference's split GEMV restated on the CPU (the
 reference has no CPU GEMV of its own; this is the oracle port, OpenMP over
@@ -249,21 +253,30 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
 
     import dyn_quant
     from dyn_quant import _lib
+    from dyn_quant.sharded import shard_rows
 
     L = _lib.lib()
     spec = WORKLOADS[args.workload]
-    acts_np = activations(args.workload, 1000 * rank)
+    sharded = world > 1
+    # Row sharding across the ranks (N > 1): every rank holds whole 16-row
+    # blocks of each GEMV, sees the same x, and the output slices are
+    # all-gathered with NCCL after every GEMV.
+    acts_np = activations(args.workload, 0)
     acts = {k: torch.from_numpy(v).to(dev) for k, v in acts_np.items()}
+    rows = [shard_rows(o, world, rank) if sharded else (0, o, o) for _, o, _, _, _ in spec]
 
     # detected outliers per activation (the mask the kernel applies)
     n_o = {}
     for key, x in acts.items():
         n_o[key] = int(dyn_quant.detect_outliers(x, K_OUTLIER)[0].sum().item())
+    # whole-job algorithmic bytes of one step (the full GEMVs, whatever the sharding)
     step_bytes = sum(gemv_bytes(o, i, n_o[key]) for _, o, i, _, key in spec)
+    # this rank's kernel bytes of one step
+    local_bytes = [gemv_bytes(max(r1 - r0, 0), i, n_o[key]) for (_, _, i, _, key), (r0, r1, _) in zip(spec, rows)]
     n_gemv = len(spec)
 
     # weight sets, rotated so each step reads its weights from HBM
-    n_sets = max(2, math.ceil(3 * L2_BYTES / step_bytes))
+    n_sets = max(2, math.ceil(3 * L2_BYTES / max(sum(local_bytes), 1)))
     if args.max_sets:
         n_sets = min(n_sets, args.max_sets)  # profiling runs: ncu flushes caches itself
     gen = torch.Generator(device=dev)
@@ -272,15 +285,20 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         mods = []
         for gi, (name, d_out, d_in, frac, key) in enumerate(spec):
             gen.manual_seed(10_000 * rank + 100 * s + gi)
-            w = (torch.randn(d_out, d_in, generator=gen, device=dev, dtype=torch.float32) / math.sqrt(d_in)).half()
-            lin = dyn_quant.DynQuantLinear(d_in, d_out, K_OUTLIER)
+            n_rows = rows[gi][1] - rows[gi][0]
+            if n_rows <= 0:
+                raise SystemExit(f"{name}: {d_out} rows do not give every one of {world} ranks a row block")
+            w = (torch.randn(n_rows, d_in, generator=gen, device=dev, dtype=torch.float32) / math.sqrt(d_in)).half()
+            lin = dyn_quant.DynQuantLinear(d_in, n_rows, K_OUTLIER)
             lin.load_weight(w)
             del w
             mods.append(lin)
         sets.append(mods)
     torch.cuda.synchronize()
 
-    outs = [torch.empty(o, dtype=torch.float16, device=dev) for _, o, _, _, _ in spec]
+    # local outputs (padded to the common slice height) and the gathered outputs
+    outs = [torch.zeros(per, dtype=torch.float16, device=dev) for (_, _, per) in rows]
+    fulls = [torch.empty(world * per, dtype=torch.float16, device=dev) for (_, _, per) in rows]
     ws_bytes = max(L.dq_workspace_bytes(o, i) for _, o, i, _, _ in spec)
     wspace = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)  # zero-filled once, left zeroed by every call
     structs = []
@@ -291,13 +309,15 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                                     lin.fp16_w.data_ptr(), lin.d_out, lin.d_in, lin._native.data_ptr()))
         structs.append(row)
 
-    def launch_gemv(s: int, gi: int, stream):
+    def launch_gemv(s: int, gi: int, stream, gather: bool = True):
         name, d_out, d_in, frac, key = spec[gi]
         st = L.dq_split_gemv(C.byref(structs[s][gi]), C.c_void_p(acts[key].data_ptr()),
                              C.c_void_p(outs[gi].data_ptr()), K_OUTLIER, C.c_void_p(wspace.data_ptr()),
                              ws_bytes, C.c_void_p(stream.cuda_stream))
         if st != 0:
             raise RuntimeError(f"dq_split_gemv: {_lib.status_string(st)}")
+        if sharded and gather:
+            dist.all_gather_into_tensor(fulls[gi], outs[gi])
 
     def launch_step(s: int, stream):
         for gi in range(n_gemv):
@@ -311,12 +331,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     # Graphs of back-to-back launches (no events between kernels, so each launch
     # overlaps its predecessor's tail as it would in a decode step).  Weight sets
     # rotate, so every launch streams its weights from HBM.
-    def capture(launches):
+    def capture(launches, gather: bool = True):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
             cur = torch.cuda.current_stream()
             for s, gi in launches:
-                launch_gemv(s, gi, cur)
+                launch_gemv(s, gi, cur, gather)
         return g
 
     def steps(first: int, count: int):
@@ -324,7 +344,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
 
     warm_graph = capture(steps(0, max(args.warmup, n_sets)))
     timed_graph = capture(steps(0, args.steps))
-    per_gemv_graphs = [capture([(i % n_sets, gi) for i in range(args.steps)]) for gi in range(n_gemv)]
+    per_gemv_graphs = [capture([(i % n_sets, gi) for i in range(args.steps)], gather=False) for gi in range(n_gemv)]
     torch.cuda.synchronize()
 
     with torch.cuda.stream(stream):
@@ -380,17 +400,23 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             per_gemv_us.append(e0.elapsed_time(e1) * 1e3 / args.steps)
 
     per_gemv_bytes = [gemv_bytes(o, i, n_o[key]) for _, o, i, _, key in spec]
-    # Every launch in the timed region is the split GEMV kernel: its average launch
-    # duration is the timed region over the launches, and achieved = algorithmic
-    # bytes per launch / that duration.
-    achieved = sum(per_gemv_bytes) * args.steps / (elapsed_ms * 1e-3) / 1e9
+    # The split GEMV kernel is the dominant (on one GPU the only) kernel: its
+    # average launch duration is the timed region over the launches, and achieved
+    # = algorithmic bytes per launch / that duration.  Sharded runs time the
+    # kernel alone in the per-GEMV graphs (the timed region also holds the
+    # all-gathers).
     peak, peak_note = measured_peak_gbs()
+    if sharded:
+        achieved = sum(local_bytes) / (sum(per_gemv_us) * 1e-6) / 1e9
+    else:
+        achieved = sum(per_gemv_bytes) * args.steps / (elapsed_ms * 1e-3) / 1e9
 
-    value = world * step_bytes * args.steps / (elapsed_ms * 1e-3) / 1e9
+    # whole-job throughput: the full GEMVs' bytes over the max-over-ranks time
+    value = step_bytes * args.steps / (elapsed_ms * 1e-3) / 1e9
     us_per_gemv = elapsed_ms * 1e3 / (args.steps * n_gemv)
 
     # end to end through the public API: pinned host x in, host y out, every step
-    e2e = run_e2e(args, spec, sets, acts_np, dev, step_bytes, world)
+    e2e = run_e2e(args, spec, sets, acts_np, dev, step_bytes, world, rows)
 
     # CPU baseline on rank 0 at N = 1
     cpu = None
@@ -401,28 +427,32 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         per_name = {}
         for j, (name, d_out, d_in, _, key) in enumerate(spec):
             us = per_gemv_us[j]
-            per_name[name] = {"shape": [d_out, d_in], "n_outliers": n_o[key], "bytes": per_gemv_bytes[j],
-                              "us": round(us, 3), "gb_s": round(per_gemv_bytes[j] / (us * 1e-6) / 1e9, 1)}
+            per_name[name] = {"shape": [d_out, d_in], "n_outliers": n_o[key], "bytes": local_bytes[j],
+                              "us": round(us, 3), "gb_s": round(local_bytes[j] / (us * 1e-6) / 1e9, 1)}
+            if sharded:
+                per_name[name]["rows"] = [rows[j][0], rows[j][1]]
         traffic = ncu_traffic(args.workload)
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(elapsed_ms / args.steps, 5),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if sharded else "weak", "vs_baseline": None,
             "dtype": "w4a16 (fp32 accumulate)", "data": "synthetic (seeded N(0,1/d_in) weights, N(0,1) "
                                                         "activations with U[10,100] outliers)",
             "config": {"workload": args.workload, "gemvs": [[n, o, i] for n, o, i, *_ in spec], "batch": 1,
                        "group": 128, "outlier_k": K_OUTLIER, "outlier_frac": spec[0][3],
                        "l2": f"inputs larger than L2: {n_sets} rotating weight sets "
                              f"({n_sets * step_bytes / 1e6:.0f} MB streamed per cycle)",
-                       "graphs": "the K timed steps are one CUDA graph of back-to-back launches"},
+                       "graphs": "the K timed steps are one CUDA graph of back-to-back launches",
+                       "parallelism": (f"row-sharded over {world} GPUs, NCCL all-gather of the output slices "
+                                       "after every GEMV" if sharded else "1 GPU")},
             "us_per_gemv": round(us_per_gemv, 3),
             "gemvs": per_name,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_note": peak_note,
                          "kernel": "b1_kernel<split, native unit layout, staged outlier segments>",
-                         "algorithmic_bytes_per_launch": round(sum(per_gemv_bytes) / n_gemv),
+                         "algorithmic_bytes_per_launch": round(sum(local_bytes) / n_gemv),
                          "traffic": traffic},
-            "gpu_launches": args.steps * n_gemv,
+            "gpu_launches": args.steps * n_gemv,  # our kernel launches in the timed region (NCCL not counted)
             "e2e": e2e,
             "clocks": clocks,
             "cpu_baseline": cpu,
@@ -435,11 +465,17 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         dist.destroy_process_group()
 
 
-def run_e2e(args, spec, sets, acts_np, dev, step_bytes, world):
+def run_e2e(args, spec, sets, acts_np, dev, step_bytes, world, rows):
+    """The same steps through DynQuantLinear.forward from pinned host buffers.
+
+    Row-sharded runs (world > 1) gather each GEMV's output slices with
+    dyn_quant.sharded.gather_rows, so every rank copies the full y back."""
     import torch
+    from dyn_quant.sharded import gather_rows
     xh = {k: torch.from_numpy(v).pin_memory() for k, v in acts_np.items()}
     xd = {k: torch.empty(v.shape, dtype=torch.float16, device=dev) for k, v in acts_np.items()}
     yh = [torch.empty(o, dtype=torch.float16).pin_memory() for _, o, _, _, _ in spec]
+    gbuf = [torch.empty(world * per, dtype=torch.float16, device=dev) for (_, _, per) in rows]
     h2d = sum(v.numel() * 2 for v in xh.values())
     d2h = sum(v.numel() * 2 for v in yh)
     stream = torch.cuda.current_stream(dev)
@@ -453,6 +489,8 @@ def run_e2e(args, spec, sets, acts_np, dev, step_bytes, world):
             xd[k].copy_(xh[k], non_blocking=True)
         for gi, (name, d_out, d_in, frac, key) in enumerate(spec):
             y = sets[s][gi](xd[key])
+            if world > 1:
+                y = gather_rows(y, d_out, rows[gi][2], None, gbuf[gi])
             yh[gi].copy_(y, non_blocking=True)
         end.record(stream)
         end.synchronize()
@@ -469,9 +507,11 @@ def run_e2e(args, spec, sets, acts_np, dev, step_bytes, world):
         t = torch.tensor([ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    return {"value": round(world * step_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+    return {"value": round(step_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 4),
-            "api": "DynQuantLinear.forward, pinned host buffers, synchronised every step"}
+            "api": ("DynQuantLinear.forward, pinned host buffers, synchronised every step" if world == 1 else
+                    "DynQuantLinear.forward on each rank's rows + NCCL all-gather, pinned host buffers on "
+                    "every rank (bytes per rank), synchronised every step")}
 
 
 def main(argv=None) -> None:
