@@ -63,20 +63,38 @@ WORKLOADS = {
     "llama2_70b_mlp": [("gate", 28672, 8192, 0.03, "h"), ("up", 28672, 8192, 0.03, "h"),
                        ("down", 8192, 28672, 0.03, "ff")],
     "llama2_70b_q": [("q", 8192, 8192, 0.03, "h")],
+    # the outlier / batch sweep: one 8192 x 8192 GEMV (--batch, --frac, --k, --dist)
+    "sweep_8192": [("w", 8192, 8192, 0.01, "h")],
 }
 
 
-def gemv_bytes(d_out: int, d_in: int, n_o: int) -> int:
-    return d_out * d_in // 2 + 4 * d_out * (d_in // 128) + 2 * d_out * n_o + 2 * d_in + 2 * d_out
+def gemv_bytes(d_out: int, d_in: int, n_o: int, m: int = 1) -> int:
+    """Algorithmic bytes of one (batched) split GEMV: INT4 codes, FP16 scale and
+    zero, the FP16 columns of the n_o outlier channels (for m > 1 the union of
+    the vectors' masks), m activation vectors and m outputs."""
+    return d_out * d_in // 2 + 4 * d_out * (d_in // 128) + 2 * d_out * n_o + 2 * m * (d_in + d_out)
 
 
-def activations(workload: str, seed_base: int):
-    """Seeded activation vectors per key (numpy f16)."""
+def workload_spec(args):
+    """The workload's GEMVs, with --frac applied."""
+    spec = WORKLOADS[args.workload]
+    if args.frac is not None:
+        spec = [(n, o, i, args.frac, key) for n, o, i, _, key in spec]
+    return spec
+
+
+def activations(args, seed_base: int = 0):
+    """Seeded activations per key (numpy f16): [d_in], or [batch, d_in] with
+    vector t drawn from seed + t."""
     from dyn_quant import synth
     acts = {}
-    for name, d_out, d_in, frac, key in WORKLOADS[workload]:
+    for name, d_out, d_in, frac, key in workload_spec(args):
         if key not in acts:
-            acts[key] = synth.activation(d_in, frac, seed=seed_base + (1 if key == "h" else 2))
+            seed = seed_base + (1 if key == "h" else 2)
+            if args.batch == 1:
+                acts[key] = synth.activation(d_in, frac, seed=seed, dist=args.dist)
+            else:
+                acts[key] = synth.activations(args.batch, d_in, frac, seed=seed, dist=args.dist)
     return acts
 
 
@@ -165,36 +183,43 @@ def ncu_traffic(workload: str):
 # ---------------------------------------------------------------------------
 # CPU legs (oracle port of the reference's split GEMV)
 # ---------------------------------------------------------------------------
-def cpu_prepare(workload: str):
+def cpu_prepare(args):
     import oracle as O
     from dyn_quant import synth
-    acts = activations(workload, 0)
+    acts = activations(args)
     mats = []
-    for i, (name, d_out, d_in, frac, key) in enumerate(WORKLOADS[workload]):
+    for i, (name, d_out, d_in, frac, key) in enumerate(workload_spec(args)):
         w = synth.weights(d_out, d_in, seed=100 + i)
         mats.append((name, w, *O.quantize(w), acts[key]))
     return mats
 
 
-def cpu_step(mats):
+def cpu_step(mats, k: float):
+    """One step on the host: every GEMV, each activation vector separately
+    (the reference computes one vector per call)."""
     import oracle as O
     total = 0
     for name, w, packed, scales, zeros, x in mats:
-        _, _, mask = O.split_gemv(packed, scales, zeros, w, x, K_OUTLIER)
-        total += gemv_bytes(w.shape[0], w.shape[1], int(mask.sum()))
+        xs = x.reshape(-1, w.shape[1])
+        union = np.zeros(w.shape[1], bool)
+        for row in xs:
+            _, _, mask = O.split_gemv(packed, scales, zeros, w, row, k)
+            union |= mask.astype(bool)
+        total += gemv_bytes(w.shape[0], w.shape[1], int(union.sum()), xs.shape[0])
     return total
 
 
-def cpu_baseline(workload: str, budget_s: float = 10.0) -> dict:
+def cpu_baseline(args, budget_s: float = 10.0) -> dict:
     import oracle as O
+    workload = args.workload
     cores = os.cpu_count() or 1
     O.set_num_threads(cores)
-    mats = cpu_prepare(workload)
-    cpu_step(mats)  # warm
+    mats = cpu_prepare(args)
+    cpu_step(mats, args.k)  # warm
     t0 = time.perf_counter()
     nbytes, n = 0, 0
     while True:
-        nbytes += cpu_step(mats)
+        nbytes += cpu_step(mats, args.k)
         n += 1
         if time.perf_counter() - t0 >= budget_s:
             break
@@ -212,23 +237,24 @@ def run_reference(args, rank: int, world: int) -> None:
     import oracle as O
     cores = os.cpu_count() or 1
     O.set_num_threads(cores)
-    mats = cpu_prepare(args.workload)
+    mats = cpu_prepare(args)
     for _ in range(args.warmup):
-        cpu_step(mats)
+        cpu_step(mats, args.k)
     t0 = time.perf_counter()
     nbytes = 0
     for _ in range(args.steps):
-        nbytes += cpu_step(mats)
+        nbytes += cpu_step(mats, args.k)
     dt = time.perf_counter() - t0
     value = nbytes / dt / 1e9
     ngemv = len(mats)
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None, "dtype": "w4a16 (fp32 accumulate)", "data": "synthetic",
-        "config": {"workload": args.workload, "gemvs": [[n, o, i] for n, o, i, *_ in WORKLOADS[args.workload]],
-                   "batch": 1, "group": 128, "outlier_k": K_OUTLIER},
+        "config": {"workload": args.workload, "gemvs": [[n, o, i] for n, o, i, *_ in workload_spec(args)],
+                   "batch": args.batch, "outlier_k": args.k, "group": 128, "dist": args.dist},
         "us_per_gemv": round(dt / (args.steps * ngemv) * 1e6, 2),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": O.num_threads(), "kind": "port",
                          "sample": f"{args.steps} full {args.workload} steps on the host cores (the reference "
@@ -256,24 +282,29 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     from dyn_quant.sharded import shard_rows
 
     L = _lib.lib()
-    spec = WORKLOADS[args.workload]
+    spec = workload_spec(args)
+    M = args.batch
     sharded = world > 1
     # Row sharding across the ranks (N > 1): every rank holds whole 16-row
     # blocks of each GEMV, sees the same x, and the output slices are
     # all-gathered with NCCL after every GEMV.
-    acts_np = activations(args.workload, 0)
+    acts_np = activations(args)
     acts = {k: torch.from_numpy(v).to(dev) for k, v in acts_np.items()}
     rows = [shard_rows(o, world, rank) if sharded else (0, o, o) for _, o, _, _, _ in spec]
 
-    # detected outliers per activation (the mask the kernel applies)
+    # detected outliers per activation (the mask the kernel applies; for a
+    # batch, the union of the vectors' masks, whose FP16 columns are read)
     n_o = {}
     for key, x in acts.items():
-        n_o[key] = int(dyn_quant.detect_outliers(x, K_OUTLIER)[0].sum().item())
+        masks = [dyn_quant.detect_outliers(r, args.k)[0] for r in x.reshape(-1, x.shape[-1])]
+        n_o[key] = int(torch.stack(masks).any(0).sum().item())
     # whole-job algorithmic bytes of one step (the full GEMVs, whatever the sharding)
-    step_bytes = sum(gemv_bytes(o, i, n_o[key]) for _, o, i, _, key in spec)
+    step_bytes = sum(gemv_bytes(o, i, n_o[key], M) for _, o, i, _, key in spec)
     # this rank's kernel bytes of one step
-    local_bytes = [gemv_bytes(max(r1 - r0, 0), i, n_o[key]) for (_, _, i, _, key), (r0, r1, _) in zip(spec, rows)]
+    local_bytes = [gemv_bytes(max(r1 - r0, 0), i, n_o[key], M)
+                   for (_, _, i, _, key), (r0, r1, _) in zip(spec, rows)]
     n_gemv = len(spec)
+    kernels_per_gemv = 1 if M == 1 else 3  # batched: plan, FP16 part, INT4 part
 
     # weight sets, rotated so each step reads its weights from HBM
     n_sets = max(2, math.ceil(3 * L2_BYTES / max(sum(local_bytes), 1)))
@@ -289,7 +320,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             if n_rows <= 0:
                 raise SystemExit(f"{name}: {d_out} rows do not give every one of {world} ranks a row block")
             w = (torch.randn(n_rows, d_in, generator=gen, device=dev, dtype=torch.float32) / math.sqrt(d_in)).half()
-            lin = dyn_quant.DynQuantLinear(d_in, n_rows, K_OUTLIER)
+            lin = dyn_quant.DynQuantLinear(d_in, n_rows, args.k)
             lin.load_weight(w)
             del w
             mods.append(lin)
@@ -297,9 +328,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     torch.cuda.synchronize()
 
     # local outputs (padded to the common slice height) and the gathered outputs
-    outs = [torch.zeros(per, dtype=torch.float16, device=dev) for (_, _, per) in rows]
-    fulls = [torch.empty(world * per, dtype=torch.float16, device=dev) for (_, _, per) in rows]
-    ws_bytes = max(L.dq_workspace_bytes(o, i) for _, o, i, _, _ in spec)
+    outs = [torch.zeros(M * per, dtype=torch.float16, device=dev) for (_, _, per) in rows]
+    fulls = [torch.empty(world * M * per, dtype=torch.float16, device=dev) for (_, _, per) in rows]
+    ws_bytes = max(L.dq_workspace_bytes(r1 - r0, i) if M == 1 else L.dq_workspace_bytes_batched(r1 - r0, i, M)
+                   for (_, _, i, _, _), (r0, r1, _) in zip(spec, rows))
     wspace = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)  # zero-filled once, left zeroed by every call
     structs = []
     for mods in sets:
@@ -311,11 +343,16 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
 
     def launch_gemv(s: int, gi: int, stream, gather: bool = True):
         name, d_out, d_in, frac, key = spec[gi]
-        st = L.dq_split_gemv(C.byref(structs[s][gi]), C.c_void_p(acts[key].data_ptr()),
-                             C.c_void_p(outs[gi].data_ptr()), K_OUTLIER, C.c_void_p(wspace.data_ptr()),
-                             ws_bytes, C.c_void_p(stream.cuda_stream))
+        if M == 1:
+            st = L.dq_split_gemv(C.byref(structs[s][gi]), C.c_void_p(acts[key].data_ptr()),
+                                 C.c_void_p(outs[gi].data_ptr()), args.k, C.c_void_p(wspace.data_ptr()),
+                                 ws_bytes, C.c_void_p(stream.cuda_stream))
+        else:
+            st = L.dq_split_gemv_batched(C.byref(structs[s][gi]), C.c_void_p(acts[key].data_ptr()),
+                                         C.c_void_p(outs[gi].data_ptr()), M, args.k, C.c_void_p(wspace.data_ptr()),
+                                         ws_bytes, C.c_void_p(stream.cuda_stream))
         if st != 0:
-            raise RuntimeError(f"dq_split_gemv: {_lib.status_string(st)}")
+            raise RuntimeError(f"split GEMV: {_lib.status_string(st)}")
         if sharded and gather:
             dist.all_gather_into_tensor(fulls[gi], outs[gi])
 
@@ -399,7 +436,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             e1.synchronize()
             per_gemv_us.append(e0.elapsed_time(e1) * 1e3 / args.steps)
 
-    per_gemv_bytes = [gemv_bytes(o, i, n_o[key]) for _, o, i, _, key in spec]
+    per_gemv_bytes = [gemv_bytes(o, i, n_o[key], M) for _, o, i, _, key in spec]
     # The split GEMV kernel is the dominant (on one GPU the only) kernel: its
     # average launch duration is the timed region over the launches, and achieved
     # = algorithmic bytes per launch / that duration.  Sharded runs time the
@@ -418,17 +455,28 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     # end to end through the public API: pinned host x in, host y out, every step
     e2e = run_e2e(args, spec, sets, acts_np, dev, step_bytes, world, rows)
 
+    # accuracy of this rank's rows (weight set 0) against an FP32 dense GEMV on
+    # the original FP16 weights and activations
+    rel_l2 = []
+    for gi, (name, d_out, d_in, frac, key) in enumerate(spec):
+        lin = sets[0][gi]
+        x = acts[key].reshape(-1, d_in)
+        y = lin(x.squeeze(0) if M == 1 else x).float().reshape(M, -1)
+        y32 = x.float() @ lin.fp16_w.float().t()
+        rel_l2.append(float((torch.linalg.vector_norm(y - y32) / torch.linalg.vector_norm(y32)).item()))
+
     # CPU baseline on rank 0 at N = 1
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(args.workload, args.cpu_budget)
+        cpu = cpu_baseline(args, args.cpu_budget)
 
     if rank == 0:
         per_name = {}
         for j, (name, d_out, d_in, _, key) in enumerate(spec):
             us = per_gemv_us[j]
             per_name[name] = {"shape": [d_out, d_in], "n_outliers": n_o[key], "bytes": local_bytes[j],
-                              "us": round(us, 3), "gb_s": round(local_bytes[j] / (us * 1e-6) / 1e9, 1)}
+                              "us": round(us, 3), "gb_s": round(local_bytes[j] / (us * 1e-6) / 1e9, 1),
+                              "rel_l2_vs_fp32": float(f"{rel_l2[j]:.3e}")}
             if sharded:
                 per_name[name]["rows"] = [rows[j][0], rows[j][1]]
         traffic = ncu_traffic(args.workload)
@@ -438,8 +486,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             "higher_is_better": True, "scaling": "strong" if sharded else "weak", "vs_baseline": None,
             "dtype": "w4a16 (fp32 accumulate)", "data": "synthetic (seeded N(0,1/d_in) weights, N(0,1) "
                                                         "activations with U[10,100] outliers)",
-            "config": {"workload": args.workload, "gemvs": [[n, o, i] for n, o, i, *_ in spec], "batch": 1,
-                       "group": 128, "outlier_k": K_OUTLIER, "outlier_frac": spec[0][3],
+            "config": {"workload": args.workload, "gemvs": [[n, o, i] for n, o, i, *_ in spec], "batch": M,
+                       "group": 128, "outlier_k": args.k, "outlier_frac": spec[0][3], "dist": args.dist,
                        "l2": f"inputs larger than L2: {n_sets} rotating weight sets "
                              f"({n_sets * step_bytes / 1e6:.0f} MB streamed per cycle)",
                        "graphs": "the K timed steps are one CUDA graph of back-to-back launches",
@@ -449,10 +497,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             "gemvs": per_name,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_note": peak_note,
-                         "kernel": "b1_kernel<split, native unit layout, staged outlier segments>",
+                         "kernel": ("b1_kernel<split, native unit layout, staged outlier segments>" if M == 1 else
+                                    "bplan_kernel + bout_kernel + bdense_kernel (one batched split GEMV call)"),
                          "algorithmic_bytes_per_launch": round(sum(local_bytes) / n_gemv),
                          "traffic": traffic},
-            "gpu_launches": args.steps * n_gemv,  # our kernel launches in the timed region (NCCL not counted)
+            # our kernel launches in the timed region (NCCL not counted)
+            "gpu_launches": args.steps * n_gemv * kernels_per_gemv,
             "e2e": e2e,
             "clocks": clocks,
             "cpu_baseline": cpu,
@@ -471,11 +521,16 @@ def run_e2e(args, spec, sets, acts_np, dev, step_bytes, world, rows):
     Row-sharded runs (world > 1) gather each GEMV's output slices with
     dyn_quant.sharded.gather_rows, so every rank copies the full y back."""
     import torch
+    import torch.distributed as dist
     from dyn_quant.sharded import gather_rows
+    M = args.batch
     xh = {k: torch.from_numpy(v).pin_memory() for k, v in acts_np.items()}
     xd = {k: torch.empty(v.shape, dtype=torch.float16, device=dev) for k, v in acts_np.items()}
-    yh = [torch.empty(o, dtype=torch.float16).pin_memory() for _, o, _, _, _ in spec]
+    yh = [torch.empty(M * (o if world == 1 else world * per), dtype=torch.float16).pin_memory()
+          for (_, o, _, _, _), (_, _, per) in zip(spec, rows)]
     gbuf = [torch.empty(world * per, dtype=torch.float16, device=dev) for (_, _, per) in rows]
+    ypad = [torch.zeros(M, per, dtype=torch.float16, device=dev) for (_, _, per) in rows]
+    gbig = [torch.empty(world * M * per, dtype=torch.float16, device=dev) for (_, _, per) in rows]
     h2d = sum(v.numel() * 2 for v in xh.values())
     d2h = sum(v.numel() * 2 for v in yh)
     stream = torch.cuda.current_stream(dev)
@@ -489,9 +544,13 @@ def run_e2e(args, spec, sets, acts_np, dev, step_bytes, world, rows):
             xd[k].copy_(xh[k], non_blocking=True)
         for gi, (name, d_out, d_in, frac, key) in enumerate(spec):
             y = sets[s][gi](xd[key])
-            if world > 1:
+            if world > 1 and M == 1:
                 y = gather_rows(y, d_out, rows[gi][2], None, gbuf[gi])
-            yh[gi].copy_(y, non_blocking=True)
+            elif world > 1:  # [M, rows] slices, gathered rank-major
+                ypad[gi][:, :y.shape[-1]].copy_(y)
+                dist.all_gather_into_tensor(gbig[gi], ypad[gi].reshape(-1))
+                y = gbig[gi]
+            yh[gi].copy_(y.reshape(-1), non_blocking=True)
         end.record(stream)
         end.synchronize()
         return start.elapsed_time(end)
@@ -525,11 +584,17 @@ def main(argv=None) -> None:
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--batch", type=int, default=1, help="activation vectors per GEMV call (1..16 per kernel)")
+    ap.add_argument("--frac", type=float, default=None, help="injected outlier fraction (default: the workload's)")
+    ap.add_argument("--k", type=float, default=K_OUTLIER, help="outlier threshold in standard deviations")
+    ap.add_argument("--dist", choices=["normal", "t3"], default="normal", help="activation distribution")
     ap.add_argument("--max-sets", type=int, default=0,
                     help="cap on rotating weight sets (profiling runs only; the default rotates through >= 3x L2)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if not 1 <= args.batch <= 16:
+        ap.error("--batch must be in 1..16")
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -138,7 +138,29 @@ dq_status_t dq_build_native(const uint8_t* packed, const uint16_t* scales, const
 
 dq_status_t dq_read_device_error(uint32_t* word, int clear) {
     if (!word) return DQ_ERR_INVALID_ARGUMENT;
-    return read_device_error(word, clear != 0);
+    uint32_t b1 = 0, bg = 0;
+    dq_status_t st = read_device_error(&b1, clear != 0);
+    if (st != DQ_OK) return st;
+    st = read_batched_error(&bg, clear != 0);
+    if (st != DQ_OK) return st;
+    *word = b1 | (bg << 8);
+    return DQ_OK;
+}
+
+size_t dq_workspace_bytes_batched(int32_t d_out, int32_t d_in, int32_t m) {
+    if (check_dims(d_out, d_in) != DQ_OK || m < 1 || m > kBgMaxM) return 0;
+    return bg_ws(bg_geom(d_out, d_in, m), d_out, d_in).total;
+}
+
+dq_status_t dq_split_gemv_batched(const dq_weights_t* w, const uint16_t* x, uint16_t* y, int32_t m,
+                                  float outlier_k, void* workspace, size_t workspace_bytes, void* stream) {
+    if (m < 1 || m > kBgMaxM) return DQ_ERR_SHAPE;
+    if (w && w->d_out == 0 && check_dims(w->d_out, w->d_in) == DQ_OK) return DQ_OK;
+    dq_status_t st = check_weights(w, x, y, true, workspace, workspace_bytes);
+    if (st != DQ_OK) return st;
+    if (!w->native) return DQ_ERR_INVALID_ARGUMENT;
+    if (workspace_bytes < bg_ws(bg_geom(w->d_out, w->d_in, m), w->d_out, w->d_in).total) return DQ_ERR_WORKSPACE;
+    return launch_gemv_batched(*w, x, y, m, outlier_k, workspace, static_cast<cudaStream_t>(stream));
 }
 
 size_t dq_workspace_bytes(int32_t d_out, int32_t d_in) {

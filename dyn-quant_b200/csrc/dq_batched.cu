@@ -1,0 +1,704 @@
+// dq_batched.cu -- the split GEMV for a batch of 1 <= M <= 16 activation
+// vectors on sm_100a: y[m] = split_gemv(W, x[m], k) for every m, i.e. the
+// reference's batch-1 split GEMV (src/split_gemv.cu:25-198 of dyn-quant)
+// applied to each vector with its own statistics and outlier mask, while the
+// weights stream from HBM once for all vectors.
+//
+// Three kernels, chained on the stream by programmatic dependent launch:
+//  1. bplan_kernel, one CTA per vector: the statistics and the outlier mask
+//     of x[m], with the code and the fixed partition of the batch-1 kernel
+//     (dq_plan.cuh), so each vector gets exactly the batch-1 mask.  The last
+//     CTA to finish builds the union of the M masks (ascending columns) and
+//     x_o[m][u] = x[m][col_u] where col_u is an outlier of vector m, else 0.
+//  2. bout_kernel: the FP16 part, Y_o = W16[:, union] x_o, as a tensor-core
+//     GEMM over the union's columns: 16 rows x 16 union columns per MMA, A
+//     from the column-major FP16 mirror (one 16-byte cp.async per lane, then
+//     ldmatrix.trans), B = x_o.  Tasks (row block, part) take the union
+//     batches part, part + P, ...; each part is written to the workspace.
+//  3. bdense_kernel: the INT4 part over x' (each vector's outliers zeroed),
+//     split over K: CTA (cx, slab) streams chunks [slab S, slab S + S) of the
+//     row blocks [rb0, rb1) through per-warp cp.async.bulk rings.  Each warp
+//     owns whole row blocks; the last slab to finish a row block (an arrival
+//     counter) sums the slabs' partial sums and the FP16 parts in fixed order
+//     and writes y, so results do not depend on timing.
+//
+// Tensor-core formulation of the INT4 part (mma.sync.m16n8k16, f16 x f16 ->
+// f32; 16 weight rows x 8 vectors x 16 columns of one 128-column group).
+// ldmatrix over the native unit layout gives lane (g, t) word t of the pieces
+// of group j at slices 0..3 for rows g and g + 8 (columns 32 sl + 8 t ..
+// 32 sl + 8 t + 7 of the group).  A keeps the exponent bias (f16 1024 + q for
+// even columns, 1024 + 16 q for odd columns); B is x' of vector g in the same
+// column order, from a per-CTA table.  Per group and vector:
+//   D_lo = 1024 Xe + sum_even q x'        D_hi = 1024 Xo + 16 sum_odd q x'
+//   y += s ((D_hi - 1024 Xo) / 16 + (D_lo - 1024 Xe) - z X)
+// which is the reference's sum over the group of s (q - z) x'.
+#include <algorithm>
+
+#include "dq_common.cuh"
+#include "dq_internal.h"
+#include "dq_plan.cuh"
+
+namespace dq {
+
+namespace {
+
+// Set by a batched kernel whose bounded wait on its own copies gave up.
+__device__ unsigned int g_berror_word;
+
+constexpr int kUnit = kB1UnitBytes;
+
+// Parts of the FP16 product for nbat union batches of 16 columns: at least
+// four batches per task, at most pmax parts.  Both the FP16-part kernel and
+// the dense kernel derive it from the union size on the device.
+__device__ __forceinline__ int bg_parts(int nbat, int pmax) {
+    if (nbat <= 0) return 0;
+    const int p = (nbat + 3) / 4;
+    return p < pmax ? p : pmax;
+}
+
+__device__ __forceinline__ float4 lds_f4(uint32_t addr) {
+    const uint4 v = lds_v4(addr);
+    return make_float4(__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z), __uint_as_float(v.w));
+}
+
+// ---------------------------------------------------------------------------
+// 1. Plan: statistics, masks, union
+// ---------------------------------------------------------------------------
+struct BPSmem {
+    int xs, mask, list, red, flag, total;
+};
+
+inline BPSmem bp_smem(int d_in) {
+    BPSmem S;
+    int off = 0;
+    S.xs = off;   off += align16(2 * d_in);
+    S.mask = off; off += align16(d_in / 8);
+    S.list = off; off += align16(d_in);
+    S.red = off;  off += kB1RedBytes;
+    S.flag = off; off += 16;
+    S.total = off;
+    return S;
+}
+
+struct BPArgs {
+    const uint16_t* x;   // [M][d_in]
+    uint32_t* masks;     // [kBgMaxM][W]
+    uint32_t* ulist;     // [d_in]
+    uint16_t* xo;        // [MP][d_in]
+    unsigned int* ctr;   // [0] arrival counter, [1] union size
+    unsigned int* rbcnt; // [NRB] the dense kernel's per-row-block counters, cleared here
+    float k, inv_n, inv_n1;
+    int M, MP, d_in, W, NRB;
+    BPSmem S;
+};
+
+__global__ void __launch_bounds__(kStatThreads, 1) bplan_kernel(const BPArgs a) {
+    constexpr int NT = kStatThreads;
+    extern __shared__ __align__(128) char smem[];
+    uint4* xs = reinterpret_cast<uint4*>(smem + a.S.xs);
+    uint32_t* mask32 = reinterpret_cast<uint32_t*>(smem + a.S.mask);
+    uint32_t* list = reinterpret_cast<uint32_t*>(smem + a.S.list);
+    float* red = reinterpret_cast<float*>(smem + a.S.red);
+    int* flag = reinterpret_cast<int*>(smem + a.S.flag);
+    const int m = blockIdx.x, tid = threadIdx.x;
+    const int n8 = a.d_in >> 3;
+
+    pdl_launch_dependents();
+    pdl_wait();  // x and the workspace may belong to the preceding kernel until here
+    // The row-block counters sit at a shape-dependent offset, where another
+    // shape's scratch may have been: clear this call's before the dense kernel.
+    for (int i = m * NT + tid; i < a.NRB; i += a.M * NT) a.rbcnt[i] = 0u;
+    load_x_async<NT>(a.x + static_cast<size_t>(m) * a.d_in, n8, xs);
+    cp_async_wait_all();
+    __syncthreads();
+    const XStats st = x_stats<NT>(xs, n8, a.d_in, a.k, a.inv_n, a.inv_n1, red);
+    x_mask_list<NT>(xs, a.d_in, st.mean, st.thresh, mask32, list,
+                    reinterpret_cast<int*>(red) + 2 * (kStatThreads / 32));
+    __syncthreads();
+    for (int i = tid; i < a.W; i += NT) a.masks[static_cast<size_t>(m) * a.W + i] = mask32[i];
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) *flag = atomicAdd(a.ctr, 1u) == static_cast<unsigned>(a.M - 1);
+    __syncthreads();
+    if (!*flag) return;
+    __threadfence();
+
+    // The last CTA: union of the M masks.  Thread tid owns the words [w0, w1),
+    // at most two (W <= kMaxDIn / 32 <= 2 NT).
+    static_assert(kMaxDIn / 32 <= 2 * NT, "union words per thread");
+    const int w0 = static_cast<int>(static_cast<long long>(tid) * a.W / NT);
+    const int w1 = static_cast<int>(static_cast<long long>(tid + 1) * a.W / NT);
+    uint32_t u[2] = {0u, 0u};
+    int cnt[1] = {0};
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+        const int wj = w0 + q;
+        if (wj < w1) {
+            for (int mm = 0; mm < a.M; ++mm) u[q] |= ldcg_u32(a.masks + static_cast<size_t>(mm) * a.W + wj);
+            cnt[0] += __popc(u[q]);
+        }
+    }
+    int pre[1], tot[1];
+    block_scan<NT, 1>(cnt, pre, tot, reinterpret_cast<int*>(red));
+    int pos = pre[0];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+        const int wj = w0 + q;
+        if (wj < w1) {
+            uint32_t mw[kBgMaxM];
+#pragma unroll
+            for (int mm = 0; mm < kBgMaxM; ++mm)
+                mw[mm] = mm < a.M ? ldcg_u32(a.masks + static_cast<size_t>(mm) * a.W + wj) : 0u;
+            uint32_t rest = u[q];
+            while (rest) {
+                const int bit = __ffs(rest) - 1;
+                const int col = 32 * wj + bit;
+                a.ulist[pos] = static_cast<uint32_t>(col);
+#pragma unroll
+                for (int mm = 0; mm < kBgMaxM; ++mm) {
+                    if (mm < a.MP) {
+                        uint16_t v = 0;
+                        if ((mw[mm] >> bit) & 1u) v = ldcg_u16(a.x + static_cast<size_t>(mm) * a.d_in + col);
+                        a.xo[static_cast<size_t>(mm) * a.d_in + pos] = v;
+                    }
+                }
+                ++pos;
+                rest &= rest - 1u;
+            }
+        }
+    }
+    // The last batch of 16 union columns is padded with column 0 and zeros.
+    const int U = tot[0];
+    const int upad = min(a.d_in, (U + 15) & ~15);
+    for (int i = U + tid; i < upad; i += NT) {
+        a.ulist[i] = 0u;
+        for (int mm = 0; mm < a.MP; ++mm) a.xo[static_cast<size_t>(mm) * a.d_in + i] = 0;
+    }
+    if (tid == 0) {
+        a.ctr[1] = static_cast<unsigned>(U);
+        a.ctr[0] = 0u;  // ready for the next call
+    }
+}
+
+// ---------------------------------------------------------------------------
+// 2. FP16 part over the union's columns
+// ---------------------------------------------------------------------------
+// How the FP16 weights of the union's columns are read (as in the batch-1 kernel).
+enum : int {
+    kBoStaged = 0,     // column-major mirror, d_out % 8 == 0: 16-byte cp.async per lane
+    kBoColDirect = 1,  // column-major mirror, other d_out: plain loads
+    kBoRowDirect = 2,  // row-major FP16 only: plain loads
+};
+
+struct BOArgs {
+    const uint16_t* w16;     // row-major FP16 [d_out][d_in]
+    const uint16_t* w16_cm;  // column-major mirror [d_in][d_out]
+    const uint32_t* ulist;
+    const uint16_t* xo;
+    const unsigned int* ctr;
+    float* opart;            // [pmax][MP][d_out]
+    int d_out, d_in, NRB, pmax;
+};
+
+template <int kOut, int NT>
+__global__ void __launch_bounds__(kBgOutWarps * 32) bout_kernel(const BOArgs a) {
+    constexpr int MP = 8 * NT;
+    __shared__ __align__(128) unsigned char buf[kBgOutWarps][kBgOutBufs][512];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+
+    pdl_launch_dependents();
+    pdl_wait();  // the union comes from the plan kernel
+    const int U = static_cast<int>(ldcg_u32(a.ctr + 1));
+    const int nbat = (U + 15) / 16;
+    const int P = bg_parts(nbat, a.pmax);
+    const int ntask = a.NRB * P;
+    const uint32_t wbuf = smem_u32(&buf[warp][0][0]);
+
+    for (int task = blockIdx.x * kBgOutWarps + warp; task < ntask; task += gridDim.x * kBgOutWarps) {
+        const int rb = task / P, p = task - rb * P;
+        const int nb = (nbat - p + P - 1) / P;  // batches p, p + P, ...
+        float d[NT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) d[nt][0] = d[nt][1] = d[nt][2] = d[nt][3] = 0.f;
+
+        // Batch k of this task into buffer k % kBgOutBufs: lane = (union column
+        // lane >> 1 of the batch, row half lane & 1), 8 rows of FP16.
+        auto issue = [&](int k) {
+            const int b = p + k * P;
+            const int kc = 16 * b + (lane >> 1);
+            const int row0 = rb * kRowBlock + 8 * (lane & 1);
+            const uint32_t dst = wbuf + (k % kBgOutBufs) * 512 + 16 * lane;
+            const bool valid = kc < U && row0 < a.d_out;
+            const int col = valid ? static_cast<int>(ldcg_u32(a.ulist + kc)) : 0;
+            if (kOut == kBoStaged) {
+                if (valid) cp_async16(dst, a.w16_cm + static_cast<size_t>(col) * a.d_out + row0);
+                else sts_v4(dst, make_uint4(0, 0, 0, 0));
+                cp_async_commit();
+            } else {
+                uint16_t h[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int r = row0 + i;
+                    h[i] = (valid && r < a.d_out)
+                               ? (kOut == kBoColDirect ? ldg_u16(a.w16_cm + static_cast<size_t>(col) * a.d_out + r)
+                                                       : ldg_u16(a.w16 + static_cast<size_t>(r) * a.d_in + col))
+                               : static_cast<uint16_t>(0);
+                }
+                sts_v4(dst, make_uint4(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]), pack_h2(h[4], h[5]),
+                                       pack_h2(h[6], h[7])));
+            }
+        };
+        for (int k = 0; k < kBgOutBufs && k < nb; ++k) issue(k);
+        for (int k = 0; k < nb; ++k) {
+            if (kOut == kBoStaged) {
+                if (k + 2 < nb) cp_async_wait_group<2>();
+                else if (k + 1 < nb) cp_async_wait_group<1>();
+                else cp_async_wait_group<0>();
+            }
+            __syncwarp();
+            const uint32_t bsm = wbuf + (k % kBgOutBufs) * 512;
+            uint32_t a0, a1, a2, a3;
+            // matrix j = (column half j >> 1, row half j & 1); lane 8j + i gives column (j >> 1) * 8 + i
+            ldmatrix_x4_trans(bsm + (((lane >> 4) * 8 + (lane & 7)) * 32) + ((lane >> 3) & 1) * 16, a0, a1, a2, a3);
+            const int k0 = 16 * (p + k * P);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                const uint16_t* xr = a.xo + static_cast<size_t>(nt * 8 + g) * a.d_in + k0 + 2 * t;
+                mma_16816(d[nt], a0, a1, a2, a3, ldcg_u32(xr), ldcg_u32(xr + 8));
+            }
+            __syncwarp();  // every lane is done with the buffer before it is refilled
+            if (k + kBgOutBufs < nb) issue(k + kBgOutBufs);
+        }
+        float* op = a.opart + static_cast<size_t>(p) * MP * a.d_out;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int row = rb * kRowBlock + g + 8 * (e >> 1);
+                const int tok = nt * 8 + 2 * t + (e & 1);
+                if (row < a.d_out) op[static_cast<size_t>(tok) * a.d_out + row] = d[nt][e];
+            }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// 3. INT4 part, split over K, and the final sums
+// ---------------------------------------------------------------------------
+struct BDArgs {
+    const uint8_t* native;   // unit layout
+    const uint16_t* x;       // [M][d_in]
+    const uint32_t* masks;   // [kBgMaxM][W]
+    const unsigned int* ctr;
+    const float* opart;      // [pmax][MP][d_out]
+    float* dpart;            // [nslab][MP][d_out]
+    unsigned int* rbcnt;     // [NRB] slabs finished per row block (cleared by the plan kernel)
+    uint16_t* y;             // [M][d_out]
+    int M, d_out, d_in, NC, NRB, S, nslab, cps, W, pmax;
+    int sm_ring, sm_bars, sm_xtab, sm_xsum;
+};
+
+struct BDSmem {
+    int ring, bars, xtab, xsum, total;
+};
+
+inline BDSmem bd_smem(int S, int MP) {
+    BDSmem L;
+    int off = 0;
+    L.ring = off; off += kBgWarps * kBgStages * kUnit;
+    L.bars = off; off += (kBgWarps * kBgStages * 8 + 127) / 128 * 128;
+    L.xtab = off; off += S * MP * 1024;
+    L.xsum = off; off += S * kB1ChunkGroups * MP * 16;
+    L.total = off;
+    return L;
+}
+
+template <int NT>
+__global__ void __launch_bounds__(kBgWarps * 32, 1) bdense_kernel(const BDArgs a) {
+    constexpr int MP = 8 * NT;
+    constexpr int kT = kBgWarps * 32;
+    extern __shared__ __align__(128) char smem[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int sb = blockIdx.y;
+    const int c0 = sb * a.S, nch = min(a.S, a.NC - c0);
+    const int rb0 = static_cast<int>(static_cast<long long>(a.NRB) * blockIdx.x / a.cps);
+    const int rb1 = static_cast<int>(static_cast<long long>(a.NRB) * (blockIdx.x + 1) / a.cps);
+    // Warp w owns the row blocks rb0 + w, rb0 + w + kBgWarps, ...; its units
+    // are their nch chunks of this slab, row block by row block.
+    const int nrw = (rb1 - rb0 > warp) ? (rb1 - rb0 - warp + kBgWarps - 1) / kBgWarps : 0;
+    const int wn = nrw * nch;
+    const uint32_t ring = smem_u32(smem + a.sm_ring) + warp * kBgStages * kUnit;
+    const uint32_t bars = smem_u32(smem + a.sm_bars) + warp * kBgStages * 8;
+    uint4* xtab = reinterpret_cast<uint4*>(smem + a.sm_xtab);
+    float4* xsum = reinterpret_cast<float4*>(smem + a.sm_xsum);
+
+    auto unit_of = [&](int j) -> long long {
+        const int r = j / nch;
+        return static_cast<long long>(rb0 + warp + kBgWarps * r) * a.NC + c0 + (j - r * nch);
+    };
+    auto issue = [&](int s, int j) {  // lane 0 only
+        const uint32_t bar = bars + 8 * s;
+        mbar_arrive_expect_tx(bar, kUnit);
+        bulk_g2s(ring + s * kUnit, a.native + unit_of(j) * kUnit, kUnit, bar);
+    };
+
+    // The weights do not depend on the preceding kernels: the first stages go
+    // out before griddepcontrol.wait.
+    uint32_t armed = 0;
+    if (lane == 0) {
+#pragma unroll
+        for (int s = 0; s < kBgStages; ++s) mbar_init(bars + 8 * s, 1);
+        fence_mbar_init();
+#pragma unroll
+        for (int s = 0; s < kBgStages; ++s)
+            if (s < wn) issue(s, s);
+    }
+#pragma unroll
+    for (int s = 0; s < kBgStages; ++s)
+        if (s < wn) armed |= 1u << s;
+    __syncwarp();
+
+    pdl_launch_dependents();
+    pdl_wait();  // x, the masks, the union and the FP16 parts come from the preceding kernels
+    if (rb1 <= rb0) return;  // no row blocks (no copies were issued)
+
+    // x' of this slab's chunks for every vector, in MMA B order: piece p
+    // (8 columns) of chunk cc, vector tok goes to [cc][group p >> 4][slice
+    // (p >> 2) & 3][tok][p & 3] as the f16 pairs (x0,x4), (x2,x6), (x1,x5),
+    // (x3,x7), outliers of tok zeroed; xsum[cc][group][tok] = (1024 sum x'
+    // even columns, 1024 sum x' odd columns, sum x', 0).  16 consecutive
+    // threads hold the 16 pieces of one (chunk, group, vector).
+    const int npc = nch * MP * 64;
+    for (int i = tid; i < npc; i += kT) {
+        const int p = i & 63, tok = (i >> 6) % MP, cc = i / (64 * MP);
+        const int col = (c0 + cc) * 512 + 8 * p;
+        uint4 w = make_uint4(0, 0, 0, 0);
+        if (tok < a.M && col < a.d_in) {
+            w = ldcg_v4(a.x + static_cast<size_t>(tok) * a.d_in + col);
+            const uint32_t mb = (ldcg_u32(a.masks + static_cast<size_t>(tok) * a.W + (col >> 5)) >> (col & 31)) & 0xFFu;
+            if (mb) {
+                uint32_t keep[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    keep[q] = ((mb >> (2 * q)) & 1u ? 0u : 0x0000FFFFu) | ((mb >> (2 * q + 1)) & 1u ? 0u : 0xFFFF0000u);
+                w.x &= keep[0];
+                w.y &= keep[1];
+                w.z &= keep[2];
+                w.w &= keep[3];
+            }
+        }
+        float pe = add_f16_f32(lo16(w.w), add_f16_f32(lo16(w.z), add_f16_f32(lo16(w.y), add_f16_f32(lo16(w.x), 0.f))));
+        float po = add_f16_f32(hi16(w.w), add_f16_f32(hi16(w.z), add_f16_f32(hi16(w.y), add_f16_f32(hi16(w.x), 0.f))));
+        xtab[(((cc * 4 + (p >> 4)) * 4 + ((p >> 2) & 3)) * MP + tok) * 4 + (p & 3)] =
+            make_uint4((w.x & 0xFFFFu) | (w.z << 16), (w.y & 0xFFFFu) | (w.w << 16), (w.x >> 16) | (w.z & 0xFFFF0000u),
+                       (w.y >> 16) | (w.w & 0xFFFF0000u));
+#pragma unroll
+        for (int o = 8; o >= 1; o >>= 1) {
+            pe += __shfl_xor_sync(0xffffffffu, pe, o);
+            po += __shfl_xor_sync(0xffffffffu, po, o);
+        }
+        if ((i & 15) == 0) xsum[(cc * 4 + (p >> 4)) * MP + tok] = make_float4(1024.f * pe, 1024.f * po, pe + po, 0.f);
+    }
+    __syncthreads();
+
+    const int U = static_cast<int>(ldcg_u32(a.ctr + 1));
+    const int nparts = bg_parts((U + 15) / 16, a.pmax);
+    const uint32_t xtab_a = smem_u32(xtab);
+    const uint32_t xsum_a = smem_u32(xsum);
+    const int lm = lane >> 3, lr = lane & 7;  // ldmatrix: this lane addresses row lr of matrix (slice) lm
+
+    float yacc[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) yacc[nt][0] = yacc[nt][1] = yacc[nt][2] = yacc[nt][3] = 0.f;
+
+    // Row block rb done by this warp (for this slab): publish, and if it is the
+    // last slab to finish, sum all slabs and the FP16 parts and write y.
+    auto finish_rb = [&](int rb) {
+        const int row0 = rb * kRowBlock + g;
+        float v[NT][4];
+        if (a.nslab == 1) {
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) v[nt][e] = yacc[nt][e];
+        } else {
+            float* dp = a.dpart + static_cast<size_t>(sb) * MP * a.d_out;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int row = row0 + 8 * (e >> 1);
+                    const int tok = nt * 8 + 2 * t + (e & 1);
+                    if (row < a.d_out) dp[static_cast<size_t>(tok) * a.d_out + row] = yacc[nt][e];
+                }
+            __threadfence();
+            __syncwarp();
+            unsigned int old = 0;
+            if (lane == 0) old = atomicAdd(a.rbcnt + rb, 1u);
+            old = __shfl_sync(0xffffffffu, old, 0);
+            if (old != static_cast<unsigned>(a.nslab - 1)) return;
+            __threadfence();
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) v[nt][e] = 0.f;
+            for (int s2 = 0; s2 < a.nslab; ++s2) {
+                const float* sp = a.dpart + static_cast<size_t>(s2) * MP * a.d_out;
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int row = row0 + 8 * (e >> 1);
+                        const int tok = nt * 8 + 2 * t + (e & 1);
+                        if (row < a.d_out) v[nt][e] += ldcg_f32(sp + static_cast<size_t>(tok) * a.d_out + row);
+                    }
+            }
+        }
+        for (int p = 0; p < nparts; ++p) {
+            const float* op = a.opart + static_cast<size_t>(p) * MP * a.d_out;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int row = row0 + 8 * (e >> 1);
+                    const int tok = nt * 8 + 2 * t + (e & 1);
+                    if (row < a.d_out) v[nt][e] += ldcg_f32(op + static_cast<size_t>(tok) * a.d_out + row);
+                }
+        }
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int row = row0 + 8 * (e >> 1);
+                const int tok = nt * 8 + 2 * t + (e & 1);
+                if (row < a.d_out && tok < a.M)
+                    a.y[static_cast<size_t>(tok) * a.d_out + row] = __half_as_ushort(__float2half_rn(v[nt][e]));
+            }
+    };
+
+    bool ok = true;
+    uint32_t phase = 0;
+    for (int j = 0; j < wn; ++j) {
+        const int s = j % kBgStages;
+        const bool got = mbar_wait_bounded(bars + 8 * s, (phase >> s) & 1u);
+        if (!__all_sync(0xffffffffu, got)) {
+            ok = false;
+            if (lane == 0) atomicOr(&g_berror_word, 1u);
+            break;
+        }
+        phase ^= 1u << s;
+        armed &= ~(1u << s);
+        const int r = j / nch, cc = j - r * nch;
+        const uint32_t st = ring + s * kUnit;
+#pragma unroll
+        for (int jg = 0; jg < kB1ChunkGroups; ++jg) {
+            uint32_t w0[4], w1[4];  // [slice]: word t of the pieces of group jg, rows g and g + 8
+            ldmatrix_x4(st + native_piece(lm, 0, lr, jg) * 16, w0[0], w0[1], w0[2], w0[3]);
+            ldmatrix_x4(st + native_piece(lm, 1, lr, jg) * 16, w1[0], w1[1], w1[2], w1[3]);
+            float dlo[NT][4], dhi[NT][4];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) dlo[nt][e] = dhi[nt][e] = 0.f;
+#pragma unroll
+            for (int sl = 0; sl < 4; ++sl) {
+                const Biased4 qa = biased_word(w0[sl]);
+                const Biased4 qb = biased_word(w1[sl]);
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    const uint4 b = lds_v4(xtab_a + ((((cc * 4 + jg) * 4 + sl) * MP + nt * 8 + g) * 4 + t) * 16);
+                    mma_16816(dlo[nt], qa.lo0, qb.lo0, qa.lo1, qb.lo1, b.x, b.y);
+                    mma_16816(dhi[nt], qa.hi0, qb.hi0, qa.hi1, qb.hi1, b.z, b.w);
+                }
+            }
+            // (scale | zero << 16) of group jg, rows g and g + 8
+            const uint32_t e0 = lds_u32(st + kB1UnitPacked + 16 * g + 4 * jg);
+            const uint32_t e8 = lds_u32(st + kB1UnitPacked + 16 * (g + 8) + 4 * jg);
+            const float s0 = h2f_bits(lo16(e0)), z0 = h2f_bits(hi16(e0));
+            const float s8 = h2f_bits(lo16(e8)), z8 = h2f_bits(hi16(e8));
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                const uint32_t xa_addr = xsum_a + ((cc * 4 + jg) * MP + nt * 8 + 2 * t) * 16;
+                const float4 xa = lds_f4(xa_addr);       // vector nt*8 + 2t
+                const float4 xb = lds_f4(xa_addr + 16);  // vector nt*8 + 2t + 1
+                yacc[nt][0] = fmaf(s0, fmaf(-z0, xa.z, fmaf(dhi[nt][0] - xa.y, 0.0625f, dlo[nt][0] - xa.x)), yacc[nt][0]);
+                yacc[nt][1] = fmaf(s0, fmaf(-z0, xb.z, fmaf(dhi[nt][1] - xb.y, 0.0625f, dlo[nt][1] - xb.x)), yacc[nt][1]);
+                yacc[nt][2] = fmaf(s8, fmaf(-z8, xa.z, fmaf(dhi[nt][2] - xa.y, 0.0625f, dlo[nt][2] - xa.x)), yacc[nt][2]);
+                yacc[nt][3] = fmaf(s8, fmaf(-z8, xb.z, fmaf(dhi[nt][3] - xb.y, 0.0625f, dlo[nt][3] - xb.x)), yacc[nt][3]);
+            }
+        }
+        __syncwarp();  // every lane is done with the stage before it is refilled
+        if (j + kBgStages < wn) {
+            if (lane == 0) issue(s, j + kBgStages);
+            armed |= 1u << s;
+        }
+        if (cc == nch - 1) {
+            finish_rb(rb0 + warp + kBgWarps * r);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) yacc[nt][0] = yacc[nt][1] = yacc[nt][2] = yacc[nt][3] = 0.f;
+        }
+    }
+    if (!ok) {
+        // Do not leave copies in flight into shared memory this CTA is about to release.
+#pragma unroll
+        for (int s = 0; s < kBgStages; ++s)
+            if (armed & (1u << s)) mbar_wait_bounded(bars + 8 * s, (phase >> s) & 1u);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+constexpr int kMaxDevices = 64;
+constexpr int kNumKernels = 16;
+int g_smem_set[kMaxDevices][kNumKernels];
+
+template <class K>
+dq_status_t ensure_smem(K kernel, int id, int bytes) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) { set_cuda_error(e); return DQ_ERR_CUDA; }
+    if (dev >= 0 && dev < kMaxDevices && __atomic_load_n(&g_smem_set[dev][id], __ATOMIC_ACQUIRE) >= bytes)
+        return DQ_OK;
+    const int want = bytes < 48 * 1024 ? 48 * 1024 : bytes;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, want);
+    if (e != cudaSuccess) { set_cuda_error(e); return DQ_ERR_CUDA; }
+    if (dev >= 0 && dev < kMaxDevices) {
+        int cur = __atomic_load_n(&g_smem_set[dev][id], __ATOMIC_ACQUIRE);
+        while (cur < want && !__atomic_compare_exchange_n(&g_smem_set[dev][id], &cur, want, false,
+                                                          __ATOMIC_ACQ_REL, __ATOMIC_ACQUIRE)) {
+        }
+    }
+    return DQ_OK;
+}
+
+// Every batched kernel is a programmatic dependent of its predecessor on the stream.
+template <class K, class A>
+dq_status_t launch_pdl(K kernel, dim3 grid, int threads, int smem, cudaStream_t stream, const A& args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) { set_cuda_error(e); return DQ_ERR_CUDA; }
+    return DQ_OK;
+}
+
+template <int kOut, int NT>
+dq_status_t launch_bout(const BOArgs& a, int grid, cudaStream_t stream) {
+    return launch_pdl(bout_kernel<kOut, NT>, dim3(grid), kBgOutWarps * 32, 0, stream, a);
+}
+
+template <int NT>
+dq_status_t launch_batched_nt(const BgGeom& G, const BPArgs& pa, const BOArgs& oa, int out_mode, int ogrid,
+                              const BDArgs& da, int dsmem, cudaStream_t stream) {
+    dq_status_t st = ensure_smem(bplan_kernel, 0, pa.S.total);
+    if (st != DQ_OK) return st;
+    st = ensure_smem(bdense_kernel<NT>, NT, dsmem);
+    if (st != DQ_OK) return st;
+    st = launch_pdl(bplan_kernel, dim3(G.M), kStatThreads, pa.S.total, stream, pa);
+    if (st != DQ_OK) return st;
+    switch (out_mode) {
+        case kBoStaged: st = launch_bout<kBoStaged, NT>(oa, ogrid, stream); break;
+        case kBoColDirect: st = launch_bout<kBoColDirect, NT>(oa, ogrid, stream); break;
+        default: st = launch_bout<kBoRowDirect, NT>(oa, ogrid, stream); break;
+    }
+    if (st != DQ_OK) return st;
+    return launch_pdl(bdense_kernel<NT>, dim3(da.cps, G.nslab), kBgWarps * 32, dsmem, stream, da);
+}
+
+}  // namespace
+
+dq_status_t launch_gemv_batched(const dq_weights_t& w, const uint16_t* x, uint16_t* y, int M, float k,
+                                void* workspace, cudaStream_t stream) {
+    DeviceInfo di;
+    dq_status_t st = device_info(&di);
+    if (st != DQ_OK) return st;
+    const BgGeom G = bg_geom(w.d_out, w.d_in, M);
+    const BgWs L = bg_ws(G, w.d_out, w.d_in);
+    char* ws = static_cast<char*>(workspace);
+    const BDSmem DS = bd_smem(G.S, G.MP);
+    if (DS.total > di.smem_optin) return DQ_ERR_UNSUPPORTED;
+
+    BPArgs pa;
+    pa.x = x;
+    pa.masks = reinterpret_cast<uint32_t*>(ws + L.masks);
+    pa.ulist = reinterpret_cast<uint32_t*>(ws + L.ulist);
+    pa.xo = reinterpret_cast<uint16_t*>(ws + L.xo);
+    pa.ctr = reinterpret_cast<unsigned int*>(ws + L.ctr);
+    pa.k = k;
+    pa.inv_n = 1.0f / static_cast<float>(w.d_in);
+    pa.inv_n1 = w.d_in > 1 ? 1.0f / static_cast<float>(w.d_in - 1) : 0.f;
+    pa.M = M;
+    pa.MP = G.MP;
+    pa.d_in = w.d_in;
+    pa.W = G.W;
+    pa.rbcnt = reinterpret_cast<unsigned int*>(ws + L.rbcnt);
+    pa.NRB = G.NRB;
+    pa.S = bp_smem(w.d_in);
+    if (pa.S.total > di.smem_optin) return DQ_ERR_UNSUPPORTED;
+
+    BOArgs oa;
+    oa.w16 = w.fp16;
+    oa.w16_cm = w.fp16_cm;
+    oa.ulist = pa.ulist;
+    oa.xo = pa.xo;
+    oa.ctr = pa.ctr;
+    oa.opart = reinterpret_cast<float*>(ws + L.opart);
+    oa.d_out = w.d_out;
+    oa.d_in = w.d_in;
+    oa.NRB = G.NRB;
+    oa.pmax = G.pmax;
+    const int out_mode = w.fp16_cm ? ((w.d_out % 8) == 0 ? kBoStaged : kBoColDirect) : kBoRowDirect;
+    const long long otasks = static_cast<long long>(G.NRB) * G.pmax;
+    const long long ocap = static_cast<long long>(di.sm_count) * 8;
+    const int ogrid = static_cast<int>(std::min<long long>((otasks + kBgOutWarps - 1) / kBgOutWarps, ocap));
+
+    BDArgs da;
+    da.native = w.native;
+    da.x = x;
+    da.masks = pa.masks;
+    da.ctr = pa.ctr;
+    da.opart = oa.opart;
+    da.dpart = reinterpret_cast<float*>(ws + L.dpart);
+    da.rbcnt = reinterpret_cast<unsigned int*>(ws + L.rbcnt);
+    da.y = y;
+    da.M = M;
+    da.d_out = w.d_out;
+    da.d_in = w.d_in;
+    da.NC = G.NC;
+    da.NRB = G.NRB;
+    da.S = G.S;
+    da.nslab = G.nslab;
+    da.cps = std::max(1, std::min(G.NRB, di.sm_count / G.nslab));
+    da.W = G.W;
+    da.pmax = G.pmax;
+    da.sm_ring = DS.ring;
+    da.sm_bars = DS.bars;
+    da.sm_xtab = DS.xtab;
+    da.sm_xsum = DS.xsum;
+
+    return G.NT == 1 ? launch_batched_nt<1>(G, pa, oa, out_mode, ogrid, da, DS.total, stream)
+                     : launch_batched_nt<2>(G, pa, oa, out_mode, ogrid, da, DS.total, stream);
+}
+
+dq_status_t read_batched_error(uint32_t* word, bool clear) {
+    cudaError_t e = cudaMemcpyFromSymbol(word, g_berror_word, sizeof(uint32_t));
+    if (e != cudaSuccess) { set_cuda_error(e); return DQ_ERR_CUDA; }
+    if (clear) {
+        const uint32_t z = 0;
+        e = cudaMemcpyToSymbol(g_berror_word, &z, sizeof(uint32_t));
+        if (e != cudaSuccess) { set_cuda_error(e); return DQ_ERR_CUDA; }
+    }
+    return DQ_OK;
+}
+
+}  // namespace dq

@@ -44,6 +44,7 @@
 
 #include "dq_common.cuh"
 #include "dq_internal.h"
+#include "dq_plan.cuh"
 
 namespace dq {
 
@@ -56,229 +57,6 @@ constexpr int kStageBytes = kB1StageBytes;
 // Set (bit 0) by a kernel whose bounded wait on its own copies gave up.
 __device__ unsigned int g_error_word;
 
-// ---------------------------------------------------------------------------
-// Block-wide helpers (NT threads)
-// ---------------------------------------------------------------------------
-
-// Exclusive prefix sums over the threads (in thread order) of NV ints per
-// thread, plus the totals.  scratch: NW * NV ints used by nothing else; one
-// barrier.
-template <int NT, int NV>
-__device__ __forceinline__ void block_scan(const int (&v)[NV], int (&pre)[NV], int (&tot)[NV], int* scratch) {
-    constexpr int NW = NT / 32;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    int incl[NV];
-#pragma unroll
-    for (int i = 0; i < NV; ++i) incl[i] = v[i];
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-#pragma unroll
-        for (int i = 0; i < NV; ++i) {
-            const int n = __shfl_up_sync(0xffffffffu, incl[i], o);
-            if (lane >= o) incl[i] += n;
-        }
-    }
-    if (lane == 31)
-#pragma unroll
-        for (int i = 0; i < NV; ++i) scratch[warp * NV + i] = incl[i];
-    __syncthreads();
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-        int before = 0, all = 0;
-#pragma unroll
-        for (int w = 0; w < NW; ++w) {
-            const int s = scratch[w * NV + i];
-            before += (w < warp) ? s : 0;
-            all += s;
-        }
-        pre[i] = before + incl[i] - v[i];
-        tot[i] = all;
-    }
-}
-
-__device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
-    return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
-}
-
-// ---------------------------------------------------------------------------
-// Activation plan (per CTA, NT threads)
-//
-// The outlier mask follows the reference's detector definition
-// (src/outlier_detect.cuh:104-205): mean and unbiased variance of x in FP32,
-// thresh = k * sqrt(max(var, 1e-8)), outlier iff |x - mean| > thresh, and at
-// most (d_in/4)/4 outliers kept per stripe class (columns c with
-// (c/32) % 4 == w, the first ones in ascending order), as the reference's
-// per-warp capacity does (src/outlier_detect.cuh:160-178).  Mean and variance
-// are merged from per-thread two-pass summaries in a fixed order, so every CTA
-// (and the standalone detector, which runs the same code with the same thread
-// count) derives the same mask.
-// ---------------------------------------------------------------------------
-
-// x (d_in = 8 * n8 halves) from global memory into xs, natural order, as
-// 16-byte cp.async copies (completed by cp_async_wait_all + a barrier).
-template <int NT>
-__device__ __forceinline__ void load_x_async(const uint16_t* __restrict__ x, int n8, uint4* xs) {
-    for (int ch = threadIdx.x; ch < n8; ch += NT) cp_async16(smem_u32(xs + ch), x + 8 * static_cast<size_t>(ch));
-    cp_async_commit();
-}
-
-struct XStats {
-    float mean, thresh, var, m2;
-};
-
-// Mean and unbiased variance of x (in xs), threshold k * sqrt(max(var, 1e-8)).
-// Two passes (sum, then sum of squared deviations) over a fixed partition of
-// kStatThreads virtual threads (virtual thread v: pieces v, v + 512, ...;
-// xor butterfly within each virtual warp; virtual-warp totals summed in
-// order), run by the NT real threads: every CTA of a launch, whatever its warp
-// count, and the standalone detector get bit-identical statistics.
-// inv_n = 1/d_in and inv_n1 = 1/(d_in - 1) come from the host.
-// red: >= 32 floats, not in use; two barriers.
-template <int NT>
-__device__ __forceinline__ XStats x_stats(const uint4* xs, int n8, int d_in, float k, float inv_n, float inv_n1,
-                                          float* red) {
-    constexpr int NW = NT / 32;
-    constexpr int NWV = kStatThreads / 32;
-    static_assert(NT <= kStatThreads && NT % 32 == 0, "statistics partition");
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (int vw = warp; vw < NWV; vw += NW) {
-        float s[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-        for (int ch = 32 * vw + lane; ch < n8; ch += kStatThreads) {
-            const uint4 v = xs[ch];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint32_t w = word_of(v, i);
-                s[i] = add_f16_f32(hi16(w), add_f16_f32(lo16(w), s[i]));
-            }
-        }
-        const float ws = warp_sum((s[0] + s[1]) + (s[2] + s[3]));
-        if (lane == 0) red[vw] = ws;
-    }
-    __syncthreads();
-    float total = 0.f;
-#pragma unroll
-    for (int w = 0; w < NWV; ++w) total += red[w];
-    XStats r;
-    r.mean = __fmul_rn(total, inv_n);
-    for (int vw = warp; vw < NWV; vw += NW) {
-        float m[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-        for (int ch = 32 * vw + lane; ch < n8; ch += kStatThreads) {
-            const uint4 v = xs[ch];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint32_t w = word_of(v, i);
-                const float d0 = sub_f16_f32(lo16(w), r.mean);
-                const float d1 = sub_f16_f32(hi16(w), r.mean);
-                m[i] = __fmaf_rn(d1, d1, __fmaf_rn(d0, d0, m[i]));
-            }
-        }
-        const float wq = warp_sum((m[0] + m[1]) + (m[2] + m[3]));
-        if (lane == 0) red[NWV + vw] = wq;
-    }
-    __syncthreads();
-    float m2 = 0.f;
-#pragma unroll
-    for (int w = 0; w < NWV; ++w) m2 += red[NWV + w];
-    r.m2 = m2;
-    r.var = (d_in > 1) ? __fmul_rn(m2, inv_n1) : 0.f;
-    r.thresh = __fmul_rn(k, __fsqrt_rn(fmaxf(r.var, 1e-8f)));
-    return r;
-}
-
-// Outlier mask with the reference's capacity rule, and the ascending outlier
-// list (column | FP16 bits of x << 16).  Thread tid owns the 32-column stripe
-// words [w0, w1) (at most 4; word wj = columns 32 wj .. 32 wj + 31, stripe
-// class wj % 4): it computes their bits, the block scan of the per-class
-// counts gives each class's count before it, and the capacity keeps the first
-// (d_in/4)/4 of each class in column order.  Writes mask32 and list; returns
-// the outlier count.  Barrier-synchronised; the list and mask are complete
-// after the caller's next barrier.  scratch: >= NW * 5 ints used by nothing
-// else.
-template <int NT>
-__device__ int x_mask_list(const uint4* xs, int d_in, float mean, float thresh, uint32_t* mask32, uint32_t* list,
-                           int* scratch) {
-    constexpr int kMaxWords = 4;
-    static_assert(kMaxDIn / 32 <= kMaxWords * NT, "stripe words per thread");
-    const int nw = d_in / 32;
-    const int tid = threadIdx.x;
-    const int w0 = static_cast<int>(static_cast<long long>(tid) * nw / NT);
-    const int w1 = static_cast<int>(static_cast<long long>(tid + 1) * nw / NT);
-    uint32_t bits[kMaxWords];
-    int cnt[4] = {0, 0, 0, 0};
-#pragma unroll
-    for (int q = 0; q < kMaxWords; ++q) {
-        bits[q] = 0;
-        const int wj = w0 + q;
-        if (wj < w1) {
-#pragma unroll
-            for (int p = 0; p < 4; ++p) {
-                const uint4 v = xs[4 * wj + p];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const uint32_t w = word_of(v, i);
-                    bits[q] |= (fabsf(sub_f16_f32(lo16(w), mean)) > thresh ? 1u : 0u) << (8 * p + 2 * i);
-                    bits[q] |= (fabsf(sub_f16_f32(hi16(w), mean)) > thresh ? 1u : 0u) << (8 * p + 2 * i + 1);
-                }
-            }
-            const int c = __popc(bits[q]);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) cnt[i] += (wj & 3) == i ? c : 0;
-        }
-    }
-    int pre[4], tot[4];
-    block_scan<NT, 4>(cnt, pre, tot, scratch);
-    const int cap = (d_in / 4) / 4;
-    int pos;
-    if (tot[0] > cap || tot[1] > cap || tot[2] > cap || tot[3] > cap) {
-        int kept[1] = {0};
-#pragma unroll
-        for (int q = 0; q < kMaxWords; ++q) {
-            const int wj = w0 + q;
-            if (wj < w1) {
-                uint32_t m = bits[q];
-                const int c = __popc(m);
-                const int w = wj & 3;
-                const int before = w == 0 ? pre[0] : (w == 1 ? pre[1] : (w == 2 ? pre[2] : pre[3]));
-                if (before + c > cap) {
-                    int keep = cap - before;
-                    uint32_t out = 0;
-                    for (; keep > 0 && m; --keep) {
-                        out |= m & (~m + 1u);
-                        m &= m - 1u;
-                    }
-                    bits[q] = out;
-                }
-                kept[0] += __popc(bits[q]);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) pre[i] += w == i ? c : 0;
-            }
-        }
-        int p1[1], t1[1];
-        block_scan<NT, 1>(kept, p1, t1, scratch + (NT / 32) * 4);
-        pos = p1[0];
-        tot[0] = t1[0];
-        tot[1] = tot[2] = tot[3] = 0;
-    } else {
-        pos = (pre[0] + pre[1]) + (pre[2] + pre[3]);
-    }
-    const uint16_t* xh = reinterpret_cast<const uint16_t*>(xs);
-#pragma unroll
-    for (int q = 0; q < kMaxWords; ++q) {
-        const int wj = w0 + q;
-        if (wj < w1) {
-            mask32[wj] = bits[q];
-            uint32_t m = bits[q];
-            while (m) {
-                const int col = 32 * wj + (__ffs(m) - 1);
-                list[pos++] = static_cast<uint32_t>(col) | (static_cast<uint32_t>(xh[col]) << 16);
-                m &= m - 1u;
-            }
-        }
-    }
-    return (tot[0] + tot[1]) + (tot[2] + tot[3]);
-}
 
 // One warp, in place over xb: the 64 natural 8-column pieces of each of the
 // 512-column chunks ca and cb (cb < 0: none) -> MMA B order [word wi][slice
@@ -645,7 +423,7 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
                     for (int sl = 0; sl < 4; ++sl)
 #pragma unroll
                         for (int h = 0; h < 2; ++h)
-                            aw[sl][h] = kNative ? lds_v4(st + ((sl * 2 + h) * 32 + lane) * 16)
+                            aw[sl][h] = kNative ? lds_v4(st + native_piece(sl, h, g, t) * 16)
                                                 : lds_v4(st + (g + 8 * h) * kB1RowPitch + 64 * t + 16 * sl);
                     const uint32_t bb = (b_owner ? bsm_a + cc * kB1ChunkB : zero_a) + b_lane;
                     float dl[4][4], dh[4][4];
@@ -771,9 +549,9 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
 }
 
 // Native unit layout: per (row-block rb, 4-group chunk c) one block of
-// kB1UnitBytes = 4096 bytes of packed codes ordered [slice sl][half h][lane]
-// (16 bytes each: row rb*16 + g + 8h, group 4c + t, columns 32 sl .. 32 sl + 31
-// of that group, with lane = 4g + t) followed by 256 bytes of
+// kB1UnitBytes = 4096 bytes of packed codes, 256 pieces of 16 bytes (piece
+// native_piece(sl, h, g, t): row rb*16 + g + 8h, group 4c + t, columns
+// 32 sl .. 32 sl + 31 of that group) followed by 256 bytes of
 // (scale | zero << 16) for [16 rows][4 groups].  Rows past d_out and groups
 // past G are zero.
 __global__ void build_native_kernel(const uint8_t* __restrict__ packed, const uint16_t* __restrict__ scales,
@@ -789,9 +567,10 @@ __global__ void build_native_kernel(const uint8_t* __restrict__ packed, const ui
     const int rb = static_cast<int>(unit / NC), c = static_cast<int>(unit % NC);
     uint4 v = make_uint4(0, 0, 0, 0);
     if (i < kB1UnitPacked / 16) {
-        const int sl = i >> 6, h = (i >> 5) & 1, ln = i & 31;
-        const int row = rb * kRowBlock + (ln >> 2) + 8 * h;
-        const int grp = kCG * c + (ln & 3);
+        const int sl = i >> 6, h = (i >> 5) & 1, pos = i & 31;
+        const int t = pos >> 3, g = (pos & 7) ^ (2 * t);  // inverse of native_piece
+        const int row = rb * kRowBlock + g + 8 * h;
+        const int grp = kCG * c + t;
         if (row < d_out && grp < G)
             v = *reinterpret_cast<const uint4*>(packed + static_cast<size_t>(row) * (d_in / 2) + 64 * grp + 16 * sl);
     } else {

@@ -86,13 +86,76 @@ inline WsLayout ws_layout(int d_out, int d_in) {
     return W;
 }
 
-// Bytes of the native unit layout the batch-1 kernel streams with one bulk
-// copy per unit: [row-block][4-group chunk] blocks of kB1UnitBytes.
+// Position of the 16-byte piece (slice sl, half h; row g + 8h of the row
+// block, group t of the chunk) among the 256 pieces of a unit's packed codes.
+// Within each (sl, h) block of 32 pieces, (g, t) sits at 8 t + (g ^ 2t): the
+// batch-1 kernel (lane 4g + t loads its own piece) and the batched kernel
+// (ldmatrix rows g = 0..7 of one group t) both touch 8 distinct 16-byte bank
+// groups per shared-memory wavefront.
+__host__ __device__ inline int native_piece(int sl, int h, int g, int t) {
+    return (sl * 2 + h) * 32 + 8 * t + (g ^ (2 * t));
+}
+
+// Bytes of the native unit layout the GEMV kernels stream with one bulk copy
+// per unit: [row-block][4-group chunk] blocks of kB1UnitBytes.
 inline size_t native_bytes(int d_out, int d_in) {
     const size_t n_rb = (static_cast<size_t>(d_out) + 15) / 16;
     const size_t nc = (static_cast<size_t>(d_in / 128) + kB1ChunkGroups - 1) / kB1ChunkGroups;
     return n_rb * nc * kB1UnitBytes;
 }
+
+// ---------------------------------------------------------------------------
+// Batched split GEMV (1 <= M <= 16 activation vectors, dq_batched.cu)
+// ---------------------------------------------------------------------------
+constexpr int kBgMaxM = 16;       // vectors per call
+constexpr int kBgWarps = 16;      // warps of a dense CTA (one CTA per SM)
+constexpr int kBgStages = 2;      // bulk-copy ring stages per warp
+constexpr int kBgOutWarps = 8;    // warps of an FP16-part CTA
+constexpr int kBgOutBufs = 3;     // per-warp outlier segment buffers in flight
+constexpr int kBgMaxParts = 16;   // FP16-part split over the union batches, at most
+constexpr int kBgRefSMs = 148;    // SM count the slab width is chosen for (keeps the workspace device-independent)
+
+// Split of one batched call.  NT tiles of 8 vectors (MP = 8 NT columns of the
+// MMA); S chunks (512 columns) per slab, nslab slabs; pmax bounds the parts
+// of the FP16 product.
+struct BgGeom {
+    int M, NT, MP, NC, NRB, S, nslab, W, pmax;
+};
+
+inline BgGeom bg_geom(int d_out, int d_in, int M) {
+    BgGeom g;
+    g.M = M;
+    g.NT = (M + 7) / 8;
+    g.MP = 8 * g.NT;
+    g.NC = (d_in / 128 + kB1ChunkGroups - 1) / kB1ChunkGroups;
+    g.NRB = (d_out + 15) / 16;
+    g.W = d_in / 32;
+    // The x' table of a slab (S chunks x MP vectors x 1 KB) sits next to the
+    // weight rings; narrower slabs when there are too few (row block, slab)
+    // tasks to keep every warp of every SM streaming.
+    g.S = g.NT == 1 ? 8 : 4;
+    while (g.S > 1 && static_cast<long long>((g.NC + g.S - 1) / g.S) * g.NRB < kBgRefSMs * kBgWarps * 3 / 4) g.S /= 2;
+    g.nslab = (g.NC + g.S - 1) / g.S;
+    long long p = (static_cast<long long>(kBgRefSMs) * 64 + g.NRB - 1) / g.NRB;
+    g.pmax = static_cast<int>(p < 1 ? 1 : (p > kBgMaxParts ? kBgMaxParts : p));
+    return g;
+}
+
+// Workspace of a batched call, after the batch-1 region (ws_layout): byte
+// offsets from the start of the workspace.  Only ctr[0] must be zero on entry
+// (at a fixed offset; every call leaves it zero); the rest is scratch.
+//   ctr    [0] plan arrival counter, [1] union size
+//   rbcnt  per row block, slabs finished (cleared by the plan kernel)
+//   masks  [kBgMaxM][W] outlier bits of each vector
+//   ulist  [d_in] the union of the masks, ascending columns
+//   xo     [MP][d_in] FP16: x[m][ulist[u]] where that column is an outlier of m, else 0
+//   opart  [pmax][MP][d_out] FP32 parts of the FP16 product
+//   dpart  [nslab][MP][d_out] FP32 per-slab partial sums of the INT4 part (nslab > 1)
+struct BgWs {
+    size_t ctr, rbcnt, masks, ulist, xo, opart, dpart, total;
+};
+
+inline BgWs bg_ws(const BgGeom& g, int d_out, int d_in);
 
 // Device facts cached per ordinal.
 struct DeviceInfo {
@@ -117,6 +180,24 @@ dq_status_t launch_quantize(const uint16_t* w16, int d_out, int d_in, uint8_t* p
                             uint16_t* scales, uint16_t* zeros, cudaStream_t stream);
 dq_status_t launch_colmajor(const uint16_t* w16, int d_out, int d_in, uint16_t* cm,
                             cudaStream_t stream);
+
+inline BgWs bg_ws(const BgGeom& g, int d_out, int d_in) {
+    BgWs L;
+    size_t off = ws_layout(d_out, d_in).total;
+    L.ctr = off;   off += 256;
+    L.rbcnt = off; off += align256(static_cast<size_t>(g.NRB) * 4);
+    L.masks = off; off += align256(static_cast<size_t>(kBgMaxM) * g.W * 4);
+    L.ulist = off; off += align256(static_cast<size_t>(d_in) * 4);
+    L.xo = off;    off += align256(static_cast<size_t>(g.MP) * d_in * 2);
+    L.opart = off; off += align256(static_cast<size_t>(g.pmax) * g.MP * d_out * 4);
+    L.dpart = off; off += g.nslab > 1 ? align256(static_cast<size_t>(g.nslab) * g.MP * d_out * 4) : 0;
+    L.total = off;
+    return L;
+}
+
+dq_status_t launch_gemv_batched(const dq_weights_t& w, const uint16_t* x, uint16_t* y, int M, float k,
+                                void* workspace, cudaStream_t stream);
+dq_status_t read_batched_error(uint32_t* word, bool clear);
 
 // Largest d_in the single-pass kernels accept (x, its B fragments and the
 // outlier list live in shared memory next to the weight rings).

@@ -1,7 +1,8 @@
 // torch_ext.cpp -- the dyn_quant._C torch extension: the reference's four
 // bindings (csrc/bindings.cpp:184-193 of dyn-quant) with the same names,
 // argument meaning and RuntimeError behaviour, implemented over the C ABI of
-// libdq_b200.so.  Extra functions: build_colmajor, build_native, detect_outliers.
+// libdq_b200.so.  Extra functions: build_colmajor, build_native, detect_outliers,
+// split_gemv_batched.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -15,10 +16,12 @@
 
 namespace {
 
-// Zero-filled GEMV workspace per (device, stream), grown on demand.  The
-// kernels leave it zeroed after every call, so it is reused as is; calls on one
-// stream are ordered, and each stream has its own.  Kept for the life of the
-// process (never destroyed: no CUDA calls during static destruction).
+// GEMV workspace per (device, stream), zero-filled when allocated and grown on
+// demand.  The kernels leave the parts that must start at zero (counters,
+// published partial sums) at zero after every call, so it is reused as is;
+// calls on one stream are ordered, and each stream has its own.  Kept for the
+// life of the process (never destroyed: no CUDA calls during static
+// destruction).
 torch::Tensor& workspace_for(const torch::Device& dev, void* stream, size_t bytes) {
     static std::mutex mu;
     static auto* cache = new std::map<std::pair<int, void*>, torch::Tensor>();
@@ -172,6 +175,29 @@ torch::Tensor split_gemv(const torch::Tensor& packed, const torch::Tensor& scale
     return y;
 }
 
+// split_gemv_batched(packed, scales, zeros, fp16_weights, x [m, d_in], outlier_k, native)
+//   -> y [m, d_out] f16, 1 <= m <= 16: the split GEMV of every row of x.
+torch::Tensor split_gemv_batched(const torch::Tensor& packed, const torch::Tensor& scales,
+                                 const torch::Tensor& zeros, const torch::Tensor& fp16_w,
+                                 const torch::Tensor& x, double outlier_k, const torch::Tensor& native) {
+    check_fp16_contiguous(x, "x");
+    TORCH_CHECK(x.dim() == 2, "x must be 2D [m, d_in]");
+    TORCH_CHECK(fp16_w.dim() == 2 && x.size(1) == fp16_w.size(1), "x must be [m, d_in] with d_in=", fp16_w.size(1));
+    const int64_t m = x.size(0);
+    TORCH_CHECK(m >= 1 && m <= 16, "split_gemv_batched takes 1 to 16 rows, got ", m);
+    dq_weights_t w = make_weights(packed, scales, zeros, fp16_w, x[0], true, native);
+    TORCH_CHECK(w.native != nullptr, "split_gemv_batched needs the native layout (build_native)");
+    const at::cuda::CUDAGuard guard(x.device());
+    auto y = torch::empty({m, w.d_out}, x.options());
+    void* stream = stream_of(x);
+    const size_t wsb = dq_workspace_bytes_batched(w.d_out, w.d_in, static_cast<int32_t>(m));
+    auto& ws = workspace_for(x.device(), stream, wsb);
+    check_status(dq_split_gemv_batched(&w, h16(x), h16m(y), static_cast<int32_t>(m), static_cast<float>(outlier_k),
+                                       ws.data_ptr(), static_cast<size_t>(ws.numel()), stream),
+                 "split_gemv_batched");
+    return y;
+}
+
 // int4_gemv(packed, scales, zeros, fp16_weights, x) -> y [d_out] f16
 torch::Tensor int4_gemv(const torch::Tensor& packed, const torch::Tensor& scales,
                         const torch::Tensor& zeros, const torch::Tensor& fp16_w,
@@ -252,6 +278,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("split_gemv", &split_gemv, "Fused dynamic-precision GEMV with runtime outlier detection",
           py::arg("packed"), py::arg("scales"), py::arg("zeros"), py::arg("fp16_weights"), py::arg("x"),
           py::arg("outlier_k"), py::arg("native") = py::none());
+    m.def("split_gemv_batched", &split_gemv_batched, "Split GEMV of 1 to 16 activation vectors",
+          py::arg("packed"), py::arg("scales"), py::arg("zeros"), py::arg("fp16_weights"), py::arg("x"),
+          py::arg("outlier_k"), py::arg("native"));
     m.def("int4_gemv", &int4_gemv, "Dense INT4 GEMV baseline", py::arg("packed"), py::arg("scales"),
           py::arg("zeros"), py::arg("fp16_weights"), py::arg("x"), py::arg("native") = py::none());
     m.def("build_native", &build_native, "Unit layout streamed by the GEMV kernels");

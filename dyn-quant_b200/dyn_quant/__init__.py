@@ -117,16 +117,41 @@ def split_gemv(
         zeros:     [d_out, d_in//128] float16 per-group zero-points.
         fp16_w:    [d_out, d_in] float16 original weights: contiguous, or the
                    transpose of a column-major mirror (see build_colmajor).
-        x:         [d_in] float16 activation vector.
+        x:         [d_in] float16 activation vector, or [m, d_in] for m
+                   vectors at once (each with its own outlier mask; the
+                   reference accepts one vector only).
         outlier_k: sigma threshold for outlier detection (default 3.0).
         native:    optional unit layout from build_native(packed, scales,
-                   zeros) -- the fast path (one bulk copy per unit).
+                   zeros) -- the fast path (one bulk copy per unit).  Built
+                   here when a batch of vectors is given without it.
 
     Returns:
-        y: [d_out] float16 output vector.
+        y: [d_out] float16 output vector ([m, d_out] for a batch).
     """
     _require_extension()
+    if x.dim() == 2 and x.numel() != fp16_w.shape[1]:
+        return _split_gemv_rows(packed, scales, zeros, fp16_w, x, outlier_k, native)
     return _C.split_gemv(packed, scales, zeros, fp16_w, _aligned(x), float(outlier_k), native)
+
+
+MAX_BATCH = 16  # vectors per batched kernel call
+
+
+def _split_gemv_rows(packed, scales, zeros, fp16_w, x, outlier_k, native):
+    """Rows of x [m, d_in] through the batched kernel, up to 16 rows per call."""
+    if x.dtype != torch.float16:
+        x = x.to(torch.float16)
+    x = x.contiguous()
+    if x.shape[1] != fp16_w.shape[1]:
+        raise RuntimeError(f"x must be [m, d_in] with d_in={fp16_w.shape[1]}, got {tuple(x.shape)}")
+    if x.shape[0] == 0:
+        return x.new_empty((0, fp16_w.shape[0]))
+    if native is None:
+        native = _C.build_native(packed, scales, zeros)
+    outs = [_C.split_gemv_batched(packed, scales, zeros, fp16_w, _aligned(x[i:i + MAX_BATCH].contiguous()),
+                                  float(outlier_k), native)
+            for i in range(0, x.shape[0], MAX_BATCH)]
+    return outs[0] if len(outs) == 1 else torch.cat(outs)
 
 
 def int4_gemv(
@@ -224,13 +249,14 @@ class DynQuantLinear(nn.Module):
         self._quantized = True
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        """y = W_split x for one activation vector.
+        """y = W_split x for one activation vector, or for each row of a batch.
 
         Args:
-            x: [d_in] float16 activation vector.
+            x: [d_in] float16 activation vector, or [m, d_in] (each row with
+               its own outlier mask; up to 16 rows share one weight stream).
 
         Returns:
-            y: [d_out] float16.
+            y: [d_out] float16 ([m, d_out] for a batch).
         """
         if not self._quantized:
             raise RuntimeError("Call load_weight() before forward()")

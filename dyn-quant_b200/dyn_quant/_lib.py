@@ -31,6 +31,8 @@ EXPORTED_SYMBOLS = (
     "dq_build_colmajor",
     "dq_split_gemv",
     "dq_split_gemv_noalloc",
+    "dq_split_gemv_batched",
+    "dq_workspace_bytes_batched",
     "dq_int4_gemv",
     "dq_reference_gemv",
     "dq_detect_outliers",
@@ -92,6 +94,10 @@ def lib() -> C.CDLL:
         L.dq_split_gemv.argtypes = [C.POINTER(DqWeights), P, P, f32, P, C.c_size_t, P]
         L.dq_split_gemv_noalloc.restype = st
         L.dq_split_gemv_noalloc.argtypes = [C.POINTER(DqWeights), P, P, f32, P]
+        L.dq_split_gemv_batched.restype = st
+        L.dq_split_gemv_batched.argtypes = [C.POINTER(DqWeights), P, P, i32, f32, P, C.c_size_t, P]
+        L.dq_workspace_bytes_batched.restype = C.c_size_t
+        L.dq_workspace_bytes_batched.argtypes = [i32, i32, i32]
         L.dq_int4_gemv.restype = st
         L.dq_int4_gemv.argtypes = [C.POINTER(DqWeights), P, P, P, C.c_size_t, P]
         L.dq_workspace_bytes.restype = C.c_size_t

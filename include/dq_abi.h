@@ -163,6 +163,37 @@ DQ_API dq_status_t dq_split_gemv_noalloc(const dq_weights_t* w, const uint16_t* 
                                          float outlier_k, void* stream);
 
 /*
+ * Workspace of dq_split_gemv_batched for m vectors: at least
+ * dq_workspace_bytes_batched(d_out, d_in, m) bytes, 256-byte aligned and
+ * ZERO-FILLED before its first use.  It begins with the batch-1 region (so one
+ * workspace serves both entry points and every shape it is large enough for),
+ * then one arrival counter that every call leaves at zero again, then scratch
+ * that each call overwrites (per-row-block counters, masks, the outlier union,
+ * partial sums).  Calls that share a workspace must not overlap on the GPU.
+ * After a call reports a device error (dq_read_device_error) zero-fill the
+ * workspace again.  0 on invalid shapes.
+ */
+DQ_API size_t dq_workspace_bytes_batched(int32_t d_out, int32_t d_in, int32_t m);
+
+/*
+ * Split GEMV of m activation vectors at once (1 <= m <= 16): for every i,
+ * y[i] = the split GEMV of x[i] as dq_split_gemv computes it, with x[i]'s own
+ * statistics and outlier mask (bit-identical to the batch-1 mask).  The INT4
+ * weights are streamed once for all vectors; the FP16 weights of the union of
+ * the m masks' columns are read once.  FP32 accumulation, y rounded to FP16
+ * once; results are bit-reproducible run to run (fixed summation order), and
+ * agree with m separate dq_split_gemv calls within FP32 rounding.
+ * The reference has a batch-1 entry point only (launch_split_gemv,
+ * src/split_gemv.cu:160-198); this is that computation per row of x.
+ * Needs w->native (dq_build_native) and w->fp16_cm or w->fp16.
+ * x: device [m][d_in] f16 (rows contiguous), y: device [m][d_out] f16.
+ * Enqueues three kernels, each a programmatic dependent of its predecessor.
+ */
+DQ_API dq_status_t dq_split_gemv_batched(const dq_weights_t* w, const uint16_t* x, uint16_t* y, int32_t m,
+                                         float outlier_k, void* workspace, size_t workspace_bytes,
+                                         void* stream);
+
+/*
  * Dense INT4 GEMV (no outlier handling): y = dequant(W) x.
  * Replaces: launch_int4_gemv (src/int4_gemv.cu:80-100, src/int4_gemv.cuh:9).
  * Only packed/scales/zeros (or native) of *w are read.
@@ -195,9 +226,12 @@ DQ_API dq_status_t dq_detect_outliers(const uint16_t* x, int32_t d_in, float out
 
 /*
  * Device error word of this library on the current device: bit 0 is set by a
- * kernel whose bounded wait for its own bulk copies gave up (the kernel then
- * drains its copies, skips the remaining work and returns; its output is not
- * valid).  Synchronous; clear != 0 resets the word.  No reference counterpart.
+ * batch-1 kernel whose bounded wait for its own bulk copies gave up (the
+ * kernel then drains its copies, skips the remaining work and returns; its
+ * output is not valid), bit 1 by a batch-1 kernel whose bounded wait for a
+ * neighbouring CTA's partial sums gave up, bit 8 by a batched kernel whose
+ * bounded wait for its own bulk copies gave up.  Synchronous; clear != 0
+ * resets the word.  No reference counterpart.
  */
 DQ_API dq_status_t dq_read_device_error(uint32_t* word, int clear);
 

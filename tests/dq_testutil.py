@@ -172,6 +172,24 @@ def abi_split_gemv(wts, x_t, k: float):
     return y
 
 
+def abi_split_gemv_batched(wts, x_t, k: float, ws=None):
+    """x_t [m, d_in] -> y [m, d_out] through dq_split_gemv_batched."""
+    import torch
+    _lib = abi()
+    m = x_t.shape[0]
+    y = torch.empty((m, wts.d_out), dtype=torch.float16, device=x_t.device)
+    if ws is None:
+        need = _lib.lib().dq_workspace_bytes_batched(wts.d_out, wts.d_in, m)
+        key = ("batched", torch.cuda.current_device(), torch.cuda.current_stream().cuda_stream)
+        ws = _workspaces.get(key)
+        if ws is None or ws.numel() < need:
+            ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device="cuda")
+            _workspaces[key] = ws
+    _lib.check(_lib.lib().dq_split_gemv_batched(C.byref(wts), _ptr(x_t), _ptr(y), m, float(k), _ptr(ws), ws.numel(),
+                                                stream_ptr()), "dq_split_gemv_batched")
+    return y
+
+
 def abi_int4_gemv(wts, x_t):
     import torch
     _lib = abi()

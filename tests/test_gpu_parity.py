@@ -195,14 +195,16 @@ def test_native_layout():
     for rb in range(n_rb):
         for c in range(NC):
             blk = ref[rb, c]
-            # [slice sl][half h][lane = 4g + t]: row rb*16 + g + 8h, group 4c + t, columns 32 sl .. +31
+            # piece (sl * 2 + h) * 32 + 8 t + (g ^ 2t): row rb*16 + g + 8h, group 4c + t, columns 32 sl .. +31
             for sl in range(4):
                 for h in range(2):
-                    for ln in range(32):
-                        row = rb * 16 + ln // 4 + 8 * h
-                        grp = 4 * c + ln % 4
-                        if row < d_out and grp < G:
-                            o = ((sl * 2 + h) * 32 + ln) * 16
+                    for g in range(8):
+                        for t in range(4):
+                            row = rb * 16 + g + 8 * h
+                            grp = 4 * c + t
+                            if row >= d_out or grp >= G:
+                                continue
+                            o = ((sl * 2 + h) * 32 + 8 * t + (g ^ (2 * t))) * 16
                             blk[o:o + 16] = packed[row, 64 * grp + 16 * sl:64 * grp + 16 * sl + 16]
             sz = np.zeros((16, 4), np.uint32)
             for r in range(16):
