@@ -186,6 +186,12 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity)
     return true;
 }
 
+// Bulk prefetch of global memory into L2 (16-byte aligned address, size a
+// multiple of 16); no completion to wait for.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // Global -> shared bulk copy completing on an mbarrier (16-byte aligned
 // addresses, size a multiple of 16).
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {

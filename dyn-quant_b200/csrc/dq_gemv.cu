@@ -58,75 +58,6 @@ constexpr int kStageBytes = kB1StageBytes;
 __device__ unsigned int g_error_word;
 
 
-// One warp, in place over xb: the 64 natural 8-column pieces of each of the
-// 512-column chunks ca and cb (cb < 0: none) -> MMA B order [word wi][slice
-// sl][group jj] (16 bytes each: the f16 pairs (x0,x4), (x2,x6), (x1,x5),
-// (x3,x7) of the piece, outliers zeroed), and per group xp = (1024 sum x' even
-// columns, 1024 sum x' odd columns, sum x', 0).  Pieces past d_in are zero.
-// Two chunks at a time keep two independent instruction streams in flight.
-template <bool kMask>
-__device__ __forceinline__ void build_chunks(uint4* xb, int n8, int ca, int cb, const uint8_t* mask, float4* xp4) {
-    const int lane = threadIdx.x & 31;
-    uint4 v[2][2];
-    float pe[2][2], po[2][2];
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-        const int c = k == 0 ? ca : cb;
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-            const int n = 64 * c + lane + 32 * q;
-            uint4 w = make_uint4(0, 0, 0, 0);
-            if (c >= 0 && n < n8) {
-                w = xb[n];
-                if (kMask) {
-                    const uint32_t mb = mask[n];
-                    if (mb) {
-                        uint32_t keep[4];
-#pragma unroll
-                        for (int i = 0; i < 4; ++i)
-                            keep[i] = ((mb >> (2 * i)) & 1u ? 0u : 0x0000FFFFu) |
-                                      ((mb >> (2 * i + 1)) & 1u ? 0u : 0xFFFF0000u);
-                        w.x &= keep[0];
-                        w.y &= keep[1];
-                        w.z &= keep[2];
-                        w.w &= keep[3];
-                    }
-                }
-            }
-            pe[k][q] = add_f16_f32(lo16(w.w), add_f16_f32(lo16(w.z), add_f16_f32(lo16(w.y), add_f16_f32(lo16(w.x), 0.f))));
-            po[k][q] = add_f16_f32(hi16(w.w), add_f16_f32(hi16(w.z), add_f16_f32(hi16(w.y), add_f16_f32(hi16(w.x), 0.f))));
-            v[k][q] = make_uint4((w.x & 0xFFFFu) | (w.z << 16), (w.y & 0xFFFFu) | (w.w << 16),
-                                 (w.x >> 16) | (w.z & 0xFFFF0000u), (w.y >> 16) | (w.w & 0xFFFF0000u));
-        }
-    }
-    __syncwarp();
-#pragma unroll
-    for (int o = 8; o >= 1; o >>= 1) {
-#pragma unroll
-        for (int k = 0; k < 2; ++k)
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-                pe[k][q] += __shfl_xor_sync(0xffffffffu, pe[k][q], o);
-                po[k][q] += __shfl_xor_sync(0xffffffffu, po[k][q], o);
-            }
-    }
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-        const int c = k == 0 ? ca : cb;
-        if (c >= 0) {
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-                const int i = lane + 32 * q;
-                const int jj = i >> 4, sl = (i >> 2) & 3, wi = i & 3;
-                xb[64 * c + (wi * 4 + sl) * 4 + jj] = v[k][q];
-                if ((lane & 15) == 0)
-                    xp4[kCG * c + jj] = make_float4(1024.f * pe[k][q], 1024.f * po[k][q], pe[k][q] + po[k][q], 0.f);
-            }
-        }
-    }
-    __syncwarp();
-}
-
 // ---------------------------------------------------------------------------
 // Fused batch-1 GEMV
 // ---------------------------------------------------------------------------
@@ -254,43 +185,56 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
     // The first unit of each warp goes out before the previous kernel has
     // finished; x is requested next, ahead of the second stage, because the
     // plan (and so every MMA) waits for it.
+    // The first units of each warp do not depend on the preceding kernel: they
+    // are pulled into L2 before griddepcontrol.wait.  After it, x is requested
+    // first (straight into registers), then the units' bulk copies, which hit
+    // L2 and so do not hold x up behind the weight stream.
+    if (kNative && lane == 0) {
+#pragma unroll
+        for (int s = 0; s < kStages; ++s)
+            if (s < wn)
+                prefetch_l2_bulk(a.native + static_cast<size_t>(cu0 + warp + kW * s) * kB1UnitBytes, kB1UnitBytes);
+    }
+    pdl_launch_dependents();
+    pdl_wait();  // x, y and the workspace may belong to the preceding kernel until here
+    XRegs<kT> xr;
+    x_regs_load_global<kT>(a.x, n8, xr);
     uint32_t armed = 0;
 #pragma unroll
     for (int s = 0; s < kStages; ++s) {
-        if (s == 1) {
-            pdl_launch_dependents();
-            pdl_wait();  // x, y and the workspace may belong to the preceding kernel until here
-            load_x_async<kT>(a.x, n8, xb);
-        }
         if (s < wn) {
             issue(s, cu0 + warp + kW * s);
             armed |= 1u << s;
         }
     }
-    cp_async_wait_all();
-    __syncthreads();
 
-    // ---- activation plan ----
+    // ---- activation plan: statistics, mask, MMA B fragments of x', outlier list ----
     int n_out = 0;
+    int* wcnt = reinterpret_cast<int*>(red) + 2 * (kStatThreads / 32);
     if (kSplit) {
-        const XStats st = x_stats<kT>(xb, n8, a.d_in, a.k, a.inv_n, a.inv_n1, red);
-        n_out = x_mask_list<kT>(xb, a.d_in, st.mean, st.thresh, reinterpret_cast<uint32_t*>(mask), list,
-                                reinterpret_cast<int*>(red) + 2 * (kStatThreads / 32));
-        __syncthreads();  // mask and list complete; x no longer read in natural order by other warps
-    }
-    // MMA B fragments.  When NC is a multiple of the warp count, warp w only
-    // ever meets the chunks (cu0 + w + kW i) mod NC, i < NC/kW, and builds
-    // exactly those, in place, without waiting for the other warps; otherwise
-    // all warps build all chunks and meet on a barrier.
-    if ((NC % kW) == 0) {
-        const int nbw = min(wn, NC / kW);
-        for (int i = 0; i < nbw; i += 2)
-            build_chunks<kSplit>(xb, n8, (cu0 + warp + kW * i) % NC,
-                                 i + 1 < nbw ? (cu0 + warp + kW * (i + 1)) % NC : -1, mask, xp4);
+        const XStats st = x_stats_regs<kT>(xr, n8, a.d_in, a.k, a.inv_n, a.inv_n1, red);
+        const int cap = a.d_in / 16;  // no stripe class can exceed its capacity below this total
+        n_out = x_frags_regs<kT, true>(xr, n8, NC, st.mean, st.thresh, nullptr, cap, xb, xp4, list, wcnt);
+        if (n_out > cap) {
+            // The reference's capacity rule may drop outliers: derive the mask
+            // from x in natural order, then rebuild the fragments and the list.
+#pragma unroll
+            for (int q = 0; q < XRegs<kT>::VPT; ++q)
+#pragma unroll
+                for (int rr = 0; rr < kPlanRounds; ++rr) {
+                    const int v = plan_vthread<kT>(q), p = v + kStatThreads * rr;
+                    if (v < kStatThreads && p < n8) xb[p] = xr.v[q][rr];
+                }
+            __syncthreads();
+            x_mask_list<kT>(xb, a.d_in, st.mean, st.thresh, reinterpret_cast<uint32_t*>(mask), list,
+                            reinterpret_cast<int*>(red) + 2 * (kStatThreads / 32));
+            __syncthreads();
+            n_out = x_frags_regs<kT, true>(xr, n8, NC, st.mean, st.thresh, reinterpret_cast<const uint32_t*>(mask),
+                                           INT_MAX, xb, xp4, list, wcnt);
+        }
+        __syncthreads();  // list complete
     } else {
-        for (int cb = warp; cb < NC; cb += 2 * kW)
-            build_chunks<kSplit>(xb, n8, cb, cb + kW < NC ? cb + kW : -1, mask, xp4);
-        __syncthreads();
+        x_frags_regs<kT, false>(xr, n8, NC, 0.f, 0.f, nullptr, 0, xb, xp4, nullptr, wcnt);
     }
 
     // ---- outlier columns: y[r] += W16[r][c] * x[c] for the rows of row blocks orb0 .. rbz ----
@@ -603,7 +547,7 @@ __host__ __device__ inline DetectSmem detect_smem(int d_in) {
     S.xs = off;   off += 2 * d_in;
     S.mask = off; off += align16(d_in / 8);
     S.list = off; off += align16(d_in);
-    S.red = off;  off += 1024;
+    S.red = off;  off += 2048;  // statistics and scan scratch; the exact sum of x at +1024
     S.total = off;
     return S;
 }
