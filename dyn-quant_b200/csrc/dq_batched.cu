@@ -7,14 +7,16 @@
 // Three kernels, chained on the stream by programmatic dependent launch:
 //  1. bplan_kernel, one CTA per vector: the statistics and the outlier mask
 //     of x[m], with the code and the fixed partition of the batch-1 kernel
-//     (dq_plan.cuh), so each vector gets exactly the batch-1 mask.  The last
-//     CTA to finish builds the union of the M masks (ascending columns) and
-//     x_o[m][u] = x[m][col_u] where col_u is an outlier of vector m, else 0.
-//  2. bout_kernel: the FP16 part, Y_o = W16[:, union] x_o, as a tensor-core
-//     GEMM over the union's columns: 16 rows x 16 union columns per MMA, A
-//     from the column-major FP16 mirror (one 16-byte cp.async per lane, then
-//     ldmatrix.trans), B = x_o.  Tasks (row block, part) take the union
-//     batches part, part + P, ...; each part is written to the workspace.
+//     (dq_plan.cuh), so each vector gets exactly the batch-1 mask; the CTA
+//     writes its vector's column of x_o (x[m][c] where c is an outlier of m,
+//     else 0; column-major, one column's vectors contiguous).  The last CTA to
+//     finish builds the union of the M masks (ascending columns).
+//  2. bout_kernel, one CTA per 16-row block: the FP16 part,
+//     Y_o = W16[:, union] x_o, on the tensor cores.  Each warp takes every
+//     eighth 16-column batch of the union; the A segments (16 rows of a
+//     column, contiguous in the column-major mirror) and the B segments (the
+//     column's x_o values) come in by 16-byte cp.async and ldmatrix.trans; the
+//     eight warps' sums are added in a fixed order.
 //  3. bdense_kernel: the INT4 part over x' (each vector's outliers zeroed),
 //     split over K: CTA (cx, slab) streams chunks [slab S, slab S + S) of the
 //     row blocks [rb0, rb1) through per-warp cp.async.bulk rings.  Each warp
@@ -47,15 +49,6 @@ __device__ unsigned int g_berror_word;
 
 constexpr int kUnit = kB1UnitBytes;
 
-// Parts of the FP16 product for nbat union batches of 16 columns: at least
-// four batches per task, at most pmax parts.  Both the FP16-part kernel and
-// the dense kernel derive it from the union size on the device.
-__device__ __forceinline__ int bg_parts(int nbat, int pmax) {
-    if (nbat <= 0) return 0;
-    const int p = (nbat + 3) / 4;
-    return p < pmax ? p : pmax;
-}
-
 __device__ __forceinline__ float4 lds_f4(uint32_t addr) {
     const uint4 v = lds_v4(addr);
     return make_float4(__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z), __uint_as_float(v.w));
@@ -84,7 +77,7 @@ struct BPArgs {
     const uint16_t* x;   // [M][d_in]
     uint32_t* masks;     // [kBgMaxM][W]
     uint32_t* ulist;     // [d_in]
-    uint16_t* xo;        // [MP][d_in]
+    uint16_t* xo;        // [d_in][MP]
     unsigned int* ctr;   // [0] arrival counter, [1] union size
     unsigned int* rbcnt; // [NRB] the dense kernel's per-row-block counters, cleared here
     float k, inv_n, inv_n1;
@@ -116,6 +109,15 @@ __global__ void __launch_bounds__(kStatThreads, 1) bplan_kernel(const BPArgs a) 
                     reinterpret_cast<int*>(red) + 2 * (kStatThreads / 32));
     __syncthreads();
     for (int i = tid; i < a.W; i += NT) a.masks[static_cast<size_t>(m) * a.W + i] = mask32[i];
+    // Column m of x_o, and the all-zero columns of the padding vectors M .. MP-1.
+    {
+        const uint16_t* xh = reinterpret_cast<const uint16_t*>(xs);
+        for (int c = tid; c < a.d_in; c += NT) {
+            const bool out = (mask32[c >> 5] >> (c & 31)) & 1u;
+            a.xo[static_cast<size_t>(c) * a.MP + m] = out ? xh[c] : static_cast<uint16_t>(0);
+            for (int mm = a.M + m; mm < a.MP; mm += a.M) a.xo[static_cast<size_t>(c) * a.MP + mm] = 0;
+        }
+    }
     __threadfence();
     __syncthreads();
     if (tid == 0) *flag = atomicAdd(a.ctr, 1u) == static_cast<unsigned>(a.M - 1);
@@ -123,8 +125,8 @@ __global__ void __launch_bounds__(kStatThreads, 1) bplan_kernel(const BPArgs a) 
     if (!*flag) return;
     __threadfence();
 
-    // The last CTA: union of the M masks.  Thread tid owns the words [w0, w1),
-    // at most two (W <= kMaxDIn / 32 <= 2 NT).
+    // The last CTA: union of the M masks, ascending.  Thread tid owns the
+    // words [w0, w1), at most two (W <= kMaxDIn / 32 <= 2 NT).
     static_assert(kMaxDIn / 32 <= 2 * NT, "union words per thread");
     const int w0 = static_cast<int>(static_cast<long long>(tid) * a.W / NT);
     const int w1 = static_cast<int>(static_cast<long long>(tid + 1) * a.W / NT);
@@ -145,37 +147,15 @@ __global__ void __launch_bounds__(kStatThreads, 1) bplan_kernel(const BPArgs a) 
     for (int q = 0; q < 2; ++q) {
         const int wj = w0 + q;
         if (wj < w1) {
-            uint32_t mw[kBgMaxM];
-#pragma unroll
-            for (int mm = 0; mm < kBgMaxM; ++mm)
-                mw[mm] = mm < a.M ? ldcg_u32(a.masks + static_cast<size_t>(mm) * a.W + wj) : 0u;
             uint32_t rest = u[q];
             while (rest) {
-                const int bit = __ffs(rest) - 1;
-                const int col = 32 * wj + bit;
-                a.ulist[pos] = static_cast<uint32_t>(col);
-#pragma unroll
-                for (int mm = 0; mm < kBgMaxM; ++mm) {
-                    if (mm < a.MP) {
-                        uint16_t v = 0;
-                        if ((mw[mm] >> bit) & 1u) v = ldcg_u16(a.x + static_cast<size_t>(mm) * a.d_in + col);
-                        a.xo[static_cast<size_t>(mm) * a.d_in + pos] = v;
-                    }
-                }
-                ++pos;
+                a.ulist[pos++] = static_cast<uint32_t>(32 * wj + __ffs(rest) - 1);
                 rest &= rest - 1u;
             }
         }
     }
-    // The last batch of 16 union columns is padded with column 0 and zeros.
-    const int U = tot[0];
-    const int upad = min(a.d_in, (U + 15) & ~15);
-    for (int i = U + tid; i < upad; i += NT) {
-        a.ulist[i] = 0u;
-        for (int mm = 0; mm < a.MP; ++mm) a.xo[static_cast<size_t>(mm) * a.d_in + i] = 0;
-    }
     if (tid == 0) {
-        a.ctr[1] = static_cast<unsigned>(U);
+        a.ctr[1] = static_cast<unsigned>(tot[0]);
         a.ctr[0] = 0u;  // ready for the next call
     }
 }
@@ -194,91 +174,95 @@ struct BOArgs {
     const uint16_t* w16;     // row-major FP16 [d_out][d_in]
     const uint16_t* w16_cm;  // column-major mirror [d_in][d_out]
     const uint32_t* ulist;
-    const uint16_t* xo;
+    const uint16_t* xo;      // [d_in][MP]
     const unsigned int* ctr;
-    float* opart;            // [pmax][MP][d_out]
-    int d_out, d_in, NRB, pmax;
+    float* opart;            // [MP][d_out]
+    int d_out, d_in, MP;
 };
 
+// One CTA per 16-row block.
 template <int kOut, int NT>
 __global__ void __launch_bounds__(kBgOutWarps * 32) bout_kernel(const BOArgs a) {
     constexpr int MP = 8 * NT;
-    __shared__ __align__(128) unsigned char buf[kBgOutWarps][kBgOutBufs][512];
+    __shared__ __align__(128) unsigned char abuf[kBgOutWarps][kBgOutBufs][512];  // 16 columns x 16 rows
+    __shared__ __align__(128) unsigned char bbuf[kBgOutWarps][kBgOutBufs][512];  // 16 columns x 16 vectors
+    __shared__ float red[kBgOutWarps][NT][4][32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int g = lane >> 2, t = lane & 3;
+    const int rb = blockIdx.x;
 
     pdl_launch_dependents();
-    pdl_wait();  // the union comes from the plan kernel
+    pdl_wait();  // the union and x_o come from the plan kernel
     const int U = static_cast<int>(ldcg_u32(a.ctr + 1));
     const int nbat = (U + 15) / 16;
-    const int P = bg_parts(nbat, a.pmax);
-    const int ntask = a.NRB * P;
-    const uint32_t wbuf = smem_u32(&buf[warp][0][0]);
+    if (nbat == 0) return;
+    const int nb = (nbat - warp + kBgOutWarps - 1) / kBgOutWarps;  // batches warp, warp + 8, ...
+    const uint32_t wa = smem_u32(&abuf[warp][0][0]), wb = smem_u32(&bbuf[warp][0][0]);
 
-    for (int task = blockIdx.x * kBgOutWarps + warp; task < ntask; task += gridDim.x * kBgOutWarps) {
-        const int rb = task / P, p = task - rb * P;
-        const int nb = (nbat - p + P - 1) / P;  // batches p, p + P, ...
-        float d[NT][4];
+    // Batch k of this warp into buffer k % kBgOutBufs: lane = (column lane >> 1
+    // of the batch, half lane & 1): 8 rows of W16 and 8 vectors of x_o.
+    auto issue = [&](int k) {
+        const int kc = 16 * (warp + kBgOutWarps * k) + (lane >> 1);
+        const int half = lane & 1;
+        const int row0 = rb * kRowBlock + 8 * half;
+        const uint32_t da = wa + (k % kBgOutBufs) * 512 + 16 * lane;
+        const uint32_t db = wb + (k % kBgOutBufs) * 512 + 16 * lane;
+        const bool valid = kc < U;
+        const int col = valid ? static_cast<int>(ldcg_u32(a.ulist + kc)) : 0;
+        if (valid && (MP == 16 || half == 0)) cp_async16(db, a.xo + static_cast<size_t>(col) * MP + 8 * half);
+        else sts_v4(db, make_uint4(0, 0, 0, 0));
+        if (kOut == kBoStaged) {
+            if (valid && row0 < a.d_out) cp_async16(da, a.w16_cm + static_cast<size_t>(col) * a.d_out + row0);
+            else sts_v4(da, make_uint4(0, 0, 0, 0));
+        } else {
+            uint16_t h[8];
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) d[nt][0] = d[nt][1] = d[nt][2] = d[nt][3] = 0.f;
-
-        // Batch k of this task into buffer k % kBgOutBufs: lane = (union column
-        // lane >> 1 of the batch, row half lane & 1), 8 rows of FP16.
-        auto issue = [&](int k) {
-            const int b = p + k * P;
-            const int kc = 16 * b + (lane >> 1);
-            const int row0 = rb * kRowBlock + 8 * (lane & 1);
-            const uint32_t dst = wbuf + (k % kBgOutBufs) * 512 + 16 * lane;
-            const bool valid = kc < U && row0 < a.d_out;
-            const int col = valid ? static_cast<int>(ldcg_u32(a.ulist + kc)) : 0;
-            if (kOut == kBoStaged) {
-                if (valid) cp_async16(dst, a.w16_cm + static_cast<size_t>(col) * a.d_out + row0);
-                else sts_v4(dst, make_uint4(0, 0, 0, 0));
-                cp_async_commit();
-            } else {
-                uint16_t h[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int r = row0 + i;
-                    h[i] = (valid && r < a.d_out)
-                               ? (kOut == kBoColDirect ? ldg_u16(a.w16_cm + static_cast<size_t>(col) * a.d_out + r)
-                                                       : ldg_u16(a.w16 + static_cast<size_t>(r) * a.d_in + col))
-                               : static_cast<uint16_t>(0);
-                }
-                sts_v4(dst, make_uint4(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]), pack_h2(h[4], h[5]),
-                                       pack_h2(h[6], h[7])));
+            for (int i = 0; i < 8; ++i) {
+                const int r = row0 + i;
+                h[i] = (valid && r < a.d_out)
+                           ? (kOut == kBoColDirect ? ldg_u16(a.w16_cm + static_cast<size_t>(col) * a.d_out + r)
+                                                   : ldg_u16(a.w16 + static_cast<size_t>(r) * a.d_in + col))
+                           : static_cast<uint16_t>(0);
             }
-        };
-        for (int k = 0; k < kBgOutBufs && k < nb; ++k) issue(k);
-        for (int k = 0; k < nb; ++k) {
-            if (kOut == kBoStaged) {
-                if (k + 2 < nb) cp_async_wait_group<2>();
-                else if (k + 1 < nb) cp_async_wait_group<1>();
-                else cp_async_wait_group<0>();
-            }
-            __syncwarp();
-            const uint32_t bsm = wbuf + (k % kBgOutBufs) * 512;
-            uint32_t a0, a1, a2, a3;
-            // matrix j = (column half j >> 1, row half j & 1); lane 8j + i gives column (j >> 1) * 8 + i
-            ldmatrix_x4_trans(bsm + (((lane >> 4) * 8 + (lane & 7)) * 32) + ((lane >> 3) & 1) * 16, a0, a1, a2, a3);
-            const int k0 = 16 * (p + k * P);
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                const uint16_t* xr = a.xo + static_cast<size_t>(nt * 8 + g) * a.d_in + k0 + 2 * t;
-                mma_16816(d[nt], a0, a1, a2, a3, ldcg_u32(xr), ldcg_u32(xr + 8));
-            }
-            __syncwarp();  // every lane is done with the buffer before it is refilled
-            if (k + kBgOutBufs < nb) issue(k + kBgOutBufs);
+            sts_v4(da, make_uint4(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]), pack_h2(h[4], h[5]),
+                                  pack_h2(h[6], h[7])));
         }
-        float* op = a.opart + static_cast<size_t>(p) * MP * a.d_out;
+        cp_async_commit();
+    };
+    float d[NT][4];
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
+    for (int nt = 0; nt < NT; ++nt) d[nt][0] = d[nt][1] = d[nt][2] = d[nt][3] = 0.f;
+    for (int k = 0; k < kBgOutBufs && k < nb; ++k) issue(k);
+    for (int k = 0; k < nb; ++k) {
+        if (k + 2 < nb) cp_async_wait_group<2>();
+        else if (k + 1 < nb) cp_async_wait_group<1>();
+        else cp_async_wait_group<0>();
+        __syncwarp();
+        const uint32_t ab = wa + (k % kBgOutBufs) * 512, bb = wb + (k % kBgOutBufs) * 512;
+        uint32_t a0, a1, a2, a3;
+        // A: matrix j = (column half j >> 1, row half j & 1); lane 8j + i gives column (j >> 1) * 8 + i
+        ldmatrix_x4_trans(ab + (((lane >> 4) * 8 + (lane & 7)) * 32) + ((lane >> 3) & 1) * 16, a0, a1, a2, a3);
+        // B: matrix j = (column half j & 1, vector half j >> 1); rows are columns (32 bytes each)
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4_trans(bb + ((((lane >> 3) & 1) * 8 + (lane & 7)) * 32) + (lane >> 4) * 16, b0, b1, b2, b3);
+        mma_16816(d[0], a0, a1, a2, a3, b0, b1);
+        if (NT == 2) mma_16816(d[NT - 1], a0, a1, a2, a3, b2, b3);
+        __syncwarp();  // every lane is done with the buffers before they are refilled
+        if (k + kBgOutBufs < nb) issue(k + kBgOutBufs);
+    }
+    // The warps' sums in warp order.
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int row = rb * kRowBlock + g + 8 * (e >> 1);
-                const int tok = nt * 8 + 2 * t + (e & 1);
-                if (row < a.d_out) op[static_cast<size_t>(tok) * a.d_out + row] = d[nt][e];
-            }
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) red[warp][nt][e][lane] = d[nt][e];
+    __syncthreads();
+    for (int i = threadIdx.x; i < NT * 4 * 32; i += kBgOutWarps * 32) {
+        const int nt = i >> 7, e = (i >> 5) & 3, ln = i & 31;
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kBgOutWarps; ++w) v += red[w][nt][e][ln];
+        const int row = rb * kRowBlock + (ln >> 2) + 8 * (e >> 1);
+        const int tok = nt * 8 + 2 * (ln & 3) + (e & 1);
+        if (row < a.d_out) a.opart[static_cast<size_t>(tok) * a.d_out + row] = v;
     }
 }
 
@@ -290,11 +274,11 @@ struct BDArgs {
     const uint16_t* x;       // [M][d_in]
     const uint32_t* masks;   // [kBgMaxM][W]
     const unsigned int* ctr;
-    const float* opart;      // [pmax][MP][d_out]
+    const float* opart;      // [MP][d_out]
     float* dpart;            // [nslab][MP][d_out]
     unsigned int* rbcnt;     // [NRB] slabs finished per row block (cleared by the plan kernel)
     uint16_t* y;             // [M][d_out]
-    int M, d_out, d_in, NC, NRB, S, nslab, cps, W, pmax;
+    int M, d_out, d_in, NC, NRB, S, nslab, cps, W;
     int sm_ring, sm_bars, sm_xtab, sm_xsum;
 };
 
@@ -369,24 +353,42 @@ __global__ void __launch_bounds__(kBgWarps * 32, 1) bdense_kernel(const BDArgs a
     // (x3,x7), outliers of tok zeroed; xsum[cc][group][tok] = (1024 sum x'
     // even columns, 1024 sum x' odd columns, sum x', 0).  16 consecutive
     // threads hold the 16 pieces of one (chunk, group, vector).
+    // All of a thread's loads go out first (at most kMaxXP pieces), then the
+    // pieces are processed.
+    constexpr int kMaxXP = 4096 / kT;  // S * MP <= 64
+    static_assert(kMaxXP * kT == 4096, "x' pieces per thread");
     const int npc = nch * MP * 64;
-    for (int i = tid; i < npc; i += kT) {
+    uint4 xv[kMaxXP];
+    uint32_t xm[kMaxXP];
+#pragma unroll
+    for (int k = 0; k < kMaxXP; ++k) {
+        const int i = tid + k * kT;
         const int p = i & 63, tok = (i >> 6) % MP, cc = i / (64 * MP);
         const int col = (c0 + cc) * 512 + 8 * p;
-        uint4 w = make_uint4(0, 0, 0, 0);
-        if (tok < a.M && col < a.d_in) {
-            w = ldcg_v4(a.x + static_cast<size_t>(tok) * a.d_in + col);
-            const uint32_t mb = (ldcg_u32(a.masks + static_cast<size_t>(tok) * a.W + (col >> 5)) >> (col & 31)) & 0xFFu;
-            if (mb) {
-                uint32_t keep[4];
+        xv[k] = make_uint4(0, 0, 0, 0);
+        xm[k] = 0;
+        if (i < npc && tok < a.M && col < a.d_in) {
+            xv[k] = ldcg_v4(a.x + static_cast<size_t>(tok) * a.d_in + col);
+            xm[k] = ldcg_u32(a.masks + static_cast<size_t>(tok) * a.W + (col >> 5));
+        }
+    }
 #pragma unroll
-                for (int q = 0; q < 4; ++q)
-                    keep[q] = ((mb >> (2 * q)) & 1u ? 0u : 0x0000FFFFu) | ((mb >> (2 * q + 1)) & 1u ? 0u : 0xFFFF0000u);
-                w.x &= keep[0];
-                w.y &= keep[1];
-                w.z &= keep[2];
-                w.w &= keep[3];
-            }
+    for (int k = 0; k < kMaxXP; ++k) {
+        const int i = tid + k * kT;
+        if (k * kT >= npc) break;  // uniform
+        const int p = i & 63, tok = (i >> 6) % MP, cc = i / (64 * MP);
+        const int col = (c0 + cc) * 512 + 8 * p;
+        uint4 w = xv[k];
+        const uint32_t mb = (xm[k] >> (col & 31)) & 0xFFu;
+        if (mb) {
+            uint32_t keep[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                keep[q] = ((mb >> (2 * q)) & 1u ? 0u : 0x0000FFFFu) | ((mb >> (2 * q + 1)) & 1u ? 0u : 0xFFFF0000u);
+            w.x &= keep[0];
+            w.y &= keep[1];
+            w.z &= keep[2];
+            w.w &= keep[3];
         }
         float pe = add_f16_f32(lo16(w.w), add_f16_f32(lo16(w.z), add_f16_f32(lo16(w.y), add_f16_f32(lo16(w.x), 0.f))));
         float po = add_f16_f32(hi16(w.w), add_f16_f32(hi16(w.z), add_f16_f32(hi16(w.y), add_f16_f32(hi16(w.x), 0.f))));
@@ -402,8 +404,7 @@ __global__ void __launch_bounds__(kBgWarps * 32, 1) bdense_kernel(const BDArgs a
     }
     __syncthreads();
 
-    const int U = static_cast<int>(ldcg_u32(a.ctr + 1));
-    const int nparts = bg_parts((U + 15) / 16, a.pmax);
+    const bool with_out = ldcg_u32(a.ctr + 1) != 0u;  // the FP16 part was written
     const uint32_t xtab_a = smem_u32(xtab);
     const uint32_t xsum_a = smem_u32(xsum);
     const int lm = lane >> 3, lr = lane & 7;  // ldmatrix: this lane addresses row lr of matrix (slice) lm
@@ -416,8 +417,20 @@ __global__ void __launch_bounds__(kBgWarps * 32, 1) bdense_kernel(const BDArgs a
     // last slab to finish, sum all slabs and the FP16 parts and write y.
     auto finish_rb = [&](int rb) {
         const int row0 = rb * kRowBlock + g;
-        float v[NT][4];
+        float v[NT][4], fo[NT][4];  // fo: the FP16 part, fetched with the first partials
+        auto fetch_fp16 = [&]() {
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int row = row0 + 8 * (e >> 1);
+                    const int tok = nt * 8 + 2 * t + (e & 1);
+                    fo[nt][e] = (with_out && row < a.d_out)
+                                    ? ldcg_f32(a.opart + static_cast<size_t>(tok) * a.d_out + row) : 0.f;
+                }
+        };
         if (a.nslab == 1) {
+            fetch_fp16();
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -439,33 +452,39 @@ __global__ void __launch_bounds__(kBgWarps * 32, 1) bdense_kernel(const BDArgs a
             old = __shfl_sync(0xffffffffu, old, 0);
             if (old != static_cast<unsigned>(a.nslab - 1)) return;
             __threadfence();
+            fetch_fp16();
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) v[nt][e] = 0.f;
-            for (int s2 = 0; s2 < a.nslab; ++s2) {
-                const float* sp = a.dpart + static_cast<size_t>(s2) * MP * a.d_out;
+            // slabs in order, four at a time with their loads in flight together
+            for (int s0 = 0; s0 < a.nslab; s0 += 4) {
+                float q[4][NT][4];
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt)
+                for (int j = 0; j < 4; ++j) {
+                    const float* sp = a.dpart + static_cast<size_t>(s0 + j) * MP * a.d_out;
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int row = row0 + 8 * (e >> 1);
-                        const int tok = nt * 8 + 2 * t + (e & 1);
-                        if (row < a.d_out) v[nt][e] += ldcg_f32(sp + static_cast<size_t>(tok) * a.d_out + row);
-                    }
+                    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int row = row0 + 8 * (e >> 1);
+                            const int tok = nt * 8 + 2 * t + (e & 1);
+                            q[j][nt][e] = (s0 + j < a.nslab && row < a.d_out)
+                                              ? ldcg_f32(sp + static_cast<size_t>(tok) * a.d_out + row) : 0.f;
+                        }
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) v[nt][e] += q[j][nt][e];
             }
         }
-        for (int p = 0; p < nparts; ++p) {
-            const float* op = a.opart + static_cast<size_t>(p) * MP * a.d_out;
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
+        for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int row = row0 + 8 * (e >> 1);
-                    const int tok = nt * 8 + 2 * t + (e & 1);
-                    if (row < a.d_out) v[nt][e] += ldcg_f32(op + static_cast<size_t>(tok) * a.d_out + row);
-                }
-        }
+            for (int e = 0; e < 4; ++e) v[nt][e] += fo[nt][e];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -655,12 +674,9 @@ dq_status_t launch_gemv_batched(const dq_weights_t& w, const uint16_t* x, uint16
     oa.opart = reinterpret_cast<float*>(ws + L.opart);
     oa.d_out = w.d_out;
     oa.d_in = w.d_in;
-    oa.NRB = G.NRB;
-    oa.pmax = G.pmax;
+    oa.MP = G.MP;
     const int out_mode = w.fp16_cm ? ((w.d_out % 8) == 0 ? kBoStaged : kBoColDirect) : kBoRowDirect;
-    const long long otasks = static_cast<long long>(G.NRB) * G.pmax;
-    const long long ocap = static_cast<long long>(di.sm_count) * 8;
-    const int ogrid = static_cast<int>(std::min<long long>((otasks + kBgOutWarps - 1) / kBgOutWarps, ocap));
+    const int ogrid = G.NRB;
 
     BDArgs da;
     da.native = w.native;
@@ -680,7 +696,6 @@ dq_status_t launch_gemv_batched(const dq_weights_t& w, const uint16_t* x, uint16
     da.nslab = G.nslab;
     da.cps = std::max(1, std::min(G.NRB, di.sm_count / G.nslab));
     da.W = G.W;
-    da.pmax = G.pmax;
     da.sm_ring = DS.ring;
     da.sm_bars = DS.bars;
     da.sm_xtab = DS.xtab;

@@ -112,14 +112,12 @@ constexpr int kBgWarps = 16;      // warps of a dense CTA (one CTA per SM)
 constexpr int kBgStages = 2;      // bulk-copy ring stages per warp
 constexpr int kBgOutWarps = 8;    // warps of an FP16-part CTA
 constexpr int kBgOutBufs = 3;     // per-warp outlier segment buffers in flight
-constexpr int kBgMaxParts = 16;   // FP16-part split over the union batches, at most
 constexpr int kBgRefSMs = 148;    // SM count the slab width is chosen for (keeps the workspace device-independent)
 
 // Split of one batched call.  NT tiles of 8 vectors (MP = 8 NT columns of the
-// MMA); S chunks (512 columns) per slab, nslab slabs; pmax bounds the parts
-// of the FP16 product.
+// MMA); S chunks (512 columns) per slab, nslab slabs.
 struct BgGeom {
-    int M, NT, MP, NC, NRB, S, nslab, W, pmax;
+    int M, NT, MP, NC, NRB, S, nslab, W;
 };
 
 inline BgGeom bg_geom(int d_out, int d_in, int M) {
@@ -136,8 +134,6 @@ inline BgGeom bg_geom(int d_out, int d_in, int M) {
     g.S = g.NT == 1 ? 8 : 4;
     while (g.S > 1 && static_cast<long long>((g.NC + g.S - 1) / g.S) * g.NRB < kBgRefSMs * kBgWarps * 3 / 4) g.S /= 2;
     g.nslab = (g.NC + g.S - 1) / g.S;
-    long long p = (static_cast<long long>(kBgRefSMs) * 64 + g.NRB - 1) / g.NRB;
-    g.pmax = static_cast<int>(p < 1 ? 1 : (p > kBgMaxParts ? kBgMaxParts : p));
     return g;
 }
 
@@ -148,8 +144,8 @@ inline BgGeom bg_geom(int d_out, int d_in, int M) {
 //   rbcnt  per row block, slabs finished (cleared by the plan kernel)
 //   masks  [kBgMaxM][W] outlier bits of each vector
 //   ulist  [d_in] the union of the masks, ascending columns
-//   xo     [MP][d_in] FP16: x[m][ulist[u]] where that column is an outlier of m, else 0
-//   opart  [pmax][MP][d_out] FP32 parts of the FP16 product
+//   xo     [d_in][MP] FP16: x[m][c] where column c is an outlier of vector m, else 0
+//   opart  [MP][d_out] FP32, the FP16 product over the union's columns
 //   dpart  [nslab][MP][d_out] FP32 per-slab partial sums of the INT4 part (nslab > 1)
 struct BgWs {
     size_t ctr, rbcnt, masks, ulist, xo, opart, dpart, total;
@@ -188,8 +184,8 @@ inline BgWs bg_ws(const BgGeom& g, int d_out, int d_in) {
     L.rbcnt = off; off += align256(static_cast<size_t>(g.NRB) * 4);
     L.masks = off; off += align256(static_cast<size_t>(kBgMaxM) * g.W * 4);
     L.ulist = off; off += align256(static_cast<size_t>(d_in) * 4);
-    L.xo = off;    off += align256(static_cast<size_t>(g.MP) * d_in * 2);
-    L.opart = off; off += align256(static_cast<size_t>(g.pmax) * g.MP * d_out * 4);
+    L.xo = off;    off += align256(static_cast<size_t>(d_in) * g.MP * 2);
+    L.opart = off; off += align256(static_cast<size_t>(g.MP) * d_out * 4);
     L.dpart = off; off += g.nslab > 1 ? align256(static_cast<size_t>(g.nslab) * g.MP * d_out * 4) : 0;
     L.total = off;
     return L;
