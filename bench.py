@@ -68,6 +68,13 @@ WORKLOADS = {
 }
 
 
+# Mixtral-8x7B-shaped MoE FFN decode step: E experts (w1/w3 D->F, w2 F->D),
+# T tokens with top-K experts drawn uniformly from a seed.
+MOE_WORKLOADS = {
+    "mixtral_moe": dict(E=8, D=4096, F=14336, T=16, K=2, frac=0.02),
+}
+
+
 def gemv_bytes(d_out: int, d_in: int, n_o: int, m: int = 1) -> int:
     """Algorithmic bytes of one (batched) split GEMV: INT4 codes, FP16 scale and
     zero, the FP16 columns of the n_o outlier channels (for m > 1 the union of
@@ -573,13 +580,284 @@ def run_e2e(args, spec, sets, acts_np, dev, step_bytes, world, rows):
                     "every rank (bytes per rank), synchronised every step")}
 
 
+# ---------------------------------------------------------------------------
+# MoE FFN step (expert-per-GPU under torchrun)
+# ---------------------------------------------------------------------------
+def moe_routing_np(cfg: dict, seed: int = 0):
+    """Top-K experts per token (uniform without replacement) and weights
+    (uniform, normalised per token), from one seed."""
+    rng = np.random.default_rng(seed)
+    ex = np.stack([rng.choice(cfg["E"], cfg["K"], replace=False) for _ in range(cfg["T"])])
+    w = rng.random((cfg["T"], cfg["K"])).astype(np.float32)
+    return ex, w / w.sum(1, keepdims=True)
+
+
+def moe_step_bytes(cfg: dict, routing, x, layer, experts) -> int:
+    """Algorithmic bytes of the experts' GEMVs in one step: per expert and
+    matrix, the weights once, the FP16 columns of the union of the routed
+    tokens' outliers (for w2, of the gated activations' outliers), the
+    tokens' inputs and outputs."""
+    import torch
+    import dyn_quant
+    from dyn_quant.moe import silu_mul
+    D, F = cfg["D"], cfg["F"]
+    total = 0
+    for e in experts:
+        rows = routing.tokens64.get(e)
+        if rows is None:
+            continue
+        xe = x.index_select(0, rows)
+        m = xe.shape[0]
+
+        def union(v):
+            return int(torch.stack([dyn_quant.detect_outliers(r, cfg.get("k", 3.0))[0] for r in v]).any(0).sum())
+        n_x = union(xe)
+        a = layer.w1[str(e)](xe).reshape(m, -1)
+        b = layer.w3[str(e)](xe).reshape(m, -1)
+        n_h = union(silu_mul(a, b))
+        total += 2 * gemv_bytes(F, D, n_x, m) + gemv_bytes(D, F, n_h, m)
+    return total
+
+
+def run_moe(args, rank: int, world: int, local_rank: int) -> None:
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    from dyn_quant import synth
+    from dyn_quant.moe import MoEFFN, MoERouting
+
+    cfg = dict(MOE_WORKLOADS[args.workload], k=args.k)
+    if args.frac is not None:
+        cfg["frac"] = args.frac
+    E, D, F, T = cfg["E"], cfg["D"], cfg["F"], cfg["T"]
+    local = [e for e in range(E) if e % world == rank]
+    ex, w = moe_routing_np(cfg)
+    routing = MoERouting(torch.from_numpy(ex), torch.from_numpy(w), E, device=dev)
+    x = torch.from_numpy(synth.activations(T, D, cfg["frac"], seed=1, dist=args.dist)).to(dev)
+    # this rank's experts; several copies when they would fit in L2, so that
+    # every step streams its weights from HBM
+    per_copy = sum((2 * F * D + D * F) // 2 for _ in local)
+    n_sets = max(1, math.ceil(3 * L2_BYTES / max(per_copy, 1)))
+    if args.max_sets:
+        n_sets = min(n_sets, args.max_sets)
+    gen = torch.Generator(device=dev)
+    layers = []
+    for s_ in range(n_sets):
+        layer = MoEFFN(E, D, F, args.k, experts=local)
+        for e in local:
+            ws = []
+            for j, (o, i) in enumerate(((F, D), (F, D), (D, F))):
+                gen.manual_seed(100_000 * s_ + 100 * e + j)
+                ws.append((torch.randn(o, i, generator=gen, device=dev, dtype=torch.float32) / math.sqrt(i)).half())
+            layer.load_expert(e, *ws)
+            del ws
+        layers.append(layer)
+    torch.cuda.synchronize()
+    local_bytes = moe_step_bytes(cfg, routing, x, layers[0], local)
+    tot = torch.tensor([local_bytes], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(tot)
+    step_bytes = int(tot.item())
+    outs = [torch.zeros(T, D, dtype=torch.float32, device=dev) for _ in range(n_sets)]
+    group = None
+
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        for s_ in range(n_sets):
+            layers[s_](x, routing, group, outs[s_])  # first calls: workspaces, kernel attributes
+    stream.synchronize()
+
+    def capture(n):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(n):
+                layers[i % n_sets](x, routing, group, outs[i % n_sets])
+        return g
+
+    warm = capture(max(args.warmup, n_sets))
+    timed = capture(args.steps)
+    with torch.cuda.stream(stream):
+        warm.replay()
+    stream.synchronize()
+    sampler = ClockSampler(local_rank) if not args.no_clocks else None
+    if sampler:
+        sampler.start()
+    t_end = time.perf_counter() + args.soak
+    with torch.cuda.stream(stream):
+        while time.perf_counter() < t_end:
+            warm.replay()
+            stream.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        timed.replay()
+        e1.record(stream)
+    stream.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop() if sampler else None
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = step_bytes * args.steps / (ms * 1e-3) / 1e9
+    achieved = local_bytes * args.steps / (ms * 1e-3) / 1e9
+    peak, peak_note = measured_peak_gbs()
+
+    # end to end: pinned host tokens in, combined output back, every step
+    xh = x.cpu().pin_memory()
+    yh = torch.empty(T, D, dtype=torch.float16).pin_memory()
+    xd = torch.empty_like(x)
+    cur = torch.cuda.current_stream(dev)
+    times = []
+    for i in range(max(3, args.warmup) + args.steps):
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(cur)
+        xd.copy_(xh, non_blocking=True)
+        yh.copy_(layers[i % n_sets](xd, routing, group, outs[i % n_sets]), non_blocking=True)
+        a1.record(cur)
+        a1.synchronize()
+        if i >= max(3, args.warmup):
+            times.append(a0.elapsed_time(a1))
+    e2e_ms = max(statistics.mean(times), 1e-9)
+    if world > 1:
+        t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = moe_cpu_baseline(args, cfg, args.cpu_budget)
+    if rank == 0:
+        n_tok = {e: routing.count(e) for e in range(E)}
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
+            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+            "dtype": "w4a16 (fp32 accumulate)",
+            "data": "synthetic (seeded N(0,1/d_in) weights, N(0,1) tokens with U[10,100] outliers, seeded top-2 routing)",
+            "config": {"workload": args.workload, "experts": E, "d_model": D, "d_ff": F, "tokens": T, "top_k": cfg["K"],
+                       "outlier_frac": cfg["frac"], "outlier_k": args.k, "tokens_per_expert": n_tok,
+                       "parallelism": (f"expert-parallel over {world} GPUs (expert e on rank e % {world}), "
+                                       "NCCL all-reduce of the FP32 combined outputs") if world > 1 else "1 GPU, all experts",
+                       "l2": f"{n_sets} rotating weight copies per rank",
+                       "graphs": "the K timed steps are one CUDA graph"},
+            "step_bytes": step_bytes,
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_note": peak_note,
+                         "kernel": "one MoE step on rank 0: per expert the batched split GEMV (plan, FP16 part, "
+                                   "INT4 part) x3, dq_silu_mul, dq_moe_combine",
+                         "algorithmic_bytes_per_step": local_bytes, "traffic": None},
+            "gpu_launches": args.steps * sum(11 for e in local if routing.count(e)),
+            "e2e": {"value": round(step_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": T * D * 2, "d2h_bytes_per_step": T * D * 2, "ms_per_step": round(e2e_ms, 4),
+                    "api": "MoEFFN.forward, pinned host buffers, synchronised every step"},
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    del warm, timed
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def moe_cpu_sample(cfg: dict, n_pairs: int, seed: int = 0):
+    """The first n_pairs (token, expert) pairs of the routing, with each
+    expert's matrices quantized by the oracle (seeded, smaller seeds than the
+    GPU copies: a CPU sample of the same shapes)."""
+    import oracle as O
+    from dyn_quant import synth
+    ex, w = moe_routing_np(cfg, seed)
+    x = synth.activations(cfg["T"], cfg["D"], cfg["frac"], seed=1)
+    pairs = [(t, int(ex[t, j])) for t in range(cfg["T"]) for j in range(cfg["K"])][:n_pairs]
+    mats = {}
+    for _, e in pairs:
+        if e not in mats:
+            mats[e] = [(m, *O.quantize(m)) for m in (synth.weights(cfg["F"], cfg["D"], seed=10 + e),
+                                                     synth.weights(cfg["F"], cfg["D"], seed=20 + e),
+                                                     synth.weights(cfg["D"], cfg["F"], seed=30 + e))]
+    return x, pairs, mats
+
+
+def moe_cpu_pairs(cfg: dict, x, pairs, mats, k: float) -> int:
+    """The reference's computation of the pairs on the host; returns their algorithmic bytes."""
+    import oracle as O
+    total = 0
+    for t, e in pairs:
+        (w1, p1, s1, z1), (w3, p3, s3, z3), (w2, p2, s2, z2) = mats[e]
+        a, _, m1 = O.split_gemv(p1, s1, z1, w1, x[t], k)
+        b, _, m3 = O.split_gemv(p3, s3, z3, w3, x[t], k)
+        af, bf = a.astype(np.float32), b.astype(np.float32)
+        h = (af / (np.float32(1) + np.exp(-af)) * bf).astype(np.float16)
+        _, _, m2 = O.split_gemv(p2, s2, z2, w2, h, k)
+        total += (gemv_bytes(cfg["F"], cfg["D"], int(m1.sum())) + gemv_bytes(cfg["F"], cfg["D"], int(m3.sum()))
+                  + gemv_bytes(cfg["D"], cfg["F"], int(m2.sum())))
+    return total
+
+
+def moe_cpu_baseline(args, cfg: dict, budget_s: float) -> dict:
+    import oracle as O
+    O.set_num_threads(os.cpu_count() or 1)
+    x, pairs, mats = moe_cpu_sample(cfg, 4)
+    moe_cpu_pairs(cfg, x, pairs[:1], mats, args.k)  # warm
+    t0 = time.perf_counter()
+    nbytes, n = 0, 0
+    while True:
+        nbytes += moe_cpu_pairs(cfg, x, pairs, mats, args.k)
+        n += len(pairs)
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": O.num_threads(), "kind": "port",
+            "sample": f"{n} (token, expert) FFN evaluations (3 split GEMVs each, per token as the reference "
+                      f"computes them) in {dt:.1f} s, OpenMP over rows, oracle/dq_oracle.c -O3"}
+
+
+def run_moe_reference(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    import oracle as O
+    O.set_num_threads(os.cpu_count() or 1)
+    cfg = dict(MOE_WORKLOADS[args.workload], k=args.k)
+    x, pairs, mats = moe_cpu_sample(cfg, 2)
+    for _ in range(max(1, args.warmup // 3)):
+        moe_cpu_pairs(cfg, x, pairs[:1], mats, args.k)
+    t0 = time.perf_counter()
+    nbytes = 0
+    for _ in range(args.steps):
+        nbytes += moe_cpu_pairs(cfg, x, pairs, mats, args.k)
+    dt = time.perf_counter() - t0
+    value = nbytes / dt / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+        "dtype": "w4a16 (fp32 accumulate)", "data": "synthetic",
+        "config": {"workload": args.workload, **{k: v for k, v in cfg.items()}},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": O.num_threads(), "kind": "port",
+                         "sample": f"each step: {len(pairs)} (token, expert) FFN evaluations of the workload on the "
+                                   "host cores (the reference computes one split GEMV per token and expert)"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="llama2_7b_mlp")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(MOE_WORKLOADS), default="llama2_7b_mlp")
     ap.add_argument("--soak", type=float, default=0.6, help="seconds of replays before/after the timed region")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -598,7 +876,12 @@ def main(argv=None) -> None:
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.impl == "reference":
+    if args.workload in MOE_WORKLOADS:
+        if args.impl == "reference":
+            run_moe_reference(args, rank, world)
+        else:
+            run_moe(args, rank, world, local_rank)
+    elif args.impl == "reference":
         run_reference(args, rank, world)
     else:
         run_ours(args, rank, world, local_rank)

@@ -147,6 +147,25 @@ dq_status_t dq_read_device_error(uint32_t* word, int clear) {
     return DQ_OK;
 }
 
+dq_status_t dq_silu_mul(const uint16_t* a, const uint16_t* b, uint16_t* h, int64_t n, void* stream) {
+    if (n < 0 || n % 8 != 0) return DQ_ERR_SHAPE;
+    if (n == 0) return DQ_OK;
+    if (!a || !b || !h) return DQ_ERR_INVALID_ARGUMENT;
+    if (!aligned16(a) || !aligned16(b) || !aligned16(h)) return DQ_ERR_ALIGNMENT;
+    return launch_silu_mul(a, b, h, n, static_cast<cudaStream_t>(stream));
+}
+
+dq_status_t dq_moe_combine(const uint16_t* y, const int32_t* rows, const float* weight, float* out, int32_t m,
+                           int32_t d, void* stream) {
+    if (m < 0 || d <= 0 || d % 8 != 0) return DQ_ERR_SHAPE;
+    if (m == 0) return DQ_OK;
+    if (!y || !rows || !weight || !out) return DQ_ERR_INVALID_ARGUMENT;
+    if (!aligned16(y) || !aligned16(out) || (reinterpret_cast<uintptr_t>(rows) & 3u) ||
+        (reinterpret_cast<uintptr_t>(weight) & 3u))
+        return DQ_ERR_ALIGNMENT;
+    return launch_combine(y, rows, weight, out, m, d, static_cast<cudaStream_t>(stream));
+}
+
 size_t dq_workspace_bytes_batched(int32_t d_out, int32_t d_in, int32_t m) {
     if (check_dims(d_out, d_in) != DQ_OK || m < 1 || m > kBgMaxM) return 0;
     return bg_ws(bg_geom(d_out, d_in, m), d_out, d_in).total;

@@ -28,11 +28,12 @@
 // f32; 16 weight rows x 8 vectors x 16 columns of one 128-column group).
 // ldmatrix over the native unit layout gives lane (g, t) word t of the pieces
 // of group j at slices 0..3 for rows g and g + 8 (columns 32 sl + 8 t ..
-// 32 sl + 8 t + 7 of the group).  A keeps the exponent bias (f16 1024 + q for
-// even columns, 1024 + 16 q for odd columns); B is x' of vector g in the same
-// column order, from a per-CTA table.  Per group and vector:
-//   D_lo = 1024 Xe + sum_even q x'        D_hi = 1024 Xo + 16 sum_odd q x'
-//   y += s ((D_hi - 1024 Xo) / 16 + (D_lo - 1024 Xe) - z X)
+// 32 sl + 8 t + 7 of the group).  A holds the codes as exact FP16 integers
+// (q for even columns, 16 q for odd columns: the exponent-bias trick, then the
+// bias subtracted); B is x' of vector g in the same column order, from a
+// per-CTA table.  Per group and vector:
+//   D_lo = sum_even q x'        D_hi = 16 sum_odd q x'
+//   y += s (D_hi / 16 + D_lo - z X)
 // which is the reference's sum over the group of s (q - z) x'.
 #include <algorithm>
 
@@ -48,6 +49,22 @@ namespace {
 __device__ unsigned int g_berror_word;
 
 constexpr int kUnit = kB1UnitBytes;
+
+// The codes of a word as exact FP16 integers: q for the even columns, 16 q for
+// the odd ones (the exponent-biased values with the bias 1024 taken off, one
+// exact HSUB2 per register).  Without the bias the MMA sums q x' directly:
+// with large activations (the gated activations of an MoE expert run into
+// the hundreds) a sum that carries 1024 X loses low bits in the tensor core's
+// accumulation.
+__device__ __forceinline__ Biased4 exact_word(uint32_t w) {
+    constexpr uint32_t kMagic = 0x64006400u;
+    Biased4 r = biased_word(w);
+    r.lo0 = hsub2_u32(r.lo0, kMagic);
+    r.lo1 = hsub2_u32(r.lo1, kMagic);
+    r.hi0 = hsub2_u32(r.hi0, kMagic);
+    r.hi1 = hsub2_u32(r.hi1, kMagic);
+    return r;
+}
 
 __device__ __forceinline__ float4 lds_f4(uint32_t addr) {
     const uint4 v = lds_v4(addr);
@@ -522,8 +539,8 @@ __global__ void __launch_bounds__(kBgWarps * 32, 1) bdense_kernel(const BDArgs a
                 for (int e = 0; e < 4; ++e) dlo[nt][e] = dhi[nt][e] = 0.f;
 #pragma unroll
             for (int sl = 0; sl < 4; ++sl) {
-                const Biased4 qa = biased_word(w0[sl]);
-                const Biased4 qb = biased_word(w1[sl]);
+                const Biased4 qa = exact_word(w0[sl]);
+                const Biased4 qb = exact_word(w1[sl]);
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
                     const uint4 b = lds_v4(xtab_a + ((((cc * 4 + jg) * 4 + sl) * MP + nt * 8 + g) * 4 + t) * 16);
@@ -541,10 +558,10 @@ __global__ void __launch_bounds__(kBgWarps * 32, 1) bdense_kernel(const BDArgs a
                 const uint32_t xa_addr = xsum_a + ((cc * 4 + jg) * MP + nt * 8 + 2 * t) * 16;
                 const float4 xa = lds_f4(xa_addr);       // vector nt*8 + 2t
                 const float4 xb = lds_f4(xa_addr + 16);  // vector nt*8 + 2t + 1
-                yacc[nt][0] = fmaf(s0, fmaf(-z0, xa.z, fmaf(dhi[nt][0] - xa.y, 0.0625f, dlo[nt][0] - xa.x)), yacc[nt][0]);
-                yacc[nt][1] = fmaf(s0, fmaf(-z0, xb.z, fmaf(dhi[nt][1] - xb.y, 0.0625f, dlo[nt][1] - xb.x)), yacc[nt][1]);
-                yacc[nt][2] = fmaf(s8, fmaf(-z8, xa.z, fmaf(dhi[nt][2] - xa.y, 0.0625f, dlo[nt][2] - xa.x)), yacc[nt][2]);
-                yacc[nt][3] = fmaf(s8, fmaf(-z8, xb.z, fmaf(dhi[nt][3] - xb.y, 0.0625f, dlo[nt][3] - xb.x)), yacc[nt][3]);
+                yacc[nt][0] = fmaf(s0, fmaf(-z0, xa.z, fmaf(dhi[nt][0], 0.0625f, dlo[nt][0])), yacc[nt][0]);
+                yacc[nt][1] = fmaf(s0, fmaf(-z0, xb.z, fmaf(dhi[nt][1], 0.0625f, dlo[nt][1])), yacc[nt][1]);
+                yacc[nt][2] = fmaf(s8, fmaf(-z8, xa.z, fmaf(dhi[nt][2], 0.0625f, dlo[nt][2])), yacc[nt][2]);
+                yacc[nt][3] = fmaf(s8, fmaf(-z8, xb.z, fmaf(dhi[nt][3], 0.0625f, dlo[nt][3])), yacc[nt][3]);
             }
         }
         __syncwarp();  // every lane is done with the stage before it is refilled

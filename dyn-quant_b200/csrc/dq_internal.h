@@ -194,6 +194,9 @@ inline BgWs bg_ws(const BgGeom& g, int d_out, int d_in) {
 dq_status_t launch_gemv_batched(const dq_weights_t& w, const uint16_t* x, uint16_t* y, int M, float k,
                                 void* workspace, cudaStream_t stream);
 dq_status_t read_batched_error(uint32_t* word, bool clear);
+dq_status_t launch_silu_mul(const uint16_t* a, const uint16_t* b, uint16_t* h, long long n, cudaStream_t stream);
+dq_status_t launch_combine(const uint16_t* y, const int32_t* rows, const float* weight, float* out, int m, int d,
+                           cudaStream_t stream);
 
 // Largest d_in the single-pass kernels accept (x, its B fragments and the
 // outlier list live in shared memory next to the weight rings).

@@ -33,6 +33,8 @@ EXPORTED_SYMBOLS = (
     "dq_split_gemv_noalloc",
     "dq_split_gemv_batched",
     "dq_workspace_bytes_batched",
+    "dq_silu_mul",
+    "dq_moe_combine",
     "dq_int4_gemv",
     "dq_reference_gemv",
     "dq_detect_outliers",
@@ -98,6 +100,10 @@ def lib() -> C.CDLL:
         L.dq_split_gemv_batched.argtypes = [C.POINTER(DqWeights), P, P, i32, f32, P, C.c_size_t, P]
         L.dq_workspace_bytes_batched.restype = C.c_size_t
         L.dq_workspace_bytes_batched.argtypes = [i32, i32, i32]
+        L.dq_silu_mul.restype = st
+        L.dq_silu_mul.argtypes = [P, P, P, C.c_int64, P]
+        L.dq_moe_combine.restype = st
+        L.dq_moe_combine.argtypes = [P, P, P, P, i32, i32, P]
         L.dq_int4_gemv.restype = st
         L.dq_int4_gemv.argtypes = [C.POINTER(DqWeights), P, P, P, C.c_size_t, P]
         L.dq_workspace_bytes.restype = C.c_size_t

@@ -1,0 +1,151 @@
+"""Mixture-of-experts FFN decode step on the dynamic-precision split GEMV.
+
+Mixtral-style experts, y = w2 (silu(w1 x) * (w3 x)), top-k routing: each
+(token, expert) pair is the reference's split GEMV of that token through the
+expert's three matrices, each vector with its own statistics and outlier mask.
+Here the tokens routed to one expert go through the batched split GEMV
+together (the expert's weights stream once for all of them), the gated
+activation is one kernel (dq_silu_mul) and the weighted outputs are added
+into an FP32 buffer (dq_moe_combine).  With the experts spread over the ranks
+of a process group, every rank runs its own experts on the tokens routed to
+them and the partial outputs are summed with one all-reduce.
+
+Routing (which experts, with which weights) is fixed per step by a
+``MoERouting`` built on the host, so a step issues kernel launches only and
+can be captured in a CUDA graph.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Callable, Dict, Iterable, List, Sequence
+
+import torch
+import torch.distributed as dist
+
+from dyn_quant import DynQuantLinear, _lib
+
+
+class MoERouting:
+    """Per-expert token lists of a top-k routing.
+
+    experts: [T, k] expert index of each token's choices; weights: [T, k]
+    combine weights.  Built once on the host; ``tokens[e]`` (int32) and
+    ``weight[e]`` (float32) are the rows routed to expert e and their weights
+    (a token lists an expert at most once)."""
+
+    def __init__(self, experts: torch.Tensor, weights: torch.Tensor, n_experts: int,
+                 device: torch.device | str | None = None) -> None:
+        ex = experts.detach().cpu().long()
+        wt = weights.detach().cpu().float()
+        if ex.shape != wt.shape or ex.dim() != 2:
+            raise ValueError("experts and weights must both be [tokens, k]")
+        if ex.numel() and (ex.min() < 0 or ex.max() >= n_experts):
+            raise ValueError("expert index out of range")
+        self.n_tokens, self.k = ex.shape
+        self.n_experts = n_experts
+        dev = torch.device(device) if device is not None else experts.device
+        self.tokens: Dict[int, torch.Tensor] = {}
+        self.tokens64: Dict[int, torch.Tensor] = {}
+        self.weight: Dict[int, torch.Tensor] = {}
+        for e in range(n_experts):
+            rows, slots = (ex == e).nonzero(as_tuple=True)
+            if len(set(rows.tolist())) != len(rows):
+                raise ValueError(f"a token selects expert {e} twice")
+            if rows.numel():
+                self.tokens[e] = rows.to(torch.int32).to(dev)
+                self.tokens64[e] = rows.to(dev)
+                self.weight[e] = wt[rows, slots].contiguous().to(dev)
+
+    def count(self, e: int) -> int:
+        t = self.tokens.get(e)
+        return 0 if t is None else int(t.numel())
+
+
+def silu_mul(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """fp16(silu(a) * b), silu(v) = v / (1 + exp(-v)) in FP32 (dq_silu_mul)."""
+    if a.shape != b.shape or a.dtype != torch.float16 or b.dtype != torch.float16:
+        raise RuntimeError("silu_mul takes two float16 tensors of one shape")
+    a, b = a.contiguous(), b.contiguous()
+    h = torch.empty_like(a)
+    _lib.check(_lib.lib().dq_silu_mul(C.c_void_p(a.data_ptr()), C.c_void_p(b.data_ptr()), C.c_void_p(h.data_ptr()),
+                                      a.numel(), C.c_void_p(torch.cuda.current_stream(a.device).cuda_stream)),
+               "dq_silu_mul")
+    return h
+
+
+def combine_(out: torch.Tensor, y: torch.Tensor, rows: torch.Tensor, weight: torch.Tensor) -> None:
+    """out[rows[i]] += weight[i] * y[i] in place (out float32 [T, d], y float16 [m, d])."""
+    if y.numel() == 0:
+        return
+    y = y.contiguous()
+    _lib.check(_lib.lib().dq_moe_combine(C.c_void_p(y.data_ptr()), C.c_void_p(rows.data_ptr()),
+                                         C.c_void_p(weight.data_ptr()), C.c_void_p(out.data_ptr()),
+                                         int(y.shape[0]), int(y.shape[1]),
+                                         C.c_void_p(torch.cuda.current_stream(out.device).cuda_stream)),
+               "dq_moe_combine")
+
+
+class MoEFFN(torch.nn.Module):
+    """The experts of one MoE FFN layer, or this rank's share of them.
+
+    experts: the expert indices held here (default: all).  load_expert(e, w1,
+    w3, w2) quantizes expert e's FP16 matrices ([d_ff, d_model], [d_ff,
+    d_model], [d_model, d_ff]); forward(x, routing, group) returns the
+    combined output [T, d_model] (float16) on every rank of group (the sum
+    over the ranks' experts)."""
+
+    def __init__(self, n_experts: int, d_model: int, d_ff: int, outlier_k: float = 3.0,
+                 experts: Iterable[int] | None = None) -> None:
+        super().__init__()
+        self.n_experts, self.d_model, self.d_ff, self.outlier_k = n_experts, d_model, d_ff, outlier_k
+        self.local: List[int] = sorted(experts) if experts is not None else list(range(n_experts))
+        self.w1 = torch.nn.ModuleDict({str(e): DynQuantLinear(d_model, d_ff, outlier_k) for e in self.local})
+        self.w3 = torch.nn.ModuleDict({str(e): DynQuantLinear(d_model, d_ff, outlier_k) for e in self.local})
+        self.w2 = torch.nn.ModuleDict({str(e): DynQuantLinear(d_ff, d_model, outlier_k) for e in self.local})
+
+    def load_expert(self, e: int, w1: torch.Tensor, w3: torch.Tensor, w2: torch.Tensor) -> None:
+        self.w1[str(e)].load_weight(w1)
+        self.w3[str(e)].load_weight(w3)
+        self.w2[str(e)].load_weight(w2)
+
+    def expert(self, e: int, x: torch.Tensor) -> torch.Tensor:
+        """The expert's FFN on the rows of x ([m, d_model] -> [m, d_model], float16)."""
+        a = self.w1[str(e)](x)
+        b = self.w3[str(e)](x)
+        return self.w2[str(e)](silu_mul(a.reshape(x.shape[0], -1), b.reshape(x.shape[0], -1)))
+
+    def forward(self, x: torch.Tensor, routing: MoERouting, group=None, out: torch.Tensor | None = None
+                ) -> torch.Tensor:
+        """Combined output [T, d_model] float16.  When this module holds only
+        some of the experts, the ranks of group (default: the default group)
+        hold the others and the partial outputs are all-reduced."""
+        if out is None:
+            out = torch.zeros(x.shape[0], self.d_model, dtype=torch.float32, device=x.device)
+        else:
+            out.zero_()
+        reduce = len(self.local) < self.n_experts
+        return moe_forward(x, routing, self.local, self.expert, out, reduce, group).to(torch.float16)
+
+
+def moe_forward(x: torch.Tensor, routing: MoERouting, local: Sequence[int],
+                expert: Callable[[int, torch.Tensor], torch.Tensor], out: torch.Tensor, reduce: bool,
+                group=None) -> torch.Tensor:
+    """Run the local experts on their routed tokens and add their weighted
+    outputs into out (float32 [T, d]), experts in the order of local; with
+    reduce, sum out over the ranks of group.  expert(e, xe) is expert e's FFN
+    on the rows xe."""
+    if x.dtype != torch.float16:
+        x = x.to(torch.float16)
+    for e in local:
+        rows = routing.tokens.get(e)
+        if rows is None:
+            continue
+        xe = x.index_select(0, routing.tokens64[e]).contiguous()
+        ye = expert(e, xe).reshape(xe.shape[0], -1)
+        if out.is_cuda:
+            combine_(out, ye, rows, routing.weight[e])
+        else:  # CPU ranks (tests of the distribution logic)
+            out.index_add_(0, rows.long(), routing.weight[e][:, None] * ye.float())
+    if reduce:
+        dist.all_reduce(out, group=group)
+    return out

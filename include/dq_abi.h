@@ -194,6 +194,24 @@ DQ_API dq_status_t dq_split_gemv_batched(const dq_weights_t* w, const uint16_t* 
                                          void* stream);
 
 /*
+ * Gated activation of a mixture-of-experts FFN (Mixtral-style
+ * y = w2 (silu(w1 x) * (w3 x))): h = fp16(silu(a) * b) elementwise over n
+ * values (n a multiple of 8), silu(v) = v / (1 + exp(-v)) in FP32.  No
+ * counterpart in the reference (its MoE use is one split GEMV per token and
+ * expert); the step between the batched GEMVs of an expert.
+ */
+DQ_API dq_status_t dq_silu_mul(const uint16_t* a, const uint16_t* b, uint16_t* h, int64_t n, void* stream);
+
+/*
+ * Weighted combine of one expert's outputs: out[rows[i]][:] += weight[i] *
+ * y[i][:] for i < m (y FP16 [m][d], out FP32 [tokens][d], d a multiple of 8,
+ * the rows of one call distinct).  Stream-ordered calls accumulate the
+ * experts in call order.  No counterpart in the reference.
+ */
+DQ_API dq_status_t dq_moe_combine(const uint16_t* y, const int32_t* rows, const float* weight, float* out,
+                                  int32_t m, int32_t d, void* stream);
+
+/*
  * Dense INT4 GEMV (no outlier handling): y = dequant(W) x.
  * Replaces: launch_int4_gemv (src/int4_gemv.cu:80-100, src/int4_gemv.cuh:9).
  * Only packed/scales/zeros (or native) of *w are read.
