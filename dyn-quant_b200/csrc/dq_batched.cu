@@ -11,18 +11,19 @@
 //     writes its vector's column of x_o (x[m][c] where c is an outlier of m,
 //     else 0; column-major, one column's vectors contiguous).  The last CTA to
 //     finish builds the union of the M masks (ascending columns).
-//  2. bout_kernel, one CTA per 16-row block: the FP16 part,
-//     Y_o = W16[:, union] x_o, on the tensor cores.  Each warp takes every
-//     eighth 16-column batch of the union; the A segments (16 rows of a
-//     column, contiguous in the column-major mirror) and the B segments (the
-//     column's x_o values) come in by 16-byte cp.async and ldmatrix.trans; the
-//     eight warps' sums are added in a fixed order.
-//  3. bdense_kernel: the INT4 part over x' (each vector's outliers zeroed),
+//  2. bdense_kernel: the INT4 part over x' (each vector's outliers zeroed),
 //     split over K: CTA (cx, slab) streams chunks [slab S, slab S + S) of the
 //     row blocks [rb0, rb1) through per-warp cp.async.bulk rings.  Each warp
-//     owns whole row blocks; the last slab to finish a row block (an arrival
-//     counter) sums the slabs' partial sums and the FP16 parts in fixed order
-//     and writes y, so results do not depend on timing.
+//     owns whole row blocks and writes its slab's partial sums.
+//  3. bout_kernel, one CTA per 16-row block: the FP16 part,
+//     Y_o = W16[:, union] x_o, on the tensor cores, then y = the slabs'
+//     partial sums + Y_o, in a fixed order (results do not depend on timing).
+//     Each warp takes every eighth 16-column batch of the union; the A
+//     segments (16 rows of a column, contiguous in the column-major mirror)
+//     and the B segments (the column's x_o values) come in by 16-byte cp.async
+//     and ldmatrix.trans; the eight warps' sums are added in a fixed order.
+//     It depends on the plan only until the INT4 part is needed, so its
+//     tensor-core work starts as the dense kernel's CTAs drain.
 //
 // Tensor-core formulation of the INT4 part (mma.sync.m16n8k16, f16 x f16 ->
 // f32; 16 weight rows x 8 vectors x 16 columns of one 128-column group).
@@ -96,7 +97,6 @@ struct BPArgs {
     uint32_t* ulist;     // [d_in]
     uint16_t* xo;        // [d_in][MP]
     unsigned int* ctr;   // [0] arrival counter, [1] union size
-    unsigned int* rbcnt; // [NRB] the dense kernel's per-row-block counters, cleared here
     float k, inv_n, inv_n1;
     int M, MP, d_in, W, NRB;
     BPSmem S;
@@ -115,9 +115,6 @@ __global__ void __launch_bounds__(kStatThreads, 1) bplan_kernel(const BPArgs a) 
 
     pdl_launch_dependents();
     pdl_wait();  // x and the workspace may belong to the preceding kernel until here
-    // The row-block counters sit at a shape-dependent offset, where another
-    // shape's scratch may have been: clear this call's before the dense kernel.
-    for (int i = m * NT + tid; i < a.NRB; i += a.M * NT) a.rbcnt[i] = 0u;
     load_x_async<NT>(a.x + static_cast<size_t>(m) * a.d_in, n8, xs);
     cp_async_wait_all();
     __syncthreads();
@@ -193,8 +190,9 @@ struct BOArgs {
     const uint32_t* ulist;
     const uint16_t* xo;      // [d_in][MP]
     const unsigned int* ctr;
-    float* opart;            // [MP][d_out]
-    int d_out, d_in, MP;
+    const float* dpart;      // [nslab][MP][d_out] the INT4 part's partial sums
+    uint16_t* y;             // [M][d_out]
+    int d_out, d_in, MP, M, nslab;
 };
 
 // One CTA per 16-row block.
@@ -207,12 +205,12 @@ __global__ void __launch_bounds__(kBgOutWarps * 32) bout_kernel(const BOArgs a) 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int rb = blockIdx.x;
 
+    // The plan kernel has completed (the dense kernel let this grid launch
+    // only after its own wait for it): the union and x_o can be read now.
     pdl_launch_dependents();
-    pdl_wait();  // the union and x_o come from the plan kernel
     const int U = static_cast<int>(ldcg_u32(a.ctr + 1));
     const int nbat = (U + 15) / 16;
-    if (nbat == 0) return;
-    const int nb = (nbat - warp + kBgOutWarps - 1) / kBgOutWarps;  // batches warp, warp + 8, ...
+    const int nb = warp < nbat ? (nbat - warp + kBgOutWarps - 1) / kBgOutWarps : 0;  // batches warp, warp + 8, ...
     const uint32_t wa = smem_u32(&abuf[warp][0][0]), wb = smem_u32(&bbuf[warp][0][0]);
 
     // Batch k of this warp into buffer k % kBgOutBufs: lane = (column lane >> 1
@@ -266,20 +264,32 @@ __global__ void __launch_bounds__(kBgOutWarps * 32) bout_kernel(const BOArgs a) 
         __syncwarp();  // every lane is done with the buffers before they are refilled
         if (k + kBgOutBufs < nb) issue(k + kBgOutBufs);
     }
-    // The warps' sums in warp order.
+    // The warps' sums in warp order, then the INT4 part's slabs in order.
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int e = 0; e < 4; ++e) red[warp][nt][e][lane] = d[nt][e];
     __syncthreads();
+    pdl_wait();  // the dense kernel's partial sums
     for (int i = threadIdx.x; i < NT * 4 * 32; i += kBgOutWarps * 32) {
         const int nt = i >> 7, e = (i >> 5) & 3, ln = i & 31;
-        float v = 0.f;
-#pragma unroll
-        for (int w = 0; w < kBgOutWarps; ++w) v += red[w][nt][e][ln];
         const int row = rb * kRowBlock + (ln >> 2) + 8 * (e >> 1);
         const int tok = nt * 8 + 2 * (ln & 3) + (e & 1);
-        if (row < a.d_out) a.opart[static_cast<size_t>(tok) * a.d_out + row] = v;
+        if (row >= a.d_out || tok >= a.M) continue;
+        float v = 0.f;
+        for (int s0 = 0; s0 < a.nslab; s0 += 4) {
+            float q[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                q[j] = s0 + j < a.nslab
+                           ? ldcg_f32(a.dpart + (static_cast<size_t>(s0 + j) * MP + tok) * a.d_out + row) : 0.f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) v += q[j];
+        }
+        float o = 0.f;
+#pragma unroll
+        for (int w = 0; w < kBgOutWarps; ++w) o += red[w][nt][e][ln];
+        a.y[static_cast<size_t>(tok) * a.d_out + row] = __half_as_ushort(__float2half_rn(v + o));
     }
 }
 
@@ -290,11 +300,7 @@ struct BDArgs {
     const uint8_t* native;   // unit layout
     const uint16_t* x;       // [M][d_in]
     const uint32_t* masks;   // [kBgMaxM][W]
-    const unsigned int* ctr;
-    const float* opart;      // [MP][d_out]
     float* dpart;            // [nslab][MP][d_out]
-    unsigned int* rbcnt;     // [NRB] slabs finished per row block (cleared by the plan kernel)
-    uint16_t* y;             // [M][d_out]
     int M, d_out, d_in, NC, NRB, S, nslab, cps, W;
     int sm_ring, sm_bars, sm_xtab, sm_xsum;
 };
@@ -360,8 +366,8 @@ __global__ void __launch_bounds__(kBgWarps * 32, 1) bdense_kernel(const BDArgs a
         if (s < wn) armed |= 1u << s;
     __syncwarp();
 
-    pdl_launch_dependents();
-    pdl_wait();  // x, the masks, the union and the FP16 parts come from the preceding kernels
+    pdl_wait();  // x and the masks come from the plan kernel
+    pdl_launch_dependents();  // only now: the FP16-part kernel reads the plan before its own wait
     if (rb1 <= rb0) return;  // no row blocks (no copies were issued)
 
     // x' of this slab's chunks for every vector, in MMA B order: piece p
@@ -421,7 +427,6 @@ __global__ void __launch_bounds__(kBgWarps * 32, 1) bdense_kernel(const BDArgs a
     }
     __syncthreads();
 
-    const bool with_out = ldcg_u32(a.ctr + 1) != 0u;  // the FP16 part was written
     const uint32_t xtab_a = smem_u32(xtab);
     const uint32_t xsum_a = smem_u32(xsum);
     const int lm = lane >> 3, lr = lane & 7;  // ldmatrix: this lane addresses row lr of matrix (slice) lm
@@ -430,86 +435,17 @@ __global__ void __launch_bounds__(kBgWarps * 32, 1) bdense_kernel(const BDArgs a
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) yacc[nt][0] = yacc[nt][1] = yacc[nt][2] = yacc[nt][3] = 0.f;
 
-    // Row block rb done by this warp (for this slab): publish, and if it is the
-    // last slab to finish, sum all slabs and the FP16 parts and write y.
+    // Row block rb done by this warp: its partial sums for this slab.
     auto finish_rb = [&](int rb) {
+        float* dp = a.dpart + static_cast<size_t>(sb) * MP * a.d_out;
         const int row0 = rb * kRowBlock + g;
-        float v[NT][4], fo[NT][4];  // fo: the FP16 part, fetched with the first partials
-        auto fetch_fp16 = [&]() {
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int row = row0 + 8 * (e >> 1);
-                    const int tok = nt * 8 + 2 * t + (e & 1);
-                    fo[nt][e] = (with_out && row < a.d_out)
-                                    ? ldcg_f32(a.opart + static_cast<size_t>(tok) * a.d_out + row) : 0.f;
-                }
-        };
-        if (a.nslab == 1) {
-            fetch_fp16();
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) v[nt][e] = yacc[nt][e];
-        } else {
-            float* dp = a.dpart + static_cast<size_t>(sb) * MP * a.d_out;
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int row = row0 + 8 * (e >> 1);
-                    const int tok = nt * 8 + 2 * t + (e & 1);
-                    if (row < a.d_out) dp[static_cast<size_t>(tok) * a.d_out + row] = yacc[nt][e];
-                }
-            __threadfence();
-            __syncwarp();
-            unsigned int old = 0;
-            if (lane == 0) old = atomicAdd(a.rbcnt + rb, 1u);
-            old = __shfl_sync(0xffffffffu, old, 0);
-            if (old != static_cast<unsigned>(a.nslab - 1)) return;
-            __threadfence();
-            fetch_fp16();
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) v[nt][e] = 0.f;
-            // slabs in order, four at a time with their loads in flight together
-            for (int s0 = 0; s0 < a.nslab; s0 += 4) {
-                float q[4][NT][4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const float* sp = a.dpart + static_cast<size_t>(s0 + j) * MP * a.d_out;
-#pragma unroll
-                    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int row = row0 + 8 * (e >> 1);
-                            const int tok = nt * 8 + 2 * t + (e & 1);
-                            q[j][nt][e] = (s0 + j < a.nslab && row < a.d_out)
-                                              ? ldcg_f32(sp + static_cast<size_t>(tok) * a.d_out + row) : 0.f;
-                        }
-                }
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-#pragma unroll
-                    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) v[nt][e] += q[j][nt][e];
-            }
-        }
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) v[nt][e] += fo[nt][e];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const int row = row0 + 8 * (e >> 1);
                 const int tok = nt * 8 + 2 * t + (e & 1);
-                if (row < a.d_out && tok < a.M)
-                    a.y[static_cast<size_t>(tok) * a.d_out + row] = __half_as_ushort(__float2half_rn(v[nt][e]));
+                if (row < a.d_out) dp[static_cast<size_t>(tok) * a.d_out + row] = yacc[nt][e];
             }
     };
 
@@ -642,13 +578,13 @@ dq_status_t launch_batched_nt(const BgGeom& G, const BPArgs& pa, const BOArgs& o
     if (st != DQ_OK) return st;
     st = launch_pdl(bplan_kernel, dim3(G.M), kStatThreads, pa.S.total, stream, pa);
     if (st != DQ_OK) return st;
-    switch (out_mode) {
-        case kBoStaged: st = launch_bout<kBoStaged, NT>(oa, ogrid, stream); break;
-        case kBoColDirect: st = launch_bout<kBoColDirect, NT>(oa, ogrid, stream); break;
-        default: st = launch_bout<kBoRowDirect, NT>(oa, ogrid, stream); break;
-    }
+    st = launch_pdl(bdense_kernel<NT>, dim3(da.cps, G.nslab), kBgWarps * 32, dsmem, stream, da);
     if (st != DQ_OK) return st;
-    return launch_pdl(bdense_kernel<NT>, dim3(da.cps, G.nslab), kBgWarps * 32, dsmem, stream, da);
+    switch (out_mode) {
+        case kBoStaged: return launch_bout<kBoStaged, NT>(oa, ogrid, stream);
+        case kBoColDirect: return launch_bout<kBoColDirect, NT>(oa, ogrid, stream);
+        default: return launch_bout<kBoRowDirect, NT>(oa, ogrid, stream);
+    }
 }
 
 }  // namespace
@@ -677,7 +613,6 @@ dq_status_t launch_gemv_batched(const dq_weights_t& w, const uint16_t* x, uint16
     pa.MP = G.MP;
     pa.d_in = w.d_in;
     pa.W = G.W;
-    pa.rbcnt = reinterpret_cast<unsigned int*>(ws + L.rbcnt);
     pa.NRB = G.NRB;
     pa.S = bp_smem(w.d_in);
     if (pa.S.total > di.smem_optin) return DQ_ERR_UNSUPPORTED;
@@ -688,10 +623,13 @@ dq_status_t launch_gemv_batched(const dq_weights_t& w, const uint16_t* x, uint16
     oa.ulist = pa.ulist;
     oa.xo = pa.xo;
     oa.ctr = pa.ctr;
-    oa.opart = reinterpret_cast<float*>(ws + L.opart);
+    oa.dpart = reinterpret_cast<float*>(ws + L.dpart);
+    oa.y = y;
     oa.d_out = w.d_out;
     oa.d_in = w.d_in;
     oa.MP = G.MP;
+    oa.M = M;
+    oa.nslab = G.nslab;
     const int out_mode = w.fp16_cm ? ((w.d_out % 8) == 0 ? kBoStaged : kBoColDirect) : kBoRowDirect;
     const int ogrid = G.NRB;
 
@@ -699,11 +637,7 @@ dq_status_t launch_gemv_batched(const dq_weights_t& w, const uint16_t* x, uint16
     da.native = w.native;
     da.x = x;
     da.masks = pa.masks;
-    da.ctr = pa.ctr;
-    da.opart = oa.opart;
     da.dpart = reinterpret_cast<float*>(ws + L.dpart);
-    da.rbcnt = reinterpret_cast<unsigned int*>(ws + L.rbcnt);
-    da.y = y;
     da.M = M;
     da.d_out = w.d_out;
     da.d_in = w.d_in;

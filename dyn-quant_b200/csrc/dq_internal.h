@@ -141,14 +141,12 @@ inline BgGeom bg_geom(int d_out, int d_in, int M) {
 // offsets from the start of the workspace.  Only ctr[0] must be zero on entry
 // (at a fixed offset; every call leaves it zero); the rest is scratch.
 //   ctr    [0] plan arrival counter, [1] union size
-//   rbcnt  per row block, slabs finished (cleared by the plan kernel)
 //   masks  [kBgMaxM][W] outlier bits of each vector
 //   ulist  [d_in] the union of the masks, ascending columns
 //   xo     [d_in][MP] FP16: x[m][c] where column c is an outlier of vector m, else 0
-//   opart  [MP][d_out] FP32, the FP16 product over the union's columns
-//   dpart  [nslab][MP][d_out] FP32 per-slab partial sums of the INT4 part (nslab > 1)
+//   dpart  [nslab][MP][d_out] FP32 per-slab partial sums of the INT4 part
 struct BgWs {
-    size_t ctr, rbcnt, masks, ulist, xo, opart, dpart, total;
+    size_t ctr, masks, ulist, xo, dpart, total;
 };
 
 inline BgWs bg_ws(const BgGeom& g, int d_out, int d_in);
@@ -181,12 +179,10 @@ inline BgWs bg_ws(const BgGeom& g, int d_out, int d_in) {
     BgWs L;
     size_t off = ws_layout(d_out, d_in).total;
     L.ctr = off;   off += 256;
-    L.rbcnt = off; off += align256(static_cast<size_t>(g.NRB) * 4);
     L.masks = off; off += align256(static_cast<size_t>(kBgMaxM) * g.W * 4);
     L.ulist = off; off += align256(static_cast<size_t>(d_in) * 4);
     L.xo = off;    off += align256(static_cast<size_t>(d_in) * g.MP * 2);
-    L.opart = off; off += align256(static_cast<size_t>(g.MP) * d_out * 4);
-    L.dpart = off; off += g.nslab > 1 ? align256(static_cast<size_t>(g.nslab) * g.MP * d_out * 4) : 0;
+    L.dpart = off; off += align256(static_cast<size_t>(g.nslab) * g.MP * d_out * 4);
     L.total = off;
     return L;
 }

@@ -53,10 +53,10 @@ def main() -> None:
             ref16, ref32, _ = O.split_gemv(packed, scales, zeros, w, x, 3.0)
             err = check_y(y, ref16, what=f"{d_out}x{d_in} rank {rank}")
             # every rank must hold the same gathered y, bit for bit
-            yt = torch.from_numpy(y.view(np.int16).copy()).to(dev)
+            yt = torch.from_numpy(y.copy()).to(dev)  # float16 (NCCL has no int16)
             y0 = yt.clone()
             dist.broadcast(y0, 0)
-            same = bool(torch.equal(yt, y0))
+            same = bool(torch.equal(yt.view(torch.int16), y0.view(torch.int16)))
             r0, r1, per = shard_rows(d_out, world, rank)
             results.append({"shape": [d_out, d_in], "rows": [r0, r1], "same_as_rank0": same, **err})
         ok = all(r["same_as_rank0"] for r in results)
