@@ -16,13 +16,15 @@ copies that every step reads them from HBM, not L2).  Algorithmic bytes per
 GEMV = d_out*d_in/2 (INT4) + 4*d_out*d_in/128 (FP16 scale + zero)
 + 2*d_out*n_o (FP16 outlier columns, n_o = detected outliers) + 2*d_in (x) + 2*d_out (y).
 
-One process per GPU.  Under torchrun (N > 1) every GEMV of the workload is
-row-sharded: each rank holds whole 16-row blocks of the weights, runs the
-split GEMV on its slice with the same x, and the output slices are
-all-gathered with NCCL after every GEMV ("scaling": "strong": the total work
-is the workload's, whatever N).  The time is the max over ranks; value is the
-full GEMVs' algorithmic bytes over that time.  The roofline line describes
-this rank's kernel alone (its slice's bytes over its launch time).
+One process per GPU.  Under torchrun (N > 1) the 70B workloads are
+row-sharded, as a 70B model is deployed: each rank holds whole 16-row blocks
+of the weights, runs the split GEMV on its slice with the same x, and the
+output slices are all-gathered with NCCL after every GEMV ("scaling":
+"strong": the total work is the workload's, whatever N).  The 7B and sweep
+workloads fit one GPU and run as N independent replicas (data parallel, no
+collective, "scaling": "weak"); --shard overrides either choice.  The time is
+the max over ranks; value is the algorithmic bytes of the whole job over that
+time.  The roofline line describes this rank's kernel alone.
 
 --impl reference times the reference's split GEMV restated on the CPU (the
 reference has no CPU GEMV of its own; this is the oracle port, OpenMP over
@@ -80,6 +82,13 @@ def gemv_bytes(d_out: int, d_in: int, n_o: int, m: int = 1) -> int:
     zero, the FP16 columns of the n_o outlier channels (for m > 1 the union of
     the vectors' masks), m activation vectors and m outputs."""
     return d_out * d_in // 2 + 4 * d_out * (d_in // 128) + 2 * d_out * n_o + 2 * m * (d_in + d_out)
+
+
+def shard_mode(args) -> str:
+    """How N > 1 ranks split a GEMV workload (see --shard)."""
+    if args.shard != "auto":
+        return args.shard
+    return "rows" if args.workload.startswith("llama2_70b") else "replicas"
 
 
 def workload_spec(args):
@@ -291,11 +300,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     L = _lib.lib()
     spec = workload_spec(args)
     M = args.batch
-    sharded = world > 1
-    # Row sharding across the ranks (N > 1): every rank holds whole 16-row
-    # blocks of each GEMV, sees the same x, and the output slices are
-    # all-gathered with NCCL after every GEMV.
-    acts_np = activations(args)
+    sharded = world > 1 and shard_mode(args) == "rows"
+    # Row sharding across the ranks: every rank holds whole 16-row blocks of
+    # each GEMV, sees the same x, and the output slices are all-gathered with
+    # NCCL after every GEMV.  Replicas: every rank runs the whole workload on
+    # its own weights and activations (data parallel, no collective).
+    acts_np = activations(args, 0 if sharded else 1000 * rank)
     acts = {k: torch.from_numpy(v).to(dev) for k, v in acts_np.items()}
     rows = [shard_rows(o, world, rank) if sharded else (0, o, o) for _, o, _, _, _ in spec]
 
@@ -305,8 +315,13 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     for key, x in acts.items():
         masks = [dyn_quant.detect_outliers(r, args.k)[0] for r in x.reshape(-1, x.shape[-1])]
         n_o[key] = int(torch.stack(masks).any(0).sum().item())
-    # whole-job algorithmic bytes of one step (the full GEMVs, whatever the sharding)
+    # algorithmic bytes of one step (the full GEMVs, whatever the sharding)
     step_bytes = sum(gemv_bytes(o, i, n_o[key], M) for _, o, i, _, key in spec)
+    job_step_bytes = step_bytes  # the whole job's: replicas add theirs
+    if world > 1 and not sharded:
+        t = torch.tensor([step_bytes], dtype=torch.float64, device=dev)
+        dist.all_reduce(t)
+        job_step_bytes = int(t.item())
     # this rank's kernel bytes of one step
     local_bytes = [gemv_bytes(max(r1 - r0, 0), i, n_o[key], M)
                    for (_, _, i, _, key), (r0, r1, _) in zip(spec, rows)]
@@ -455,12 +470,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     else:
         achieved = sum(per_gemv_bytes) * args.steps / (elapsed_ms * 1e-3) / 1e9
 
-    # whole-job throughput: the full GEMVs' bytes over the max-over-ranks time
-    value = step_bytes * args.steps / (elapsed_ms * 1e-3) / 1e9
+    # whole-job throughput: the full GEMVs' bytes (every replica's) over the max-over-ranks time
+    value = job_step_bytes * args.steps / (elapsed_ms * 1e-3) / 1e9
     us_per_gemv = elapsed_ms * 1e3 / (args.steps * n_gemv)
 
     # end to end through the public API: pinned host x in, host y out, every step
-    e2e = run_e2e(args, spec, sets, acts_np, dev, step_bytes, world, rows)
+    e2e = run_e2e(args, spec, sets, acts_np, dev, job_step_bytes, world, rows, sharded)
 
     # accuracy of this rank's rows (weight set 0) against an FP32 dense GEMV on
     # the original FP16 weights and activations
@@ -499,7 +514,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                              f"({n_sets * step_bytes / 1e6:.0f} MB streamed per cycle)",
                        "graphs": "the K timed steps are one CUDA graph of back-to-back launches",
                        "parallelism": (f"row-sharded over {world} GPUs, NCCL all-gather of the output slices "
-                                       "after every GEMV" if sharded else "1 GPU")},
+                                       "after every GEMV" if sharded else
+                                       (f"{world} independent replicas (data parallel, no collective)"
+                                        if world > 1 else "1 GPU"))},
             "us_per_gemv": round(us_per_gemv, 3),
             "gemvs": per_name,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -522,18 +539,20 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         dist.destroy_process_group()
 
 
-def run_e2e(args, spec, sets, acts_np, dev, step_bytes, world, rows):
+def run_e2e(args, spec, sets, acts_np, dev, job_step_bytes, world, rows, sharded):
     """The same steps through DynQuantLinear.forward from pinned host buffers.
 
-    Row-sharded runs (world > 1) gather each GEMV's output slices with
-    dyn_quant.sharded.gather_rows, so every rank copies the full y back."""
+    Row-sharded runs gather each GEMV's output slices with
+    dyn_quant.sharded.gather_rows, so every rank copies the full y back;
+    replicas (world > 1, not sharded) each run the whole workload and the
+    value counts the bytes of all of them over the max-over-ranks time."""
     import torch
     import torch.distributed as dist
     from dyn_quant.sharded import gather_rows
     M = args.batch
     xh = {k: torch.from_numpy(v).pin_memory() for k, v in acts_np.items()}
     xd = {k: torch.empty(v.shape, dtype=torch.float16, device=dev) for k, v in acts_np.items()}
-    yh = [torch.empty(M * (o if world == 1 else world * per), dtype=torch.float16).pin_memory()
+    yh = [torch.empty(M * (world * per if sharded else o), dtype=torch.float16).pin_memory()
           for (_, o, _, _, _), (_, _, per) in zip(spec, rows)]
     gbuf = [torch.empty(world * per, dtype=torch.float16, device=dev) for (_, _, per) in rows]
     ypad = [torch.zeros(M, per, dtype=torch.float16, device=dev) for (_, _, per) in rows]
@@ -551,9 +570,9 @@ def run_e2e(args, spec, sets, acts_np, dev, step_bytes, world, rows):
             xd[k].copy_(xh[k], non_blocking=True)
         for gi, (name, d_out, d_in, frac, key) in enumerate(spec):
             y = sets[s][gi](xd[key])
-            if world > 1 and M == 1:
+            if sharded and M == 1:
                 y = gather_rows(y, d_out, rows[gi][2], None, gbuf[gi])
-            elif world > 1:  # [M, rows] slices, gathered rank-major
+            elif sharded:  # [M, rows] slices, gathered rank-major
                 ypad[gi][:, :y.shape[-1]].copy_(y)
                 dist.all_gather_into_tensor(gbig[gi], ypad[gi].reshape(-1))
                 y = gbig[gi]
@@ -573,11 +592,16 @@ def run_e2e(args, spec, sets, acts_np, dev, step_bytes, world, rows):
         t = torch.tensor([ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    return {"value": round(step_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 4),
-            "api": ("DynQuantLinear.forward, pinned host buffers, synchronised every step" if world == 1 else
-                    "DynQuantLinear.forward on each rank's rows + NCCL all-gather, pinned host buffers on "
-                    "every rank (bytes per rank), synchronised every step")}
+    if world == 1:
+        api = "DynQuantLinear.forward, pinned host buffers, synchronised every step"
+    elif sharded:
+        api = ("DynQuantLinear.forward on each rank's rows + NCCL all-gather, pinned host buffers on "
+               "every rank (bytes per rank), synchronised every step")
+    else:
+        api = (f"DynQuantLinear.forward on {world} replicas, pinned host buffers on every rank (bytes per "
+               "rank), synchronised every step; value: all replicas' bytes over the max-over-ranks time")
+    return {"value": round(job_step_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 4), "api": api}
 
 
 # ---------------------------------------------------------------------------
@@ -866,6 +890,9 @@ def main(argv=None) -> None:
     ap.add_argument("--frac", type=float, default=None, help="injected outlier fraction (default: the workload's)")
     ap.add_argument("--k", type=float, default=K_OUTLIER, help="outlier threshold in standard deviations")
     ap.add_argument("--dist", choices=["normal", "t3"], default="normal", help="activation distribution")
+    ap.add_argument("--shard", choices=["auto", "rows", "replicas"], default="auto",
+                    help="N > 1: row sharding with an all-gather, or independent replicas; auto follows the "
+                         "deployment of each shape: rows for the 70B workloads, replicas for the 7B and sweep ones")
     ap.add_argument("--max-sets", type=int, default=0,
                     help="cap on rotating weight sets (profiling runs only; the default rotates through >= 3x L2)")
     args = ap.parse_args(argv)

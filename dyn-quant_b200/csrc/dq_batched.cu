@@ -8,9 +8,10 @@
 //  1. bplan_kernel, one CTA per vector: the statistics and the outlier mask
 //     of x[m], with the code and the fixed partition of the batch-1 kernel
 //     (dq_plan.cuh), so each vector gets exactly the batch-1 mask; the CTA
-//     writes its vector's column of x_o (x[m][c] where c is an outlier of m,
-//     else 0; column-major, one column's vectors contiguous).  The last CTA to
-//     finish builds the union of the M masks (ascending columns).
+//     writes its vector's outlier-only row (x[m][c] where c is an outlier of
+//     m, else 0).  The last CTA to finish builds the union of the M masks
+//     (ascending columns) and gathers the union's columns of those rows into
+//     x_o[u][m], one union column's vectors contiguous.
 //  2. bdense_kernel: the INT4 part over x' (each vector's outliers zeroed),
 //     split over K: CTA (cx, slab) streams chunks [slab S, slab S + S) of the
 //     row blocks [rb0, rb1) through per-warp cp.async.bulk rings.  Each warp
@@ -95,7 +96,8 @@ struct BPArgs {
     const uint16_t* x;   // [M][d_in]
     uint32_t* masks;     // [kBgMaxM][W]
     uint32_t* ulist;     // [d_in]
-    uint16_t* xo;        // [d_in][MP]
+    uint16_t* xrow;      // [MP][d_in] outlier-only rows
+    uint16_t* xo;        // [d_in][MP] by union position
     unsigned int* ctr;   // [0] arrival counter, [1] union size
     float k, inv_n, inv_n1;
     int M, MP, d_in, W, NRB;
@@ -123,13 +125,24 @@ __global__ void __launch_bounds__(kStatThreads, 1) bplan_kernel(const BPArgs a) 
                     reinterpret_cast<int*>(red) + 2 * (kStatThreads / 32));
     __syncthreads();
     for (int i = tid; i < a.W; i += NT) a.masks[static_cast<size_t>(m) * a.W + i] = mask32[i];
-    // Column m of x_o, and the all-zero columns of the padding vectors M .. MP-1.
+    // Row m of the outlier-only rows (16-byte stores), and the all-zero rows of
+    // the padding vectors M .. MP-1.
     {
-        const uint16_t* xh = reinterpret_cast<const uint16_t*>(xs);
-        for (int c = tid; c < a.d_in; c += NT) {
-            const bool out = (mask32[c >> 5] >> (c & 31)) & 1u;
-            a.xo[static_cast<size_t>(c) * a.MP + m] = out ? xh[c] : static_cast<uint16_t>(0);
-            for (int mm = a.M + m; mm < a.MP; mm += a.M) a.xo[static_cast<size_t>(c) * a.MP + mm] = 0;
+        const uint8_t* mb = reinterpret_cast<const uint8_t*>(mask32);
+        for (int p = tid; p < n8; p += NT) {
+            const uint32_t b = mb[p];
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (b) {
+                const uint4 w = xs[p];
+                uint32_t keep[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    keep[i] = ((b >> (2 * i)) & 1u ? 0x0000FFFFu : 0u) | ((b >> (2 * i + 1)) & 1u ? 0xFFFF0000u : 0u);
+                v = make_uint4(w.x & keep[0], w.y & keep[1], w.z & keep[2], w.w & keep[3]);
+            }
+            *reinterpret_cast<uint4*>(a.xrow + static_cast<size_t>(m) * a.d_in + 8 * p) = v;
+            for (int mm = a.M + m; mm < a.MP; mm += a.M)
+                *reinterpret_cast<uint4*>(a.xrow + static_cast<size_t>(mm) * a.d_in + 8 * p) = make_uint4(0, 0, 0, 0);
         }
     }
     __threadfence();
@@ -157,19 +170,38 @@ __global__ void __launch_bounds__(kStatThreads, 1) bplan_kernel(const BPArgs a) 
     int pre[1], tot[1];
     block_scan<NT, 1>(cnt, pre, tot, reinterpret_cast<int*>(red));
     int pos = pre[0];
+    uint16_t* ucols = reinterpret_cast<uint16_t*>(xs);  // x of this CTA is no longer needed
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
         const int wj = w0 + q;
         if (wj < w1) {
             uint32_t rest = u[q];
             while (rest) {
-                a.ulist[pos++] = static_cast<uint32_t>(32 * wj + __ffs(rest) - 1);
+                const int col = 32 * wj + __ffs(rest) - 1;
+                a.ulist[pos] = static_cast<uint32_t>(col);
+                ucols[pos++] = static_cast<uint16_t>(col);
                 rest &= rest - 1u;
             }
         }
     }
-    if (tid == 0) {
-        a.ctr[1] = static_cast<unsigned>(tot[0]);
+    __syncthreads();
+    // x_o[u][:] = the outlier-only rows at union column u, all loads of a
+    // thread in flight together; the last batch of 16 is padded with zeros.
+    const int U = tot[0];
+    const int upad = (U + 15) & ~15;
+    for (int u0 = tid; u0 < upad; u0 += NT) {
+        uint16_t v[kBgMaxM];
+        const int col = u0 < U ? ucols[u0] : 0;
+#pragma unroll
+        for (int mm = 0; mm < kBgMaxM; ++mm)
+            v[mm] = (u0 < U && mm < a.MP) ? ldcg_u16(a.xrow + static_cast<size_t>(mm) * a.d_in + col)
+                                          : static_cast<uint16_t>(0);
+        uint4* dst = reinterpret_cast<uint4*>(a.xo + static_cast<size_t>(u0) * a.MP);
+        dst[0] = make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], v[3]), pack_h2(v[4], v[5]), pack_h2(v[6], v[7]));
+        if (a.MP == 16)
+            dst[1] = make_uint4(pack_h2(v[8], v[9]), pack_h2(v[10], v[11]), pack_h2(v[12], v[13]), pack_h2(v[14], v[15]));
+    }
+    if (tid == 0) {        a.ctr[1] = static_cast<unsigned>(tot[0]);
         a.ctr[0] = 0u;  // ready for the next call
     }
 }
@@ -188,7 +220,7 @@ struct BOArgs {
     const uint16_t* w16;     // row-major FP16 [d_out][d_in]
     const uint16_t* w16_cm;  // column-major mirror [d_in][d_out]
     const uint32_t* ulist;
-    const uint16_t* xo;      // [d_in][MP]
+    const uint16_t* xo;      // [d_in][MP] by union position
     const unsigned int* ctr;
     const float* dpart;      // [nslab][MP][d_out] the INT4 part's partial sums
     uint16_t* y;             // [M][d_out]
@@ -223,7 +255,8 @@ __global__ void __launch_bounds__(kBgOutWarps * 32) bout_kernel(const BOArgs a) 
         const uint32_t db = wb + (k % kBgOutBufs) * 512 + 16 * lane;
         const bool valid = kc < U;
         const int col = valid ? static_cast<int>(ldcg_u32(a.ulist + kc)) : 0;
-        if (valid && (MP == 16 || half == 0)) cp_async16(db, a.xo + static_cast<size_t>(col) * MP + 8 * half);
+        if (kc < ((U + 15) & ~15) && (MP == 16 || half == 0))
+            cp_async16(db, a.xo + static_cast<size_t>(kc) * MP + 8 * half);
         else sts_v4(db, make_uint4(0, 0, 0, 0));
         if (kOut == kBoStaged) {
             if (valid && row0 < a.d_out) cp_async16(da, a.w16_cm + static_cast<size_t>(col) * a.d_out + row0);
@@ -605,6 +638,7 @@ dq_status_t launch_gemv_batched(const dq_weights_t& w, const uint16_t* x, uint16
     pa.masks = reinterpret_cast<uint32_t*>(ws + L.masks);
     pa.ulist = reinterpret_cast<uint32_t*>(ws + L.ulist);
     pa.xo = reinterpret_cast<uint16_t*>(ws + L.xo);
+    pa.xrow = reinterpret_cast<uint16_t*>(ws + L.xrow);
     pa.ctr = reinterpret_cast<unsigned int*>(ws + L.ctr);
     pa.k = k;
     pa.inv_n = 1.0f / static_cast<float>(w.d_in);

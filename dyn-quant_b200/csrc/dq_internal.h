@@ -143,10 +143,11 @@ inline BgGeom bg_geom(int d_out, int d_in, int M) {
 //   ctr    [0] plan arrival counter, [1] union size
 //   masks  [kBgMaxM][W] outlier bits of each vector
 //   ulist  [d_in] the union of the masks, ascending columns
-//   xo     [d_in][MP] FP16: x[m][c] where column c is an outlier of vector m, else 0
+//   xrow   [MP][d_in] FP16: x[m][c] where column c is an outlier of vector m, else 0
+//   xo     [d_in][MP] FP16: xrow[m][ulist[u]] at [u][m], u < U rounded up to 16
 //   dpart  [nslab][MP][d_out] FP32 per-slab partial sums of the INT4 part
 struct BgWs {
-    size_t ctr, masks, ulist, xo, dpart, total;
+    size_t ctr, masks, ulist, xrow, xo, dpart, total;
 };
 
 inline BgWs bg_ws(const BgGeom& g, int d_out, int d_in);
@@ -181,6 +182,7 @@ inline BgWs bg_ws(const BgGeom& g, int d_out, int d_in) {
     L.ctr = off;   off += 256;
     L.masks = off; off += align256(static_cast<size_t>(kBgMaxM) * g.W * 4);
     L.ulist = off; off += align256(static_cast<size_t>(d_in) * 4);
+    L.xrow = off;  off += align256(static_cast<size_t>(d_in) * g.MP * 2);
     L.xo = off;    off += align256(static_cast<size_t>(d_in) * g.MP * 2);
     L.dpart = off; off += align256(static_cast<size_t>(g.nslab) * g.MP * d_out * 4);
     L.total = off;
