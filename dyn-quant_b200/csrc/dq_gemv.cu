@@ -7,26 +7,27 @@
 // src/quant_format.cuh:48-97.
 //
 // One split / INT4 GEMV call is ONE kernel (b1_kernel): a persistent grid of
-// one 256-thread CTA per SM, launched as a programmatic dependent of whatever
-// precedes it on the stream.
-//   1. Each warp starts streaming its first weight units into a 3-stage
-//      shared-memory ring (cp.async.bulk, the non-tensor TMA form, completing
-//      on per-stage mbarriers) before griddepcontrol.wait, so the weight
-//      stream overlaps the tail of the previous kernel.
+// one CTA of 16 warps (12 for the longest rows) per SM, launched as a
+// programmatic dependent of whatever precedes it on the stream.
+//   1. Before griddepcontrol.wait, each CTA pulls its first weight units into
+//      L2 (cp.async.bulk.prefetch), so the weight stream overlaps the previous
+//      kernel.  After the wait each warp streams its units into a ring of
+//      shared-memory stages (cp.async.bulk, the non-tensor TMA form,
+//      completing on per-stage mbarriers).
 //   2. Each CTA derives the activation plan itself from x (<= 60 KB, an L2
 //      hit after the first CTA): the statistics, the outlier mask with the
 //      reference's capacity rule, the ascending outlier list, and the MMA B
 //      fragments of the masked activation x' with per-group sums.
 //   3. The warps run dequant + tensor-core MMAs over their units.  A unit is
 //      16 rows x 4 groups of 128 columns; the units are split evenly across
-//      CTAs (and across the 8 warps of a CTA) in (row block, column chunk)
-//      order.  A 16-row block that straddles two CTAs is finished by whichever
-//      of them arrives last, summing the partial row sums in CTA order (fixed
-//      order: results are bit-reproducible).
-//   4. Outlier columns add W16[r][c] * x[c]: the CTA's row segment of each
-//      outlier column of the column-major FP16 mirror (contiguous, 32 bytes per
-//      row block) is brought into shared memory by one bulk copy per column,
-//      issued right after the list is known, and summed after the unit loop.
+//      CTAs (and across the warps of a CTA) in (row block, column chunk)
+//      order.  A 16-row block that straddles CTAs is finished by the CTA
+//      holding its first chunk, which adds the later CTAs' published partial
+//      row sums in CTA order (fixed order: results are bit-reproducible).
+//   4. Outlier columns add W16[r][c] * x[c] on the tensor cores as well: tasks
+//      of (16-row block, 16 outlier columns) run between a warp's units, their
+//      column segments (32 contiguous bytes per row block in the column-major
+//      FP16 mirror) brought in by cp.async and read with ldmatrix.trans.
 //
 // Tensor-core formulation (mma.sync.m16n8k16, f16 x f16 -> f32).  Lane
 // (g, t) of a warp holds group t of the unit's 4-group chunk: A comes from the
@@ -74,6 +75,7 @@ struct B1Args {
     float k;
     float inv_n, inv_n1;      // 1/d_in, 1/(d_in - 1) for the statistics of x
     int d_out, d_in, NC, U, nrb_max;
+    int depth;                // ring stages per warp (reference layout: kB1Stages)
     B1Smem S;
 };
 
@@ -94,8 +96,9 @@ __host__ __device__ inline int unit_owner(long long u, int P, long long U) {
 
 // kNative: weights in the unit layout (one bulk copy per unit, scale/zero
 // inside); otherwise the reference layout (one bulk copy per weight row of the
-// unit, scale/zero by plain loads).
-template <bool kSplit, bool kNative, int kOut, int kW>
+// unit, scale/zero by plain loads).  kR: rounds of x held in registers by the
+// plan (at least ceil(NC / 8)).
+template <bool kSplit, bool kNative, int kOut, int kW, int kR>
 __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
     constexpr int kT = kW * 32;
     extern __shared__ __align__(128) char smem[];
@@ -126,8 +129,12 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
     const int orb0 = contrib ? rbf + 1 : rbf;  // outlier rows of this CTA: row blocks orb0 .. rbz
     const size_t row_stride = static_cast<size_t>(a.d_in) / 2;
 
-    const uint32_t ring = smem_u32(smem + a.S.ring) + warp * kStages * kStageBytes;
-    const uint32_t bars = smem_u32(smem + a.S.bars) + warp * kStages * 8;
+    // Ring: this warp's i-th unit goes to slot warp + kW (i % D), D stages per
+    // warp (as many as fit next to the plan, at least kB1Stages).
+    const int D = kNative ? a.depth : kStages;
+    const uint32_t ring = smem_u32(smem + a.S.ring);
+    const uint32_t bars = smem_u32(smem + a.S.bars);
+    auto slot_of = [&](int k) -> int { return warp + kW * k; };
     float* part = reinterpret_cast<float*>(smem + a.S.part);    // [row block][warp][16]
     float* opart = reinterpret_cast<float*>(smem + a.S.opart);  // [warp][row block][16]
     uint4* xb = reinterpret_cast<uint4*>(smem + a.S.bsm);
@@ -137,8 +144,7 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
     uint32_t* list = reinterpret_cast<uint32_t*>(smem + a.S.list);
 
     if (lane == 0) {
-#pragma unroll
-        for (int s = 0; s < kStages; ++s) mbar_init(bars + 8 * s, 1);
+        for (int k = 0; k < D && k < wn; ++k) mbar_init(bars + 8 * slot_of(k), 1);
         fence_mbar_init();
     }
     for (int i = tid; i < nrb * kW * 16; i += kT) part[i] = 0.f;
@@ -149,14 +155,16 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
 
     uint32_t szr0[kStages], szr8[kStages];  // reference layout: (scale, zero) of lane t's group, rows g, g+8
 
-    // Weight bytes of unit u into stage s.
+    // Weight bytes of unit u into stage s (s < D; compile-time for the
+    // reference layout, whose scale/zero go to registers).
     auto issue = [&](int s, int u) {
         const int rb = u / NC, cc = u - rb * NC;
-        const uint32_t bar = bars + 8 * s;
+        const uint32_t bar = bars + 8 * slot_of(s);
+        const uint32_t dst = ring + slot_of(s) * kStageBytes;
         if (kNative) {
             if (lane == 0) {
                 mbar_arrive_expect_tx(bar, kB1UnitBytes);
-                bulk_g2s(ring + s * kStageBytes, a.native + static_cast<size_t>(u) * kB1UnitBytes, kB1UnitBytes, bar);
+                bulk_g2s(dst, a.native + static_cast<size_t>(u) * kB1UnitBytes, kB1UnitBytes, bar);
             }
         } else {
             const int rbase = rb * kRowBlock;
@@ -166,7 +174,7 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
             if (lane == 0) mbar_arrive_expect_tx(bar, vrows * rbytes);
             __syncwarp();
             if (lane < vrows)
-                bulk_g2s(ring + s * kStageBytes + lane * kB1RowPitch,
+                bulk_g2s(dst + lane * kB1RowPitch,
                          a.packed + static_cast<size_t>(rbase + lane) * row_stride + 256 * static_cast<size_t>(cc),
                          rbytes, bar);
             const int j = kCG * cc + t;
@@ -182,29 +190,34 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
         }
     };
 
-    // The first unit of each warp goes out before the previous kernel has
-    // finished; x is requested next, ahead of the second stage, because the
-    // plan (and so every MMA) waits for it.
-    // The first units of each warp do not depend on the preceding kernel: they
-    // are pulled into L2 before griddepcontrol.wait.  After it, x is requested
-    // first (straight into registers), then the units' bulk copies, which hit
-    // L2 and so do not hold x up behind the weight stream.
-    if (kNative && lane == 0) {
-#pragma unroll
-        for (int s = 0; s < kStages; ++s)
-            if (s < wn)
-                prefetch_l2_bulk(a.native + static_cast<size_t>(cu0 + warp + kW * s) * kB1UnitBytes, kB1UnitBytes);
-    }
+    // The weights do not depend on the preceding kernel: each warp's first
+    // kB1Stages units are pulled into L2 before griddepcontrol.wait (native
+    // layout).  After the wait x is requested first, straight into registers,
+    // then the ring's first fill, which so does not hold x up.  (Copying the
+    // units into shared memory before the wait, or all of a CTA's share at
+    // once, puts the weight stream in front of x on the SM's return path and
+    // made chains of GEMVs slower.)
+    const int fill = min(wn, D);
+    uint32_t armed = 0;  // stages with a copy in flight
+    if (kNative && lane == 0)
+        for (int k = 0; k < fill && k < kB1Stages; ++k)
+            prefetch_l2_bulk(a.native + static_cast<size_t>(cu0 + warp + kW * k) * kB1UnitBytes, kB1UnitBytes);
     pdl_launch_dependents();
     pdl_wait();  // x, y and the workspace may belong to the preceding kernel until here
-    XRegs<kT> xr;
+    XRegs<kT, kR> xr;
     x_regs_load_global<kT>(a.x, n8, xr);
-    uint32_t armed = 0;
+    if (kNative) {
+        for (int k = 0; k < fill; ++k) {
+            issue(k, cu0 + warp + kW * k);
+            armed |= 1u << k;
+        }
+    } else {
 #pragma unroll
-    for (int s = 0; s < kStages; ++s) {
-        if (s < wn) {
-            issue(s, cu0 + warp + kW * s);
-            armed |= 1u << s;
+        for (int s = 0; s < kStages; ++s) {
+            if (s < wn) {
+                issue(s, cu0 + warp + kW * s);
+                armed |= 1u << s;
+            }
         }
     }
 
@@ -219,9 +232,9 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
             // The reference's capacity rule may drop outliers: derive the mask
             // from x in natural order, then rebuild the fragments and the list.
 #pragma unroll
-            for (int q = 0; q < XRegs<kT>::VPT; ++q)
+            for (int q = 0; q < XRegs<kT, kR>::VPT; ++q)
 #pragma unroll
-                for (int rr = 0; rr < kPlanRounds; ++rr) {
+                for (int rr = 0; rr < kR; ++rr) {
                     const int v = plan_vthread<kT>(q), p = v + kStatThreads * rr;
                     if (v < kStatThreads && p < n8) xb[p] = xr.v[q][rr];
                 }
@@ -346,101 +359,115 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
     const uint32_t b_lane = t * 16 + (g & 1) * 8;
     float acc0 = 0.f, acc8 = 0.f;
     bool ok = true;
-    uint32_t phase = 0;
-    for (int ib = 0; ib < wn && ok; ib += kStages) {
+    uint32_t phase = 0;  // per stage: parity of the next completion
+    // Unit i of this warp, in stage s, whose copy has landed.  sz0 / sz8: the
+    // reference layout's (scale, zero) registers of the stage.
+    auto consume = [&](int i, int s, uint32_t sz0, uint32_t sz8) {
+        const uint32_t st = ring + slot_of(s) * kStageBytes;
+        const int u = cu0 + warp + kW * i;
+        const int rb = u / NC, cc = u - rb * NC;
+        uint4 aw[4][2];  // [slice][row g / g+8]: 32 columns of group t
 #pragma unroll
-        for (int s = 0; s < kStages; ++s) {
-            const int i = ib + s;
-            if (i < wn && ok) {
-                const bool got = mbar_wait_bounded(bars + 8 * s, (phase >> s) & 1u);
-                if (!__all_sync(0xffffffffu, got)) {
-                    ok = false;
-                    if (lane == 0) atomicOr(&g_error_word, 1u);
-                } else {
-                    phase ^= 1u << s;
-                    armed &= ~(1u << s);
-                    const int u = cu0 + warp + kW * i;
-                    const int rb = u / NC, cc = u - rb * NC;
-                    const uint32_t st = ring + s * kStageBytes;
-                    uint4 aw[4][2];  // [slice][row g / g+8]: 32 columns of group t
+        for (int sl = 0; sl < 4; ++sl)
 #pragma unroll
-                    for (int sl = 0; sl < 4; ++sl)
+            for (int h = 0; h < 2; ++h)
+                aw[sl][h] = kNative ? lds_v4(st + native_piece(sl, h, g, t) * 16)
+                                    : lds_v4(st + (g + 8 * h) * kB1RowPitch + 64 * t + 16 * sl);
+        const uint32_t bb = (b_owner ? bsm_a + cc * kB1ChunkB : zero_a) + b_lane;
+        float dl[4][4], dh[4][4];
 #pragma unroll
-                        for (int h = 0; h < 2; ++h)
-                            aw[sl][h] = kNative ? lds_v4(st + native_piece(sl, h, g, t) * 16)
-                                                : lds_v4(st + (g + 8 * h) * kB1RowPitch + 64 * t + 16 * sl);
-                    const uint32_t bb = (b_owner ? bsm_a + cc * kB1ChunkB : zero_a) + b_lane;
-                    float dl[4][4], dh[4][4];
+        for (int sl = 0; sl < 4; ++sl)
 #pragma unroll
-                    for (int sl = 0; sl < 4; ++sl)
+            for (int q = 0; q < 4; ++q) dl[sl][q] = dh[sl][q] = 0.f;
 #pragma unroll
-                        for (int q = 0; q < 4; ++q) dl[sl][q] = dh[sl][q] = 0.f;
+        for (int wi = 0; wi < 4; ++wi) {
 #pragma unroll
-                    for (int wi = 0; wi < 4; ++wi) {
+            for (int sl = 0; sl < 4; ++sl) {
+                const Biased4 qa = biased_word(word_of(aw[sl][0], wi));
+                const Biased4 qb = biased_word(word_of(aw[sl][1], wi));
+                const uint2 b = lds_v2(bb + (wi * 4 + sl) * 64);
+                mma_16816(dl[sl], qa.lo0, qb.lo0, qa.lo1, qb.lo1, b.x, b.y);
+                mma_16816(dh[sl], qa.hi0, qb.hi0, qa.hi1, qb.hi1, b.x, b.y);
+            }
+        }
+        const float lo0 = (dl[0][0] + dl[1][0]) + (dl[2][0] + dl[3][0]);
+        const float hi0 = (dh[0][1] + dh[1][1]) + (dh[2][1] + dh[3][1]);
+        const float lo8 = (dl[0][2] + dl[1][2]) + (dl[2][2] + dl[3][2]);
+        const float hi8 = (dh[0][3] + dh[1][3]) + (dh[2][3] + dh[3][3]);
+        if (kNative) {
+            sz0 = lds_u32(st + kB1UnitPacked + 16 * g + 4 * t);
+            sz8 = lds_u32(st + kB1UnitPacked + 16 * (g + 8) + 4 * t);
+        }
+        const uint4 xqb = lds_v4(xp_a + (kCG * cc + t) * 16);
+        const float xe = __uint_as_float(xqb.x), xo = __uint_as_float(xqb.y), xs = __uint_as_float(xqb.z);
+        const float S0 = fmaf(hi0 - xo, 0.0625f, lo0 - xe);
+        const float S8 = fmaf(hi8 - xo, 0.0625f, lo8 - xe);
+        acc0 = fmaf(h2f_bits(lo16(sz0)), fmaf(-h2f_bits(hi16(sz0)), xs, S0), acc0);
+        acc8 = fmaf(h2f_bits(lo16(sz8)), fmaf(-h2f_bits(hi16(sz8)), xs, S8), acc8);
+        const bool last_in_rb = i == wn - 1 || u + kW >= (rb + 1) * NC;
+        if (last_in_rb) {
+            // This warp is done with row block rb: publish its row sums.
+            acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+            acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+            acc8 += __shfl_xor_sync(0xffffffffu, acc8, 1);
+            acc8 += __shfl_xor_sync(0xffffffffu, acc8, 2);
+            if (t == 0) {
+                float* pp = part + ((rb - rbf) * kW + warp) * 16;
+                pp[g] = acc0;
+                pp[g + 8] = acc8;
+            }
+            acc0 = acc8 = 0.f;
+        }
+        __syncwarp();
+        if (i + D < wn) {
+            issue(s, u + kW * D);
+            armed |= 1u << s;
+        }
+        if (last_in_rb && rb == rbf && pub_pending) {
+            publish_first();
+            pub_pending = false;
+        }
+        if (finaliser && c_hi == c + 1 && warp == 0 && i == wn / 2)
+            early = ld_relaxed_gpu_u64(a.fix + (c + 1) * 16 + (lane & 15));
+        // outlier tasks, spread evenly over this warp's units
+        const int target = min(ntk, (ntk * (i + 1) + wn - 1) / wn);
+        for (; o_done < target; ++o_done) o_step(o_done);
+    };
+    if (kNative) {
+        for (int i = 0, s = 0; i < wn && ok; ++i, s = (s + 1 == D) ? 0 : s + 1) {
+            const bool got = mbar_wait_bounded(bars + 8 * slot_of(s), (phase >> s) & 1u);
+            if (!__all_sync(0xffffffffu, got)) {
+                ok = false;
+                if (lane == 0) atomicOr(&g_error_word, 1u);
+            } else {
+                phase ^= 1u << s;
+                armed &= ~(1u << s);
+                consume(i, s, 0u, 0u);
+            }
+        }
+    } else {
+        for (int ib = 0; ib < wn && ok; ib += kStages) {
 #pragma unroll
-                        for (int sl = 0; sl < 4; ++sl) {
-                            const Biased4 qa = biased_word(word_of(aw[sl][0], wi));
-                            const Biased4 qb = biased_word(word_of(aw[sl][1], wi));
-                            const uint2 b = lds_v2(bb + (wi * 4 + sl) * 64);
-                            mma_16816(dl[sl], qa.lo0, qb.lo0, qa.lo1, qb.lo1, b.x, b.y);
-                            mma_16816(dh[sl], qa.hi0, qb.hi0, qa.hi1, qb.hi1, b.x, b.y);
-                        }
-                    }
-                    const float lo0 = (dl[0][0] + dl[1][0]) + (dl[2][0] + dl[3][0]);
-                    const float hi0 = (dh[0][1] + dh[1][1]) + (dh[2][1] + dh[3][1]);
-                    const float lo8 = (dl[0][2] + dl[1][2]) + (dl[2][2] + dl[3][2]);
-                    const float hi8 = (dh[0][3] + dh[1][3]) + (dh[2][3] + dh[3][3]);
-                    uint32_t sz0, sz8;
-                    if (kNative) {
-                        sz0 = lds_u32(st + kB1UnitPacked + 16 * g + 4 * t);
-                        sz8 = lds_u32(st + kB1UnitPacked + 16 * (g + 8) + 4 * t);
+            for (int s = 0; s < kStages; ++s) {
+                const int i = ib + s;
+                if (i < wn && ok) {
+                    const bool got = mbar_wait_bounded(bars + 8 * slot_of(s), (phase >> s) & 1u);
+                    if (!__all_sync(0xffffffffu, got)) {
+                        ok = false;
+                        if (lane == 0) atomicOr(&g_error_word, 1u);
                     } else {
-                        sz0 = szr0[s];
-                        sz8 = szr8[s];
+                        phase ^= 1u << s;
+                        armed &= ~(1u << s);
+                        consume(i, s, szr0[s], szr8[s]);
                     }
-                    const uint4 xqb = lds_v4(xp_a + (kCG * cc + t) * 16);
-                    const float xe = __uint_as_float(xqb.x), xo = __uint_as_float(xqb.y), xs = __uint_as_float(xqb.z);
-                    const float S0 = fmaf(hi0 - xo, 0.0625f, lo0 - xe);
-                    const float S8 = fmaf(hi8 - xo, 0.0625f, lo8 - xe);
-                    acc0 = fmaf(h2f_bits(lo16(sz0)), fmaf(-h2f_bits(hi16(sz0)), xs, S0), acc0);
-                    acc8 = fmaf(h2f_bits(lo16(sz8)), fmaf(-h2f_bits(hi16(sz8)), xs, S8), acc8);
-                    const bool last_in_rb = i == wn - 1 || u + kW >= (rb + 1) * NC;
-                    if (last_in_rb) {
-                        // This warp is done with row block rb: publish its row sums.
-                        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
-                        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
-                        acc8 += __shfl_xor_sync(0xffffffffu, acc8, 1);
-                        acc8 += __shfl_xor_sync(0xffffffffu, acc8, 2);
-                        if (t == 0) {
-                            float* pp = part + ((rb - rbf) * kW + warp) * 16;
-                            pp[g] = acc0;
-                            pp[g + 8] = acc8;
-                        }
-                        acc0 = acc8 = 0.f;
-                    }
-                    __syncwarp();
-                    if (i + kStages < wn) {
-                        issue(s, u + kW * kStages);
-                        armed |= 1u << s;
-                    }
-                    if (last_in_rb && rb == rbf && pub_pending) {
-                        publish_first();
-                        pub_pending = false;
-                    }
-                    if (finaliser && c_hi == c + 1 && warp == 0 && i == wn / 2)
-                        early = ld_relaxed_gpu_u64(a.fix + (c + 1) * 16 + (lane & 15));
-                    // outlier tasks, spread evenly over this warp's units
-                    const int target = min(ntk, (ntk * (i + 1) + wn - 1) / wn);
-                    for (; o_done < target; ++o_done) o_step(o_done);
                 }
             }
         }
     }
     if (!ok) {
         // Do not leave copies in flight into shared memory this CTA is about to release.
-#pragma unroll
-        for (int s = 0; s < kStages; ++s)
-            if (armed & (1u << s)) mbar_wait_bounded(bars + 8 * s, (phase >> s) & 1u);
+        for (int k = 0; k < D; ++k)
+            if (armed & (1u << k)) mbar_wait_bounded(bars + 8 * slot_of(k), (phase >> k) & 1u);
     }
     if (pub_pending) publish_first();  // error path: keep named barrier 1 balanced
     for (; o_done < ntk; ++o_done) o_step(o_done);  // warps without units, error path
@@ -784,7 +811,7 @@ __global__ void colmajor_kernel(const uint16_t* __restrict__ w, int d_out, int d
 
 // Per-device, per-kernel "max dynamic shared memory" opt-in, done once.
 constexpr int kMaxDevices = 64;
-constexpr int kNumKernels = 64;
+constexpr int kNumKernels = 144;
 int g_smem_set[kMaxDevices][kNumKernels];  // bytes already opted in (0 = none)
 
 template <class K>
@@ -796,6 +823,9 @@ dq_status_t ensure_smem(K kernel, int id, int bytes) {
         return DQ_OK;
     const int want = bytes < 48 * 1024 ? 48 * 1024 : bytes;
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, want);
+    if (e != cudaSuccess) { set_cuda_error(e); return DQ_ERR_CUDA; }
+    // all of the unified L1 / shared memory as shared memory (two 113 KB CTAs per SM)
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) { set_cuda_error(e); return DQ_ERR_CUDA; }
     if (dev >= 0 && dev < kMaxDevices) {
         int cur = __atomic_load_n(&g_smem_set[dev][id], __ATOMIC_ACQUIRE);
@@ -813,10 +843,13 @@ dq_status_t check_launch() {
 }
 
 
-template <bool kSplit, bool kNative, int kOut, int kW>
+template <bool kSplit, bool kNative, int kOut, int kW, int kR>
 dq_status_t launch_b1(const B1Args& a, int grid, cudaStream_t stream) {
-    constexpr int id = 4 + (kW == kB1Warps ? 0 : 16) + (kSplit ? 8 : 0) + (kNative ? 4 : 0) + kOut;
-    const dq_status_t st = ensure_smem(b1_kernel<kSplit, kNative, kOut, kW>, id, a.S.total);
+    constexpr int wi = kW == kB1Warps ? 0 : 1;
+    constexpr int ri = kR == 1 ? 0 : kR == 2 ? 1 : kR == 4 ? 2 : 3;
+    constexpr int id = 4 + 16 * (4 * wi + ri) + (kSplit ? 8 : 0) + (kNative ? 4 : 0) + kOut;
+    static_assert(id < kNumKernels, "kernel attribute slot");
+    const dq_status_t st = ensure_smem(b1_kernel<kSplit, kNative, kOut, kW, kR>, id, a.S.total);
     if (st != DQ_OK) return st;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -828,25 +861,35 @@ dq_status_t launch_b1(const B1Args& a, int grid, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, b1_kernel<kSplit, kNative, kOut, kW>, a);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, b1_kernel<kSplit, kNative, kOut, kW, kR>, a);
     if (e != cudaSuccess) { set_cuda_error(e); return DQ_ERR_CUDA; }
     return check_launch();
 }
 
-template <bool kSplit, int kOut, int kW>
-dq_status_t launch_b1_layout(const B1Args& a, int grid, cudaStream_t stream) {
-    return a.native ? launch_b1<kSplit, true, kOut, kW>(a, grid, stream)
-                    : launch_b1<kSplit, false, kOut, kW>(a, grid, stream);
+template <bool kNative, int kW, int kR>
+dq_status_t launch_b1_out(const B1Args& a, int out_mode, int grid, cudaStream_t stream) {
+    switch (out_mode) {
+        case kOutStaged: return launch_b1<true, kNative, kOutStaged, kW, kR>(a, grid, stream);
+        case kOutColDirect: return launch_b1<true, kNative, kOutColDirect, kW, kR>(a, grid, stream);
+        case kOutRowDirect: return launch_b1<true, kNative, kOutRowDirect, kW, kR>(a, grid, stream);
+        default: return launch_b1<false, kNative, kOutNone, kW, kR>(a, grid, stream);
+    }
 }
 
 template <int kW>
-dq_status_t launch_b1_warps(const B1Args& a, int out_mode, int grid, cudaStream_t stream) {
-    switch (out_mode) {
-        case kOutStaged: return launch_b1_layout<true, kOutStaged, kW>(a, grid, stream);
-        case kOutColDirect: return launch_b1_layout<true, kOutColDirect, kW>(a, grid, stream);
-        case kOutRowDirect: return launch_b1_layout<true, kOutRowDirect, kW>(a, grid, stream);
-        default: return launch_b1_layout<false, kOutNone, kW>(a, grid, stream);
-    }
+dq_status_t launch_b1_native(const B1Args& a, int out_mode, int rounds, int grid, cudaStream_t stream) {
+    if (rounds <= 1) return launch_b1_out<true, kW, 1>(a, out_mode, grid, stream);
+    if (rounds <= 2) return launch_b1_out<true, kW, 2>(a, out_mode, grid, stream);
+    if (rounds <= 4) return launch_b1_out<true, kW, 4>(a, out_mode, grid, stream);
+    return launch_b1_out<true, kW, kPlanRounds>(a, out_mode, grid, stream);
+}
+
+dq_status_t launch_b1_warps(const B1Args& a, int warps, int out_mode, int rounds, int grid, cudaStream_t stream) {
+    if (!a.native)
+        return warps == kB1Warps ? launch_b1_out<false, kB1Warps, kPlanRounds>(a, out_mode, grid, stream)
+                                 : launch_b1_out<false, kB1WarpsSmall, kPlanRounds>(a, out_mode, grid, stream);
+    return warps == kB1Warps ? launch_b1_native<kB1Warps>(a, out_mode, rounds, grid, stream)
+                             : launch_b1_native<kB1WarpsSmall>(a, out_mode, rounds, grid, stream);
 }
 
 }  // namespace
@@ -888,19 +931,37 @@ dq_status_t launch_gemv_b1(const dq_weights_t& w, const uint16_t* x, uint16_t* y
         if (n > nrb_max) nrb_max = n;
     }
     a.nrb_max = nrb_max;
+    const int rounds = (NC + 7) / 8;  // plan rounds of x per virtual thread
 
     int out_mode = kOutNone;
     if (split) out_mode = w.fp16_cm ? ((w.d_out % 8) == 0 ? kOutStaged : kOutColDirect) : kOutRowDirect;
-    // 16 warps where their rings fit next to x and the plan, else 12.
+    if (w.native) {
+        // A ring of as many stages per warp as fit (at least kB1Stages, no more
+        // than a warp has units), 16 warps or 12.
+        const int u_warp = ((a.U + grid - 1) / grid + kB1WarpsSmall - 1) / kB1WarpsSmall;
+        const int ring_warps[2] = {kB1Warps, kB1WarpsSmall};
+        for (int warps : ring_warps) {
+            for (int depth = kB1MaxDepth; depth >= kB1Stages; --depth) {
+                if (depth > kB1Stages && depth > u_warp) continue;
+                a.S = b1_smem(w.d_in, nrb_max, split, warps, warps * depth);
+                if (a.S.total > di.smem_optin) continue;
+                a.depth = depth;
+                return launch_b1_warps(a, warps, out_mode, rounds, grid, stream);
+            }
+        }
+        return DQ_ERR_UNSUPPORTED;
+    }
+    // Reference layout: kB1Stages per warp, 16 warps where their rings fit next
+    // to x and the plan, else 12.
+    a.depth = kB1Stages;
     int warps = kB1Warps;
-    a.S = b1_smem(w.d_in, nrb_max, split, warps);
+    a.S = b1_smem(w.d_in, nrb_max, split, warps, warps * kB1Stages);
     if (a.S.total > di.smem_optin) {
         warps = kB1WarpsSmall;
-        a.S = b1_smem(w.d_in, nrb_max, split, warps);
+        a.S = b1_smem(w.d_in, nrb_max, split, warps, warps * kB1Stages);
     }
     if (a.S.total > di.smem_optin) return DQ_ERR_UNSUPPORTED;
-    return warps == kB1Warps ? launch_b1_warps<kB1Warps>(a, out_mode, grid, stream)
-                             : launch_b1_warps<kB1WarpsSmall>(a, out_mode, grid, stream);
+    return launch_b1_warps(a, warps, out_mode, rounds, grid, stream);
 }
 
 dq_status_t launch_build_native(const uint8_t* packed, const uint16_t* scales, const uint16_t* zeros,

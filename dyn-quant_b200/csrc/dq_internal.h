@@ -13,7 +13,8 @@ namespace dq {
 // device carving).
 constexpr int kB1Warps = 16;                         // warps per CTA (one CTA per SM), at most
 constexpr int kB1WarpsSmall = 12;                    // when 16 warps' rings do not fit next to x
-constexpr int kB1Stages = 2;                         // bulk-copy ring stages per warp
+constexpr int kB1MaxDepth = 8;                       // ring stages per warp, at most
+constexpr int kB1Stages = 2;                         // ring stages per warp, reference layout (native: at least)
 constexpr int kB1ChunkGroups = 4;                    // 128-column groups per unit
 constexpr int kB1UnitPacked = 4096;                  // packed INT4 of one unit (16 rows x 512 columns)
 constexpr int kB1StageSZ = 256;                      // 16 rows x 4 groups x (scale, zero)
@@ -25,7 +26,6 @@ constexpr int kB1RedBytes = 2048;                    // reduction / scan scratch
 constexpr int kB1OutBatch = 16;                      // outlier columns per tensor-core task
 constexpr int kB1OutBufs = 3;                        // per-warp task buffers in flight
 constexpr int kB1OutBufBytes = kB1OutBatch * 32;     // 16 columns x 16 rows of FP16
-constexpr int kB1BarBytes = (kB1Warps * kB1Stages * 8 + 127) / 128 * 128;  // one mbarrier per stage and warp
 constexpr int kStatThreads = 512;                    // fixed partition of the statistics of x
 constexpr int kMaxCtas = 1024;                       // bound on the GEMV grid (workspace sizing)
 
@@ -33,8 +33,8 @@ __host__ __device__ inline int align16(int v) { return (v + 15) & ~15; }
 
 // Shared memory of one batch-1 GEMV CTA with `warps` warps.  Every CTA derives
 // the activation plan itself (x is at most 60 KB and stays in L2):
-//   ring  per-warp stages of weight units
-//   bars  the stage barriers
+//   ring  slots of weight units (a warp's i-th unit in slot warp + warps (i % depth))
+//   bars  one mbarrier per slot
 //   zero  1 KB of zeros (B operand of lanes outside their column pair)
 //   bsm   x, then in place the MMA B fragments of x' (outliers zeroed), NC chunks
 //   xp    per group float4 (1024 sum x' even cols, 1024 sum x' odd cols, sum x', 0)
@@ -48,12 +48,13 @@ struct B1Smem {
     int ring, bars, zero, bsm, xp, mask, red, part, opart, list, obuf, total;
 };
 
-inline B1Smem b1_smem(int d_in, int nrb_max, bool split, int warps) {
+// slots: ring slots of kB1StageBytes, each with its mbarrier.
+inline B1Smem b1_smem(int d_in, int nrb_max, bool split, int warps, int slots) {
     const int NC = (d_in / 128 + kB1ChunkGroups - 1) / kB1ChunkGroups;
     B1Smem S;
     int off = 0;
-    S.ring = off;  off += warps * kB1Stages * kB1StageBytes;
-    S.bars = off;  off += kB1BarBytes;
+    S.ring = off;  off += slots * kB1StageBytes;
+    S.bars = off;  off += (slots * 8 + 127) / 128 * 128;
     S.zero = off;  off += kB1ChunkB;
     S.bsm = off;   off += NC * kB1ChunkB;
     S.xp = off;    off += NC * kB1ChunkGroups * 16;

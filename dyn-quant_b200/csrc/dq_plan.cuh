@@ -259,10 +259,13 @@ __device__ int x_mask_list(const uint4* xs, int d_in, float mean, float thresh, 
 // ---------------------------------------------------------------------------
 constexpr int kPlanRounds = (kMaxDIn / 8 + kStatThreads - 1) / kStatThreads;
 
-template <int NT>
+// R: rounds held, ceil(d_in / (8 kStatThreads)) or more (fewer registers for
+// the kernels of short rows).
+template <int NT, int R = kPlanRounds>
 struct XRegs {
     static constexpr int VPT = (kStatThreads + NT - 1) / NT;  // virtual threads per thread
-    uint4 v[VPT][kPlanRounds];
+    static constexpr int RND = R;
+    uint4 v[VPT][R];
 };
 
 // Virtual thread q of this thread (kStatThreads or more: none).
@@ -277,12 +280,12 @@ __device__ __forceinline__ bool plan_warp_has(int q) {
     return q == 0 || static_cast<int>(threadIdx.x & ~31u) + q * NT < kStatThreads;
 }
 
-template <int NT>
-__device__ __forceinline__ void x_regs_load_global(const uint16_t* __restrict__ x, int n8, XRegs<NT>& r) {
+template <int NT, int R>
+__device__ __forceinline__ void x_regs_load_global(const uint16_t* __restrict__ x, int n8, XRegs<NT, R>& r) {
 #pragma unroll
-    for (int q = 0; q < XRegs<NT>::VPT; ++q)
+    for (int q = 0; q < XRegs<NT, R>::VPT; ++q)
 #pragma unroll
-        for (int rr = 0; rr < kPlanRounds; ++rr) {
+        for (int rr = 0; rr < R; ++rr) {
             const int v = plan_vthread<NT>(q), p = v + kStatThreads * rr;
             uint4 val = make_uint4(0, 0, 0, 0);
             if (v < kStatThreads && p < n8) val = ldcg_v4(x + 8 * static_cast<size_t>(p));
@@ -292,18 +295,18 @@ __device__ __forceinline__ void x_regs_load_global(const uint16_t* __restrict__ 
 
 // x_stats over the registers (pieces past d_in hold zeros).  red: 2
 // kStatThreads/32 floats, 16-byte aligned, not in use; two barriers.
-template <int NT>
-__device__ __forceinline__ XStats x_stats_regs(const XRegs<NT>& r, int n8, int d_in, float k, float inv_n,
+template <int NT, int R>
+__device__ __forceinline__ XStats x_stats_regs(const XRegs<NT, R>& r, int n8, int d_in, float k, float inv_n,
                                                float inv_n1, float* red) {
     constexpr int NWV = kStatThreads / 32;
     const int lane = threadIdx.x & 31;
 #pragma unroll
-    for (int q = 0; q < XRegs<NT>::VPT; ++q) {
+    for (int q = 0; q < XRegs<NT, R>::VPT; ++q) {
         if (!plan_warp_has<NT>(q)) break;
         const int v = plan_vthread<NT>(q);
         float s[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int rr = 0; rr < kPlanRounds; ++rr) {
+        for (int rr = 0; rr < R; ++rr) {
             if (kStatThreads * rr >= n8) break;  // uniform
             if (v + kStatThreads * rr < n8) {
 #pragma unroll
@@ -320,12 +323,12 @@ __device__ __forceinline__ XStats x_stats_regs(const XRegs<NT>& r, int n8, int d
     XStats st;
     st.mean = __fmul_rn(sum16_tree(red), inv_n);
 #pragma unroll
-    for (int q = 0; q < XRegs<NT>::VPT; ++q) {
+    for (int q = 0; q < XRegs<NT, R>::VPT; ++q) {
         if (!plan_warp_has<NT>(q)) break;
         const int v = plan_vthread<NT>(q);
         float m[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int rr = 0; rr < kPlanRounds; ++rr) {
+        for (int rr = 0; rr < R; ++rr) {
             if (kStatThreads * rr >= n8) break;
             if (v + kStatThreads * rr < n8) {
 #pragma unroll
@@ -375,23 +378,23 @@ __device__ __forceinline__ uint32_t piece_bits(const uint4& v, float mean, float
 // returns the outlier count (every thread); the list is complete after the
 // caller's next barrier.  When the count exceeds cap the list is not written
 // (the caller applies the reference's capacity rule with x_mask_list).
-template <int NT, bool kMask>
-__device__ __forceinline__ int x_frags_regs(const XRegs<NT>& r, int n8, int NC, float mean, float thresh,
+template <int NT, bool kMask, int R>
+__device__ __forceinline__ int x_frags_regs(const XRegs<NT, R>& r, int n8, int NC, float mean, float thresh,
                                             const uint32_t* mask32, int cap, uint4* xb, float4* xp4,
                                             uint32_t* list, int* wcnt) {
     constexpr int NW = NT / 32;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int npc = 64 * NC;  // pieces of all chunks
-    uint32_t bits[XRegs<NT>::VPT][kPlanRounds];
+    uint32_t bits[XRegs<NT, R>::VPT][R];
     int cnt = 0;
 #pragma unroll
-    for (int q = 0; q < XRegs<NT>::VPT; ++q) {
+    for (int q = 0; q < XRegs<NT, R>::VPT; ++q) {
 #pragma unroll
-        for (int rr = 0; rr < kPlanRounds; ++rr) bits[q][rr] = 0;
+        for (int rr = 0; rr < R; ++rr) bits[q][rr] = 0;
         if (!plan_warp_has<NT>(q)) continue;
         const int v = plan_vthread<NT>(q);
 #pragma unroll
-        for (int rr = 0; rr < kPlanRounds; ++rr) {
+        for (int rr = 0; rr < R; ++rr) {
             if (kStatThreads * rr >= npc) break;  // uniform: no piece of this round in any chunk
             const int p = v + kStatThreads * rr;
             uint4 w = r.v[q][rr];
@@ -459,10 +462,10 @@ __device__ __forceinline__ int x_frags_regs(const XRegs<NT>& r, int n8, int NC, 
     if (total > cap) return total;
     int pos = base + before;
 #pragma unroll
-    for (int q = 0; q < XRegs<NT>::VPT; ++q) {
+    for (int q = 0; q < XRegs<NT, R>::VPT; ++q) {
         const int v = plan_vthread<NT>(q);
 #pragma unroll
-        for (int rr = 0; rr < kPlanRounds; ++rr) {
+        for (int rr = 0; rr < R; ++rr) {
             uint32_t b = bits[q][rr];
             while (b) {
                 const int e = __ffs(b) - 1;

@@ -168,8 +168,9 @@ DQ_API dq_status_t dq_split_gemv_noalloc(const dq_weights_t* w, const uint16_t* 
  * ZERO-FILLED before its first use.  It begins with the batch-1 region (so one
  * workspace serves both entry points and every shape it is large enough for),
  * then one arrival counter that every call leaves at zero again, then scratch
- * that each call overwrites (per-row-block counters, masks, the outlier union,
- * partial sums).  Calls that share a workspace must not overlap on the GPU.
+ * that each call overwrites (masks, the outlier-only rows, the outlier union
+ * and its activation table, per-slab partial sums).  Calls that share a
+ * workspace must not overlap on the GPU.
  * After a call reports a device error (dq_read_device_error) zero-fill the
  * workspace again.  0 on invalid shapes.
  */
