@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstring>
 #include <mutex>
 
 #include "dq_internal.h"
@@ -193,6 +194,69 @@ dq_status_t dq_split_gemv(const dq_weights_t* w, const uint16_t* x, uint16_t* y,
     dq_status_t st = check_weights(w, x, y, true, workspace, workspace_bytes);
     if (st != DQ_OK) return st;
     return launch_gemv_b1(*w, x, y, outlier_k, true, workspace, static_cast<cudaStream_t>(stream));
+}
+
+size_t dq_gather_region_bytes(int32_t rows_per) {
+    if (rows_per <= 0 || rows_per % 16 != 0) return 0;
+    return gather_layout(rows_per).total;
+}
+
+dq_status_t dq_split_gemv_gather(const dq_weights_t* w, const uint16_t* x, uint16_t* y, float outlier_k,
+                                 void* workspace, size_t workspace_bytes, const dq_gather_t* g, void* stream) {
+    if (!g) return DQ_ERR_INVALID_ARGUMENT;
+    if (g->world < 1 || g->world > kMaxGatherRanks || g->rank < 0 || g->rank >= g->world) return DQ_ERR_INVALID_ARGUMENT;
+    if (g->rows_per <= 0 || g->rows_per % 16 != 0) return DQ_ERR_SHAPE;
+    const long long full = static_cast<long long>(g->world) * g->rows_per;
+    if (g->d_total > full || g->d_total <= full - g->rows_per) return DQ_ERR_SHAPE;
+    for (int q = 0; q < g->world; ++q) {
+        if (!g->region[q]) return DQ_ERR_INVALID_ARGUMENT;
+        if ((reinterpret_cast<uintptr_t>(g->region[q]) & 255u) != 0) return DQ_ERR_ALIGNMENT;
+    }
+    dq_status_t st = check_weights(w, x, y, true, workspace, workspace_bytes);
+    if (st != DQ_OK) return st;
+    if (w->d_out != g->rows_per) return DQ_ERR_SHAPE;
+    if (!w->native || !w->fp16_cm) return DQ_ERR_INVALID_ARGUMENT;
+    return launch_gemv_gather(*w, x, y, outlier_k, workspace, *g, static_cast<cudaStream_t>(stream));
+}
+
+dq_status_t dq_device_alloc(size_t bytes, void** ptr) {
+    if (!ptr || bytes == 0) return DQ_ERR_INVALID_ARGUMENT;
+    const cudaError_t e = cudaMalloc(ptr, bytes);
+    if (e != cudaSuccess) { *ptr = nullptr; set_cuda_error(e); return DQ_ERR_CUDA; }
+    return DQ_OK;
+}
+
+dq_status_t dq_device_free(void* ptr) {
+    if (!ptr) return DQ_OK;
+    const cudaError_t e = cudaFree(ptr);
+    if (e != cudaSuccess) { set_cuda_error(e); return DQ_ERR_CUDA; }
+    return DQ_OK;
+}
+
+dq_status_t dq_ipc_handle(void* ptr, uint8_t handle[64]) {
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    if (!ptr || !handle) return DQ_ERR_INVALID_ARGUMENT;
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, ptr);
+    if (e != cudaSuccess) { set_cuda_error(e); return DQ_ERR_CUDA; }
+    memcpy(handle, &h, sizeof(h));
+    return DQ_OK;
+}
+
+dq_status_t dq_ipc_open(const uint8_t handle[64], void** ptr) {
+    if (!handle || !ptr) return DQ_ERR_INVALID_ARGUMENT;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) { *ptr = nullptr; set_cuda_error(e); return DQ_ERR_CUDA; }
+    return DQ_OK;
+}
+
+dq_status_t dq_ipc_close(void* ptr) {
+    if (!ptr) return DQ_OK;
+    const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+    if (e != cudaSuccess) { set_cuda_error(e); return DQ_ERR_CUDA; }
+    return DQ_OK;
 }
 
 dq_status_t dq_int4_gemv(const dq_weights_t* w, const uint16_t* x, uint16_t* y, void* workspace,

@@ -77,6 +77,10 @@ struct B1Args {
     int d_out, d_in, NC, U, nrb_max;
     int depth;                // ring stages per warp (reference layout: kB1Stages)
     B1Smem S;
+    // fused gather (kGather): ranks, slice height, output rows, every rank's region
+    int g_rank, g_world, g_rows_per, g_total;
+    uint8_t* g_region[kMaxGatherRanks];
+    GatherLayout g_lay;
 };
 
 // How the split path reads the FP16 weights of outlier columns.
@@ -97,8 +101,10 @@ __host__ __device__ inline int unit_owner(long long u, int P, long long U) {
 // kNative: weights in the unit layout (one bulk copy per unit, scale/zero
 // inside); otherwise the reference layout (one bulk copy per weight row of the
 // unit, scale/zero by plain loads).  kR: rounds of x held in registers by the
-// plan (at least ceil(NC / 8)).
-template <bool kSplit, bool kNative, int kOut, int kW, int kR>
+// plan (at least ceil(NC / 8)).  kGather: the rows are one rank's slice of a
+// row-sharded GEMV and the kernel also gathers the other ranks' slices (the
+// epilogue at the end).
+template <bool kSplit, bool kNative, int kOut, int kW, int kR, bool kGather = false>
 __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
     constexpr int kT = kW * 32;
     extern __shared__ __align__(128) char smem[];
@@ -204,6 +210,24 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
             prefetch_l2_bulk(a.native + static_cast<size_t>(cu0 + warp + kW * k) * kB1UnitBytes, kB1UnitBytes);
     pdl_launch_dependents();
     pdl_wait();  // x, y and the workspace may belong to the preceding kernel until here
+    // Gather: this call's number (CTA c's calls so far + 1) picks the slice.
+    uint32_t g_call = 0;
+    uint16_t* g_slice = nullptr;
+    if (kGather) {
+        g_call = reinterpret_cast<const uint32_t*>(a.g_region[a.g_rank] + a.g_lay.epoch)[c] + 1u;
+        g_slice = reinterpret_cast<uint16_t*>(a.g_region[a.g_rank] + (g_call & 1u) * a.g_lay.slice);
+    }
+    // Output row `row` (< d_out) of this call.
+    auto store_row = [&](int row, float v) {
+        const uint16_t h = __half_as_ushort(__float2half_rn(v));
+        if (kGather) {
+            const int grow = a.g_rank * a.g_rows_per + row;
+            if (grow < a.g_total) a.y[grow] = h;
+            g_slice[row] = h;
+        } else {
+            a.y[row] = h;
+        }
+    };
     XRegs<kT, kR> xr;
     x_regs_load_global<kT>(a.x, n8, xr);
     if (kNative) {
@@ -488,7 +512,7 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
 #pragma unroll
             for (int w = 0; w < kW; ++w) sum += opart[(w * a.nrb_max + rbl) * 16 + rr];
         const int row = rb * kRowBlock + rr;
-        if (row < a.d_out) a.y[row] = __half_as_ushort(__float2half_rn(sum));
+        if (row < a.d_out) store_row(row, sum);
     }
     if (finaliser && warp == 0) {
         const int rbl = rbz - rbf;
@@ -512,10 +536,54 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
             sum += __uint_as_float(static_cast<uint32_t>(v));
         }
         if (!__all_sync(0xffffffffu, ok_all) && lane == 0) atomicOr(&g_error_word, 2u);
-        if (lane < 16 && row < a.d_out) a.y[row] = __half_as_ushort(__float2half_rn(sum));
+        if (lane < 16 && row < a.d_out) store_row(row, sum);
         __syncwarp();
         // Leave the slots zero for the next call.
         for (int i = lane; i < (c_hi - c) * 16; i += 32) st_relaxed_gpu_u64(a.fix + (c + 1) * 16 + i, 0ull);
+    }
+
+    if constexpr (kGather) {
+        // ---- gather: publish this CTA's rows, then copy the other ranks' ----
+        // CTA c writes the rows of row blocks orb0 .. rbz on every rank (same
+        // shapes, same grid), so it takes exactly those rows of each other
+        // rank's slice once that rank's CTA c has raised its flag here.
+        unsigned int* s_ok = reinterpret_cast<unsigned int*>(red);  // the plan's scratch, free again
+        __syncthreads();  // this CTA's rows are in its slice
+        if (tid == 0) {
+            __threadfence_system();
+            for (int q = 0; q < a.g_world; ++q)
+                if (q != a.g_rank)
+                    st_release_sys_u32(reinterpret_cast<unsigned int*>(a.g_region[q] + a.g_lay.flags) +
+                                           a.g_rank * kMaxCtas + c, g_call);
+        }
+        if (warp == 0) {
+            bool ok = true;
+            if (lane < a.g_world && lane != a.g_rank) {  // lane q waits for rank q's CTA c (bounded)
+                const unsigned int* f = reinterpret_cast<const unsigned int*>(a.g_region[a.g_rank] + a.g_lay.flags) +
+                                        lane * kMaxCtas + c;
+                uint32_t v = ld_acquire_sys_u32(f);
+                const long long t0 = clock64();
+                while (static_cast<int32_t>(v - g_call) < 0 && clock64() - t0 < (1ll << 31)) v = ld_acquire_sys_u32(f);
+                ok = static_cast<int32_t>(v - g_call) >= 0;
+            }
+            const unsigned int okm = __ballot_sync(0xffffffffu, ok);
+            if (lane == 0) {
+                *s_ok = okm;
+                if (okm != 0xffffffffu) atomicOr(&g_error_word, 16u);
+            }
+        }
+        __syncthreads();
+        const unsigned int okm = *s_ok;
+        const int r_lo = orb0 * kRowBlock, r_hi = min(a.d_out, (rbz + 1) * kRowBlock);
+        const int nrows = r_hi > r_lo ? r_hi - r_lo : 0;
+        for (int i = tid; i < nrows * a.g_world; i += kT) {
+            const int q = i / nrows, row = r_lo + i % nrows;
+            const int grow = q * a.g_rows_per + row;
+            if (q == a.g_rank || !((okm >> q) & 1u) || grow >= a.g_total) continue;
+            const uint16_t* src = reinterpret_cast<const uint16_t*>(a.g_region[q] + (g_call & 1u) * a.g_lay.slice);
+            a.y[grow] = ld_relaxed_sys_u16(src + row);
+        }
+        if (tid == 0) reinterpret_cast<uint32_t*>(a.g_region[a.g_rank] + a.g_lay.epoch)[c] = g_call;
     }
 }
 
@@ -811,7 +879,7 @@ __global__ void colmajor_kernel(const uint16_t* __restrict__ w, int d_out, int d
 
 // Per-device, per-kernel "max dynamic shared memory" opt-in, done once.
 constexpr int kMaxDevices = 64;
-constexpr int kNumKernels = 144;
+constexpr int kNumKernels = 272;
 int g_smem_set[kMaxDevices][kNumKernels];  // bytes already opted in (0 = none)
 
 template <class K>
@@ -843,13 +911,13 @@ dq_status_t check_launch() {
 }
 
 
-template <bool kSplit, bool kNative, int kOut, int kW, int kR>
+template <bool kSplit, bool kNative, int kOut, int kW, int kR, bool kGather = false>
 dq_status_t launch_b1(const B1Args& a, int grid, cudaStream_t stream) {
     constexpr int wi = kW == kB1Warps ? 0 : 1;
     constexpr int ri = kR == 1 ? 0 : kR == 2 ? 1 : kR == 4 ? 2 : 3;
-    constexpr int id = 4 + 16 * (4 * wi + ri) + (kSplit ? 8 : 0) + (kNative ? 4 : 0) + kOut;
+    constexpr int id = 4 + 128 * (kGather ? 1 : 0) + 16 * (4 * wi + ri) + (kSplit ? 8 : 0) + (kNative ? 4 : 0) + kOut;
     static_assert(id < kNumKernels, "kernel attribute slot");
-    const dq_status_t st = ensure_smem(b1_kernel<kSplit, kNative, kOut, kW, kR>, id, a.S.total);
+    const dq_status_t st = ensure_smem(b1_kernel<kSplit, kNative, kOut, kW, kR, kGather>, id, a.S.total);
     if (st != DQ_OK) return st;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -861,7 +929,7 @@ dq_status_t launch_b1(const B1Args& a, int grid, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, b1_kernel<kSplit, kNative, kOut, kW, kR>, a);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, b1_kernel<kSplit, kNative, kOut, kW, kR, kGather>, a);
     if (e != cudaSuccess) { set_cuda_error(e); return DQ_ERR_CUDA; }
     return check_launch();
 }
@@ -892,10 +960,22 @@ dq_status_t launch_b1_warps(const B1Args& a, int warps, int out_mode, int rounds
                              : launch_b1_native<kB1WarpsSmall>(a, out_mode, rounds, grid, stream);
 }
 
-}  // namespace
+// The split GEMV with the fused gather: native layout, column-major mirror.
+template <int kW>
+dq_status_t launch_b1_gather(const B1Args& a, int rounds, int grid, cudaStream_t stream) {
+    if (rounds <= 1) return launch_b1<true, true, kOutStaged, kW, 1, true>(a, grid, stream);
+    if (rounds <= 2) return launch_b1<true, true, kOutStaged, kW, 2, true>(a, grid, stream);
+    if (rounds <= 4) return launch_b1<true, true, kOutStaged, kW, 4, true>(a, grid, stream);
+    return launch_b1<true, true, kOutStaged, kW, kPlanRounds, true>(a, grid, stream);
+}
 
-dq_status_t launch_gemv_b1(const dq_weights_t& w, const uint16_t* x, uint16_t* y, float k,
-                           bool split, void* workspace, cudaStream_t stream) {
+// Launch geometry of one batch-1 call.
+struct B1Plan {
+    int grid, warps, out_mode, rounds;
+};
+
+dq_status_t b1_setup(const dq_weights_t& w, const uint16_t* x, uint16_t* y, float k, bool split, void* workspace,
+                     B1Args& a, B1Plan& p) {
     DeviceInfo di;
     const dq_status_t st = device_info(&di);
     if (st != DQ_OK) return st;
@@ -903,7 +983,7 @@ dq_status_t launch_gemv_b1(const dq_weights_t& w, const uint16_t* x, uint16_t* y
     const long long n_rb = (static_cast<long long>(w.d_out) + kRowBlock - 1) / kRowBlock;
     const int NC = (G + kCG - 1) / kCG;
     if (n_rb * NC > INT_MAX) return DQ_ERR_UNSUPPORTED;
-    B1Args a;
+    a = B1Args{};
     a.packed = w.packed;
     a.scales = w.scales;
     a.zeros = w.zeros;
@@ -931,10 +1011,10 @@ dq_status_t launch_gemv_b1(const dq_weights_t& w, const uint16_t* x, uint16_t* y
         if (n > nrb_max) nrb_max = n;
     }
     a.nrb_max = nrb_max;
-    const int rounds = (NC + 7) / 8;  // plan rounds of x per virtual thread
-
-    int out_mode = kOutNone;
-    if (split) out_mode = w.fp16_cm ? ((w.d_out % 8) == 0 ? kOutStaged : kOutColDirect) : kOutRowDirect;
+    p.grid = grid;
+    p.rounds = (NC + 7) / 8;  // plan rounds of x per virtual thread
+    p.out_mode = kOutNone;
+    if (split) p.out_mode = w.fp16_cm ? ((w.d_out % 8) == 0 ? kOutStaged : kOutColDirect) : kOutRowDirect;
     if (w.native) {
         // A ring of as many stages per warp as fit (at least kB1Stages, no more
         // than a warp has units), 16 warps or 12.
@@ -946,7 +1026,8 @@ dq_status_t launch_gemv_b1(const dq_weights_t& w, const uint16_t* x, uint16_t* y
                 a.S = b1_smem(w.d_in, nrb_max, split, warps, warps * depth);
                 if (a.S.total > di.smem_optin) continue;
                 a.depth = depth;
-                return launch_b1_warps(a, warps, out_mode, rounds, grid, stream);
+                p.warps = warps;
+                return DQ_OK;
             }
         }
         return DQ_ERR_UNSUPPORTED;
@@ -954,14 +1035,42 @@ dq_status_t launch_gemv_b1(const dq_weights_t& w, const uint16_t* x, uint16_t* y
     // Reference layout: kB1Stages per warp, 16 warps where their rings fit next
     // to x and the plan, else 12.
     a.depth = kB1Stages;
-    int warps = kB1Warps;
-    a.S = b1_smem(w.d_in, nrb_max, split, warps, warps * kB1Stages);
+    p.warps = kB1Warps;
+    a.S = b1_smem(w.d_in, nrb_max, split, p.warps, p.warps * kB1Stages);
     if (a.S.total > di.smem_optin) {
-        warps = kB1WarpsSmall;
-        a.S = b1_smem(w.d_in, nrb_max, split, warps, warps * kB1Stages);
+        p.warps = kB1WarpsSmall;
+        a.S = b1_smem(w.d_in, nrb_max, split, p.warps, p.warps * kB1Stages);
     }
     if (a.S.total > di.smem_optin) return DQ_ERR_UNSUPPORTED;
-    return launch_b1_warps(a, warps, out_mode, rounds, grid, stream);
+    return DQ_OK;
+}
+
+}  // namespace
+
+dq_status_t launch_gemv_b1(const dq_weights_t& w, const uint16_t* x, uint16_t* y, float k,
+                           bool split, void* workspace, cudaStream_t stream) {
+    B1Args a;
+    B1Plan p;
+    const dq_status_t st = b1_setup(w, x, y, k, split, workspace, a, p);
+    if (st != DQ_OK) return st;
+    return launch_b1_warps(a, p.warps, p.out_mode, p.rounds, p.grid, stream);
+}
+
+dq_status_t launch_gemv_gather(const dq_weights_t& w, const uint16_t* x, uint16_t* y, float k,
+                               void* workspace, const dq_gather_t& g, cudaStream_t stream) {
+    B1Args a;
+    B1Plan p;
+    const dq_status_t st = b1_setup(w, x, y, k, true, workspace, a, p);
+    if (st != DQ_OK) return st;
+    if (p.out_mode != kOutStaged || !w.native) return DQ_ERR_INVALID_ARGUMENT;
+    a.g_rank = g.rank;
+    a.g_world = g.world;
+    a.g_rows_per = g.rows_per;
+    a.g_total = g.d_total;
+    for (int q = 0; q < kMaxGatherRanks; ++q) a.g_region[q] = static_cast<uint8_t*>(q < g.world ? g.region[q] : nullptr);
+    a.g_lay = gather_layout(g.rows_per);
+    return p.warps == kB1Warps ? launch_b1_gather<kB1Warps>(a, p.rounds, p.grid, stream)
+                               : launch_b1_gather<kB1WarpsSmall>(a, p.rounds, p.grid, stream);
 }
 
 dq_status_t launch_build_native(const uint8_t* packed, const uint16_t* scales, const uint16_t* zeros,

@@ -78,6 +78,26 @@ struct WsLayout {
 
 inline size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
+// Gather region of one rank (row-sharded split GEMV with the gather fused):
+//   slices  two FP16 copies of this rank's output rows (rows_per each), used
+//           alternately by consecutive calls, read by the other ranks
+//   flags   [kMaxGatherRanks][kMaxCtas] u32: flag (q, c) = the last call whose
+//           CTA c on rank q has published its rows (written by rank q)
+//   epoch   [kMaxCtas] u32: calls completed by this rank's CTA c
+// Zero-filled once; every rank makes the same calls with the same grid.
+constexpr int kMaxGatherRanks = DQ_MAX_GATHER_RANKS;
+struct GatherLayout {
+    size_t slice, flags, epoch, total;
+};
+inline GatherLayout gather_layout(int rows_per) {
+    GatherLayout L;
+    L.slice = align256(static_cast<size_t>(rows_per) * 2);
+    L.flags = 2 * L.slice;
+    L.epoch = L.flags + static_cast<size_t>(kMaxGatherRanks) * kMaxCtas * 4;
+    L.total = align256(L.epoch + static_cast<size_t>(kMaxCtas) * 4);
+    return L;
+}
+
 inline WsLayout ws_layout(int d_out, int d_in) {
     (void)d_out;
     (void)d_in;
@@ -163,6 +183,8 @@ dq_status_t device_info(DeviceInfo* out);
 void set_cuda_error(cudaError_t e);
 
 // Kernel launchers (arguments already validated by the C ABI layer).
+dq_status_t launch_gemv_gather(const dq_weights_t& w, const uint16_t* x, uint16_t* y, float k,
+                               void* workspace, const dq_gather_t& g, cudaStream_t stream);
 dq_status_t launch_gemv_b1(const dq_weights_t& w, const uint16_t* x, uint16_t* y, float k,
                            bool split, void* workspace, cudaStream_t stream);
 dq_status_t launch_build_native(const uint8_t* packed, const uint16_t* scales, const uint16_t* zeros,

@@ -42,7 +42,16 @@ EXPORTED_SYMBOLS = (
     "dq_build_native",
     "dq_read_device_error",
     "dq_workspace_bytes",
+    "dq_gather_region_bytes",
+    "dq_split_gemv_gather",
+    "dq_device_alloc",
+    "dq_device_free",
+    "dq_ipc_handle",
+    "dq_ipc_open",
+    "dq_ipc_close",
 )
+
+MAX_GATHER_RANKS = 8  # DQ_MAX_GATHER_RANKS
 
 
 class DqWeights(C.Structure):
@@ -57,6 +66,18 @@ class DqWeights(C.Structure):
         ("native", C.c_void_p),
         ("d_out", C.c_int32),
         ("d_in", C.c_int32),
+    ]
+
+
+class DqGather(C.Structure):
+    """dq_gather_t (include/dq_abi.h)."""
+
+    _fields_ = [
+        ("rank", C.c_int32),
+        ("world", C.c_int32),
+        ("rows_per", C.c_int32),
+        ("d_total", C.c_int32),
+        ("region", C.c_void_p * MAX_GATHER_RANKS),
     ]
 
 
@@ -118,6 +139,20 @@ def lib() -> C.CDLL:
         L.dq_build_native.argtypes = [P, P, P, i32, i32, P, P]
         L.dq_read_device_error.restype = st
         L.dq_read_device_error.argtypes = [C.POINTER(C.c_uint32), C.c_int]
+        L.dq_gather_region_bytes.restype = C.c_size_t
+        L.dq_gather_region_bytes.argtypes = [i32]
+        L.dq_split_gemv_gather.restype = st
+        L.dq_split_gemv_gather.argtypes = [C.POINTER(DqWeights), P, P, f32, P, C.c_size_t, C.POINTER(DqGather), P]
+        L.dq_device_alloc.restype = st
+        L.dq_device_alloc.argtypes = [C.c_size_t, C.POINTER(C.c_void_p)]
+        L.dq_device_free.restype = st
+        L.dq_device_free.argtypes = [P]
+        L.dq_ipc_handle.restype = st
+        L.dq_ipc_handle.argtypes = [P, C.c_char_p]
+        L.dq_ipc_open.restype = st
+        L.dq_ipc_open.argtypes = [C.c_char_p, C.POINTER(C.c_void_p)]
+        L.dq_ipc_close.restype = st
+        L.dq_ipc_close.argtypes = [P]
         _lib = L
     return _lib
 

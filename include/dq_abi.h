@@ -66,6 +66,20 @@ typedef struct dq_weights_t {
     int32_t d_in;
 } dq_weights_t;
 
+/* Row-sharded split GEMV with the gather fused (dq_split_gemv_gather): one
+ * process per GPU, every rank holding rows_per rows of the weights (the last
+ * ranks zero-padded), the ranks' gather regions mapped into each other's
+ * address space (dq_ipc_handle / dq_ipc_open).  region[rank] is this process's
+ * own region, region[q] rank q's as mapped here. */
+#define DQ_MAX_GATHER_RANKS 8
+typedef struct dq_gather_t {
+    int32_t rank;      /* this process, 0 <= rank < world */
+    int32_t world;     /* ranks, 1 .. DQ_MAX_GATHER_RANKS */
+    int32_t rows_per;  /* rows of every rank's slice, a multiple of 16 (= the local weights' d_out) */
+    int32_t d_total;   /* rows of the full output, (world - 1) * rows_per < d_total <= world * rows_per */
+    void* region[DQ_MAX_GATHER_RANKS];
+} dq_gather_t;
+
 /* Human-readable name of a status code (static string). */
 DQ_API const char* dq_status_string(dq_status_t s);
 
@@ -244,12 +258,51 @@ DQ_API dq_status_t dq_detect_outliers(const uint16_t* x, int32_t d_in, float out
                                float* stats, void* stream);
 
 /*
+ * Bytes of one rank's gather region for slices of rows_per rows (0 on a bad
+ * size).  The region is device memory, 256-byte aligned, zero-filled once
+ * before its first use, shared by all the calls of one weight matrix (every
+ * rank making the same calls in the same order).
+ */
+DQ_API size_t dq_gather_region_bytes(int32_t rows_per);
+
+/*
+ * Row-sharded split GEMV with the all-gather fused into the kernel: this
+ * rank's rows of y = the split GEMV of x (w->d_out == g->rows_per, native
+ * layout and column-major mirror required), then the full y[d_total] on every
+ * rank.  Each CTA publishes its rows in this rank's region, raises its flag
+ * in every other rank's region (system-scope release), waits for the same
+ * CTA of every other rank (bounded, about a second: on timeout bit 4 of the
+ * device error word is set and that rank's rows are left unwritten) and
+ * copies their rows from the peers' regions over NVLink.  All ranks call it
+ * with the same shapes; y is this process's own buffer.  Replaces
+ * launch_split_gemv (src/split_gemv.cu:160-198) on a slice of the rows plus
+ * the collective that would follow it.
+ */
+DQ_API dq_status_t dq_split_gemv_gather(const dq_weights_t* w, const uint16_t* x, uint16_t* y, float outlier_k,
+                                        void* workspace, size_t workspace_bytes, const dq_gather_t* g,
+                                        void* stream);
+
+/*
+ * Device memory for gather regions and its interprocess mapping (CUDA IPC,
+ * plain peer access: no multicast objects).  dq_ipc_handle writes the 64-byte
+ * handle of a block from dq_device_alloc; dq_ipc_open maps another process's
+ * block into this one (the same GPU node, peer access enabled on demand);
+ * dq_ipc_close unmaps it.
+ */
+DQ_API dq_status_t dq_device_alloc(size_t bytes, void** ptr);
+DQ_API dq_status_t dq_device_free(void* ptr);
+DQ_API dq_status_t dq_ipc_handle(void* ptr, uint8_t handle[64]);
+DQ_API dq_status_t dq_ipc_open(const uint8_t handle[64], void** ptr);
+DQ_API dq_status_t dq_ipc_close(void* ptr);
+
+/*
  * Device error word of this library on the current device: bit 0 is set by a
  * batch-1 kernel whose bounded wait for its own bulk copies gave up (the
  * kernel then drains its copies, skips the remaining work and returns; its
  * output is not valid), bit 1 by a batch-1 kernel whose bounded wait for a
- * neighbouring CTA's partial sums gave up, bit 8 by a batched kernel whose
- * bounded wait for its own bulk copies gave up.  Synchronous; clear != 0
+ * neighbouring CTA's partial sums gave up, bit 4 by a gathering kernel whose
+ * bounded wait for another rank's rows gave up, bit 8 by a batched kernel
+ * whose bounded wait for its own bulk copies gave up.  Synchronous; clear != 0
  * resets the word.  No reference counterpart.
  */
 DQ_API dq_status_t dq_read_device_error(uint32_t* word, int clear);
