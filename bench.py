@@ -19,8 +19,10 @@ GEMV = d_out*d_in/2 (INT4) + 4*d_out*d_in/128 (FP16 scale + zero)
 One process per GPU.  Under torchrun (N > 1) the 70B workloads are
 row-sharded, as a 70B model is deployed: each rank holds whole 16-row blocks
 of the weights, runs the split GEMV on its slice with the same x, and the
-output slices are all-gathered with NCCL after every GEMV ("scaling":
-"strong": the total work is the workload's, whatever N).  The 7B and sweep
+output slices are gathered inside the GEMV kernel over NVLink peer memory
+(--gather peer, the default) or all-gathered with NCCL after every GEMV
+(--gather nccl) ("scaling": "strong": the total work is the workload's,
+whatever N).  The 7B and sweep
 workloads fit one GPU and run as N independent replicas (data parallel, no
 collective, "scaling": "weak"); --shard overrides either choice.  The time is
 the max over ranks; value is the algorithmic bytes of the whole job over that
@@ -301,6 +303,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     spec = workload_spec(args)
     M = args.batch
     sharded = world > 1 and shard_mode(args) == "rows"
+    peer = sharded and args.gather == "peer"  # the all-gather fused into the GEMV kernel
     # Row sharding across the ranks: every rank holds whole 16-row blocks of
     # each GEMV, sees the same x, and the output slices are all-gathered with
     # NCCL after every GEMV.  Replicas: every rank runs the whole workload on
@@ -342,6 +345,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             if n_rows <= 0:
                 raise SystemExit(f"{name}: {d_out} rows do not give every one of {world} ranks a row block")
             w = (torch.randn(n_rows, d_in, generator=gen, device=dev, dtype=torch.float32) / math.sqrt(d_in)).half()
+            if peer and n_rows < rows[gi][2]:  # every rank runs the same shape: zero rows pad the last slices
+                w = torch.cat([w, torch.zeros(rows[gi][2] - n_rows, d_in, dtype=w.dtype, device=dev)])
+                n_rows = rows[gi][2]
             lin = dyn_quant.DynQuantLinear(d_in, n_rows, args.k)
             lin.load_weight(w)
             del w
@@ -363,8 +369,23 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                                     lin.fp16_w.data_ptr(), lin.d_out, lin.d_in, lin._native.data_ptr()))
         structs.append(row)
 
-    def launch_gemv(s: int, gi: int, stream, gather: bool = True):
+    gathers = None
+    if peer:
+        from dyn_quant.sharded import PeerGather
+        if M != 1:
+            raise SystemExit("--gather peer runs batch 1")
+        gathers = [PeerGather(per, o, None, dev) for (_, o, _, _, _), (_, _, per) in zip(spec, rows)]
+
+    def launch_gemv(s: int, gi: int, stream, gather: bool = True, x=None):
         name, d_out, d_in, frac, key = spec[gi]
+        if peer:  # one kernel: this rank's rows, then every rank's rows into the full y
+            xs = acts[key] if x is None else x
+            st = L.dq_split_gemv_gather(C.byref(structs[s][gi]), C.c_void_p(xs.data_ptr()),
+                                        C.c_void_p(fulls[gi].data_ptr()), args.k, C.c_void_p(wspace.data_ptr()),
+                                        ws_bytes, C.byref(gathers[gi].desc), C.c_void_p(stream.cuda_stream))
+            if st != 0:
+                raise RuntimeError(f"split GEMV with gather: {_lib.status_string(st)}")
+            return
         if M == 1:
             st = L.dq_split_gemv(C.byref(structs[s][gi]), C.c_void_p(acts[key].data_ptr()),
                                  C.c_void_p(outs[gi].data_ptr()), args.k, C.c_void_p(wspace.data_ptr()),
@@ -403,6 +424,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
 
     warm_graph = capture(steps(0, max(args.warmup, n_sets)))
     timed_graph = capture(steps(0, args.steps))
+    # (with the gather fused, the per-GEMV graphs time the kernel with its gather)
     per_gemv_graphs = [capture([(i % n_sets, gi) for i in range(args.steps)], gather=False) for gi in range(n_gemv)]
     torch.cuda.synchronize()
 
@@ -475,7 +497,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     us_per_gemv = elapsed_ms * 1e3 / (args.steps * n_gemv)
 
     # end to end through the public API: pinned host x in, host y out, every step
-    e2e = run_e2e(args, spec, sets, acts_np, dev, job_step_bytes, world, rows, sharded)
+    e2e = run_e2e(args, spec, sets, acts_np, dev, job_step_bytes, world, rows, sharded,
+                  launch_gemv if peer else None, fulls)
 
     # accuracy of this rank's rows (weight set 0) against an FP32 dense GEMV on
     # the original FP16 weights and activations
@@ -513,7 +536,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                        "l2": f"inputs larger than L2: {n_sets} rotating weight sets "
                              f"({n_sets * step_bytes / 1e6:.0f} MB streamed per cycle)",
                        "graphs": "the K timed steps are one CUDA graph of back-to-back launches",
-                       "parallelism": (f"row-sharded over {world} GPUs, NCCL all-gather of the output slices "
+                       "parallelism": (f"row-sharded over {world} GPUs, the output slices gathered inside the "
+                                       "GEMV kernel over NVLink peer memory" if peer else
+                                       f"row-sharded over {world} GPUs, NCCL all-gather of the output slices "
                                        "after every GEMV" if sharded else
                                        (f"{world} independent replicas (data parallel, no collective)"
                                         if world > 1 else "1 GPU"))},
@@ -534,18 +559,22 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         print(json.dumps(line), flush=True)
 
     del warm_graph, timed_graph, per_gemv_graphs
+    if gathers:
+        for g in gathers:
+            g.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
 
 
-def run_e2e(args, spec, sets, acts_np, dev, job_step_bytes, world, rows, sharded):
+def run_e2e(args, spec, sets, acts_np, dev, job_step_bytes, world, rows, sharded, fused=None, fulls=None):
     """The same steps through DynQuantLinear.forward from pinned host buffers.
 
     Row-sharded runs gather each GEMV's output slices with
-    dyn_quant.sharded.gather_rows, so every rank copies the full y back;
-    replicas (world > 1, not sharded) each run the whole workload and the
-    value counts the bytes of all of them over the max-over-ranks time."""
+    dyn_quant.sharded.gather_rows (or, given `fused`, through the kernel with
+    the gather fused, which writes `fulls`), so every rank copies the full y
+    back; replicas (world > 1, not sharded) each run the whole workload and
+    the value counts the bytes of all of them over the max-over-ranks time."""
     import torch
     import torch.distributed as dist
     from dyn_quant.sharded import gather_rows
@@ -569,6 +598,10 @@ def run_e2e(args, spec, sets, acts_np, dev, job_step_bytes, world, rows, sharded
         for k in xh:
             xd[k].copy_(xh[k], non_blocking=True)
         for gi, (name, d_out, d_in, frac, key) in enumerate(spec):
+            if fused is not None:
+                fused(s, gi, stream, True, xd[key])
+                yh[gi].copy_(fulls[gi], non_blocking=True)
+                continue
             y = sets[s][gi](xd[key])
             if sharded and M == 1:
                 y = gather_rows(y, d_out, rows[gi][2], None, gbuf[gi])
@@ -890,6 +923,9 @@ def main(argv=None) -> None:
     ap.add_argument("--frac", type=float, default=None, help="injected outlier fraction (default: the workload's)")
     ap.add_argument("--k", type=float, default=K_OUTLIER, help="outlier threshold in standard deviations")
     ap.add_argument("--dist", choices=["normal", "t3"], default="normal", help="activation distribution")
+    ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
+                    help="row-sharded runs: the output slices gathered inside the GEMV kernel over NVLink peer "
+                         "memory, or by an NCCL all-gather after it")
     ap.add_argument("--shard", choices=["auto", "rows", "replicas"], default="auto",
                     help="N > 1: row sharding with an all-gather, or independent replicas; auto follows the "
                          "deployment of each shape: rows for the 70B workloads, replicas for the 7B and sweep ones")
