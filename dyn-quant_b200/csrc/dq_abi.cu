@@ -153,7 +153,15 @@ dq_status_t dq_silu_mul(const uint16_t* a, const uint16_t* b, uint16_t* h, int64
     if (n == 0) return DQ_OK;
     if (!a || !b || !h) return DQ_ERR_INVALID_ARGUMENT;
     if (!aligned16(a) || !aligned16(b) || !aligned16(h)) return DQ_ERR_ALIGNMENT;
-    return launch_silu_mul(a, b, h, n, static_cast<cudaStream_t>(stream));
+    return launch_silu_mul(a, b, h, 1, n, n, static_cast<cudaStream_t>(stream));
+}
+
+dq_status_t dq_silu_mul_pairs(const uint16_t* ab, uint16_t* h, int32_t rows, int32_t d, void* stream) {
+    if (rows < 0 || d < 0 || d % 8 != 0) return DQ_ERR_SHAPE;
+    if (rows == 0 || d == 0) return DQ_OK;
+    if (!ab || !h) return DQ_ERR_INVALID_ARGUMENT;
+    if (!aligned16(ab) || !aligned16(h)) return DQ_ERR_ALIGNMENT;
+    return launch_silu_mul(ab, ab + d, h, rows, d, 2LL * d, static_cast<cudaStream_t>(stream));
 }
 
 dq_status_t dq_moe_combine(const uint16_t* y, const int32_t* rows, const float* weight, float* out, int32_t m,

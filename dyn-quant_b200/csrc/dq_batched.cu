@@ -201,7 +201,8 @@ __global__ void __launch_bounds__(kStatThreads, 1) bplan_kernel(const BPArgs a) 
         if (a.MP == 16)
             dst[1] = make_uint4(pack_h2(v[8], v[9]), pack_h2(v[10], v[11]), pack_h2(v[12], v[13]), pack_h2(v[14], v[15]));
     }
-    if (tid == 0) {        a.ctr[1] = static_cast<unsigned>(tot[0]);
+    if (tid == 0) {
+        a.ctr[1] = static_cast<unsigned>(tot[0]);
         a.ctr[0] = 0u;  // ready for the next call
     }
 }
@@ -335,6 +336,7 @@ struct BDArgs {
     const uint32_t* masks;   // [kBgMaxM][W]
     float* dpart;            // [nslab][MP][d_out]
     int M, d_out, d_in, NC, NRB, S, nslab, cps, W;
+    int pf_rb;               // row blocks per warp (from its first) pulled into L2 before the plan is ready
     int sm_ring, sm_bars, sm_xtab, sm_xsum;
 };
 
@@ -384,7 +386,9 @@ __global__ void __launch_bounds__(kBgWarps * 32, 1) bdense_kernel(const BDArgs a
     };
 
     // The weights do not depend on the preceding kernels: the first stages go
-    // out before griddepcontrol.wait.
+    // out before griddepcontrol.wait, and the warp's first pf_rb row blocks
+    // (each one contiguous run of nch units) are pulled into L2 meanwhile, so
+    // the stream runs while the plan kernel works.
     uint32_t armed = 0;
     if (lane == 0) {
 #pragma unroll
@@ -393,6 +397,8 @@ __global__ void __launch_bounds__(kBgWarps * 32, 1) bdense_kernel(const BDArgs a
 #pragma unroll
         for (int s = 0; s < kBgStages; ++s)
             if (s < wn) issue(s, s);
+        for (int r = 0; r < nrw && r < a.pf_rb; ++r)
+            prefetch_l2_bulk(a.native + unit_of(r * nch) * kUnit, static_cast<uint32_t>(nch) * kUnit);
     }
 #pragma unroll
     for (int s = 0; s < kBgStages; ++s)
@@ -681,6 +687,14 @@ dq_status_t launch_gemv_batched(const dq_weights_t& w, const uint16_t* x, uint16
     da.nslab = G.nslab;
     da.cps = std::max(1, std::min(G.NRB, di.sm_count / G.nslab));
     da.W = G.W;
+    {
+        // L2 prefetch of the weights during the plan: all of them when they
+        // take at most kBgPrefetchBytes, else that share of each warp's rows.
+        const double total = static_cast<double>(G.NRB) * G.NC * kUnit;
+        const int nrw_max = (G.NRB / da.cps + 1 + kBgWarps - 1) / kBgWarps + 1;
+        da.pf_rb = total <= kBgPrefetchBytes ? nrw_max
+                                             : static_cast<int>(nrw_max * (kBgPrefetchBytes / total));
+    }
     da.sm_ring = DS.ring;
     da.sm_bars = DS.bars;
     da.sm_xtab = DS.xtab;

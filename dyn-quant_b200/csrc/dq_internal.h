@@ -133,6 +133,7 @@ constexpr int kBgWarps = 16;      // warps of a dense CTA (one CTA per SM)
 constexpr int kBgStages = 2;      // bulk-copy ring stages per warp
 constexpr int kBgOutWarps = 8;    // warps of an FP16-part CTA
 constexpr int kBgOutBufs = 3;     // per-warp outlier segment buffers in flight
+constexpr double kBgPrefetchBytes = 64.0 * 1024 * 1024;  // L2 the batched INT4 part claims ahead of the plan
 constexpr int kBgRefSMs = 148;    // SM count the slab width is chosen for (keeps the workspace device-independent)
 
 // Split of one batched call.  NT tiles of 8 vectors (MP = 8 NT columns of the
@@ -215,7 +216,9 @@ inline BgWs bg_ws(const BgGeom& g, int d_out, int d_in) {
 dq_status_t launch_gemv_batched(const dq_weights_t& w, const uint16_t* x, uint16_t* y, int M, float k,
                                 void* workspace, cudaStream_t stream);
 dq_status_t read_batched_error(uint32_t* word, bool clear);
-dq_status_t launch_silu_mul(const uint16_t* a, const uint16_t* b, uint16_t* h, long long n, cudaStream_t stream);
+// h[r][:d] = fp16(silu(a[r][:d]) * b[r][:d]) for r < rows, a and b rows ld apart (d, ld multiples of 8).
+dq_status_t launch_silu_mul(const uint16_t* a, const uint16_t* b, uint16_t* h, long long rows, long long d,
+                            long long ld, cudaStream_t stream);
 dq_status_t launch_combine(const uint16_t* y, const int32_t* rows, const float* weight, float* out, int m, int d,
                            cudaStream_t stream);
 

@@ -13,14 +13,17 @@ __device__ __forceinline__ uint32_t word_of_u4(const uint4& v, int i) {
     return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
 }
 
-// h = fp16(silu(a) * b) with silu(v) = v / (1 + exp(-v)), FP32 arithmetic.
+// h = fp16(silu(a) * b) with silu(v) = v / (1 + exp(-v)), FP32 arithmetic,
+// over rows of d8 pieces of 8 values: a and b rows ld8 pieces apart, h rows
+// contiguous.
 __global__ void silu_mul_kernel(const uint16_t* __restrict__ a, const uint16_t* __restrict__ b,
-                                uint16_t* __restrict__ h, long long n8) {
+                                uint16_t* __restrict__ h, long long rows, long long d8, long long ld8) {
     const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     pdl_launch_dependents();
     pdl_wait();
-    if (i >= n8) return;
-    const uint4 va = ldcg_v4(a + 8 * i), vb = ldcg_v4(b + 8 * i);
+    if (i >= rows * d8) return;
+    const long long r = i / d8, src = r * ld8 + (i - r * d8);
+    const uint4 va = ldcg_v4(a + 8 * src), vb = ldcg_v4(b + 8 * src);
     uint32_t out[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -83,12 +86,14 @@ dq_status_t launch_pdl_plain(K kernel, dim3 grid, int threads, cudaStream_t stre
 
 }  // namespace
 
-dq_status_t launch_silu_mul(const uint16_t* a, const uint16_t* b, uint16_t* h, long long n, cudaStream_t stream) {
-    const long long n8 = n / 8;
+dq_status_t launch_silu_mul(const uint16_t* a, const uint16_t* b, uint16_t* h, long long rows, long long d,
+                            long long ld, cudaStream_t stream) {
+    const long long n8 = rows * (d / 8);
     if (n8 == 0) return DQ_OK;
     const int threads = 256;
     const long long blocks = (n8 + threads - 1) / threads;
-    return launch_pdl_plain(silu_mul_kernel, dim3(static_cast<unsigned>(blocks)), threads, stream, a, b, h, n8);
+    return launch_pdl_plain(silu_mul_kernel, dim3(static_cast<unsigned>(blocks)), threads, stream, a, b, h, rows,
+                            d / 8, ld / 8);
 }
 
 dq_status_t launch_combine(const uint16_t* y, const int32_t* rows, const float* weight, float* out, int m, int d,

@@ -34,6 +34,7 @@ EXPORTED_SYMBOLS = (
     "dq_split_gemv_batched",
     "dq_workspace_bytes_batched",
     "dq_silu_mul",
+    "dq_silu_mul_pairs",
     "dq_moe_combine",
     "dq_int4_gemv",
     "dq_reference_gemv",
@@ -123,6 +124,8 @@ def lib() -> C.CDLL:
         L.dq_workspace_bytes_batched.argtypes = [i32, i32, i32]
         L.dq_silu_mul.restype = st
         L.dq_silu_mul.argtypes = [P, P, P, C.c_int64, P]
+        L.dq_silu_mul_pairs.restype = st
+        L.dq_silu_mul_pairs.argtypes = [P, P, i32, i32, P]
         L.dq_moe_combine.restype = st
         L.dq_moe_combine.argtypes = [P, P, P, P, i32, i32, P]
         L.dq_int4_gemv.restype = st

@@ -4,9 +4,12 @@ Mixtral-style experts, y = w2 (silu(w1 x) * (w3 x)), top-k routing: each
 (token, expert) pair is the reference's split GEMV of that token through the
 expert's three matrices, each vector with its own statistics and outlier mask.
 Here the tokens routed to one expert go through the batched split GEMV
-together (the expert's weights stream once for all of them), the gated
-activation is one kernel (dq_silu_mul) and the weighted outputs are added
-into an FP32 buffer (dq_moe_combine).  With the experts spread over the ranks
+together (the expert's weights stream once for all of them).  w1 and w3 read
+the same x, so they are stacked into one [2 d_ff, d_model] matrix: one call,
+one plan of the tokens' outliers, and each row's result is the split GEMV of
+that row of w1 or w3.  The gated activation is one kernel on the stacked
+output (dq_silu_mul_pairs) and the weighted outputs are added into an FP32
+buffer (dq_moe_combine).  With the experts spread over the ranks
 of a process group, every rank runs its own experts on the tokens routed to
 them and the partial outputs are summed with one all-reduce.
 
@@ -73,6 +76,20 @@ def silu_mul(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     return h
 
 
+def silu_mul_pairs(ab: torch.Tensor) -> torch.Tensor:
+    """[rows, 2d] float16 (w1 x | w3 x per row) -> fp16(silu(first half) *
+    second half), [rows, d] (dq_silu_mul_pairs)."""
+    if ab.dtype != torch.float16 or ab.dim() != 2 or ab.shape[1] % 16 != 0:
+        raise RuntimeError("silu_mul_pairs takes a [rows, 2d] float16 tensor, d a multiple of 8")
+    ab = ab.contiguous()
+    d = ab.shape[1] // 2
+    h = torch.empty(ab.shape[0], d, dtype=torch.float16, device=ab.device)
+    _lib.check(_lib.lib().dq_silu_mul_pairs(C.c_void_p(ab.data_ptr()), C.c_void_p(h.data_ptr()), ab.shape[0], d,
+                                            C.c_void_p(torch.cuda.current_stream(ab.device).cuda_stream)),
+               "dq_silu_mul_pairs")
+    return h
+
+
 def combine_(out: torch.Tensor, y: torch.Tensor, rows: torch.Tensor, weight: torch.Tensor) -> None:
     """out[rows[i]] += weight[i] * y[i] in place (out float32 [T, d], y float16 [m, d])."""
     if y.numel() == 0:
@@ -90,29 +107,30 @@ class MoEFFN(torch.nn.Module):
 
     experts: the expert indices held here (default: all).  load_expert(e, w1,
     w3, w2) quantizes expert e's FP16 matrices ([d_ff, d_model], [d_ff,
-    d_model], [d_model, d_ff]); forward(x, routing, group) returns the
-    combined output [T, d_model] (float16) on every rank of group (the sum
-    over the ranks' experts)."""
+    d_model], [d_model, d_ff]), w1 and w3 stacked as w13[e] ([2 d_ff,
+    d_model]: rows 0 .. d_ff-1 are w1's, the rest w3's); forward(x, routing,
+    group) returns the combined output [T, d_model] (float16) on every rank of
+    group (the sum over the ranks' experts)."""
 
     def __init__(self, n_experts: int, d_model: int, d_ff: int, outlier_k: float = 3.0,
                  experts: Iterable[int] | None = None) -> None:
         super().__init__()
         self.n_experts, self.d_model, self.d_ff, self.outlier_k = n_experts, d_model, d_ff, outlier_k
         self.local: List[int] = sorted(experts) if experts is not None else list(range(n_experts))
-        self.w1 = torch.nn.ModuleDict({str(e): DynQuantLinear(d_model, d_ff, outlier_k) for e in self.local})
-        self.w3 = torch.nn.ModuleDict({str(e): DynQuantLinear(d_model, d_ff, outlier_k) for e in self.local})
+        self.w13 = torch.nn.ModuleDict({str(e): DynQuantLinear(d_model, 2 * d_ff, outlier_k) for e in self.local})
         self.w2 = torch.nn.ModuleDict({str(e): DynQuantLinear(d_ff, d_model, outlier_k) for e in self.local})
 
     def load_expert(self, e: int, w1: torch.Tensor, w3: torch.Tensor, w2: torch.Tensor) -> None:
-        self.w1[str(e)].load_weight(w1)
-        self.w3[str(e)].load_weight(w3)
+        self.w13[str(e)].load_weight(torch.cat([w1, w3]).contiguous())
         self.w2[str(e)].load_weight(w2)
+
+    def gate_up(self, e: int, x: torch.Tensor) -> torch.Tensor:
+        """[w1 x | w3 x] of the rows of x ([m, d_model] -> [m, 2 d_ff], float16)."""
+        return self.w13[str(e)](x).reshape(x.shape[0], -1)
 
     def expert(self, e: int, x: torch.Tensor) -> torch.Tensor:
         """The expert's FFN on the rows of x ([m, d_model] -> [m, d_model], float16)."""
-        a = self.w1[str(e)](x)
-        b = self.w3[str(e)](x)
-        return self.w2[str(e)](silu_mul(a.reshape(x.shape[0], -1), b.reshape(x.shape[0], -1)))
+        return self.w2[str(e)](silu_mul_pairs(self.gate_up(e, x)))
 
     def forward(self, x: torch.Tensor, routing: MoERouting, group=None, out: torch.Tensor | None = None
                 ) -> torch.Tensor:

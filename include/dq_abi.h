@@ -218,6 +218,14 @@ DQ_API dq_status_t dq_split_gemv_batched(const dq_weights_t* w, const uint16_t* 
 DQ_API dq_status_t dq_silu_mul(const uint16_t* a, const uint16_t* b, uint16_t* h, int64_t n, void* stream);
 
 /*
+ * The same gated activation on the output of the fused gate/up projection
+ * [w1; w3] (one split GEMV with both matrices stacked): ab is [rows][2d],
+ * row r holding (w1 x_r, w3 x_r); h[r][j] = fp16(silu(ab[r][j]) * ab[r][d + j]),
+ * h [rows][d] (d a multiple of 8).  No counterpart in the reference.
+ */
+DQ_API dq_status_t dq_silu_mul_pairs(const uint16_t* ab, uint16_t* h, int32_t rows, int32_t d, void* stream);
+
+/*
  * Weighted combine of one expert's outputs: out[rows[i]][:] += weight[i] *
  * y[i][:] for i < m (y FP16 [m][d], out FP32 [tokens][d], d a multiple of 8,
  * the rows of one call distinct).  Stream-ordered calls accumulate the

@@ -11,7 +11,7 @@ torch = pytest.importorskip("torch")
 
 import oracle as O  # noqa: E402
 from dyn_quant import synth  # noqa: E402
-from dyn_quant.moe import MoEFFN, MoERouting, moe_forward, silu_mul  # noqa: E402
+from dyn_quant.moe import MoEFFN, MoERouting, moe_forward, silu_mul, silu_mul_pairs  # noqa: E402
 from dq_testutil import check_y, dev, host  # noqa: E402
 from test_moe_cpu import oracle_expert  # noqa: E402
 
@@ -61,9 +61,10 @@ def test_moe_ffn_matches_oracle(E, D, F, T, K):
         (w1, p1, s1, z1), (w3, p3, s3, z3), (w2, p2, s2, z2) = mats[e]
         xe = x[rows.numpy()]
         m = len(xe)
-        a = layer.w1[str(e)](dev(xe)).reshape(m, -1)
-        b = layer.w3[str(e)](dev(xe)).reshape(m, -1)
-        h = silu_mul(a, b)
+        ab = layer.gate_up(e, dev(xe))
+        a, b = ab[:, :F], ab[:, F:]
+        h = silu_mul_pairs(ab)
+        assert torch.equal(h.view(torch.int16), silu_mul(a.contiguous(), b.contiguous()).view(torch.int16))
         y = layer.w2[str(e)](h).reshape(m, -1)
         a_h, b_h, h_h, y_h = host(a), host(b), host(h), host(y)
         for i in range(m):
