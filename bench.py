@@ -579,14 +579,23 @@ def run_e2e(args, spec, sets, acts_np, dev, job_step_bytes, world, rows, sharded
     import torch.distributed as dist
     from dyn_quant.sharded import gather_rows
     M = args.batch
-    xh = {k: torch.from_numpy(v).pin_memory() for k, v in acts_np.items()}
-    xd = {k: torch.empty(v.shape, dtype=torch.float16, device=dev) for k, v in acts_np.items()}
+    # The step's inputs sit in one pinned buffer (each 16-byte aligned) and go
+    # to the device in one copy; the outputs come back after the last GEMV, so
+    # the GEMV launches follow one another on the stream.
+    keys = list(acts_np)
+    segs = [(v.size + 7) // 8 * 8 for v in acts_np.values()]
+    offs = np.cumsum([0] + segs)
+    xh_all = torch.zeros(int(offs[-1]), dtype=torch.float16).pin_memory()
+    for i, k in enumerate(keys):
+        xh_all[int(offs[i]):int(offs[i]) + acts_np[k].size].copy_(torch.from_numpy(acts_np[k].reshape(-1)))
+    xd_all = torch.empty(int(offs[-1]), dtype=torch.float16, device=dev)
+    xd = {k: xd_all[int(offs[i]):int(offs[i]) + acts_np[k].size].view(acts_np[k].shape) for i, k in enumerate(keys)}
     yh = [torch.empty(M * (world * per if sharded else o), dtype=torch.float16).pin_memory()
           for (_, o, _, _, _), (_, _, per) in zip(spec, rows)]
     gbuf = [torch.empty(world * per, dtype=torch.float16, device=dev) for (_, _, per) in rows]
     ypad = [torch.zeros(M, per, dtype=torch.float16, device=dev) for (_, _, per) in rows]
     gbig = [torch.empty(world * M * per, dtype=torch.float16, device=dev) for (_, _, per) in rows]
-    h2d = sum(v.numel() * 2 for v in xh.values())
+    h2d = xh_all.numel() * 2
     d2h = sum(v.numel() * 2 for v in yh)
     stream = torch.cuda.current_stream(dev)
     times = []
@@ -595,12 +604,12 @@ def run_e2e(args, spec, sets, acts_np, dev, job_step_bytes, world, rows, sharded
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)
         start.record(stream)
-        for k in xh:
-            xd[k].copy_(xh[k], non_blocking=True)
+        xd_all.copy_(xh_all, non_blocking=True)
+        ys = []
         for gi, (name, d_out, d_in, frac, key) in enumerate(spec):
             if fused is not None:
                 fused(s, gi, stream, True, xd[key])
-                yh[gi].copy_(fulls[gi], non_blocking=True)
+                ys.append(fulls[gi])
                 continue
             y = sets[s][gi](xd[key])
             if sharded and M == 1:
@@ -609,6 +618,8 @@ def run_e2e(args, spec, sets, acts_np, dev, job_step_bytes, world, rows, sharded
                 ypad[gi][:, :y.shape[-1]].copy_(y)
                 dist.all_gather_into_tensor(gbig[gi], ypad[gi].reshape(-1))
                 y = gbig[gi]
+            ys.append(y)
+        for gi, y in enumerate(ys):
             yh[gi].copy_(y.reshape(-1), non_blocking=True)
         end.record(stream)
         end.synchronize()
@@ -626,7 +637,8 @@ def run_e2e(args, spec, sets, acts_np, dev, job_step_bytes, world, rows, sharded
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     if world == 1:
-        api = "DynQuantLinear.forward, pinned host buffers, synchronised every step"
+        api = ("DynQuantLinear.forward, pinned host buffers (one H2D of the step's inputs, the GEMVs, then "
+               "a D2H of each output), synchronised every step")
     elif sharded:
         api = ("DynQuantLinear.forward on each rank's rows + NCCL all-gather, pinned host buffers on "
                "every rank (bytes per rank), synchronised every step")

@@ -271,9 +271,59 @@ detect_outliers(const torch::Tensor& x, double outlier_k) {
     return {mask, idx, cnt, stats};
 }
 
+// The weights of one DynQuantLinear, checked once when the module's buffers are
+// (re)assigned, so that each forward call only checks x before the launch.
+// Holds references to the buffers, whose device addresses it keeps in a
+// dq_weights_t; the Python module drops the handle whenever a buffer object
+// changes (load_weight, load_state_dict, .to()).
+class SplitLinear {
+public:
+    SplitLinear(const torch::Tensor& packed, const torch::Tensor& scales, const torch::Tensor& zeros,
+                const torch::Tensor& fp16_w, const torch::Tensor& native, double outlier_k)
+        : packed_(packed), scales_(scales), zeros_(zeros), fp16_w_(fp16_w), native_(native), k_(outlier_k) {
+        TORCH_CHECK(fp16_w.dim() == 2, "fp16_weights must be 2D");
+        const auto probe = torch::empty({fp16_w.size(1)}, fp16_w.options());  // stands for x in the checks
+        w_ = make_weights(packed, scales, zeros, fp16_w, probe, true, native);
+        TORCH_CHECK(w_.native != nullptr, "SplitLinear needs the native layout (build_native)");
+        dev_ = fp16_w.device();
+        wsb_ = dq_workspace_bytes(w_.d_out, w_.d_in);
+    }
+
+    // y [d_out] for x [d_in] or [1, d_in] (float16, contiguous, on the weights'
+    // device); None for any other x, which the caller routes through the
+    // general path (dtype conversion, batches).
+    py::object forward(const torch::Tensor& x) {
+        if (!x.is_cuda() || x.scalar_type() != at::kHalf || !x.is_contiguous() || x.numel() != w_.d_in ||
+            x.dim() > 2 || x.device() != dev_)
+            return py::none();
+        torch::Tensor xa = (reinterpret_cast<uintptr_t>(x.data_ptr()) & 15u) ? x.clone() : x;
+        const at::cuda::CUDAGuard guard(dev_);
+        auto y = torch::empty({w_.d_out}, x.options());
+        void* stream = at::cuda::getCurrentCUDAStream().stream();
+        auto& ws = workspace_for(dev_, stream, wsb_);
+        check_status(dq_split_gemv(&w_, h16(xa), h16m(y), static_cast<float>(k_), ws.data_ptr(),
+                                   static_cast<size_t>(ws.numel()), stream),
+                     "split_gemv");
+        return py::cast(y);
+    }
+
+private:
+    torch::Tensor packed_, scales_, zeros_, fp16_w_, native_;
+    double k_;
+    dq_weights_t w_{};
+    torch::Device dev_{torch::kCPU};
+    size_t wsb_ = 0;
+};
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+    py::class_<SplitLinear>(m, "SplitLinear")
+        .def(py::init<const torch::Tensor&, const torch::Tensor&, const torch::Tensor&, const torch::Tensor&,
+                      const torch::Tensor&, double>(),
+             py::arg("packed"), py::arg("scales"), py::arg("zeros"), py::arg("fp16_weights"), py::arg("native"),
+             py::arg("outlier_k"))
+        .def("forward", &SplitLinear::forward, py::arg("x"));
     m.def("quantize_weights", &quantize_weights, "Quantize FP16 weight matrix to INT4 packed format");
     m.def("split_gemv", &split_gemv, "Fused dynamic-precision GEMV with runtime outlier detection",
           py::arg("packed"), py::arg("scales"), py::arg("zeros"), py::arg("fp16_weights"), py::arg("x"),

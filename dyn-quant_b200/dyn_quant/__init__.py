@@ -258,14 +258,50 @@ class DynQuantLinear(nn.Module):
         Returns:
             y: [d_out] float16 ([m, d_out] for a batch).
         """
+        fast = self.__dict__.get("_fast")
+        b = self._buffers
+        if (fast is not None and fast[1] is b["packed"] and fast[2] is b["fp16_w"] and fast[3] is b["_native"]
+                and fast[4] is b["scales"] and fast[5] is b["zeros"] and fast[6] == self.outlier_k):
+            y = fast[0].forward(x)
+            if y is not None:
+                return y
         if not self._quantized:
             raise RuntimeError("Call load_weight() before forward()")
+        self._refresh_fast()
         if x.dtype != torch.float16:
             x = x.to(torch.float16)
         if not x.is_contiguous():
             x = x.contiguous()
         return split_gemv(self.packed, self.scales, self.zeros, self.fp16_w, x, self.outlier_k,
                           self._native)
+
+    def _refresh_fast(self) -> None:
+        # The prebuilt weights handle for single vectors (checked once, then
+        # only x is checked per call), keyed on the buffer objects and k it
+        # was built from: forward() uses it only while all of them are the
+        # ones the module holds now.
+        b = self._buffers
+        key = (b["packed"], b["fp16_w"], b["_native"], b["scales"], b["zeros"], self.outlier_k)
+        fast = self.__dict__.get("_fast")
+        if fast is not None and all(u is v for u, v in zip(fast[1:6], key[:5])) and fast[6] == key[5]:
+            return
+        self._fast = None
+        if any(t is None or not t.is_cuda for t in key[:5]):
+            return
+        try:
+            handle = _C.SplitLinear(key[0], key[3], key[4], key[1], key[2], float(self.outlier_k))
+        except RuntimeError:
+            return  # not a layout the handle takes: the general path checks and reports
+        self._fast = (handle,) + key
+
+    def _apply(self, fn, *args, **kwargs):
+        self.__dict__["_fast"] = None  # .to() / .cuda() replace the buffers the handle refers to
+        return super()._apply(fn, *args, **kwargs)
+
+    def __getstate__(self):
+        state = self.__dict__.copy()
+        state["_fast"] = None  # the handle is rebuilt on the first forward()
+        return state
 
     def _load_from_state_dict(self, state_dict, prefix, local_metadata, strict, missing_keys,
                               unexpected_keys, error_msgs):

@@ -176,3 +176,49 @@ def test_misaligned_activation_view_is_rehomed():
     y1 = split_gemv(p, s, z, f, x, 3.0)
     y2 = split_gemv(p, s, z, f, x.clone(), 3.0)
     assert torch.equal(y1, y2)
+
+
+def test_forward_handle_follows_the_module():
+    """forward() on one vector goes through the prebuilt weights handle once
+    the module holds it; the result is the functional call's, bit for bit,
+    and the handle is rebuilt when the weights, k or the device placement of
+    the buffers change."""
+    d_out, d_in = 1024, 2048
+    w = torch.from_numpy(synth.weights(d_out, d_in, seed=11)).cuda()
+    x = torch.from_numpy(synth.activation(d_in, 0.02, seed=12)).cuda()
+    lin = DynQuantLinear(d_in, d_out, 3.0)
+    lin.load_weight(w)
+
+    def functional(m, v):
+        return split_gemv(m.packed, m.scales, m.zeros, m.fp16_w, v, m.outlier_k, m._native)
+
+    y0 = lin(x)  # first call: general path, builds the handle
+    assert lin.__dict__.get("_fast") is not None
+    assert torch.equal(lin(x), y0) and torch.equal(y0, functional(lin, x))
+    assert torch.equal(lin(x.view(1, d_in)), y0)
+    assert torch.equal(lin(x.float()), y0)  # not float16: general path, same result
+    xs = torch.from_numpy(synth.activation(d_in + 128, 0.02, seed=13)).cuda()[1:1 + d_in]
+    assert xs.data_ptr() % 16 != 0
+    assert torch.equal(lin(xs), functional(lin, xs.clone()))
+    # batches still take the batched path
+    xb = torch.stack([x, x.flip(0)])
+    assert lin(xb).shape == (2, d_out)
+    # new k: the handle must not keep the old threshold
+    lin.outlier_k = 1.5
+    y_k = lin(x)
+    assert torch.equal(y_k, functional(lin, x))
+    assert not torch.equal(y_k, y0)
+    # new weights: a rebuilt handle
+    lin.load_weight(-w)
+    y_neg = lin(x)
+    assert torch.equal(y_neg, functional(lin, x))
+    assert not torch.equal(y_neg, y_k)
+    # a module moved off the GPU and back keeps working
+    lin.cpu()
+    assert lin.__dict__.get("_fast") is None
+    lin.cuda()
+    assert torch.equal(lin(x), y_neg)
+    # the handle does not travel with a copy of the module
+    import copy
+    dup = copy.deepcopy(lin)
+    assert torch.equal(dup(x), y_neg)
