@@ -426,6 +426,22 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     timed_graph = capture(steps(0, args.steps))
     # (with the gather fused, the per-GEMV graphs time the kernel with its gather)
     per_gemv_graphs = [capture([(i % n_sets, gi) for i in range(args.steps)], gather=False) for gi in range(n_gemv)]
+
+    # For context, the INT4-only GEMV (the reference's int4_gemv: no detection,
+    # no FP16 columns) on the same weights, timed the same way (batch 1, one GPU).
+    def capture_int4(gi: int):
+        g = torch.cuda.CUDAGraph()
+        key = spec[gi][4]
+        with torch.cuda.graph(g, stream=stream):
+            cur = torch.cuda.current_stream()
+            for i in range(args.steps):
+                st = L.dq_int4_gemv(C.byref(structs[i % n_sets][gi]), C.c_void_p(acts[key].data_ptr()),
+                                    C.c_void_p(outs[gi].data_ptr()), C.c_void_p(wspace.data_ptr()), ws_bytes,
+                                    C.c_void_p(cur.cuda_stream))
+                if st != 0:
+                    raise RuntimeError(f"INT4 GEMV: {_lib.status_string(st)}")
+        return g
+    int4_graphs = [capture_int4(gi) for gi in range(n_gemv)] if (M == 1 and world == 1) else []
     torch.cuda.synchronize()
 
     with torch.cuda.stream(stream):
@@ -479,6 +495,15 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             e1.record(stream)
             e1.synchronize()
             per_gemv_us.append(e0.elapsed_time(e1) * 1e3 / args.steps)
+        int4_us = []
+        for g in int4_graphs:
+            g.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            g.replay()
+            e1.record(stream)
+            e1.synchronize()
+            int4_us.append(e0.elapsed_time(e1) * 1e3 / args.steps)
 
     per_gemv_bytes = [gemv_bytes(o, i, n_o[key], M) for _, o, i, _, key in spec]
     # The split GEMV kernel is the dominant (on one GPU the only) kernel: its
@@ -524,6 +549,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                               "rel_l2_vs_fp32": float(f"{rel_l2[j]:.3e}")}
             if sharded:
                 per_name[name]["rows"] = [rows[j][0], rows[j][1]]
+            if int4_us:
+                b4 = gemv_bytes(d_out, d_in, 0, 1)
+                per_name[name]["int4_only"] = {"us": round(int4_us[j], 3),
+                                               "gb_s": round(b4 / (int4_us[j] * 1e-6) / 1e9, 1)}
         traffic = ncu_traffic(args.workload)
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
@@ -558,7 +587,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         }
         print(json.dumps(line), flush=True)
 
-    del warm_graph, timed_graph, per_gemv_graphs
+    del warm_graph, timed_graph, per_gemv_graphs, int4_graphs
     if gathers:
         for g in gathers:
             g.close()
