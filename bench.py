@@ -624,8 +624,17 @@ def run_e2e(args, spec, sets, acts_np, dev, job_step_bytes, world, rows, sharded
     gbuf = [torch.empty(world * per, dtype=torch.float16, device=dev) for (_, _, per) in rows]
     ypad = [torch.zeros(M, per, dtype=torch.float16, device=dev) for (_, _, per) in rows]
     gbig = [torch.empty(world * M * per, dtype=torch.float16, device=dev) for (_, _, per) in rows]
+    # Unsharded at batch 1: the outputs land in slices of one device buffer (forward's
+    # out=) and come back in one copy.
+    one_out = not sharded and fused is None and M == 1
+    if one_out:
+        ysegs = [(M * o + 7) // 8 * 8 for (_, o, _, _, _) in spec]
+        yoffs = np.cumsum([0] + ysegs)
+        yd_all = torch.empty(int(yoffs[-1]), dtype=torch.float16, device=dev)
+        yh_all = torch.empty(int(yoffs[-1]), dtype=torch.float16).pin_memory()
+        yd = [yd_all[int(yoffs[gi]):int(yoffs[gi]) + o] for gi, (_, o, _, _, _) in enumerate(spec)]
     h2d = xh_all.numel() * 2
-    d2h = sum(v.numel() * 2 for v in yh)
+    d2h = yh_all.numel() * 2 if one_out else sum(v.numel() * 2 for v in yh)
     stream = torch.cuda.current_stream(dev)
     times = []
 
@@ -634,6 +643,13 @@ def run_e2e(args, spec, sets, acts_np, dev, job_step_bytes, world, rows, sharded
         end = torch.cuda.Event(enable_timing=True)
         start.record(stream)
         xd_all.copy_(xh_all, non_blocking=True)
+        if one_out:
+            for gi, (name, d_out, d_in, frac, key) in enumerate(spec):
+                sets[s][gi](xd[key], out=yd[gi])
+            yh_all.copy_(yd_all, non_blocking=True)
+            end.record(stream)
+            end.synchronize()
+            return start.elapsed_time(end)
         ys = []
         for gi, (name, d_out, d_in, frac, key) in enumerate(spec):
             if fused is not None:
@@ -666,8 +682,8 @@ def run_e2e(args, spec, sets, acts_np, dev, job_step_bytes, world, rows, sharded
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     if world == 1:
-        api = ("DynQuantLinear.forward, pinned host buffers (one H2D of the step's inputs, the GEMVs, then "
-               "a D2H of each output), synchronised every step")
+        api = ("DynQuantLinear.forward, pinned host buffers (one H2D of the step's inputs, the GEMVs writing "
+               "into one output buffer, one D2H of it), synchronised every step")
     elif sharded:
         api = ("DynQuantLinear.forward on each rank's rows + NCCL all-gather, pinned host buffers on "
                "every rank (bytes per rank), synchronised every step")

@@ -292,13 +292,19 @@ public:
     // y [d_out] for x [d_in] or [1, d_in] (float16, contiguous, on the weights'
     // device); None for any other x, which the caller routes through the
     // general path (dtype conversion, batches).
-    py::object forward(const torch::Tensor& x) {
+    // out: optional float16 [d_out] tensor on the same device to write y into
+    // (contiguous); y is returned either way.
+    py::object forward(const torch::Tensor& x, const c10::optional<torch::Tensor>& out) {
         if (!x.is_cuda() || x.scalar_type() != at::kHalf || !x.is_contiguous() || x.numel() != w_.d_in ||
             x.dim() > 2 || x.device() != dev_)
             return py::none();
+        const bool has_out = out.has_value() && out->defined();
+        if (has_out && (!out->is_cuda() || out->scalar_type() != at::kHalf || !out->is_contiguous() ||
+                        out->numel() != w_.d_out || out->device() != dev_))
+            return py::none();
         torch::Tensor xa = (reinterpret_cast<uintptr_t>(x.data_ptr()) & 15u) ? x.clone() : x;
         const at::cuda::CUDAGuard guard(dev_);
-        auto y = torch::empty({w_.d_out}, x.options());
+        auto y = has_out ? *out : torch::empty({w_.d_out}, x.options());
         void* stream = at::cuda::getCurrentCUDAStream().stream();
         auto& ws = workspace_for(dev_, stream, wsb_);
         check_status(dq_split_gemv(&w_, h16(xa), h16m(y), static_cast<float>(k_), ws.data_ptr(),
@@ -323,7 +329,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                       const torch::Tensor&, double>(),
              py::arg("packed"), py::arg("scales"), py::arg("zeros"), py::arg("fp16_weights"), py::arg("native"),
              py::arg("outlier_k"))
-        .def("forward", &SplitLinear::forward, py::arg("x"));
+        .def("forward", &SplitLinear::forward, py::arg("x"), py::arg("out") = py::none());
     m.def("quantize_weights", &quantize_weights, "Quantize FP16 weight matrix to INT4 packed format");
     m.def("split_gemv", &split_gemv, "Fused dynamic-precision GEMV with runtime outlier detection",
           py::arg("packed"), py::arg("scales"), py::arg("zeros"), py::arg("fp16_weights"), py::arg("x"),

@@ -248,21 +248,25 @@ class DynQuantLinear(nn.Module):
         self._native = _C.build_native(packed, scales, zeros)
         self._quantized = True
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         """y = W_split x for one activation vector, or for each row of a batch.
 
         Args:
-            x: [d_in] float16 activation vector, or [m, d_in] (each row with
-               its own outlier mask; up to 16 rows share one weight stream).
+            x:   [d_in] float16 activation vector, or [m, d_in] (each row with
+                 its own outlier mask; up to 16 rows share one weight stream).
+            out: optional tensor to write y into (same shape as y, float16),
+                 e.g. a slice of one buffer that gathers several layers'
+                 outputs for a single copy to the host.  Not in the reference
+                 API, which always allocates y.
 
         Returns:
-            y: [d_out] float16 ([m, d_out] for a batch).
+            y: [d_out] float16 ([m, d_out] for a batch); `out` when given.
         """
         fast = self.__dict__.get("_fast")
         b = self._buffers
         if (fast is not None and fast[1] is b["packed"] and fast[2] is b["fp16_w"] and fast[3] is b["_native"]
                 and fast[4] is b["scales"] and fast[5] is b["zeros"] and fast[6] == self.outlier_k):
-            y = fast[0].forward(x)
+            y = fast[0].forward(x, out)
             if y is not None:
                 return y
         if not self._quantized:
@@ -272,8 +276,12 @@ class DynQuantLinear(nn.Module):
             x = x.to(torch.float16)
         if not x.is_contiguous():
             x = x.contiguous()
-        return split_gemv(self.packed, self.scales, self.zeros, self.fp16_w, x, self.outlier_k,
-                          self._native)
+        y = split_gemv(self.packed, self.scales, self.zeros, self.fp16_w, x, self.outlier_k, self._native)
+        if out is None:
+            return y
+        if out.shape != y.shape:
+            raise RuntimeError(f"out has shape {tuple(out.shape)}, expected {tuple(y.shape)}")
+        return out.copy_(y)
 
     def _refresh_fast(self) -> None:
         # The prebuilt weights handle for single vectors (checked once, then

@@ -200,6 +200,15 @@ def test_forward_handle_follows_the_module():
     xs = torch.from_numpy(synth.activation(d_in + 128, 0.02, seed=13)).cuda()[1:1 + d_in]
     assert xs.data_ptr() % 16 != 0
     assert torch.equal(lin(xs), functional(lin, xs.clone()))
+    # out=: y written into a slice of a larger buffer, the slice returned
+    buf = torch.zeros(d_out + 64, dtype=torch.float16, device="cuda")
+    o = buf[8:8 + d_out]
+    r = lin(x, out=o)
+    assert r.data_ptr() == o.data_ptr() and torch.equal(o, y0)
+    assert torch.equal(buf[:8], torch.zeros(8, dtype=torch.float16, device="cuda"))
+    assert torch.equal(lin(x.float(), out=o), y0)  # general path, same result
+    with pytest.raises(RuntimeError):
+        lin(x, out=buf[:d_out - 1])
     # batches still take the batched path
     xb = torch.stack([x, x.flip(0)])
     assert lin(xb).shape == (2, d_out)
