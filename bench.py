@@ -285,6 +285,24 @@ def run_reference(args, rank: int, world: int) -> None:
 # ---------------------------------------------------------------------------
 # GPU leg
 # ---------------------------------------------------------------------------
+def init_nccl(dev) -> None:
+    """The process group (nccl) with its communicator created eagerly, while
+    file descriptor 1 points at stderr: NCCL's own start-up lines then stay
+    out of stdout, which carries rank 0's one JSON line."""
+    import datetime
+    import torch.distributed as dist
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        dist.barrier()
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved, 1)
+        os.close(saved)
+
+
 def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     import torch
     import torch.distributed as dist
@@ -292,8 +310,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        init_nccl(dev)
 
     import dyn_quant
     from dyn_quant import _lib
@@ -738,8 +755,7 @@ def run_moe(args, rank: int, world: int, local_rank: int) -> None:
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        init_nccl(dev)
     from dyn_quant import synth
     from dyn_quant.moe import MoEFFN, MoERouting
 
