@@ -19,9 +19,9 @@ GEMV = d_out*d_in/2 (INT4) + 4*d_out*d_in/128 (FP16 scale + zero)
 One process per GPU.  Under torchrun (N > 1) the 70B workloads are
 row-sharded, as a 70B model is deployed: each rank holds whole 16-row blocks
 of the weights, runs the split GEMV on its slice with the same x, and the
-output slices are gathered inside the GEMV kernel over NVLink peer memory
-(--gather peer, the default) or all-gathered with NCCL after every GEMV
-(--gather nccl) ("scaling": "strong": the total work is the workload's,
+output slices are all-gathered with NCCL after every GEMV (--gather nccl,
+the default) or gathered inside the GEMV kernel over NVLink peer memory
+(--gather peer) ("scaling": "strong": the total work is the workload's,
 whatever N).  The 7B and sweep
 workloads fit one GPU and run as N independent replicas (data parallel, no
 collective, "scaling": "weak"); --shard overrides either choice.  The time is
@@ -994,9 +994,9 @@ def main(argv=None) -> None:
     ap.add_argument("--frac", type=float, default=None, help="injected outlier fraction (default: the workload's)")
     ap.add_argument("--k", type=float, default=K_OUTLIER, help="outlier threshold in standard deviations")
     ap.add_argument("--dist", choices=["normal", "t3"], default="normal", help="activation distribution")
-    ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
-                    help="row-sharded runs: the output slices gathered inside the GEMV kernel over NVLink peer "
-                         "memory, or by an NCCL all-gather after it")
+    ap.add_argument("--gather", choices=["peer", "nccl"], default="nccl",
+                    help="row-sharded runs: the output slices gathered by an NCCL all-gather after each GEMV "
+                         "(default: the faster at 2 GPUs), or inside the GEMV kernel over NVLink peer memory")
     ap.add_argument("--shard", choices=["auto", "rows", "replicas"], default="auto",
                     help="N > 1: row sharding with an all-gather, or independent replicas; auto follows the "
                          "deployment of each shape: rows for the 70B workloads, replicas for the 7B and sweep ones")
