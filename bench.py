@@ -2,41 +2,47 @@
 """Benchmark of the dyn-quant fused split GEMV on B200.
 
 Metric: microseconds per GEMV and achieved HBM GB/s (fraction of the measured
-B200 copy bandwidth) at Llama-2 7B/70B dimensions, batch 1, INT4 group 128,
-k = 3.0.  A "step" is one batch-1 pass through the GEMVs of one workload:
+B200 copy bandwidth) at Llama-2 7B/70B dimensions, INT4 group 128, k = 3.0.
+A "step" is one batch-1 pass through the GEMVs of one workload:
 
-  llama2_7b_mlp  (default) gate 4096->11008, up 4096->11008, down 11008->4096, 1 % outliers
-  llama2_7b_q    q_proj 4096->4096, 2 % outliers
-  llama2_70b_mlp gate/up 8192->28672, down 28672->8192, 3 % outliers
+  llama2_70b_mlp (default) gate 8192->28672, up 8192->28672, down 28672->8192, 3 % outliers
   llama2_70b_q   q_proj 8192->8192, 3 % outliers
+  llama2_7b_mlp  gate 4096->11008, up 4096->11008, down 11008->4096, 1 % outliers
+  llama2_7b_q    q_proj 4096->4096, 2 % outliers
+  sweep_8192     one 8192x8192 GEMV (--batch, --frac, --k, --dist: the outlier / batch sweep)
+  mixtral_moe    Mixtral-8x7B FFN decode step: 8 experts, 16 tokens, top-2
 
-value = whole-job algorithmic bytes / time (GB/s, inputs resident in HBM,
-each step a CUDA graph of that step's launches; weights rotate over enough
-copies that every step reads them from HBM, not L2).  Algorithmic bytes per
-GEMV = d_out*d_in/2 (INT4) + 4*d_out*d_in/128 (FP16 scale + zero)
-+ 2*d_out*n_o (FP16 outlier columns, n_o = detected outliers) + 2*d_in (x) + 2*d_out (y).
+value = whole-job algorithmic bytes / time (GB/s; inputs resident in HBM; the
+K timed steps are one CUDA graph of back-to-back launches; weights rotate over
+enough copies that every step reads them from HBM, not L2).  Algorithmic bytes
+per GEMV = d_out*d_in/2 (INT4) + 4*d_out*d_in/128 (FP16 scale + zero)
++ 2*d_out*n_o (FP16 outlier columns, n_o = detected outliers; for a batch the
+union of the vectors' masks) + 2*m*d_in (x) + 2*m*d_out (y).
+
+Weights and activations are seeded synthetic tensors (dyn_quant/synth.py):
+weight matrix i of a workload is synth.weights(d_out, d_in, seed=100 + i) in
+both arms; the GPU arm's extra rotating copies are row rotations of it.
 
 One process per GPU.  Under torchrun (N > 1) the 70B workloads are
 row-sharded, as a 70B model is deployed: each rank holds whole 16-row blocks
 of the weights, runs the split GEMV on its slice with the same x, and the
-output slices are all-gathered with NCCL after every GEMV (--gather nccl,
-the default) or gathered inside the GEMV kernel over NVLink peer memory
-(--gather peer) ("scaling": "strong": the total work is the workload's,
-whatever N).  The 7B and sweep
-workloads fit one GPU and run as N independent replicas (data parallel, no
-collective, "scaling": "weak"); --shard overrides either choice.  The time is
-the max over ranks; value is the algorithmic bytes of the whole job over that
-time.  The roofline line describes this rank's kernel alone.
+output slices are gathered after every GEMV ("scaling": "strong": the total
+work is the workload's, whatever N).  The 7B and sweep workloads fit one GPU
+and run as N independent replicas ("scaling": "weak"); --shard overrides
+either choice.  The time is the max over ranks.  At N = 1 the line also
+carries extra blocks (7B MLP, 7B q_proj, the Mixtral MoE step and one point
+of the outlier / batch sweep), each with its own per-GEMV numbers.
 
 --impl reference times the reference's split GEMV restated on the CPU (the
 reference has no CPU GEMV of its own; this is the oracle port, OpenMP over
-rows) on the host cores, same workload and metric; under torchrun only rank 0
-runs it.
+rows) on the host cores, same workload, config and metric; under torchrun
+only rank 0 runs it (one host) and it loads no GPU library.
 """
 from __future__ import annotations
 
 import argparse
 import ctypes as C
+import importlib.util
 import json
 import math
 import os
@@ -71,12 +77,27 @@ WORKLOADS = {
     "sweep_8192": [("w", 8192, 8192, 0.01, "h")],
 }
 
-
 # Mixtral-8x7B-shaped MoE FFN decode step: E experts (w1/w3 D->F, w2 F->D),
 # T tokens with top-K experts drawn uniformly from a seed.
 MOE_WORKLOADS = {
     "mixtral_moe": dict(E=8, D=4096, F=14336, T=16, K=2, frac=0.02),
 }
+
+# Extra blocks of the default N = 1 line: (workload, batch, outlier fraction or None, k, dist).
+EXTRAS = [("llama2_7b_mlp", 1, None, K_OUTLIER, "normal"), ("llama2_7b_q", 1, None, K_OUTLIER, "normal"),
+          ("sweep_8192", 16, 0.05, K_OUTLIER, "normal"), ("mixtral_moe", 1, None, K_OUTLIER, "normal")]
+
+
+class WL:
+    """One measured workload: its name and the sweep parameters."""
+
+    def __init__(self, name: str, batch: int = 1, frac: float | None = None, k: float = K_OUTLIER,
+                 dist: str = "normal") -> None:
+        self.name, self.batch, self.frac, self.k, self.dist = name, batch, frac, k, dist
+
+    @classmethod
+    def from_args(cls, args) -> "WL":
+        return cls(args.workload, args.batch, args.frac, args.k, args.dist)
 
 
 def gemv_bytes(d_out: int, d_in: int, n_o: int, m: int = 1) -> int:
@@ -86,34 +107,74 @@ def gemv_bytes(d_out: int, d_in: int, n_o: int, m: int = 1) -> int:
     return d_out * d_in // 2 + 4 * d_out * (d_in // 128) + 2 * d_out * n_o + 2 * m * (d_in + d_out)
 
 
-def shard_mode(args) -> str:
+def shard_mode(wl: WL, shard: str) -> str:
     """How N > 1 ranks split a GEMV workload (see --shard)."""
-    if args.shard != "auto":
-        return args.shard
-    return "rows" if args.workload.startswith("llama2_70b") else "replicas"
+    if shard != "auto":
+        return shard
+    return "rows" if wl.name.startswith("llama2_70b") else "replicas"
 
 
-def workload_spec(args):
-    """The workload's GEMVs, with --frac applied."""
-    spec = WORKLOADS[args.workload]
-    if args.frac is not None:
-        spec = [(n, o, i, args.frac, key) for n, o, i, _, key in spec]
+def workload_spec(wl: WL):
+    """The workload's GEMVs, with the fraction override applied."""
+    spec = WORKLOADS[wl.name]
+    if wl.frac is not None:
+        spec = [(n, o, i, wl.frac, key) for n, o, i, _, key in spec]
     return spec
 
 
-def activations(args, seed_base: int = 0):
+_SYNTH = None
+
+
+def synth():
+    """dyn_quant/synth.py loaded by file path: the CPU legs use the seeded
+    generators without importing the dyn_quant package (and its GPU library)."""
+    global _SYNTH
+    if _SYNTH is None:
+        spec = importlib.util.spec_from_file_location("dq_bench_synth", os.path.join(PKG_DIR, "dyn_quant", "synth.py"))
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        _SYNTH = mod
+    return _SYNTH
+
+
+def weights_np(d_out: int, d_in: int, gi: int) -> np.ndarray:
+    """Weight matrix gi of a workload (both arms)."""
+    return synth().weights(d_out, d_in, seed=100 + gi)
+
+
+def activations(wl: WL, seed_base: int = 0):
     """Seeded activations per key (numpy f16): [d_in], or [batch, d_in] with
     vector t drawn from seed + t."""
-    from dyn_quant import synth
+    S = synth()
     acts = {}
-    for name, d_out, d_in, frac, key in workload_spec(args):
+    for name, d_out, d_in, frac, key in workload_spec(wl):
         if key not in acts:
             seed = seed_base + (1 if key == "h" else 2)
-            if args.batch == 1:
-                acts[key] = synth.activation(d_in, frac, seed=seed, dist=args.dist)
+            if wl.batch == 1:
+                acts[key] = S.activation(d_in, frac, seed=seed, dist=wl.dist)
             else:
-                acts[key] = synth.activations(args.batch, d_in, frac, seed=seed, dist=args.dist)
+                acts[key] = S.activations(wl.batch, d_in, frac, seed=seed, dist=wl.dist)
     return acts
+
+
+def workload_config(wl: WL, world: int, shard: str, gather: str) -> dict:
+    """The line's `config`: the workload and how it is run at this N (the
+    same dict in both arms)."""
+    spec = workload_spec(wl)
+    sharded = world > 1 and shard_mode(wl, shard) == "rows"
+    if sharded:
+        par = (f"row-sharded over {world} GPUs, the output slices gathered "
+               + ("by each GEMV kernel over NVLink peer memory" if gather == "peer" else
+                  "by an NCCL all-gather after every GEMV"))
+    elif world > 1:
+        par = f"{world} independent replicas (data parallel, no collective)"
+    else:
+        par = "1 GPU"
+    return {"workload": wl.name, "gemvs": [[n, o, i] for n, o, i, *_ in spec], "batch": wl.batch, "group": 128,
+            "outlier_k": wl.k, "outlier_frac": spec[0][3], "dist": wl.dist,
+            "weights": "synth.weights(d_out, d_in, seed=100 + i), FP16 N(0, 1/d_in)",
+            "l2": "inputs larger than L2: the GPU arm's steps rotate over weight copies totalling >= 3x L2",
+            "parallelism": par}
 
 
 # ---------------------------------------------------------------------------
@@ -184,30 +245,30 @@ def measured_peak_gbs():
         return FALLBACK_HBM_GBS, "of fallback"
 
 
-def ncu_traffic(workload: str):
-    """Mean DRAM bytes (read + write) per split-GEMV launch of the workload, from
-    the committed ncu summary profiles/ncu_traffic.json, if it has the workload."""
+def ncu_traffic(workload: str, batch: int):
+    """DRAM bytes (read + write) per algorithmic byte of the workload's split
+    GEMV launches, from the committed ncu summary profiles/ncu_traffic.json
+    (one capture on one GPU), and the summary it comes from."""
     p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
     try:
         with open(p) as f:
-            entry = json.load(f).get(workload)
+            entry = json.load(f).get(f"{workload}/m{batch}")
     except (OSError, ValueError):
-        return None
+        return None, None
     if not entry:
-        return None
-    return entry.get("dram_bytes_per_launch")
+        return None, None
+    return entry["dram_bytes_per_launch"] / entry["algorithmic_bytes_per_launch"], entry.get("source")
 
 
 # ---------------------------------------------------------------------------
 # CPU legs (oracle port of the reference's split GEMV)
 # ---------------------------------------------------------------------------
-def cpu_prepare(args):
+def cpu_prepare(wl: WL):
     import oracle as O
-    from dyn_quant import synth
-    acts = activations(args)
+    acts = activations(wl)
     mats = []
-    for i, (name, d_out, d_in, frac, key) in enumerate(workload_spec(args)):
-        w = synth.weights(d_out, d_in, seed=100 + i)
+    for i, (name, d_out, d_in, frac, key) in enumerate(workload_spec(wl)):
+        w = weights_np(d_out, d_in, i)
         mats.append((name, w, *O.quantize(w), acts[key]))
     return mats
 
@@ -227,25 +288,24 @@ def cpu_step(mats, k: float):
     return total
 
 
-def cpu_baseline(args, budget_s: float = 10.0) -> dict:
+def cpu_baseline(wl: WL, budget_s: float = 10.0) -> dict:
     import oracle as O
-    workload = args.workload
     cores = os.cpu_count() or 1
     O.set_num_threads(cores)
-    mats = cpu_prepare(args)
-    cpu_step(mats, args.k)  # warm
+    mats = cpu_prepare(wl)
+    cpu_step(mats, wl.k)  # warm
     t0 = time.perf_counter()
     nbytes, n = 0, 0
     while True:
-        nbytes += cpu_step(mats, args.k)
+        nbytes += cpu_step(mats, wl.k)
         n += 1
         if time.perf_counter() - t0 >= budget_s:
             break
     dt = time.perf_counter() - t0
     gb_s = nbytes / dt / 1e9
     return {"value": round(gb_s, 3), "unit": "GB/s", "cores": O.num_threads(), "kind": "port",
-            "sample": f"{n} full {workload} steps (split GEMV incl. detection) in {dt:.1f} s, "
-                      f"OpenMP over rows, oracle/dq_oracle.c -O3",
+            "sample": f"{n} full {wl.name} steps (split GEMV incl. detection, same weights and activations as the "
+                      f"GPU arm's first weight copy) in {dt:.1f} s, OpenMP over rows, oracle/dq_oracle.c -O3",
             "us_per_gemv": round(dt / (n * len(mats)) * 1e6, 1)}
 
 
@@ -253,15 +313,18 @@ def run_reference(args, rank: int, world: int) -> None:
     if rank != 0:
         return
     import oracle as O
+    wl = WL.from_args(args)
+    if wl.name in MOE_WORKLOADS:
+        return run_moe_reference(args, rank, world)
     cores = os.cpu_count() or 1
     O.set_num_threads(cores)
-    mats = cpu_prepare(args)
+    mats = cpu_prepare(wl)
     for _ in range(args.warmup):
-        cpu_step(mats, args.k)
+        cpu_step(mats, wl.k)
     t0 = time.perf_counter()
     nbytes = 0
     for _ in range(args.steps):
-        nbytes += cpu_step(mats, args.k)
+        nbytes += cpu_step(mats, wl.k)
     dt = time.perf_counter() - t0
     value = nbytes / dt / 1e9
     ngemv = len(mats)
@@ -269,21 +332,21 @@ def run_reference(args, rank: int, world: int) -> None:
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
-        "scaling": "strong" if world > 1 else "weak",
-        "vs_baseline": None, "dtype": "w4a16 (fp32 accumulate)", "data": "synthetic",
-        "config": {"workload": args.workload, "gemvs": [[n, o, i] for n, o, i, *_ in workload_spec(args)],
-                   "batch": args.batch, "outlier_k": args.k, "group": 128, "dist": args.dist},
+        "scaling": "fixed (one host)", "vs_baseline": None, "dtype": "w4a16 (fp32 accumulate)",
+        "data": "synthetic (seeded N(0,1/d_in) weights, N(0,1) activations with U[10,100] outliers)",
+        "config": workload_config(wl, world, args.shard, args.gather),
+        "execution": f"rank 0 only, on its host's {O.num_threads()} cores (the other ranks exit without work)",
         "us_per_gemv": round(dt / (args.steps * ngemv) * 1e6, 2),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": O.num_threads(), "kind": "port",
-                         "sample": f"{args.steps} full {args.workload} steps on the host cores (the reference "
-                                   f"ships no CPU split GEMV; this is its kernel restated in C, OpenMP over rows)"},
+                         "sample": f"{args.steps} full {wl.name} steps on the host cores (the reference ships no "
+                                   f"CPU split GEMV; this is its kernel restated in C, OpenMP over rows)"},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
 # ---------------------------------------------------------------------------
-# GPU leg
+# GPU legs
 # ---------------------------------------------------------------------------
 def init_nccl(dev) -> None:
     """The process group (nccl) with its communicator created eagerly, while
@@ -303,29 +366,35 @@ def init_nccl(dev) -> None:
         os.close(saved)
 
 
-def run_ours(args, rank: int, world: int, local_rank: int) -> None:
+def graph_time_us(stream, g, n: int) -> float:
+    """Mean µs per launch of a graph of n launches (one warm replay first)."""
+    import torch
+    with torch.cuda.stream(stream):
+        g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        g.replay()
+        e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1) * 1e3 / n
+
+
+def gemv_block(args, wl: WL, rank: int, world: int, dev, main: bool) -> dict:
+    """Measure one GEMV workload; returns the fields of its JSON line (rank 0)
+    or of its extra block."""
     import torch
     import torch.distributed as dist
-
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    if world > 1:
-        init_nccl(dev)
 
     import dyn_quant
     from dyn_quant import _lib
     from dyn_quant.sharded import shard_rows
 
     L = _lib.lib()
-    spec = workload_spec(args)
-    M = args.batch
-    sharded = world > 1 and shard_mode(args) == "rows"
-    peer = sharded and args.gather == "peer"  # the all-gather fused into the GEMV kernel
-    # Row sharding across the ranks: every rank holds whole 16-row blocks of
-    # each GEMV, sees the same x, and the output slices are all-gathered with
-    # NCCL after every GEMV.  Replicas: every rank runs the whole workload on
-    # its own weights and activations (data parallel, no collective).
-    acts_np = activations(args, 0 if sharded else 1000 * rank)
+    spec = workload_spec(wl)
+    M = wl.batch
+    sharded = world > 1 and shard_mode(wl, args.shard) == "rows"
+    peer = sharded and args.gather == "peer"  # the gather fused into the GEMV kernel
+    acts_np = activations(wl, 0 if sharded else 1000 * rank)
     acts = {k: torch.from_numpy(v).to(dev) for k, v in acts_np.items()}
     rows = [shard_rows(o, world, rank) if sharded else (0, o, o) for _, o, _, _, _ in spec]
 
@@ -333,58 +402,51 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     # batch, the union of the vectors' masks, whose FP16 columns are read)
     n_o = {}
     for key, x in acts.items():
-        masks = [dyn_quant.detect_outliers(r, args.k)[0] for r in x.reshape(-1, x.shape[-1])]
+        masks = [dyn_quant.detect_outliers(r, wl.k)[0] for r in x.reshape(-1, x.shape[-1])]
         n_o[key] = int(torch.stack(masks).any(0).sum().item())
-    # algorithmic bytes of one step (the full GEMVs, whatever the sharding)
     step_bytes = sum(gemv_bytes(o, i, n_o[key], M) for _, o, i, _, key in spec)
     job_step_bytes = step_bytes  # the whole job's: replicas add theirs
     if world > 1 and not sharded:
         t = torch.tensor([step_bytes], dtype=torch.float64, device=dev)
         dist.all_reduce(t)
         job_step_bytes = int(t.item())
-    # this rank's kernel bytes of one step
     local_bytes = [gemv_bytes(max(r1 - r0, 0), i, n_o[key], M)
                    for (_, _, i, _, key), (r0, r1, _) in zip(spec, rows)]
     n_gemv = len(spec)
-    kernels_per_gemv = 1 if M == 1 else 3  # batched: plan, FP16 part, INT4 part
+    kernels_per_gemv = 1 if M == 1 else 3  # batched: plan, INT4 part, FP16 part
 
-    # weight sets, rotated so each step reads its weights from HBM
+    # weight copies, rotated so each step reads its weights from HBM: copy 0 is
+    # the seeded matrix (this rank's rows), the others row rotations of it
     n_sets = max(2, math.ceil(3 * L2_BYTES / max(sum(local_bytes), 1)))
     if args.max_sets:
         n_sets = min(n_sets, args.max_sets)  # profiling runs: ncu flushes caches itself
-    gen = torch.Generator(device=dev)
-    sets = []
-    for s in range(n_sets):
-        mods = []
-        for gi, (name, d_out, d_in, frac, key) in enumerate(spec):
-            gen.manual_seed(10_000 * rank + 100 * s + gi)
-            n_rows = rows[gi][1] - rows[gi][0]
-            if n_rows <= 0:
-                raise SystemExit(f"{name}: {d_out} rows do not give every one of {world} ranks a row block")
-            w = (torch.randn(n_rows, d_in, generator=gen, device=dev, dtype=torch.float32) / math.sqrt(d_in)).half()
-            if peer and n_rows < rows[gi][2]:  # every rank runs the same shape: zero rows pad the last slices
-                w = torch.cat([w, torch.zeros(rows[gi][2] - n_rows, d_in, dtype=w.dtype, device=dev)])
-                n_rows = rows[gi][2]
-            lin = dyn_quant.DynQuantLinear(d_in, n_rows, args.k)
+    sets = [[] for _ in range(n_sets)]
+    for gi, (name, d_out, d_in, frac, key) in enumerate(spec):
+        r0, r1, per = rows[gi]
+        if r1 <= r0:
+            raise SystemExit(f"{name}: {d_out} rows do not give every one of {world} ranks a row block")
+        w0 = torch.from_numpy(weights_np(d_out, d_in, gi)[r0:r1]).to(dev)
+        n_rows = r1 - r0
+        if peer and n_rows < per:  # every rank runs the same shape: zero rows pad the last slices
+            w0 = torch.cat([w0, torch.zeros(per - n_rows, d_in, dtype=w0.dtype, device=dev)])
+            n_rows = per
+        for s in range(n_sets):
+            w = w0 if s == 0 else torch.roll(w0, shifts=s * 97, dims=0).contiguous()
+            lin = dyn_quant.DynQuantLinear(d_in, n_rows, wl.k)
             lin.load_weight(w)
             del w
-            mods.append(lin)
-        sets.append(mods)
+            sets[s].append(lin)
+        del w0
     torch.cuda.synchronize()
 
-    # local outputs (padded to the common slice height) and the gathered outputs
     outs = [torch.zeros(M * per, dtype=torch.float16, device=dev) for (_, _, per) in rows]
     fulls = [torch.empty(world * M * per, dtype=torch.float16, device=dev) for (_, _, per) in rows]
     ws_bytes = max(L.dq_workspace_bytes(r1 - r0, i) if M == 1 else L.dq_workspace_bytes_batched(r1 - r0, i, M)
                    for (_, _, i, _, _), (r0, r1, _) in zip(spec, rows))
-    wspace = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)  # zero-filled once, left zeroed by every call
-    structs = []
-    for mods in sets:
-        row = []
-        for lin in mods:
-            row.append(_lib.weights(lin.packed.data_ptr(), lin.scales.data_ptr(), lin.zeros.data_ptr(), None,
-                                    lin.fp16_w.data_ptr(), lin.d_out, lin.d_in, lin._native.data_ptr()))
-        structs.append(row)
+    wspace = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)  # zero-filled once
+    structs = [[_lib.weights(lin.packed.data_ptr(), lin.scales.data_ptr(), lin.zeros.data_ptr(), None,
+                             lin.fp16_w.data_ptr(), lin.d_out, lin.d_in, lin._native.data_ptr()) for lin in mods]
+               for mods in sets]
 
     gathers = None
     if peer:
@@ -393,47 +455,45 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             raise SystemExit("--gather peer runs batch 1")
         gathers = [PeerGather(per, o, None, dev) for (_, o, _, _, _), (_, _, per) in zip(spec, rows)]
 
-    def launch_gemv(s: int, gi: int, stream, gather: bool = True, x=None):
-        name, d_out, d_in, frac, key = spec[gi]
-        if peer:  # one kernel: this rank's rows, then every rank's rows into the full y
-            xs = acts[key] if x is None else x
+    def launch_gemv(s: int, gi: int, stream, gather: bool = True, x=None, split: bool = True):
+        key = spec[gi][4]
+        xs = acts[key] if x is None else x
+        if not split:
+            st = L.dq_int4_gemv(C.byref(structs[s][gi]), C.c_void_p(xs.data_ptr()), C.c_void_p(outs[gi].data_ptr()),
+                                C.c_void_p(wspace.data_ptr()), ws_bytes, C.c_void_p(stream.cuda_stream))
+        elif peer:  # one kernel: this rank's rows, then every rank's rows into the full y
             st = L.dq_split_gemv_gather(C.byref(structs[s][gi]), C.c_void_p(xs.data_ptr()),
-                                        C.c_void_p(fulls[gi].data_ptr()), args.k, C.c_void_p(wspace.data_ptr()),
+                                        C.c_void_p(fulls[gi].data_ptr()), wl.k, C.c_void_p(wspace.data_ptr()),
                                         ws_bytes, C.byref(gathers[gi].desc), C.c_void_p(stream.cuda_stream))
-            if st != 0:
-                raise RuntimeError(f"split GEMV with gather: {_lib.status_string(st)}")
-            return
-        if M == 1:
-            st = L.dq_split_gemv(C.byref(structs[s][gi]), C.c_void_p(acts[key].data_ptr()),
-                                 C.c_void_p(outs[gi].data_ptr()), args.k, C.c_void_p(wspace.data_ptr()),
+        elif M == 1:
+            st = L.dq_split_gemv(C.byref(structs[s][gi]), C.c_void_p(xs.data_ptr()),
+                                 C.c_void_p(outs[gi].data_ptr()), wl.k, C.c_void_p(wspace.data_ptr()),
                                  ws_bytes, C.c_void_p(stream.cuda_stream))
         else:
-            st = L.dq_split_gemv_batched(C.byref(structs[s][gi]), C.c_void_p(acts[key].data_ptr()),
-                                         C.c_void_p(outs[gi].data_ptr()), M, args.k, C.c_void_p(wspace.data_ptr()),
+            st = L.dq_split_gemv_batched(C.byref(structs[s][gi]), C.c_void_p(xs.data_ptr()),
+                                         C.c_void_p(outs[gi].data_ptr()), M, wl.k, C.c_void_p(wspace.data_ptr()),
                                          ws_bytes, C.c_void_p(stream.cuda_stream))
         if st != 0:
-            raise RuntimeError(f"split GEMV: {_lib.status_string(st)}")
-        if sharded and gather:
+            raise RuntimeError(f"GEMV: {_lib.status_string(st)}")
+        if split and sharded and not peer and gather:
             dist.all_gather_into_tensor(fulls[gi], outs[gi])
-
-    def launch_step(s: int, stream):
-        for gi in range(n_gemv):
-            launch_gemv(s, gi, stream)
 
     stream = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(stream):
-        launch_step(0, stream)  # first call: kernel attributes, module load
+        for gi in range(n_gemv):  # first calls: kernel attributes, module load
+            launch_gemv(0, gi, stream)
+            if M == 1 and world == 1:
+                launch_gemv(0, gi, stream, split=False)
     stream.synchronize()
 
     # Graphs of back-to-back launches (no events between kernels, so each launch
-    # overlaps its predecessor's tail as it would in a decode step).  Weight sets
-    # rotate, so every launch streams its weights from HBM.
-    def capture(launches, gather: bool = True):
+    # overlaps its predecessor's tail as it would in a decode step).
+    def capture(launches, gather: bool = True, split: bool = True):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
             cur = torch.cuda.current_stream()
             for s, gi in launches:
-                launch_gemv(s, gi, cur, gather)
+                launch_gemv(s, gi, cur, gather, split=split)
         return g
 
     def steps(first: int, count: int):
@@ -441,32 +501,20 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
 
     warm_graph = capture(steps(0, max(args.warmup, n_sets)))
     timed_graph = capture(steps(0, args.steps))
-    # (with the gather fused, the per-GEMV graphs time the kernel with its gather)
+    # per-GEMV graphs: one shape at a time, outside the timed region (with the
+    # gather fused, the kernel with its gather; with NCCL, the kernel alone)
     per_gemv_graphs = [capture([(i % n_sets, gi) for i in range(args.steps)], gather=False) for gi in range(n_gemv)]
-
     # For context, the INT4-only GEMV (the reference's int4_gemv: no detection,
     # no FP16 columns) on the same weights, timed the same way (batch 1, one GPU).
-    def capture_int4(gi: int):
-        g = torch.cuda.CUDAGraph()
-        key = spec[gi][4]
-        with torch.cuda.graph(g, stream=stream):
-            cur = torch.cuda.current_stream()
-            for i in range(args.steps):
-                st = L.dq_int4_gemv(C.byref(structs[i % n_sets][gi]), C.c_void_p(acts[key].data_ptr()),
-                                    C.c_void_p(outs[gi].data_ptr()), C.c_void_p(wspace.data_ptr()), ws_bytes,
-                                    C.c_void_p(cur.cuda_stream))
-                if st != 0:
-                    raise RuntimeError(f"INT4 GEMV: {_lib.status_string(st)}")
-        return g
-    int4_graphs = [capture_int4(gi) for gi in range(n_gemv)] if (M == 1 and world == 1) else []
+    int4_graphs = ([capture([(i % n_sets, gi) for i in range(args.steps)], gather=False, split=False)
+                    for gi in range(n_gemv)] if (M == 1 and world == 1) else [])
     torch.cuda.synchronize()
 
     with torch.cuda.stream(stream):
         warm_graph.replay()  # >= W untimed warm-up steps
     stream.synchronize()
 
-    # clocks: sample across a soak window that contains the timed region
-    sampler = ClockSampler(local_rank) if not args.no_clocks else None
+    sampler = ClockSampler(dev.index) if (main and not args.no_clocks) else None
     if sampler:
         sampler.start()
 
@@ -478,7 +526,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                     warm_graph.replay()
                 stream.synchronize()
 
-    soak(args.soak)
+    soak(args.soak if main else 0.1)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -492,7 +540,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    soak(args.soak)
+    soak(args.soak if main else 0.0)
     clocks = sampler.stop() if sampler else None
 
     elapsed_ms = t_start.elapsed_time(t_end)
@@ -501,49 +549,29 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         elapsed_ms = float(t.item())
 
-    # per-GEMV breakdown: the same launches, one GEMV shape at a time (outside the timed region)
-    per_gemv_us = []
-    with torch.cuda.stream(stream):
-        for g in per_gemv_graphs:
-            g.replay()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            g.replay()
-            e1.record(stream)
-            e1.synchronize()
-            per_gemv_us.append(e0.elapsed_time(e1) * 1e3 / args.steps)
-        int4_us = []
-        for g in int4_graphs:
-            g.replay()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            g.replay()
-            e1.record(stream)
-            e1.synchronize()
-            int4_us.append(e0.elapsed_time(e1) * 1e3 / args.steps)
+    per_gemv_us = [graph_time_us(stream, g, args.steps) for g in per_gemv_graphs]
+    int4_us = [graph_time_us(stream, g, args.steps) for g in int4_graphs]
 
-    per_gemv_bytes = [gemv_bytes(o, i, n_o[key], M) for _, o, i, _, key in spec]
     # The split GEMV kernel is the dominant (on one GPU the only) kernel: its
-    # average launch duration is the timed region over the launches, and achieved
-    # = algorithmic bytes per launch / that duration.  Sharded runs time the
-    # kernel alone in the per-GEMV graphs (the timed region also holds the
-    # all-gathers).
+    # average launch duration is the timed region over the launches, and
+    # achieved = algorithmic bytes per launch / that duration.  Sharded runs
+    # time the kernel alone in the per-GEMV graphs (the timed region also
+    # holds the gathers).
     peak, peak_note = measured_peak_gbs()
     if sharded:
         achieved = sum(local_bytes) / (sum(per_gemv_us) * 1e-6) / 1e9
     else:
-        achieved = sum(per_gemv_bytes) * args.steps / (elapsed_ms * 1e-3) / 1e9
-
-    # whole-job throughput: the full GEMVs' bytes (every replica's) over the max-over-ranks time
+        achieved = sum(local_bytes) * args.steps / (elapsed_ms * 1e-3) / 1e9
     value = job_step_bytes * args.steps / (elapsed_ms * 1e-3) / 1e9
     us_per_gemv = elapsed_ms * 1e3 / (args.steps * n_gemv)
 
-    # end to end through the public API: pinned host x in, host y out, every step
-    e2e = run_e2e(args, spec, sets, acts_np, dev, job_step_bytes, world, rows, sharded,
-                  launch_gemv if peer else None, fulls)
+    e2e = None
+    if main:
+        e2e = run_e2e(args, wl, spec, sets, acts_np, dev, job_step_bytes, world, rows, sharded,
+                      launch_gemv if peer else None, fulls)
 
-    # accuracy of this rank's rows (weight set 0) against an FP32 dense GEMV on
-    # the original FP16 weights and activations
+    # accuracy of this rank's rows (weight copy 0) against an FP32 dense GEMV
+    # on the original FP16 weights and activations
     rel_l2 = []
     for gi, (name, d_out, d_in, frac, key) in enumerate(spec):
         lin = sets[0][gi]
@@ -552,17 +580,14 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         y32 = x.float() @ lin.fp16_w.float().t()
         rel_l2.append(float((torch.linalg.vector_norm(y - y32) / torch.linalg.vector_norm(y32)).item()))
 
-    # CPU baseline on rank 0 at N = 1
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(args, args.cpu_budget)
-
+    out = None
     if rank == 0:
         per_name = {}
         for j, (name, d_out, d_in, _, key) in enumerate(spec):
             us = per_gemv_us[j]
             per_name[name] = {"shape": [d_out, d_in], "n_outliers": n_o[key], "bytes": local_bytes[j],
                               "us": round(us, 3), "gb_s": round(local_bytes[j] / (us * 1e-6) / 1e9, 1),
+                              "frac": round(local_bytes[j] / (us * 1e-6) / 1e9 / peak, 4),
                               "rel_l2_vs_fp32": float(f"{rel_l2[j]:.3e}")}
             if sharded:
                 per_name[name]["rows"] = [rows[j][0], rows[j][1]]
@@ -570,50 +595,36 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                 b4 = gemv_bytes(d_out, d_in, 0, 1)
                 per_name[name]["int4_only"] = {"us": round(int4_us[j], 3),
                                                "gb_s": round(b4 / (int4_us[j] * 1e-6) / 1e9, 1)}
-        traffic = ncu_traffic(args.workload)
-        line = {
-            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(elapsed_ms / args.steps, 5),
-            "higher_is_better": True, "scaling": "strong" if sharded else "weak", "vs_baseline": None,
-            "dtype": "w4a16 (fp32 accumulate)", "data": "synthetic (seeded N(0,1/d_in) weights, N(0,1) "
-                                                        "activations with U[10,100] outliers)",
-            "config": {"workload": args.workload, "gemvs": [[n, o, i] for n, o, i, *_ in spec], "batch": M,
-                       "group": 128, "outlier_k": args.k, "outlier_frac": spec[0][3], "dist": args.dist,
-                       "l2": f"inputs larger than L2: {n_sets} rotating weight sets "
-                             f"({n_sets * step_bytes / 1e6:.0f} MB streamed per cycle)",
-                       "graphs": "the K timed steps are one CUDA graph of back-to-back launches",
-                       "parallelism": (f"row-sharded over {world} GPUs, the output slices gathered inside the "
-                                       "GEMV kernel over NVLink peer memory" if peer else
-                                       f"row-sharded over {world} GPUs, NCCL all-gather of the output slices "
-                                       "after every GEMV" if sharded else
-                                       (f"{world} independent replicas (data parallel, no collective)"
-                                        if world > 1 else "1 GPU"))},
+        per_launch = sum(local_bytes) / n_gemv
+        ratio, source = ncu_traffic(wl.name, M)
+        traffic = round(ratio * per_launch) if ratio else None
+        out = {
+            "value": round(value, 2), "ms_per_step": round(elapsed_ms / args.steps, 5),
+            "scaling": "strong" if sharded else "weak",
+            "config": workload_config(wl, world, args.shard, args.gather),
             "us_per_gemv": round(us_per_gemv, 3),
             "gemvs": per_name,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_note": peak_note,
-                         "kernel": ("b1_kernel<split, native unit layout, staged outlier segments>" if M == 1 else
-                                    "bplan_kernel + bout_kernel + bdense_kernel (one batched split GEMV call)"),
-                         "algorithmic_bytes_per_launch": round(sum(local_bytes) / n_gemv),
-                         "traffic": traffic},
-            # our kernel launches in the timed region (NCCL not counted)
+                         "kernel": ("split GEMV kernel (native unit layout, staged outlier columns)" if M == 1 else
+                                    "batched split GEMV (plan, INT4 part, FP16 part)"),
+                         "algorithmic_bytes_per_launch": round(per_launch),
+                         "traffic": traffic,
+                         "traffic_note": (f"ncu dram__bytes_read.sum + dram__bytes_write.sum per algorithmic byte of "
+                                          f"one 1-GPU capture ({source}) times this rank's algorithmic bytes per "
+                                          f"launch" if ratio else "no ncu capture of this workload")},
             "gpu_launches": args.steps * n_gemv * kernels_per_gemv,
             "e2e": e2e,
             "clocks": clocks,
-            "cpu_baseline": cpu,
         }
-        print(json.dumps(line), flush=True)
-
     del warm_graph, timed_graph, per_gemv_graphs, int4_graphs
     if gathers:
         for g in gathers:
             g.close()
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    return out
 
 
-def run_e2e(args, spec, sets, acts_np, dev, job_step_bytes, world, rows, sharded, fused=None, fulls=None):
+def run_e2e(args, wl, spec, sets, acts_np, dev, job_step_bytes, world, rows, sharded, fused=None, fulls=None):
     """The same steps through DynQuantLinear.forward from pinned host buffers.
 
     Row-sharded runs gather each GEMV's output slices with
@@ -624,7 +635,7 @@ def run_e2e(args, spec, sets, acts_np, dev, job_step_bytes, world, rows, sharded
     import torch
     import torch.distributed as dist
     from dyn_quant.sharded import gather_rows
-    M = args.batch
+    M = wl.batch
     # The step's inputs sit in one pinned buffer (each 16-byte aligned) and go
     # to the device in one copy; the outputs come back after the last GEMV, so
     # the GEMV launches follow one another on the stream.
@@ -694,7 +705,6 @@ def run_e2e(args, spec, sets, acts_np, dev, job_step_bytes, world, rows, sharded
         times.append(step(i % n_sets))
     ms = max(statistics.mean(times), 1e-9)
     if world > 1:
-        import torch.distributed as dist
         t = torch.tensor([ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
@@ -702,7 +712,7 @@ def run_e2e(args, spec, sets, acts_np, dev, job_step_bytes, world, rows, sharded
         api = ("DynQuantLinear.forward, pinned host buffers (one H2D of the step's inputs, the GEMVs writing "
                "into one output buffer, one D2H of it), synchronised every step")
     elif sharded:
-        api = ("DynQuantLinear.forward on each rank's rows + NCCL all-gather, pinned host buffers on "
+        api = ("DynQuantLinear.forward on each rank's rows + the gather, pinned host buffers on "
                "every rank (bytes per rank), synchronised every step")
     else:
         api = (f"DynQuantLinear.forward on {world} replicas, pinned host buffers on every rank (bytes per "
@@ -721,6 +731,17 @@ def moe_routing_np(cfg: dict, seed: int = 0):
     ex = np.stack([rng.choice(cfg["E"], cfg["K"], replace=False) for _ in range(cfg["T"])])
     w = rng.random((cfg["T"], cfg["K"])).astype(np.float32)
     return ex, w / w.sum(1, keepdims=True)
+
+
+def moe_config(wl: WL, world: int) -> dict:
+    cfg = dict(MOE_WORKLOADS[wl.name], k=wl.k)
+    if wl.frac is not None:
+        cfg["frac"] = wl.frac
+    return {"workload": wl.name, "experts": cfg["E"], "d_model": cfg["D"], "d_ff": cfg["F"], "tokens": cfg["T"],
+            "top_k": cfg["K"], "outlier_frac": cfg["frac"], "outlier_k": wl.k, "dist": wl.dist,
+            "l2": "inputs larger than L2: the GPU arm's steps rotate over weight copies totalling >= 3x L2",
+            "parallelism": (f"expert-parallel over {world} GPUs (expert e on rank e % {world}), NCCL all-reduce "
+                            "of the FP32 combined outputs") if world > 1 else "1 GPU, all experts"}
 
 
 def moe_step_bytes(cfg: dict, routing, x, layer, experts) -> int:
@@ -748,25 +769,19 @@ def moe_step_bytes(cfg: dict, routing, x, layer, experts) -> int:
     return total
 
 
-def run_moe(args, rank: int, world: int, local_rank: int) -> None:
+def moe_block(args, wl: WL, rank: int, world: int, dev, main: bool) -> dict | None:
     import torch
     import torch.distributed as dist
-
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    if world > 1:
-        init_nccl(dev)
-    from dyn_quant import synth
     from dyn_quant.moe import MoEFFN, MoERouting
 
-    cfg = dict(MOE_WORKLOADS[args.workload], k=args.k)
-    if args.frac is not None:
-        cfg["frac"] = args.frac
+    cfg = dict(MOE_WORKLOADS[wl.name], k=wl.k)
+    if wl.frac is not None:
+        cfg["frac"] = wl.frac
     E, D, F, T = cfg["E"], cfg["D"], cfg["F"], cfg["T"]
     local = [e for e in range(E) if e % world == rank]
     ex, w = moe_routing_np(cfg)
     routing = MoERouting(torch.from_numpy(ex), torch.from_numpy(w), E, device=dev)
-    x = torch.from_numpy(synth.activations(T, D, cfg["frac"], seed=1, dist=args.dist)).to(dev)
+    x = torch.from_numpy(synth().activations(T, D, cfg["frac"], seed=1, dist=wl.dist)).to(dev)
     # this rank's experts; several copies when they would fit in L2, so that
     # every step streams its weights from HBM
     per_copy = sum((2 * F * D + D * F) // 2 for _ in local)
@@ -776,7 +791,7 @@ def run_moe(args, rank: int, world: int, local_rank: int) -> None:
     gen = torch.Generator(device=dev)
     layers = []
     for s_ in range(n_sets):
-        layer = MoEFFN(E, D, F, args.k, experts=local)
+        layer = MoEFFN(E, D, F, wl.k, experts=local)
         for e in local:
             ws = []
             for j, (o, i) in enumerate(((F, D), (F, D), (D, F))):
@@ -812,10 +827,10 @@ def run_moe(args, rank: int, world: int, local_rank: int) -> None:
     with torch.cuda.stream(stream):
         warm.replay()
     stream.synchronize()
-    sampler = ClockSampler(local_rank) if not args.no_clocks else None
+    sampler = ClockSampler(dev.index) if (main and not args.no_clocks) else None
     if sampler:
         sampler.start()
-    t_end = time.perf_counter() + args.soak
+    t_end = time.perf_counter() + (args.soak if main else 0.1)
     with torch.cuda.stream(stream):
         while time.perf_counter() < t_end:
             warm.replay()
@@ -861,58 +876,43 @@ def run_moe(args, rank: int, world: int, local_rank: int) -> None:
         t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = moe_cpu_baseline(args, cfg, args.cpu_budget)
-    if rank == 0:
-        n_tok = {e: routing.count(e) for e in range(E)}
-        line = {
-            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
-            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
-            "dtype": "w4a16 (fp32 accumulate)",
-            "data": "synthetic (seeded N(0,1/d_in) weights, N(0,1) tokens with U[10,100] outliers, seeded top-2 routing)",
-            "config": {"workload": args.workload, "experts": E, "d_model": D, "d_ff": F, "tokens": T, "top_k": cfg["K"],
-                       "outlier_frac": cfg["frac"], "outlier_k": args.k, "tokens_per_expert": n_tok,
-                       "parallelism": (f"expert-parallel over {world} GPUs (expert e on rank e % {world}), "
-                                       "NCCL all-reduce of the FP32 combined outputs") if world > 1 else "1 GPU, all experts",
-                       "l2": f"{n_sets} rotating weight copies per rank",
-                       "graphs": "the K timed steps are one CUDA graph"},
-            "step_bytes": step_bytes,
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "peak_note": peak_note,
-                         "kernel": "one MoE step on rank 0: per expert the batched split GEMV (plan, INT4 part, "
-                                   "FP16 part) on the stacked [w1; w3] and on w2, dq_silu_mul_pairs, dq_moe_combine",
-                         "algorithmic_bytes_per_step": local_bytes, "traffic": None},
-            "gpu_launches": args.steps * sum(8 for e in local if routing.count(e)),
-            "e2e": {"value": round(step_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-                    "h2d_bytes_per_step": T * D * 2, "d2h_bytes_per_step": T * D * 2, "ms_per_step": round(e2e_ms, 4),
-                    "api": "MoEFFN.forward, pinned host buffers, synchronised every step"},
-            "clocks": clocks,
-            "cpu_baseline": cpu,
-        }
-        print(json.dumps(line), flush=True)
     del warm, timed
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    if rank != 0:
+        return None
+    n_tok = {e: routing.count(e) for e in range(E)}
+    return {
+        "value": round(value, 2), "ms_per_step": round(ms / args.steps, 5),
+        "scaling": "strong" if world > 1 else "weak",
+        "config": moe_config(wl, world), "tokens_per_expert": n_tok, "step_bytes": step_bytes,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_note": peak_note,
+                     "kernel": "one MoE step on rank 0: the batched split GEMV (plan, INT4 part, FP16 part) on each "
+                               "expert's stacked [w1; w3] and w2, dq_silu_mul_pairs, dq_moe_combine",
+                     "algorithmic_bytes_per_step": local_bytes, "traffic": None,
+                     "traffic_note": "no ncu capture of this workload"},
+        "gpu_launches": args.steps * sum(8 for e in local if routing.count(e)),
+        "e2e": {"value": round(step_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": T * D * 2, "d2h_bytes_per_step": T * D * 2, "ms_per_step": round(e2e_ms, 4),
+                "api": "MoEFFN.forward, pinned host buffers, synchronised every step"},
+        "clocks": clocks,
+    }
 
 
 def moe_cpu_sample(cfg: dict, n_pairs: int, seed: int = 0):
     """The first n_pairs (token, expert) pairs of the routing, with each
-    expert's matrices quantized by the oracle (seeded, smaller seeds than the
-    GPU copies: a CPU sample of the same shapes)."""
+    expert's matrices quantized by the oracle (seeded: a CPU sample of the
+    same shapes)."""
     import oracle as O
-    from dyn_quant import synth
+    S = synth()
     ex, w = moe_routing_np(cfg, seed)
-    x = synth.activations(cfg["T"], cfg["D"], cfg["frac"], seed=1)
+    x = S.activations(cfg["T"], cfg["D"], cfg["frac"], seed=1)
     pairs = [(t, int(ex[t, j])) for t in range(cfg["T"]) for j in range(cfg["K"])][:n_pairs]
     mats = {}
     for _, e in pairs:
         if e not in mats:
-            mats[e] = [(m, *O.quantize(m)) for m in (synth.weights(cfg["F"], cfg["D"], seed=10 + e),
-                                                     synth.weights(cfg["F"], cfg["D"], seed=20 + e),
-                                                     synth.weights(cfg["D"], cfg["F"], seed=30 + e))]
+            mats[e] = [(m, *O.quantize(m)) for m in (S.weights(cfg["F"], cfg["D"], seed=10 + e),
+                                                     S.weights(cfg["F"], cfg["D"], seed=20 + e),
+                                                     S.weights(cfg["D"], cfg["F"], seed=30 + e))]
     return x, pairs, mats
 
 
@@ -932,15 +932,16 @@ def moe_cpu_pairs(cfg: dict, x, pairs, mats, k: float) -> int:
     return total
 
 
-def moe_cpu_baseline(args, cfg: dict, budget_s: float) -> dict:
+def moe_cpu_baseline(wl: WL, budget_s: float) -> dict:
     import oracle as O
+    cfg = dict(MOE_WORKLOADS[wl.name], k=wl.k)
     O.set_num_threads(os.cpu_count() or 1)
     x, pairs, mats = moe_cpu_sample(cfg, 4)
-    moe_cpu_pairs(cfg, x, pairs[:1], mats, args.k)  # warm
+    moe_cpu_pairs(cfg, x, pairs[:1], mats, wl.k)  # warm
     t0 = time.perf_counter()
     nbytes, n = 0, 0
     while True:
-        nbytes += moe_cpu_pairs(cfg, x, pairs, mats, args.k)
+        nbytes += moe_cpu_pairs(cfg, x, pairs, mats, wl.k)
         n += len(pairs)
         if time.perf_counter() - t0 >= budget_s:
             break
@@ -954,23 +955,25 @@ def run_moe_reference(args, rank: int, world: int) -> None:
     if rank != 0:
         return
     import oracle as O
+    wl = WL.from_args(args)
     O.set_num_threads(os.cpu_count() or 1)
-    cfg = dict(MOE_WORKLOADS[args.workload], k=args.k)
+    cfg = dict(MOE_WORKLOADS[wl.name], k=wl.k)
     x, pairs, mats = moe_cpu_sample(cfg, 2)
     for _ in range(max(1, args.warmup // 3)):
-        moe_cpu_pairs(cfg, x, pairs[:1], mats, args.k)
+        moe_cpu_pairs(cfg, x, pairs[:1], mats, wl.k)
     t0 = time.perf_counter()
     nbytes = 0
     for _ in range(args.steps):
-        nbytes += moe_cpu_pairs(cfg, x, pairs, mats, args.k)
+        nbytes += moe_cpu_pairs(cfg, x, pairs, mats, wl.k)
     dt = time.perf_counter() - t0
     value = nbytes / dt / 1e9
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
-        "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "fixed (one host)", "vs_baseline": None,
         "dtype": "w4a16 (fp32 accumulate)", "data": "synthetic",
-        "config": {"workload": args.workload, **{k: v for k, v in cfg.items()}},
+        "config": moe_config(wl, world),
+        "execution": f"rank 0 only, on its host's {O.num_threads()} cores (the other ranks exit without work)",
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": O.num_threads(), "kind": "port",
                          "sample": f"each step: {len(pairs)} (token, expert) FFN evaluations of the workload on the "
                                    "host cores (the reference computes one split GEMV per token and expert)"},
@@ -979,29 +982,79 @@ def run_moe_reference(args, rank: int, world: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+def run_ours(args, rank: int, world: int, local_rank: int) -> None:
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        init_nccl(dev)
+    wl = WL.from_args(args)
+    if wl.name in MOE_WORKLOADS:
+        main = moe_block(args, wl, rank, world, dev, True)
+    else:
+        main = gemv_block(args, wl, rank, world, dev, True)
+    extras = {}
+    if not args.no_extras and args.batch == 1:
+        for name, batch, frac, k, dist_ in EXTRAS:
+            if name == wl.name:
+                continue
+            if world > 1 and name not in MOE_WORKLOADS:
+                continue  # at N > 1: the main workload, and the MoE step expert-parallel
+            ewl = WL(name, batch, frac, k, dist_)
+            blk = (moe_block if name in MOE_WORKLOADS else gemv_block)(args, ewl, rank, world, dev, False)
+            torch.cuda.empty_cache()
+            if rank == 0:
+                blk.pop("clocks", None)
+                extras[name if batch == 1 else f"{name}/m{batch}/frac{frac}"] = blk
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = moe_cpu_baseline(wl, args.cpu_budget) if wl.name in MOE_WORKLOADS else cpu_baseline(wl, args.cpu_budget)
+    if rank == 0:
+        line = {"metric": METRIC, "value": main["value"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": main["ms_per_step"], "higher_is_better": True,
+                "scaling": main["scaling"], "vs_baseline": None, "dtype": "w4a16 (fp32 accumulate)",
+                "data": "synthetic (seeded N(0,1/d_in) weights, N(0,1) activations with U[10,100] outliers)",
+                "config": main["config"]}
+        for k_ in ("us_per_gemv", "gemvs", "tokens_per_expert", "step_bytes", "roofline", "gpu_launches", "e2e",
+                   "clocks"):
+            if k_ in main:
+                line[k_] = main[k_]
+        line["cpu_baseline"] = cpu
+        if extras:
+            line["extras"] = extras
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(MOE_WORKLOADS), default="llama2_7b_mlp")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(MOE_WORKLOADS), default="llama2_70b_mlp")
     ap.add_argument("--soak", type=float, default=0.6, help="seconds of replays before/after the timed region")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="measure the main workload only")
     ap.add_argument("--batch", type=int, default=1, help="activation vectors per GEMV call (1..16 per kernel)")
     ap.add_argument("--frac", type=float, default=None, help="injected outlier fraction (default: the workload's)")
     ap.add_argument("--k", type=float, default=K_OUTLIER, help="outlier threshold in standard deviations")
     ap.add_argument("--dist", choices=["normal", "t3"], default="normal", help="activation distribution")
     ap.add_argument("--gather", choices=["peer", "nccl"], default="nccl",
-                    help="row-sharded runs: the output slices gathered by an NCCL all-gather after each GEMV "
-                         "(default: the faster at 2 GPUs), or inside the GEMV kernel over NVLink peer memory")
+                    help="row-sharded runs: the output slices gathered by an NCCL all-gather after each GEMV, "
+                         "or inside the GEMV kernel over NVLink peer memory")
     ap.add_argument("--shard", choices=["auto", "rows", "replicas"], default="auto",
-                    help="N > 1: row sharding with an all-gather, or independent replicas; auto follows the "
+                    help="N > 1: row sharding with a gather, or independent replicas; auto follows the "
                          "deployment of each shape: rows for the 70B workloads, replicas for the 7B and sweep ones")
     ap.add_argument("--max-sets", type=int, default=0,
-                    help="cap on rotating weight sets (profiling runs only; the default rotates through >= 3x L2)")
+                    help="cap on rotating weight copies (profiling runs only; the default rotates through >= 3x L2)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -1010,12 +1063,7 @@ def main(argv=None) -> None:
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.workload in MOE_WORKLOADS:
-        if args.impl == "reference":
-            run_moe_reference(args, rank, world)
-        else:
-            run_moe(args, rank, world, local_rank)
-    elif args.impl == "reference":
+    if args.impl == "reference":
         run_reference(args, rank, world)
     else:
         run_ours(args, rank, world, local_rank)

@@ -22,8 +22,8 @@ CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-LIB_SOURCES = ["dq_gemv.cu", "dq_batched.cu", "dq_moe.cu", "dq_abi.cu"]
-LIB_HEADERS = ["dq_common.cuh", "dq_internal.h", "dq_plan.cuh"]
+LIB_SOURCES = ["dq_gemv.cu", "dq_stream.cu", "dq_batched.cu", "dq_moe.cu", "dq_abi.cu"]
+LIB_HEADERS = ["dq_common.cuh", "dq_internal.h", "dq_plan.cuh", "dq_gplan.cuh"]
 LIB_PATH = os.path.join(PKG, "libdq_b200.so")
 EXT_SUFFIX = sysconfig.get_config_var("EXT_SUFFIX") or ".so"
 EXT_PATH = os.path.join(PKG, "_C" + EXT_SUFFIX)

@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -139,12 +140,15 @@ dq_status_t dq_build_native(const uint8_t* packed, const uint16_t* scales, const
 
 dq_status_t dq_read_device_error(uint32_t* word, int clear) {
     if (!word) return DQ_ERR_INVALID_ARGUMENT;
-    uint32_t b1 = 0, bg = 0;
+    uint32_t b1 = 0, bg = 0, bs = 0;
     dq_status_t st = read_device_error(&b1, clear != 0);
     if (st != DQ_OK) return st;
     st = read_batched_error(&bg, clear != 0);
     if (st != DQ_OK) return st;
-    *word = b1 | (bg << 8);
+    st = read_stream_error(&bs, clear != 0);
+    if (st != DQ_OK) return st;
+    // streaming kernel: bit 0 of its word (own copies) -> bit 5, bit 1 (another rank's rows) -> bit 4
+    *word = b1 | (bg << 8) | ((bs & 1u) ? (1u << 5) : 0u) | ((bs & 2u) ? (1u << 4) : 0u);
     return DQ_OK;
 }
 
@@ -193,7 +197,35 @@ dq_status_t dq_split_gemv_batched(const dq_weights_t* w, const uint16_t* x, uint
 
 size_t dq_workspace_bytes(int32_t d_out, int32_t d_in) {
     if (check_dims(d_out, d_in) != DQ_OK) return 0;
-    return ws_layout(d_out, d_in).total;
+    return stream_ws(d_out, d_in).total;
+}
+
+dq_status_t dq_reset_workspace(void* workspace, size_t workspace_bytes, void* stream) {
+    if (!workspace) return DQ_ERR_INVALID_ARGUMENT;
+    const size_t head = ws_header().total;
+    const cudaError_t e = cudaMemsetAsync(workspace, 0, workspace_bytes < head ? workspace_bytes : head,
+                                          static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) { set_cuda_error(e); return DQ_ERR_CUDA; }
+    return DQ_OK;
+}
+
+// The plain split / INT4 GEMV runs the batch-1 kernel of dq_gemv.cu, which is
+// the faster of the two on B200 at every Llama-2 shape measured.  The
+// streaming kernel (dq_stream.cu) carries the fused row-sharded gather; with
+// DQ_STREAM=1 in the environment (read once) it also serves the plain calls
+// it supports (native layout, column-major mirror for the split GEMV), for
+// timing the two against each other.
+static bool stream_requested() {
+    static const bool on = [] {
+        const char* s = std::getenv("DQ_STREAM");
+        return s && s[0] == '1';
+    }();
+    return on;
+}
+
+static bool use_stream(const dq_weights_t& w, bool split, size_t workspace_bytes) {
+    return stream_requested() && stream_supported(w, split) && stream_geom(w.d_out, w.d_in).n_rb <= kStreamMaxRb &&
+           workspace_bytes >= stream_ws(w.d_out, w.d_in).total;
 }
 
 dq_status_t dq_split_gemv(const dq_weights_t* w, const uint16_t* x, uint16_t* y, float outlier_k,
@@ -201,6 +233,8 @@ dq_status_t dq_split_gemv(const dq_weights_t* w, const uint16_t* x, uint16_t* y,
     if (w && w->d_out == 0 && check_dims(w->d_out, w->d_in) == DQ_OK) return DQ_OK;
     dq_status_t st = check_weights(w, x, y, true, workspace, workspace_bytes);
     if (st != DQ_OK) return st;
+    if (use_stream(*w, true, workspace_bytes))
+        return launch_gemv_stream(*w, x, y, outlier_k, true, workspace, nullptr, static_cast<cudaStream_t>(stream));
     return launch_gemv_b1(*w, x, y, outlier_k, true, workspace, static_cast<cudaStream_t>(stream));
 }
 
@@ -223,8 +257,10 @@ dq_status_t dq_split_gemv_gather(const dq_weights_t* w, const uint16_t* x, uint1
     dq_status_t st = check_weights(w, x, y, true, workspace, workspace_bytes);
     if (st != DQ_OK) return st;
     if (w->d_out != g->rows_per) return DQ_ERR_SHAPE;
-    if (!w->native || !w->fp16_cm) return DQ_ERR_INVALID_ARGUMENT;
-    return launch_gemv_gather(*w, x, y, outlier_k, workspace, *g, static_cast<cudaStream_t>(stream));
+    if (!w->native || !w->fp16_cm || !stream_supported(*w, true)) return DQ_ERR_INVALID_ARGUMENT;
+    if (stream_geom(w->d_out, w->d_in).n_rb > kStreamMaxRb) return DQ_ERR_UNSUPPORTED;
+    if (workspace_bytes < stream_ws(w->d_out, w->d_in).total) return DQ_ERR_WORKSPACE;
+    return launch_gemv_stream(*w, x, y, outlier_k, true, workspace, g, static_cast<cudaStream_t>(stream));
 }
 
 dq_status_t dq_device_alloc(size_t bytes, void** ptr) {
@@ -272,6 +308,8 @@ dq_status_t dq_int4_gemv(const dq_weights_t* w, const uint16_t* x, uint16_t* y, 
     if (w && w->d_out == 0 && check_dims(w->d_out, w->d_in) == DQ_OK) return DQ_OK;
     dq_status_t st = check_weights(w, x, y, false, workspace, workspace_bytes);
     if (st != DQ_OK) return st;
+    if (use_stream(*w, false, workspace_bytes))
+        return launch_gemv_stream(*w, x, y, 0.f, false, workspace, nullptr, static_cast<cudaStream_t>(stream));
     return launch_gemv_b1(*w, x, y, 0.f, false, workspace, static_cast<cudaStream_t>(stream));
 }
 
@@ -318,8 +356,8 @@ dq_status_t dq_detect_outliers(const uint16_t* x, int32_t d_in, float outlier_k,
 // ---------------------------------------------------------------------------
 namespace {
 
-constexpr size_t kStaticScratchBytes = 128 * 1024;  // workspace of grids up to kMaxCtas CTAs
-static_assert(kStaticScratchBytes >= sizeof(unsigned long long) * 16 * dq::kMaxCtas,
+constexpr size_t kStaticScratchBytes = 132 * 1024;  // workspace of grids up to kMaxCtas CTAs
+static_assert(kStaticScratchBytes >= 256 + sizeof(unsigned long long) * 16 * dq::kMaxCtas,
               "static scratch smaller than the split GEMV workspace");
 
 static __device__ __align__(256) unsigned char g_dq_static_scratch[kStaticScratchBytes];
@@ -328,8 +366,9 @@ void* g_static_scratch_ptr[kMaxDev];  // device address per ordinal, set once
 std::mutex g_static_scratch_mu;
 
 // Device address of the static scratch on the current device.  The first call
-// on a device looks it up and clears the array on `stream` (the kernel wants
-// it zero on entry and leaves it zero on exit).
+// on a device looks it up and clears the array on `stream`: the workspace
+// starts from zeros, and every call (also one whose bounded waits gave up)
+// leaves it ready for the next call.
 dq_status_t static_scratch(void** out, cudaStream_t stream) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);

@@ -332,6 +332,9 @@ __device__ __forceinline__ uint32_t ld_acquire_sys_u32(const unsigned int* p) {
 __device__ __forceinline__ void st_release_sys_u32(unsigned int* p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ void red_release_sys_add_u32(unsigned int* p, uint32_t v) {
+    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ uint16_t ld_relaxed_sys_u16(const uint16_t* p) {
     uint16_t v;
     asm volatile("ld.relaxed.sys.global.u16 %0, [%1];" : "=h"(v) : "l"(p) : "memory");

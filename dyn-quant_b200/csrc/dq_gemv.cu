@@ -45,6 +45,7 @@
 
 #include "dq_common.cuh"
 #include "dq_internal.h"
+#include "dq_gplan.cuh"
 #include "dq_plan.cuh"
 
 namespace dq {
@@ -71,16 +72,13 @@ struct B1Args {
     const uint16_t* w16_cm;   // column-major FP16 mirror
     const uint16_t* x;
     uint16_t* y;
+    unsigned int* hdr;        // workspace: [0] tag of the last completed call, [1] CTAs done in this call
     unsigned long long* fix;  // workspace: per CTA, the published partial sums of its first row block
     float k;
     float inv_n, inv_n1;      // 1/d_in, 1/(d_in - 1) for the statistics of x
     int d_out, d_in, NC, U, nrb_max;
     int depth;                // ring stages per warp (reference layout: kB1Stages)
     B1Smem S;
-    // fused gather (kGather): ranks, slice height, output rows, every rank's region
-    int g_rank, g_world, g_rows_per, g_total;
-    uint8_t* g_region[kMaxGatherRanks];
-    GatherLayout g_lay;
 };
 
 // How the split path reads the FP16 weights of outlier columns.
@@ -101,10 +99,8 @@ __host__ __device__ inline int unit_owner(long long u, int P, long long U) {
 // kNative: weights in the unit layout (one bulk copy per unit, scale/zero
 // inside); otherwise the reference layout (one bulk copy per weight row of the
 // unit, scale/zero by plain loads).  kR: rounds of x held in registers by the
-// plan (at least ceil(NC / 8)).  kGather: the rows are one rank's slice of a
-// row-sharded GEMV and the kernel also gathers the other ranks' slices (the
-// epilogue at the end).
-template <bool kSplit, bool kNative, int kOut, int kW, int kR, bool kGather = false>
+// plan (at least ceil(NC / 8)).
+template <bool kSplit, bool kNative, int kOut, int kW, int kR>
 __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
     constexpr int kT = kW * 32;
     extern __shared__ __align__(128) char smem[];
@@ -210,24 +206,16 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
             prefetch_l2_bulk(a.native + static_cast<size_t>(cu0 + warp + kW * k) * kB1UnitBytes, kB1UnitBytes);
     pdl_launch_dependents();
     pdl_wait();  // x, y and the workspace may belong to the preceding kernel until here
-    // Gather: this call's number (CTA c's calls so far + 1) picks the slice.
-    uint32_t g_call = 0;
-    uint16_t* g_slice = nullptr;
-    if (kGather) {
-        g_call = reinterpret_cast<const uint32_t*>(a.g_region[a.g_rank] + a.g_lay.epoch)[c] + 1u;
-        g_slice = reinterpret_cast<uint16_t*>(a.g_region[a.g_rank] + (g_call & 1u) * a.g_lay.slice);
+    // This call's tag: one more than the last completed call's (never zero).
+    // Every CTA reads it before it finishes, and the last CTA to finish
+    // advances it, so all CTAs of a call see the same tag.
+    uint32_t& s_tag = *reinterpret_cast<uint32_t*>(smem + a.S.misc);
+    if (tid == 0) {
+        const uint32_t e = ldcg_u32(a.hdr) + 1u;
+        s_tag = e == 0u ? 1u : e;
     }
     // Output row `row` (< d_out) of this call.
-    auto store_row = [&](int row, float v) {
-        const uint16_t h = __half_as_ushort(__float2half_rn(v));
-        if (kGather) {
-            const int grow = a.g_rank * a.g_rows_per + row;
-            if (grow < a.g_total) a.y[grow] = h;
-            g_slice[row] = h;
-        } else {
-            a.y[row] = h;
-        }
-    };
+    auto store_row = [&](int row, float v) { a.y[row] = __half_as_ushort(__float2half_rn(v)); };
     XRegs<kT, kR> xr;
     x_regs_load_global<kT>(a.x, n8, xr);
     if (kNative) {
@@ -351,10 +339,10 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
     // Partial row sums of rbf (shared with earlier CTAs) go to the workspace as
     // soon as the warps holding its units are done with it: those warps meet on
     // named barrier 1 and the last of them publishes.  Each sum is one 64-bit
-    // word (1 << 32 | FP32 bits), written in one piece, so the finaliser needs
-    // no fence or flag: a nonzero high half marks a published value.  Called
-    // exactly once by each of warps 0 .. n_pub-1 (also on the error path, so
-    // that the barrier fills).
+    // word (this call's tag << 32 | FP32 bits), written in one piece, so the
+    // finaliser needs no fence or flag: the tag marks a value published by
+    // this call.  Called exactly once by each of warps 0 .. n_pub-1 (also on
+    // the error path, so that the barrier fills).
     bool pub_pending = contrib && warp < n_pub;
     auto publish_first = [&]() {
         if (warp == n_pub - 1) {
@@ -363,7 +351,8 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
                 float v = 0.f;
 #pragma unroll
                 for (int w = 0; w < kW; ++w) v += part[w * 16 + lane];
-                st_relaxed_gpu_u64(a.fix + c * 16 + lane, (1ull << 32) | __float_as_uint(v));
+                st_relaxed_gpu_u64(a.fix + c * 16 + lane,
+                                   (static_cast<unsigned long long>(s_tag) << 32) | __float_as_uint(v));
             }
         } else {
             named_bar_arrive(1, n_pub * 32);
@@ -523,67 +512,30 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
 #pragma unroll
             for (int w = 0; w < kW; ++w) sum += opart[(w * a.nrb_max + rbl) * 16 + (lane & 15)];
         const int row = rbz * kRowBlock + (lane & 15);
+        const uint32_t tag = s_tag;
         bool ok_all = true;
         for (int cc = c + 1; cc <= c_hi; ++cc) {
             unsigned long long* slot = a.fix + cc * 16 + (lane & 15);
             unsigned long long v = (cc == c + 1) ? early : 0ull;
-            if ((v >> 32) == 0ull) {
+            if (static_cast<uint32_t>(v >> 32) != tag) {
                 v = ld_relaxed_gpu_u64(slot);
                 const long long t0 = clock64();
-                while ((v >> 32) == 0ull && clock64() - t0 < (1ll << 31)) v = ld_relaxed_gpu_u64(slot);
+                while (static_cast<uint32_t>(v >> 32) != tag && clock64() - t0 < (1ll << 31))
+                    v = ld_relaxed_gpu_u64(slot);
             }
-            ok_all = ok_all && (v >> 32) != 0ull;
+            ok_all = ok_all && static_cast<uint32_t>(v >> 32) == tag;
             sum += __uint_as_float(static_cast<uint32_t>(v));
         }
         if (!__all_sync(0xffffffffu, ok_all) && lane == 0) atomicOr(&g_error_word, 2u);
         if (lane < 16 && row < a.d_out) store_row(row, sum);
-        __syncwarp();
-        // Leave the slots zero for the next call.
-        for (int i = lane; i < (c_hi - c) * 16; i += 32) st_relaxed_gpu_u64(a.fix + (c + 1) * 16 + i, 0ull);
     }
 
-    if constexpr (kGather) {
-        // ---- gather: publish this CTA's rows, then copy the other ranks' ----
-        // CTA c writes the rows of row blocks orb0 .. rbz on every rank (same
-        // shapes, same grid), so it takes exactly those rows of each other
-        // rank's slice once that rank's CTA c has raised its flag here.
-        unsigned int* s_ok = reinterpret_cast<unsigned int*>(red);  // the plan's scratch, free again
-        __syncthreads();  // this CTA's rows are in its slice
-        if (tid == 0) {
-            __threadfence_system();
-            for (int q = 0; q < a.g_world; ++q)
-                if (q != a.g_rank)
-                    st_release_sys_u32(reinterpret_cast<unsigned int*>(a.g_region[q] + a.g_lay.flags) +
-                                           a.g_rank * kMaxCtas + c, g_call);
-        }
-        if (warp == 0) {
-            bool ok = true;
-            if (lane < a.g_world && lane != a.g_rank) {  // lane q waits for rank q's CTA c (bounded)
-                const unsigned int* f = reinterpret_cast<const unsigned int*>(a.g_region[a.g_rank] + a.g_lay.flags) +
-                                        lane * kMaxCtas + c;
-                uint32_t v = ld_acquire_sys_u32(f);
-                const long long t0 = clock64();
-                while (static_cast<int32_t>(v - g_call) < 0 && clock64() - t0 < (1ll << 31)) v = ld_acquire_sys_u32(f);
-                ok = static_cast<int32_t>(v - g_call) >= 0;
-            }
-            const unsigned int okm = __ballot_sync(0xffffffffu, ok);
-            if (lane == 0) {
-                *s_ok = okm;
-                if (okm != 0xffffffffu) atomicOr(&g_error_word, 16u);
-            }
-        }
-        __syncthreads();
-        const unsigned int okm = *s_ok;
-        const int r_lo = orb0 * kRowBlock, r_hi = min(a.d_out, (rbz + 1) * kRowBlock);
-        const int nrows = r_hi > r_lo ? r_hi - r_lo : 0;
-        for (int i = tid; i < nrows * a.g_world; i += kT) {
-            const int q = i / nrows, row = r_lo + i % nrows;
-            const int grow = q * a.g_rows_per + row;
-            if (q == a.g_rank || !((okm >> q) & 1u) || grow >= a.g_total) continue;
-            const uint16_t* src = reinterpret_cast<const uint16_t*>(a.g_region[q] + (g_call & 1u) * a.g_lay.slice);
-            a.y[grow] = ld_relaxed_sys_u16(src + row);
-        }
-        if (tid == 0) reinterpret_cast<uint32_t*>(a.g_region[a.g_rank] + a.g_lay.epoch)[c] = g_call;
+    // This CTA is done with the workspace (its tag read, its words published,
+    // its finaliser wait over): the last CTA of the call advances the tag.
+    __syncthreads();
+    if (tid == 0 && atomicAdd(a.hdr + 1, 1u) == gridDim.x - 1u) {
+        a.hdr[1] = 0u;
+        a.hdr[0] = s_tag;
     }
 }
 
@@ -661,7 +613,7 @@ __global__ void __launch_bounds__(kStatThreads, 1)
     load_x_async<kStatThreads>(x, n8, xs);
     cp_async_wait_all();
     __syncthreads();
-    const XStats st = x_stats<kStatThreads>(xs, n8, d_in, k, inv_n, inv_n1, red);
+    const GpStats st = gp_stats_smem<kStatThreads>(xs, d_in / kGroup, d_in, k, inv_n, inv_n1, red);
     const int n = x_mask_list<kStatThreads>(xs, d_in, st.mean, st.thresh, reinterpret_cast<uint32_t*>(mask), list,
                                             reinterpret_cast<int*>(red) + 2 * (kStatThreads / 32));
     __syncthreads();
@@ -911,13 +863,13 @@ dq_status_t check_launch() {
 }
 
 
-template <bool kSplit, bool kNative, int kOut, int kW, int kR, bool kGather = false>
+template <bool kSplit, bool kNative, int kOut, int kW, int kR>
 dq_status_t launch_b1(const B1Args& a, int grid, cudaStream_t stream) {
     constexpr int wi = kW == kB1Warps ? 0 : 1;
     constexpr int ri = kR == 1 ? 0 : kR == 2 ? 1 : kR == 4 ? 2 : 3;
-    constexpr int id = 4 + 128 * (kGather ? 1 : 0) + 16 * (4 * wi + ri) + (kSplit ? 8 : 0) + (kNative ? 4 : 0) + kOut;
+    constexpr int id = 4 + 16 * (4 * wi + ri) + (kSplit ? 8 : 0) + (kNative ? 4 : 0) + kOut;
     static_assert(id < kNumKernels, "kernel attribute slot");
-    const dq_status_t st = ensure_smem(b1_kernel<kSplit, kNative, kOut, kW, kR, kGather>, id, a.S.total);
+    const dq_status_t st = ensure_smem(b1_kernel<kSplit, kNative, kOut, kW, kR>, id, a.S.total);
     if (st != DQ_OK) return st;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -929,7 +881,7 @@ dq_status_t launch_b1(const B1Args& a, int grid, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, b1_kernel<kSplit, kNative, kOut, kW, kR, kGather>, a);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, b1_kernel<kSplit, kNative, kOut, kW, kR>, a);
     if (e != cudaSuccess) { set_cuda_error(e); return DQ_ERR_CUDA; }
     return check_launch();
 }
@@ -958,15 +910,6 @@ dq_status_t launch_b1_warps(const B1Args& a, int warps, int out_mode, int rounds
                                  : launch_b1_out<false, kB1WarpsSmall, kPlanRounds>(a, out_mode, grid, stream);
     return warps == kB1Warps ? launch_b1_native<kB1Warps>(a, out_mode, rounds, grid, stream)
                              : launch_b1_native<kB1WarpsSmall>(a, out_mode, rounds, grid, stream);
-}
-
-// The split GEMV with the fused gather: native layout, column-major mirror.
-template <int kW>
-dq_status_t launch_b1_gather(const B1Args& a, int rounds, int grid, cudaStream_t stream) {
-    if (rounds <= 1) return launch_b1<true, true, kOutStaged, kW, 1, true>(a, grid, stream);
-    if (rounds <= 2) return launch_b1<true, true, kOutStaged, kW, 2, true>(a, grid, stream);
-    if (rounds <= 4) return launch_b1<true, true, kOutStaged, kW, 4, true>(a, grid, stream);
-    return launch_b1<true, true, kOutStaged, kW, kPlanRounds, true>(a, grid, stream);
 }
 
 // Launch geometry of one batch-1 call.
@@ -1001,6 +944,7 @@ dq_status_t b1_setup(const dq_weights_t& w, const uint16_t* x, uint16_t* y, floa
     a.U = static_cast<int>(n_rb * NC);
     const WsLayout W = ws_layout(w.d_out, w.d_in);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
+    a.hdr = reinterpret_cast<unsigned int*>(ws + W.hdr);
     a.fix = reinterpret_cast<unsigned long long*>(ws + W.fix);
     int grid = di.sm_count < a.U ? di.sm_count : a.U;
     if (grid > kMaxCtas) grid = kMaxCtas;
@@ -1054,23 +998,6 @@ dq_status_t launch_gemv_b1(const dq_weights_t& w, const uint16_t* x, uint16_t* y
     const dq_status_t st = b1_setup(w, x, y, k, split, workspace, a, p);
     if (st != DQ_OK) return st;
     return launch_b1_warps(a, p.warps, p.out_mode, p.rounds, p.grid, stream);
-}
-
-dq_status_t launch_gemv_gather(const dq_weights_t& w, const uint16_t* x, uint16_t* y, float k,
-                               void* workspace, const dq_gather_t& g, cudaStream_t stream) {
-    B1Args a;
-    B1Plan p;
-    const dq_status_t st = b1_setup(w, x, y, k, true, workspace, a, p);
-    if (st != DQ_OK) return st;
-    if (p.out_mode != kOutStaged || !w.native) return DQ_ERR_INVALID_ARGUMENT;
-    a.g_rank = g.rank;
-    a.g_world = g.world;
-    a.g_rows_per = g.rows_per;
-    a.g_total = g.d_total;
-    for (int q = 0; q < kMaxGatherRanks; ++q) a.g_region[q] = static_cast<uint8_t*>(q < g.world ? g.region[q] : nullptr);
-    a.g_lay = gather_layout(g.rows_per);
-    return p.warps == kB1Warps ? launch_b1_gather<kB1Warps>(a, p.rounds, p.grid, stream)
-                               : launch_b1_gather<kB1WarpsSmall>(a, p.rounds, p.grid, stream);
 }
 
 dq_status_t launch_build_native(const uint8_t* packed, const uint16_t* scales, const uint16_t* zeros,

@@ -35,6 +35,7 @@ __host__ __device__ inline int align16(int v) { return (v + 15) & ~15; }
 // the activation plan itself (x is at most 60 KB and stays in L2):
 //   ring  slots of weight units (a warp's i-th unit in slot warp + warps (i % depth))
 //   bars  one mbarrier per slot
+//   misc  this call's tag (workspace protocol)
 //   zero  1 KB of zeros (B operand of lanes outside their column pair)
 //   bsm   x, then in place the MMA B fragments of x' (outliers zeroed), NC chunks
 //   xp    per group float4 (1024 sum x' even cols, 1024 sum x' odd cols, sum x', 0)
@@ -45,7 +46,7 @@ __host__ __device__ inline int align16(int v) { return (v + 15) & ~15; }
 //   list  outliers, column | FP16 bits of x << 16, capacity d_in/4 (split only)
 //   obuf  per warp, kB1OutBufs buffers of 16 outlier columns x 16 rows (split only)
 struct B1Smem {
-    int ring, bars, zero, bsm, xp, mask, red, part, opart, list, obuf, total;
+    int ring, bars, misc, zero, bsm, xp, mask, red, part, opart, list, obuf, total;
 };
 
 // slots: ring slots of kB1StageBytes, each with its mbarrier.
@@ -55,6 +56,7 @@ inline B1Smem b1_smem(int d_in, int nrb_max, bool split, int warps, int slots) {
     int off = 0;
     S.ring = off;  off += slots * kB1StageBytes;
     S.bars = off;  off += (slots * 8 + 127) / 128 * 128;
+    S.misc = off;  off += 128;  // this call's tag
     S.zero = off;  off += kB1ChunkB;
     S.bsm = off;   off += NC * kB1ChunkB;
     S.xp = off;    off += NC * kB1ChunkGroups * 16;
@@ -68,33 +70,42 @@ inline B1Smem b1_smem(int d_in, int nrb_max, bool split, int warps, int slots) {
     return S;
 }
 
-// Workspace of a batch-1 GEMV call: per CTA, the 16 partial row sums of its
-// first row block when that block is shared with the preceding CTA, each a
-// 64-bit word (1 << 32 | FP32 bits; zero = not yet published).  Zero before
-// first use; every call leaves it zero.
+// Workspace of a batch-1 GEMV call:
+//   hdr  [0] the number of the last completed call (its tag), [1] CTAs of the
+//        running call that have finished (the last one resets it to zero and
+//        advances [0])
+//   fix  per CTA, the 16 partial row sums of its first row block when that
+//        block is shared with the preceding CTA, each a 64-bit word
+//        (tag << 32 | FP32 bits): a word is this call's only if it carries
+//        this call's tag, so words left by an earlier call are never taken.
+// Zero before first use; every call leaves it ready for the next one (also a
+// call whose bounded waits gave up).
 struct WsLayout {
-    size_t fix, total;
+    size_t hdr, fix, total;
 };
 
 inline size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
 // Gather region of one rank (row-sharded split GEMV with the gather fused):
-//   slices  two FP16 copies of this rank's output rows (rows_per each), used
-//           alternately by consecutive calls, read by the other ranks
-//   flags   [kMaxGatherRanks][kMaxCtas] u32: flag (q, c) = the last call whose
-//           CTA c on rank q has published its rows (written by rank q)
-//   epoch   [kMaxCtas] u32: calls completed by this rank's CTA c
-// Zero-filled once; every rank makes the same calls with the same grid.
+//   hdr    u32 [0] calls this rank has completed, [1] / [2] the other ranks'
+//          arrivals for the running call of parity 0 / 1 (every other rank
+//          adds 1 once its rows are in this region)
+//   yfull  two FP16 copies of the full output (kMaxGatherRanks x rows_per
+//          rows), for calls of parity 0 and 1: rank q stores its rows of a
+//          call straight into every other rank's copy of that parity
+// Zero-filled once; every rank makes the same calls in the same order.  A
+// rank is at most one call ahead of another (it waits for every other
+// rank's rows of each call), so the copy it writes is never the one read.
 constexpr int kMaxGatherRanks = DQ_MAX_GATHER_RANKS;
 struct GatherLayout {
-    size_t slice, flags, epoch, total;
+    size_t hdr, yfull, ybytes, total;
 };
 inline GatherLayout gather_layout(int rows_per) {
     GatherLayout L;
-    L.slice = align256(static_cast<size_t>(rows_per) * 2);
-    L.flags = 2 * L.slice;
-    L.epoch = L.flags + static_cast<size_t>(kMaxGatherRanks) * kMaxCtas * 4;
-    L.total = align256(L.epoch + static_cast<size_t>(kMaxCtas) * 4);
+    L.hdr = 0;
+    L.yfull = 256;
+    L.ybytes = align256(static_cast<size_t>(kMaxGatherRanks) * rows_per * 2);
+    L.total = L.yfull + 2 * L.ybytes;
     return L;
 }
 
@@ -102,9 +113,119 @@ inline WsLayout ws_layout(int d_out, int d_in) {
     (void)d_out;
     (void)d_in;
     WsLayout W;
-    W.fix = 0;
-    W.total = align256(static_cast<size_t>(kMaxCtas) * 16 * sizeof(unsigned long long));
+    W.hdr = 0;
+    W.fix = 256;
+    W.total = W.fix + align256(static_cast<size_t>(kMaxCtas) * 16 * sizeof(unsigned long long));
     return W;
+}
+
+// ---------------------------------------------------------------------------
+// The streaming batch-1 GEMV (dq_stream.cu): tasks of at most
+// kStreamTaskUnits units from a queue in the workspace.
+// ---------------------------------------------------------------------------
+constexpr int kStreamTaskUnits = 8;   // units per task, at most
+constexpr int kStreamMaxSlots = 45;   // ring slots per CTA, at most
+constexpr int kStreamConsumers = 15;  // consumer warps of a streaming CTA; ring slots are a multiple of it
+constexpr int kStreamMaxRb = 16384;   // row blocks the arrival counters cover (262144 rows)
+
+// Tasks of one shape: a row block of NC >= kStreamTaskUnits chunks is cut into
+// tpr chunk ranges (one task each); shorter row blocks go m to a task.
+struct StreamGeom {
+    int NC, n_rb, tpr, m, n_tasks;
+};
+inline StreamGeom stream_geom(int d_out, int d_in) {
+    StreamGeom g;
+    g.NC = (d_in / 128 + kB1ChunkGroups - 1) / kB1ChunkGroups;
+    g.n_rb = (d_out + 15) / 16;
+    if (g.NC >= kStreamTaskUnits) {
+        g.tpr = (g.NC + kStreamTaskUnits - 1) / kStreamTaskUnits;
+        g.m = 1;
+        g.n_tasks = g.n_rb * g.tpr;
+    } else {
+        g.tpr = 1;
+        g.m = kStreamTaskUnits / g.NC;
+        g.n_tasks = (g.n_rb + g.m - 1) / g.m;
+    }
+    return g;
+}
+
+// The workspace of every batch-1 and batched call starts with a fixed header
+// of counters that must be zero on entry and that every call leaves zero (or,
+// for the b1 kernel, tagged with the call's number); no kernel uses the
+// header as scratch, so calls of any shapes can share one workspace.
+//   [0, ws_layout().total)   the b1 kernel's tag, arrivals and tagged partial sums
+//   stream_ctr               [0] tasks taken from the queue, [1] CTAs done
+//   stream_rbcnt             [kStreamMaxRb] tasks of each row block done
+//   batched_ctr              the batched plan's arrival counter and union size
+// After the header, per-shape scratch that each call overwrites.
+struct WsHeader {
+    size_t stream_ctr, stream_rbcnt, batched_ctr, total;
+};
+inline WsHeader ws_header() {
+    WsHeader H;
+    size_t off = ws_layout(0, 128).total;
+    H.stream_ctr = off;   off += 256;
+    H.stream_rbcnt = off; off += align256(static_cast<size_t>(kStreamMaxRb) * 4);
+    H.batched_ctr = off;  off += 256;
+    H.total = off;
+    return H;
+}
+
+struct StreamWs {
+    size_t ctr, rbcnt, part, total;
+};
+inline StreamWs stream_ws(int d_out, int d_in) {
+    const StreamGeom g = stream_geom(d_out, d_in);
+    const WsHeader H = ws_header();
+    StreamWs L;
+    L.ctr = H.stream_ctr;
+    L.rbcnt = H.stream_rbcnt;
+    L.part = H.total;
+    L.total = H.total + (g.tpr > 1 ? align256(static_cast<size_t>(g.n_rb) * g.tpr * 64) : 0);
+    return L;
+}
+
+// Shared memory of one streaming CTA (R ring slots):
+//   ring   R slots of kB1UnitBytes
+//   full   R mbarriers (copy landed), empty R mbarriers (slot free)
+//   obbar  2 full + 2 empty mbarriers of the outlier staging buffers
+//   desc   R x int4 (unit, task number, unit in task, units of the task)
+//   ttab   the tasks in flight (8 x 32 bytes)
+//   upart  per task in flight and unit, 16 row sums
+//   misc   task counters and generations, plan flag
+//   red    statistics and scan scratch
+//   zero   1 KB of zeros (B operand of lanes outside their column pair)
+//   xb     MMA B fragments of x' (NC chunks)
+//   xp     per group (1024 sum x' even, 1024 sum x' odd, sum x', 0)
+//   mask   capacity-rule mask words (split)
+//   list   outliers: column | FP16 bits of x << 16 (split)
+//   obuf   2 staging buffers of 512 outlier segments of 32 bytes (split)
+//   otile  per consumer warp, a 16-column x 16-row tile (split)
+struct SSmem {
+    int ring, full, empty, obbar, desc, ttab, upart, misc, red, zero, xb, xp, mask, list, obuf, otile, total;
+};
+inline SSmem stream_smem(int d_in, bool split, int R) {
+    const int NC = (d_in / 128 + kB1ChunkGroups - 1) / kB1ChunkGroups;
+    SSmem S;
+    int off = 0;
+    S.ring = off;  off += R * kB1UnitBytes;
+    S.full = off;  off += align16(R * 8);
+    S.empty = off; off += align16(R * 8);
+    S.obbar = off; off += 32;
+    S.desc = off;  off += R * 16;
+    S.ttab = off;  off += 8 * 32;
+    S.upart = off; off += 8 * kStreamTaskUnits * 16 * 4;
+    S.misc = off;  off += 128;
+    S.red = off;   off += 1024;
+    S.zero = off;  off += kB1ChunkB;
+    S.xb = off;    off += NC * kB1ChunkB;
+    S.xp = off;    off += NC * kB1ChunkGroups * 16;
+    S.mask = off;  off += split ? NC * 64 : 0;
+    S.list = off;  off += split ? align16(d_in) : 0;
+    S.obuf = off;  off += split ? 2 * 512 * 32 : 0;
+    S.otile = off; off += split ? 15 * 512 : 0;
+    S.total = off;
+    return S;
 }
 
 // Position of the 16-byte piece (slice sl, half h; row g + 8h of the row
@@ -184,8 +305,6 @@ dq_status_t device_info(DeviceInfo* out);
 void set_cuda_error(cudaError_t e);
 
 // Kernel launchers (arguments already validated by the C ABI layer).
-dq_status_t launch_gemv_gather(const dq_weights_t& w, const uint16_t* x, uint16_t* y, float k,
-                               void* workspace, const dq_gather_t& g, cudaStream_t stream);
 dq_status_t launch_gemv_b1(const dq_weights_t& w, const uint16_t* x, uint16_t* y, float k,
                            bool split, void* workspace, cudaStream_t stream);
 dq_status_t launch_build_native(const uint8_t* packed, const uint16_t* scales, const uint16_t* zeros,
@@ -201,9 +320,12 @@ dq_status_t launch_colmajor(const uint16_t* w16, int d_out, int d_in, uint16_t* 
                             cudaStream_t stream);
 
 inline BgWs bg_ws(const BgGeom& g, int d_out, int d_in) {
+    (void)d_out;
+    (void)d_in;
     BgWs L;
-    size_t off = ws_layout(d_out, d_in).total;
-    L.ctr = off;   off += 256;
+    const WsHeader H = ws_header();
+    L.ctr = H.batched_ctr;
+    size_t off = H.total;
     L.masks = off; off += align256(static_cast<size_t>(kBgMaxM) * g.W * 4);
     L.ulist = off; off += align256(static_cast<size_t>(d_in) * 4);
     L.xrow = off;  off += align256(static_cast<size_t>(d_in) * g.MP * 2);
@@ -212,6 +334,12 @@ inline BgWs bg_ws(const BgGeom& g, int d_out, int d_in) {
     L.total = off;
     return L;
 }
+
+bool stream_supported(const dq_weights_t& w, bool split);
+// g: the row-sharded gather (null: none; y then holds d_out rows, else g->d_total).
+dq_status_t launch_gemv_stream(const dq_weights_t& w, const uint16_t* x, uint16_t* y, float k, bool split,
+                               void* workspace, const dq_gather_t* g, cudaStream_t stream);
+dq_status_t read_stream_error(uint32_t* word, bool clear);
 
 dq_status_t launch_gemv_batched(const dq_weights_t& w, const uint16_t* x, uint16_t* y, int M, float k,
                                 void* workspace, cudaStream_t stream);

@@ -22,10 +22,18 @@ namespace {
 // calls on one stream are ordered, and each stream has its own.  Kept for the
 // life of the process (never destroyed: no CUDA calls during static
 // destruction).
-torch::Tensor& workspace_for(const torch::Device& dev, void* stream, size_t bytes) {
+std::mutex& workspace_mu() {
     static std::mutex mu;
+    return mu;
+}
+std::map<std::pair<int, void*>, torch::Tensor>& workspace_cache() {
     static auto* cache = new std::map<std::pair<int, void*>, torch::Tensor>();
-    std::lock_guard<std::mutex> lock(mu);
+    return *cache;
+}
+
+torch::Tensor workspace_for(const torch::Device& dev, void* stream, size_t bytes) {
+    std::lock_guard<std::mutex> lock(workspace_mu());
+    auto* cache = &workspace_cache();
     const auto key = std::make_pair(static_cast<int>(dev.index()), stream);
     auto it = cache->find(key);
     if (it == cache->end() || static_cast<size_t>(it->second.numel()) < bytes) {
@@ -34,6 +42,18 @@ torch::Tensor& workspace_for(const torch::Device& dev, void* stream, size_t byte
         it = cache->find(key);
     }
     return it->second;
+}
+
+// Zero-fill the counters of every cached workspace on its own stream (after
+// dq_read_device_error reported an error; see include/dq_abi.h).
+void reset_workspaces() {
+    std::lock_guard<std::mutex> lock(workspace_mu());
+    for (auto& kv : workspace_cache()) {
+        const auto& t = kv.second;
+        const at::cuda::CUDAGuard guard(t.device());
+        const dq_status_t s = dq_reset_workspace(t.data_ptr(), static_cast<size_t>(t.numel()), kv.first.second);
+        TORCH_CHECK(s == DQ_OK, "reset_workspaces failed: ", dq_status_string(s));
+    }
 }
 
 void check_status(dq_status_t s, const char* what) {
@@ -123,9 +143,11 @@ dq_weights_t make_weights(const torch::Tensor& packed, const torch::Tensor& scal
 }
 
 // quantize_weights(weight [d_out, d_in] f16) -> (packed, scales, zeros, fp16_copy)
-// (csrc/bindings.cpp:25-75; quantized on the device, bit-exact with the host loop)
+// (csrc/bindings.cpp:25-75; quantized on the device, bit-exact with the host loop).
+// with_copy=false returns an undefined (None) fp16_copy: for callers that keep
+// the weights in another form (DynQuantLinear keeps the column-major mirror).
 std::tuple<torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor>
-quantize_weights(const torch::Tensor& weight) {
+quantize_weights(const torch::Tensor& weight, bool with_copy) {
     check_fp16_contiguous(weight, "weight");
     TORCH_CHECK(weight.dim() == 2, "weight must be 2D [d_out, d_in]");
     const int64_t d_out = weight.size(0), d_in = weight.size(1);
@@ -136,7 +158,8 @@ quantize_weights(const torch::Tensor& weight) {
     auto packed = torch::empty({d_out, d_in / 2}, u8);
     auto scales = torch::empty({d_out, d_in / 128}, f16);
     auto zeros = torch::empty({d_out, d_in / 128}, f16);
-    auto copy = weight.clone();
+    torch::Tensor copy;
+    if (with_copy) copy = weight.clone();
     check_status(dq_quantize(h16(weight), static_cast<int32_t>(d_out), static_cast<int32_t>(d_in),
                              reinterpret_cast<uint8_t*>(packed.data_ptr()), h16m(scales), h16m(zeros),
                              stream_of(weight)),
@@ -168,7 +191,7 @@ torch::Tensor split_gemv(const torch::Tensor& packed, const torch::Tensor& scale
     auto y = torch::empty({w.d_out}, x.options());
     void* stream = stream_of(x);
     const size_t wsb = dq_workspace_bytes(w.d_out, w.d_in);
-    auto& ws = workspace_for(x.device(), stream, wsb);
+    auto ws = workspace_for(x.device(), stream, wsb);
     check_status(dq_split_gemv(&w, h16(x), h16m(y), static_cast<float>(outlier_k), ws.data_ptr(),
                                static_cast<size_t>(ws.numel()), stream),
                  "split_gemv");
@@ -191,7 +214,7 @@ torch::Tensor split_gemv_batched(const torch::Tensor& packed, const torch::Tenso
     auto y = torch::empty({m, w.d_out}, x.options());
     void* stream = stream_of(x);
     const size_t wsb = dq_workspace_bytes_batched(w.d_out, w.d_in, static_cast<int32_t>(m));
-    auto& ws = workspace_for(x.device(), stream, wsb);
+    auto ws = workspace_for(x.device(), stream, wsb);
     check_status(dq_split_gemv_batched(&w, h16(x), h16m(y), static_cast<int32_t>(m), static_cast<float>(outlier_k),
                                        ws.data_ptr(), static_cast<size_t>(ws.numel()), stream),
                  "split_gemv_batched");
@@ -207,7 +230,7 @@ torch::Tensor int4_gemv(const torch::Tensor& packed, const torch::Tensor& scales
     auto y = torch::empty({w.d_out}, x.options());
     void* stream = stream_of(x);
     const size_t wsb = dq_workspace_bytes(w.d_out, w.d_in);
-    auto& ws = workspace_for(x.device(), stream, wsb);
+    auto ws = workspace_for(x.device(), stream, wsb);
     check_status(dq_int4_gemv(&w, h16(x), h16m(y), ws.data_ptr(), static_cast<size_t>(ws.numel()), stream),
                  "int4_gemv");
     return y;
@@ -306,7 +329,7 @@ public:
         const at::cuda::CUDAGuard guard(dev_);
         auto y = has_out ? *out : torch::empty({w_.d_out}, x.options());
         void* stream = at::cuda::getCurrentCUDAStream().stream();
-        auto& ws = workspace_for(dev_, stream, wsb_);
+        auto ws = workspace_for(dev_, stream, wsb_);
         check_status(dq_split_gemv(&w_, h16(xa), h16m(y), static_cast<float>(k_), ws.data_ptr(),
                                    static_cast<size_t>(ws.numel()), stream),
                      "split_gemv");
@@ -330,7 +353,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
              py::arg("packed"), py::arg("scales"), py::arg("zeros"), py::arg("fp16_weights"), py::arg("native"),
              py::arg("outlier_k"))
         .def("forward", &SplitLinear::forward, py::arg("x"), py::arg("out") = py::none());
-    m.def("quantize_weights", &quantize_weights, "Quantize FP16 weight matrix to INT4 packed format");
+    m.def("quantize_weights", &quantize_weights, "Quantize FP16 weight matrix to INT4 packed format",
+          py::arg("weight"), py::arg("with_copy") = true);
     m.def("split_gemv", &split_gemv, "Fused dynamic-precision GEMV with runtime outlier detection",
           py::arg("packed"), py::arg("scales"), py::arg("zeros"), py::arg("fp16_weights"), py::arg("x"),
           py::arg("outlier_k"), py::arg("native") = py::none());
@@ -344,4 +368,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("build_colmajor", &build_colmajor, "Column-major FP16 mirror of a weight matrix");
     m.def("detect_outliers", &detect_outliers, "Standalone outlier detector");
     m.def("version", []() { return dq_version(); });
+    m.def("reset_workspaces", &reset_workspaces, "Zero the counters of the cached GEMV workspaces");
+    m.def("read_device_error", [](bool clear) {
+        uint32_t w = 0;
+        check_status(dq_read_device_error(&w, clear ? 1 : 0), "read_device_error");
+        return w;
+    }, py::arg("clear") = false);
 }

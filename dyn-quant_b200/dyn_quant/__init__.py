@@ -239,8 +239,7 @@ class DynQuantLinear(nn.Module):
         if weight.dtype != torch.float16:
             weight = weight.to(torch.float16)
         weight = _aligned(weight.contiguous())
-        packed, scales, zeros, _copy = _C.quantize_weights(weight)
-        del _copy
+        packed, scales, zeros, _ = _C.quantize_weights(weight, with_copy=False)
         self.packed = packed
         self.scales = scales
         self.zeros = zeros

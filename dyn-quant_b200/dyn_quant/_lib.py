@@ -43,6 +43,7 @@ EXPORTED_SYMBOLS = (
     "dq_build_native",
     "dq_read_device_error",
     "dq_workspace_bytes",
+    "dq_reset_workspace",
     "dq_gather_region_bytes",
     "dq_split_gemv_gather",
     "dq_device_alloc",
@@ -132,6 +133,8 @@ def lib() -> C.CDLL:
         L.dq_int4_gemv.argtypes = [C.POINTER(DqWeights), P, P, P, C.c_size_t, P]
         L.dq_workspace_bytes.restype = C.c_size_t
         L.dq_workspace_bytes.argtypes = [i32, i32]
+        L.dq_reset_workspace.restype = st
+        L.dq_reset_workspace.argtypes = [P, C.c_size_t, P]
         L.dq_reference_gemv.restype = st
         L.dq_reference_gemv.argtypes = [P, P, P, i32, i32, P]
         L.dq_detect_outliers.restype = st

@@ -129,14 +129,26 @@ DQ_API dq_status_t dq_build_native(const uint8_t* packed, const uint16_t* scales
 
 /*
  * Workspace of the batch-1 GEMVs: device memory of at least
- * dq_workspace_bytes(d_out, d_in) bytes, 256-byte aligned, ZERO-FILLED before
- * its first use.  It holds the partial row sums of the 16-row blocks that two
- * CTAs share and one arrival counter per row block; every call leaves the
- * counters at zero again, so one zero-filled workspace serves any number of
- * stream-ordered calls of any shape it is large enough for.  Calls that share
- * a workspace must not overlap on the GPU.
+ * dq_workspace_bytes(d_out, d_in) bytes (a fixed 256 + 128 KiB, whatever the
+ * shape), 256-byte aligned, ZERO-FILLED before its first use.  It holds a call
+ * counter, an arrival counter and, per CTA, the partial row sums of the
+ * 16-row block that CTA shares with the one before it, each tagged with the
+ * call's number so that a sum left by an earlier call is never taken.  Every
+ * call leaves it ready for the next one, so one zero-filled workspace serves
+ * any number of stream-ordered calls of any shape; after a call that reported
+ * a device error (dq_read_device_error), reset it with dq_reset_workspace.
+ * Calls that share a workspace must not overlap on the GPU.
  */
 DQ_API size_t dq_workspace_bytes(int32_t d_out, int32_t d_in);
+
+/*
+ * Zero-fill the counters at the head of a workspace on `stream` (an
+ * asynchronous memset of its first bytes, no allocation).  Needed only after
+ * dq_read_device_error reported an error of a call that used the workspace:
+ * such a call may leave a row block's arrival counter short.  No reference
+ * counterpart.
+ */
+DQ_API dq_status_t dq_reset_workspace(void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Fused dynamic-precision GEMV, batch 1: y = W_split x.
@@ -161,16 +173,18 @@ DQ_API dq_status_t dq_split_gemv(const dq_weights_t* w, const uint16_t* x, uint1
  * interfaces whose execute step must not allocate and pass no scratch buffer,
  * hosts with a device-memory budget fixed at start-up, C hosts that receive
  * device pointers from another runtime and have no allocator of their own.
- * The workspace is a 128 KiB static device array inside the library; every GPU
+ * The workspace is a 132 KiB static device array inside the library; every GPU
  * that loads the library holds it until the process exits.  A shape whose
- * workspace (dq_workspace_bytes) would exceed 128 KiB is rejected with
- * DQ_ERR_WORKSPACE.  Arguments, validation and results are otherwise those
- * of dq_split_gemv.
+ * workspace (dq_workspace_bytes) would exceed 132 KiB is rejected with
+ * DQ_ERR_WORKSPACE (with the present kernels no shape does).  Arguments,
+ * validation and results are otherwise those of dq_split_gemv.
  * The first call on each device (with that device current) looks up the
  * array's address and clears it on `stream`; make that first call before any
  * stream capture.  All calls on a device share the array, and each call leaves
- * it zero for the next: calls whose GPU work overlaps (unordered streams, or
- * several host threads at once) race on it and give wrong results.
+ * it ready for the next (also after a device error: the partial sums carry
+ * their call's number, so a late word of a call whose wait gave up is never
+ * taken by a later call): calls whose GPU work overlaps (unordered streams,
+ * or several host threads at once) race on it and give wrong results.
  * Allocates nothing: no cudaMalloc, cudaFree or allocating library routine.
  */
 DQ_API dq_status_t dq_split_gemv_noalloc(const dq_weights_t* w, const uint16_t* x, uint16_t* y,
@@ -184,9 +198,8 @@ DQ_API dq_status_t dq_split_gemv_noalloc(const dq_weights_t* w, const uint16_t* 
  * then one arrival counter that every call leaves at zero again, then scratch
  * that each call overwrites (masks, the outlier-only rows, the outlier union
  * and its activation table, per-slab partial sums).  Calls that share a
- * workspace must not overlap on the GPU.
- * After a call reports a device error (dq_read_device_error) zero-fill the
- * workspace again.  0 on invalid shapes.
+ * workspace must not overlap on the GPU.  Every call leaves it ready for the
+ * next one (after a device error: dq_reset_workspace).  0 on invalid shapes.
  */
 DQ_API size_t dq_workspace_bytes_batched(int32_t d_out, int32_t d_in, int32_t m);
 
@@ -309,7 +322,9 @@ DQ_API dq_status_t dq_ipc_close(void* ptr);
  * kernel then drains its copies, skips the remaining work and returns; its
  * output is not valid), bit 1 by a batch-1 kernel whose bounded wait for a
  * neighbouring CTA's partial sums gave up, bit 4 by a gathering kernel whose
- * bounded wait for another rank's rows gave up, bit 8 by a batched kernel
+ * bounded wait for another rank's rows gave up, bit 5 by the streaming kernel
+ * (the gathering kernel, or DQ_STREAM=1) whose bounded wait for its own bulk
+ * copies gave up (it carries on; its output is not valid), bit 8 by a batched kernel
  * whose bounded wait for its own bulk copies gave up.  Synchronous; clear != 0
  * resets the word.  No reference counterpart.
  */

@@ -13,7 +13,7 @@
  *   dqo_detect            src/outlier_detect.cuh:18-49, 104-205
  *   dqo_split_gemv        src/split_gemv.cu:75-158
  *   dqo_int4_gemv         src/int4_gemv.cu:30-78
- *   dqo_reference_gemv    src/reference_gemv.cu:357-383 (kernel body :9-57)
+ *   dqo_reference_gemv    src/reference_gemv.cu:9-57 (kernel), :59-78 (launcher)
  *   dqo_dense_gemv_f64    (no counterpart: FP32/FP64 dense accuracy yardstick)
  *
  * Arithmetic is IEEE-754 binary32 in the reference's order of operations.
@@ -281,7 +281,7 @@ int dqo_detect(const uint16_t* x, int n, float k,
 /* ------------------------------------------------------------------------ */
 
 /* The 32-lane __shfl_down_sync tree of src/split_gemv.cu:144-148 (same in
- * int4_gemv.cu:61-65 and reference_gemv.cu:375-379); returns lane 0's value. */
+ * int4_gemv.cu:61-65 and reference_gemv.cu:43-47); returns lane 0's value. */
 static float shfl_down_tree(float acc[32]) {
     float a[32];
     memcpy(a, acc, sizeof(a));

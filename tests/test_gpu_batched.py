@@ -30,6 +30,7 @@ CASES = [
     (37, 1152, 0.10, 2.0, "normal", 2),       # ragged rows, many outliers
     (1, 128, 0.05, 2.0, "normal", 1),         # smallest
     (1024, 4096, 0.10, 1.0, "normal", 12),    # most channels outliers: capacity rule per vector
+    (8192, 8192, 0.05, 3.0, "normal", 16),    # the sweep's full 8192 x 8192 shape at its largest batch
 ]
 IDS = [f"{a}x{b}-f{c}-k{d}-{e}-m{f}" for a, b, c, d, e, f in CASES]
 

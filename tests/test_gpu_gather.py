@@ -1,41 +1,41 @@
 """The split GEMV with the row-sharded gather fused (dq_split_gemv_gather), on
 one GPU.
 
-* world 1: the gathered call is the plain split GEMV, bit for bit, call after
-  call (the two slices of the region alternate).
+* world 1: the gathered call agrees with the plain split GEMV and the
+  oracle (the parity tolerance; the two kernels sum in different orders),
+  and repeats itself bit for bit.
 * rank 0 of 2: the other rank is emulated from the host, which plants that
-  rank's published rows in its region and its flags in rank 0's region before
-  each call; rank 0's kernel must return its own rows, the planted rows in
-  the other rank's place, and raise its own flags in the other region.  No
-  second kernel runs: nothing on this GPU waits for another kernel.
-* the bounded wait running out: no flags planted, so the wait gives up after
-  about a second; the kernel reports bit 4 of the device error word, writes
-  its own rows and leaves the other rank's rows untouched.
+  rank's rows in rank 0's region (the copy of the call's parity) and its
+  arrival in rank 0's header before each call.  Rank 0's kernel must return
+  its own rows and the planted rows in the other rank's place, store its own
+  rows in the other region's copy and add its arrival there.  No second
+  kernel runs: nothing on this GPU waits for another kernel.
+* the bounded wait running out: no arrival planted, so the wait gives up
+  after about a second; the kernel reports bit 4 of the device error word,
+  writes its own rows and leaves the other rank's rows untouched.
 
-Region layout (include/dq_abi.h, dq_gather_t): two slices of rows_per FP16
-rows (each padded to 256 bytes), flags [8][1024] u32, epoch [1024] u32.
+Region layout (include/dq_abi.h, dq_gather_t): a 256-byte header (u32 calls
+completed, arrivals for calls of parity 0 and 1), then two copies of the
+full output (8 x rows_per FP16 rows, padded to 256 bytes) for calls of parity
+0 and 1.
 """
 import ctypes as C
 
 import numpy as np
 import pytest
 
-from dq_testutil import (_ptr, abi, abi_build_native, abi_colmajor, abi_quantize, abi_split_gemv, abi_weights,
-                         dev, host, stream_ptr, workspace)
+from dq_testutil import _ptr, abi, abi_build_native, abi_colmajor, abi_quantize, abi_split_gemv, abi_weights, check_y, \
+    dev, host, stream_ptr, workspace
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
-MAX_CTAS = 1024
 MAX_RANKS = 8
 
 
 def _layout(rows_per):
-    slice_b = (rows_per * 2 + 255) // 256 * 256
-    flags = 2 * slice_b
-    epoch = flags + MAX_RANKS * MAX_CTAS * 4
-    total = (epoch + MAX_CTAS * 4 + 255) // 256 * 256
-    return slice_b, flags, epoch, total
+    ybytes = (MAX_RANKS * rows_per * 2 + 255) // 256 * 256
+    return 256, ybytes, 256 + 2 * ybytes  # copies start, bytes per copy, total
 
 
 def _weights(d_out, d_in, seed):
@@ -58,77 +58,100 @@ def _desc(rank, world, rows_per, d_total, regions):
     return _lib.DqGather(rank, world, rows_per, d_total, arr)
 
 
-def _u32(region, off, n):
-    return region[off:off + 4 * n].view(torch.int32)
+def _hdr(region):
+    return host(region[:12].view(torch.int32))
+
+
+def _copy(region, rows_per, par, n):
+    start, ybytes, _ = _layout(rows_per)
+    return region[start + par * ybytes:start + par * ybytes + 2 * n].view(torch.float16)
 
 
 def test_region_bytes():
     L = abi().lib()
     for rows in (16, 1024, 3584, 11008):
-        assert L.dq_gather_region_bytes(rows) == _layout(rows)[3]
+        assert L.dq_gather_region_bytes(rows) == _layout(rows)[2]
     assert L.dq_gather_region_bytes(0) == 0 and L.dq_gather_region_bytes(100) == 0
 
 
+def _own_rows(wts, x):
+    """This rank's rows as the gathering kernel computes them: a world-1 call
+    on a region of its own."""
+    region = torch.zeros(_layout(wts.d_out)[2], dtype=torch.uint8, device="cuda")
+    y = torch.empty(wts.d_out, dtype=torch.float16, device="cuda")
+    assert _gather(wts, x, y, _desc(0, 1, wts.d_out, wts.d_out, [region])) == 0
+    return y
+
+
 def test_world_one_is_the_split_gemv():
+    import oracle as O
     from dyn_quant import synth
     rows_per, d_in = 1024, 4096
+    w = synth.weights(rows_per, d_in, seed=3)
+    packed, scales, zeros = O.quantize(w)
     wts = _weights(rows_per, d_in, seed=3)
-    region = torch.zeros(_layout(rows_per)[3], dtype=torch.uint8, device="cuda")
+    region = torch.zeros(_layout(rows_per)[2], dtype=torch.uint8, device="cuda")
     g = _desc(0, 1, rows_per, rows_per, [region])
     for call in range(1, 4):
-        x = dev(synth.activation(d_in, 0.02, seed=30 + call))
+        xh = synth.activation(d_in, 0.02, seed=30 + call)
+        x = dev(xh)
         y = torch.empty(rows_per, dtype=torch.float16, device="cuda")
+        assert _gather(wts, x, y, g) == 0
+        torch.cuda.synchronize()
+        first = host(y).copy()
+        assert list(_hdr(region)) == [2 * call - 1, 0, 0]
         assert _gather(wts, x, y, g) == 0
         ref = abi_split_gemv(wts, x, 3.0)
         torch.cuda.synchronize()
-        assert torch.equal(y.view(torch.int16), ref.view(torch.int16)), f"call {call}"
-        epoch = host(_u32(region, _layout(rows_per)[2], MAX_CTAS))
-        grid = int((epoch > 0).sum())
-        assert grid > 0 and (epoch[:grid] == call).all() and (epoch[grid:] == 0).all()
+        assert np.array_equal(host(y).view(np.int16), first.view(np.int16)), f"call {call}: not reproducible"
+        check_y(first, host(ref), what=f"call {call} vs dq_split_gemv")
+        y16, _, _ = O.split_gemv(packed, scales, zeros, w, xh, 3.0)
+        check_y(first, y16, what=f"call {call} vs the oracle")
+        assert list(_hdr(region)) == [2 * call, 0, 0]
 
 
 @pytest.mark.parametrize("rows_per,d_in,tail", [(1024, 4096, 5), (3584, 8192, 0), (512, 11008, 16)])
 def test_rank0_of_two_with_planted_peer(rows_per, d_in, tail):
     from dyn_quant import synth
-    slice_b, flags_off, epoch_off, total = _layout(rows_per)
     d_total = 2 * rows_per - tail
     wts = _weights(rows_per, d_in, seed=4)
+    total = _layout(rows_per)[2]
     r0 = torch.zeros(total, dtype=torch.uint8, device="cuda")
     r1 = torch.zeros(total, dtype=torch.uint8, device="cuda")
     g = _desc(0, 2, rows_per, d_total, [r0, r1])
     rng = np.random.default_rng(5)
+    sent = [0, 0]  # arrivals rank 0 has added to rank 1's header, per parity
     for call in range(1, 4):
-        x = dev(synth.activation(d_in, 0.02, seed=40 + call))
-        # rank 1 has published call `call`: its rows in its slice, its flags in rank 0's region
-        peer_rows = rng.standard_normal(rows_per).astype(np.float16)
         par = call & 1
-        r1[par * slice_b:par * slice_b + 2 * rows_per].view(torch.float16).copy_(dev(peer_rows))
-        _u32(r0, flags_off + 1 * MAX_CTAS * 4, MAX_CTAS).fill_(call)
+        x = dev(synth.activation(d_in, 0.02, seed=40 + call))
+        # rank 1 has stored its rows of this call in rank 0's copy and arrived
+        peer_rows = rng.standard_normal(d_total - rows_per).astype(np.float16)
+        _copy(r0, rows_per, par, d_total)[rows_per:].copy_(dev(peer_rows))
+        r0[4 + 4 * par:8 + 4 * par].view(torch.int32).fill_(1)
         y = torch.full((d_total,), float("nan"), dtype=torch.float16, device="cuda")
         assert _gather(wts, x, y, g) == 0
-        own = abi_split_gemv(wts, x, 3.0)
+        own = _own_rows(wts, x)
         torch.cuda.synchronize()
+        sent[par] += 1
         yh = host(y)
         assert np.array_equal(yh[:rows_per].view(np.int16), host(own).view(np.int16)), f"call {call}: own rows"
-        assert np.array_equal(yh[rows_per:].view(np.int16), peer_rows[:d_total - rows_per].view(np.int16)), \
-            f"call {call}: the other rank's rows"
-        # rank 0 published in its own slice and raised its flags in rank 1's region
-        mine = host(r0[par * slice_b:par * slice_b + 2 * rows_per].view(torch.float16))
-        assert np.array_equal(mine.view(np.int16), host(own).view(np.int16))
-        epoch = host(_u32(r0, epoch_off, MAX_CTAS))
-        grid = int((epoch > 0).sum())
-        raised = host(_u32(r1, flags_off + 0 * MAX_CTAS * 4, MAX_CTAS))
-        assert (epoch[:grid] == call).all() and (raised[:grid] == call).all() and (raised[grid:] == 0).all()
+        assert np.array_equal(yh[rows_per:].view(np.int16), peer_rows.view(np.int16)), f"call {call}: peer rows"
+        # rank 0 stored its rows in rank 1's copy of this parity and arrived there
+        theirs = host(_copy(r1, rows_per, par, rows_per))
+        assert np.array_equal(theirs.view(np.int16), host(own).view(np.int16)), f"call {call}: rows sent"
+        h0, h1 = _hdr(r0), _hdr(r1)
+        assert h0[0] == call and h0[1 + par] == 0, f"call {call}: own header {h0}"
+        assert h1[1 + par] == sent[par], f"call {call}: arrivals sent {h1}"
     err = C.c_uint32(0)
     assert abi().lib().dq_read_device_error(C.byref(err), 0) == 0 and err.value & 16 == 0
 
 
 def test_wait_runs_out():
-    """No flags from the other rank: the bounded wait gives up (about a second)."""
+    """No arrival from the other rank: the bounded wait gives up (about a second)."""
     from dyn_quant import synth
     _lib = abi()
     rows_per, d_in = 256, 4096
-    _, _, _, total = _layout(rows_per)
+    total = _layout(rows_per)[2]
     wts = _weights(rows_per, d_in, seed=6)
     r0 = torch.zeros(total, dtype=torch.uint8, device="cuda")
     r1 = torch.zeros(total, dtype=torch.uint8, device="cuda")
@@ -138,9 +161,10 @@ def test_wait_runs_out():
     err = C.c_uint32(0)
     assert _lib.lib().dq_read_device_error(C.byref(err), 1) == 0
     assert _gather(wts, x, y, g) == 0
-    own = abi_split_gemv(wts, x, 3.0)
     torch.cuda.synchronize()
     assert _lib.lib().dq_read_device_error(C.byref(err), 1) == 0
+    own = _own_rows(wts, x)
+    torch.cuda.synchronize()
     assert err.value & 16, f"error word {err.value:#x}: the wait should have run out"
     yh = host(y)
     assert np.array_equal(yh[:rows_per].view(np.int16), host(own).view(np.int16))
@@ -152,7 +176,7 @@ def test_bad_arguments():
     L = _lib.lib()
     rows_per, d_in = 256, 4096
     wts = _weights(rows_per, d_in, seed=8)
-    region = torch.zeros(_layout(rows_per)[3], dtype=torch.uint8, device="cuda")
+    region = torch.zeros(_layout(rows_per)[2], dtype=torch.uint8, device="cuda")
     x = torch.zeros(d_in, dtype=torch.float16, device="cuda")
     y = torch.zeros(rows_per, dtype=torch.float16, device="cuda")
     ws = workspace(rows_per, d_in)
@@ -170,4 +194,8 @@ def test_bad_arguments():
     assert call(g) == _lib.DQ_ERR_INVALID_ARGUMENT
     no_native = abi_weights(*wts._keep[:3], w_cm=wts._keep[4])
     assert call(_desc(0, 1, rows_per, rows_per, [region]), no_native) == _lib.DQ_ERR_INVALID_ARGUMENT
+    small = torch.zeros(256 + 16 * 8 * 1024, dtype=torch.uint8, device="cuda")
+    assert L.dq_split_gemv_gather(C.byref(wts), _ptr(x), _ptr(y), 3.0, _ptr(small), small.numel(),
+                                  C.byref(_desc(0, 1, rows_per, rows_per, [region])), stream_ptr()) == \
+        _lib.DQ_ERR_WORKSPACE
     torch.cuda.synchronize()

@@ -28,7 +28,8 @@ def test_silu_mul_matches_numpy():
     assert (diff <= ulp).all()  # at most one FP16 ulp (exp differs by an FP32 ulp at most)
 
 
-@pytest.mark.parametrize("E,D,F,T,K", [(4, 512, 1024, 8, 2), (8, 1024, 2048, 16, 2)])
+@pytest.mark.parametrize("E,D,F,T,K", [(4, 512, 1024, 8, 2), (8, 1024, 2048, 16, 2), (8, 4096, 14336, 16, 2)],
+                         ids=["4x512x1024", "8x1024x2048", "mixtral-8x4096x14336"])
 def test_moe_ffn_matches_oracle(E, D, F, T, K):
     """Every stage against the oracle given the GPU's own inputs to that stage
     (w1 and w3 on x, the gated activation on the GPU's a and b, w2 on the

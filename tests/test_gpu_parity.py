@@ -257,7 +257,8 @@ def test_abi_rejects_bad_arguments():
 
 
 FULL = [("llama2_7b_gate", 11008, 4096, 0.01), ("llama2_7b_down", 4096, 11008, 0.01),
-        ("llama2_70b_q", 8192, 8192, 0.03), ("llama2_70b_down", 8192, 28672, 0.03)]
+        ("llama2_70b_q", 8192, 8192, 0.03), ("llama2_70b_gate", 28672, 8192, 0.03),
+        ("llama2_70b_down", 8192, 28672, 0.03)]
 
 
 @pytest.mark.parametrize("name,d_out,d_in,frac", FULL, ids=[f[0] for f in FULL])
