@@ -209,12 +209,12 @@ dq_status_t dq_reset_workspace(void* workspace, size_t workspace_bytes, void* st
     return DQ_OK;
 }
 
-// The plain split / INT4 GEMV runs the batch-1 kernel of dq_gemv.cu, which is
-// the faster of the two on B200 at every Llama-2 shape measured.  The
-// streaming kernel (dq_stream.cu) carries the fused row-sharded gather; with
-// DQ_STREAM=1 in the environment (read once) it also serves the plain calls
-// it supports (native layout, column-major mirror for the split GEMV), for
-// timing the two against each other.
+// The split / INT4 GEMV (plain or with the fused gather) runs the batch-1
+// kernel of dq_gemv.cu, which is the faster of the two on B200 at every
+// Llama-2 shape measured.  With DQ_STREAM=1 in the environment (read once)
+// the streaming kernel (dq_stream.cu) serves the calls it supports instead
+// (native layout, column-major mirror for the split GEMV), for timing the
+// two against each other.
 static bool stream_requested() {
     static const bool on = [] {
         const char* s = std::getenv("DQ_STREAM");
@@ -260,7 +260,9 @@ dq_status_t dq_split_gemv_gather(const dq_weights_t* w, const uint16_t* x, uint1
     if (!w->native || !w->fp16_cm || !stream_supported(*w, true)) return DQ_ERR_INVALID_ARGUMENT;
     if (stream_geom(w->d_out, w->d_in).n_rb > kStreamMaxRb) return DQ_ERR_UNSUPPORTED;
     if (workspace_bytes < stream_ws(w->d_out, w->d_in).total) return DQ_ERR_WORKSPACE;
-    return launch_gemv_stream(*w, x, y, outlier_k, true, workspace, g, static_cast<cudaStream_t>(stream));
+    if (stream_requested())
+        return launch_gemv_stream(*w, x, y, outlier_k, true, workspace, g, static_cast<cudaStream_t>(stream));
+    return launch_gemv_b1_gather(*w, x, y, outlier_k, workspace, *g, static_cast<cudaStream_t>(stream));
 }
 
 dq_status_t dq_device_alloc(size_t bytes, void** ptr) {

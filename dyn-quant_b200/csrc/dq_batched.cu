@@ -40,7 +40,6 @@
 #include <algorithm>
 
 #include "dq_common.cuh"
-#include "dq_gplan.cuh"
 #include "dq_internal.h"
 #include "dq_plan.cuh"
 
@@ -121,7 +120,7 @@ __global__ void __launch_bounds__(kStatThreads, 1) bplan_kernel(const BPArgs a) 
     load_x_async<NT>(a.x + static_cast<size_t>(m) * a.d_in, n8, xs);
     cp_async_wait_all();
     __syncthreads();
-    const GpStats st = gp_stats_smem<NT>(xs, a.d_in / kGroup, a.d_in, a.k, a.inv_n, a.inv_n1, red);
+    const XStats st = x_stats<NT>(xs, n8, a.d_in, a.k, a.inv_n, a.inv_n1, red);
     x_mask_list<NT>(xs, a.d_in, st.mean, st.thresh, mask32, list,
                     reinterpret_cast<int*>(red) + 2 * (kStatThreads / 32));
     __syncthreads();

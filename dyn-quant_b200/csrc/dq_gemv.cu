@@ -16,8 +16,9 @@
 //      completing on per-stage mbarriers).
 //   2. Each CTA derives the activation plan itself from x (<= 60 KB, an L2
 //      hit after the first CTA): the statistics, the outlier mask with the
-//      reference's capacity rule, the ascending outlier list, and the MMA B
-//      fragments of the masked activation x' with per-group sums.
+//      reference's capacity rule, the outlier list, and the MMA B fragments
+//      of the masked activation x' with per-group sums (dq_plan.cuh; the
+//      pieces of x spread evenly over all threads).
 //   3. The warps run dequant + tensor-core MMAs over their units.  A unit is
 //      16 rows x 4 groups of 128 columns; the units are split evenly across
 //      CTAs (and across the warps of a CTA) in (row block, column chunk)
@@ -45,7 +46,6 @@
 
 #include "dq_common.cuh"
 #include "dq_internal.h"
-#include "dq_gplan.cuh"
 #include "dq_plan.cuh"
 
 namespace dq {
@@ -79,6 +79,11 @@ struct B1Args {
     int d_out, d_in, NC, U, nrb_max;
     int depth;                // ring stages per warp (reference layout: kB1Stages)
     B1Smem S;
+    // fused gather (kGather): this rank, the ranks, slice height, output rows,
+    // every rank's gather region as mapped here
+    int g_rank, g_world, g_rows_per, g_total;
+    uint8_t* g_region[kMaxGatherRanks];
+    GatherLayout g_lay;
 };
 
 // How the split path reads the FP16 weights of outlier columns.
@@ -96,11 +101,63 @@ __host__ __device__ inline int unit_owner(long long u, int P, long long U) {
     return static_cast<int>((u * P + P - 1) / U);
 }
 
+// The fused gather's last step, by the last CTA of this rank's call (every
+// CTA's rows are in the other ranks' regions: each fenced before it counted
+// itself done).  Tell every other rank that this rank's rows of the call are
+// in its region, wait (bounded, about a second: on timeout bit 4 of the error
+// word, the other ranks' rows left unwritten) until every other rank's rows
+// are in this one, copy them into y, and count the call completed.
+template <int kT>
+__device__ void gather_finish(const B1Args& a, uint32_t* gmisc) {
+    const int tid = threadIdx.x;
+    const uint32_t call = gmisc[1], par = call & 1u;
+    uint8_t* own = a.g_region[a.g_rank];
+    unsigned int* arrived = reinterpret_cast<unsigned int*>(own + a.g_lay.hdr) + 1 + par;
+    if (tid == 0) {
+        __threadfence_system();
+        for (int q = 0; q < a.g_world; ++q)
+            if (q != a.g_rank)
+                red_release_sys_add_u32(reinterpret_cast<unsigned int*>(a.g_region[q] + a.g_lay.hdr) + 1 + par, 1u);
+        const unsigned int want = static_cast<unsigned int>(a.g_world - 1);
+        uint32_t v = ld_acquire_sys_u32(arrived);
+        const long long t0 = clock64();
+        while (v < want && clock64() - t0 < (1ll << 31)) v = ld_acquire_sys_u32(arrived);
+        gmisc[3] = v >= want;
+        if (v < want) atomicOr(&g_error_word, 16u);
+    }
+    __syncthreads();
+    if (gmisc[3]) {
+        // The rows came over NVLink into this GPU's memory: read them at L2.
+        const uint16_t* src = reinterpret_cast<const uint16_t*>(own + a.g_lay.yfull + par * a.g_lay.ybytes);
+        const bool vec = (reinterpret_cast<uintptr_t>(a.y) & 15u) == 0;
+        for (int q = 0; q < a.g_world; ++q) {
+            if (q == a.g_rank) continue;
+            const int r0 = q * a.g_rows_per, r1 = min(r0 + a.g_rows_per, a.g_total);
+            const int nv = vec ? (r1 - r0) / 8 : 0;  // r0 is a multiple of 16 rows: 32-byte aligned
+            for (int i = tid; i < nv; i += kT)
+                reinterpret_cast<uint4*>(a.y + r0)[i] = ldcg_v4(reinterpret_cast<const uint4*>(src + r0) + i);
+            for (int r = r0 + 8 * nv + tid; r < r1; r += kT) a.y[r] = ldcg_u16(src + r);
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        *arrived = 0u;  // every other rank's arrival for this call is in
+        reinterpret_cast<unsigned int*>(own + a.g_lay.hdr)[0] = call;
+    }
+}
+
+// Rounds of the balanced plan partition (pieces of x per thread) for the
+// longest rows (kMaxDIn) in a CTA of kW warps.
+template <int kW>
+constexpr int plan_rounds_max() { return (kMaxDIn / 8 + 32 * kW - 1) / (32 * kW); }
+
 // kNative: weights in the unit layout (one bulk copy per unit, scale/zero
 // inside); otherwise the reference layout (one bulk copy per weight row of the
-// unit, scale/zero by plain loads).  kR: rounds of x held in registers by the
-// plan (at least ceil(NC / 8)).
-template <bool kSplit, bool kNative, int kOut, int kW, int kR>
+// unit, scale/zero by plain loads).  kR: rounds of the plan's balanced
+// partition (at least ceil(64 NC / threads)).  kGather: the row-sharded gather is fused
+// (each output row also goes to every other rank's gather region; the last
+// CTA exchanges the arrivals and copies the other ranks' rows into y).
+template <bool kSplit, bool kNative, int kOut, int kW, int kR, bool kGather>
 __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
     constexpr int kT = kW * 32;
     extern __shared__ __align__(128) char smem[];
@@ -194,8 +251,8 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
 
     // The weights do not depend on the preceding kernel: each warp's first
     // kB1Stages units are pulled into L2 before griddepcontrol.wait (native
-    // layout).  After the wait x is requested first, straight into registers,
-    // then the ring's first fill, which so does not hold x up.  (Copying the
+    // layout).  After the wait x is requested first (cp.async into shared
+    // memory), then the ring's first fill, which so does not hold x up.  (Copying the
     // units into shared memory before the wait, or all of a CTA's share at
     // once, puts the weight stream in front of x on the SM's return path and
     // made chains of GEMVs slower.)
@@ -210,14 +267,33 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
     // Every CTA reads it before it finishes, and the last CTA to finish
     // advances it, so all CTAs of a call see the same tag.
     uint32_t& s_tag = *reinterpret_cast<uint32_t*>(smem + a.S.misc);
+    // Gather: misc[1] this call's number (calls this rank completed + 1; its
+    // parity picks the copy written in the ranks' regions), misc[2] last CTA,
+    // misc[3] the other ranks' rows are in.
+    uint32_t* gmisc = reinterpret_cast<uint32_t*>(smem + a.S.misc);
     if (tid == 0) {
         const uint32_t e = ldcg_u32(a.hdr) + 1u;
         s_tag = e == 0u ? 1u : e;
+        if (kGather) gmisc[1] = ldcg_u32(a.g_region[a.g_rank] + a.g_lay.hdr) + 1u;
     }
-    // Output row `row` (< d_out) of this call.
-    auto store_row = [&](int row, float v) { a.y[row] = __half_as_ushort(__float2half_rn(v)); };
-    XRegs<kT, kR> xr;
-    x_regs_load_global<kT>(a.x, n8, xr);
+    // Output row `row` (< d_out) of this call: y, and with the gather also
+    // every other rank's copy (peer stores over NVLink).
+    auto store_row = [&](int row, float v) {
+        const uint16_t h = __half_as_ushort(__float2half_rn(v));
+        if (!kGather) {
+            a.y[row] = h;
+            return;
+        }
+        const int grow = a.g_rank * a.g_rows_per + row;
+        if (grow >= a.g_total) return;
+        a.y[grow] = h;
+        const size_t off = a.g_lay.yfull + static_cast<size_t>(gmisc[1] & 1u) * a.g_lay.ybytes + 2 * static_cast<size_t>(grow);
+        for (int q = 0; q < a.g_world; ++q)
+            if (q != a.g_rank) *reinterpret_cast<uint16_t*>(a.g_region[q] + off) = h;
+    };
+    // x into xb in natural order (requested before the weight copies, so that
+    // it does not queue behind them on the SM's return path).
+    load_x_async<kT>(a.x, n8, xb);
     if (kNative) {
         for (int k = 0; k < fill; ++k) {
             issue(k, cu0 + warp + kW * k);
@@ -232,34 +308,18 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
             }
         }
     }
+    cp_async_wait_all();
+    __syncthreads();
 
     // ---- activation plan: statistics, mask, MMA B fragments of x', outlier list ----
     int n_out = 0;
-    int* wcnt = reinterpret_cast<int*>(red) + 2 * (kStatThreads / 32);
+    int* pscratch = reinterpret_cast<int*>(red) + 32;  // after the statistics' 32 floats
     if (kSplit) {
-        const XStats st = x_stats_regs<kT>(xr, n8, a.d_in, a.k, a.inv_n, a.inv_n1, red);
-        const int cap = a.d_in / 16;  // no stripe class can exceed its capacity below this total
-        n_out = x_frags_regs<kT, true>(xr, n8, NC, st.mean, st.thresh, nullptr, cap, xb, xp4, list, wcnt);
-        if (n_out > cap) {
-            // The reference's capacity rule may drop outliers: derive the mask
-            // from x in natural order, then rebuild the fragments and the list.
-#pragma unroll
-            for (int q = 0; q < XRegs<kT, kR>::VPT; ++q)
-#pragma unroll
-                for (int rr = 0; rr < kR; ++rr) {
-                    const int v = plan_vthread<kT>(q), p = v + kStatThreads * rr;
-                    if (v < kStatThreads && p < n8) xb[p] = xr.v[q][rr];
-                }
-            __syncthreads();
-            x_mask_list<kT>(xb, a.d_in, st.mean, st.thresh, reinterpret_cast<uint32_t*>(mask), list,
-                            reinterpret_cast<int*>(red) + 2 * (kStatThreads / 32));
-            __syncthreads();
-            n_out = x_frags_regs<kT, true>(xr, n8, NC, st.mean, st.thresh, reinterpret_cast<const uint32_t*>(mask),
-                                           INT_MAX, xb, xp4, list, wcnt);
-        }
-        __syncthreads();  // list complete
+        const XStats st = x_stats<kT>(xb, n8, a.d_in, a.k, a.inv_n, a.inv_n1, red);
+        n_out = plan_balanced<kT, kR, true>(xb, n8, NC, a.d_in, st.mean, st.thresh, xp4, list,
+                                            reinterpret_cast<uint32_t*>(mask), pscratch);
     } else {
-        x_frags_regs<kT, false>(xr, n8, NC, 0.f, 0.f, nullptr, 0, xb, xp4, nullptr, wcnt);
+        plan_balanced<kT, kR, false>(xb, n8, NC, a.d_in, 0.f, 0.f, xp4, nullptr, nullptr, pscratch);
     }
 
     // ---- outlier columns: y[r] += W16[r][c] * x[c] for the rows of row blocks orb0 .. rbz ----
@@ -533,9 +593,18 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
     // This CTA is done with the workspace (its tag read, its words published,
     // its finaliser wait over): the last CTA of the call advances the tag.
     __syncthreads();
-    if (tid == 0 && atomicAdd(a.hdr + 1, 1u) == gridDim.x - 1u) {
-        a.hdr[1] = 0u;
-        a.hdr[0] = s_tag;
+    if (tid == 0) {
+        if (kGather) __threadfence_system();  // this CTA's rows are in the other ranks' regions
+        const bool last = atomicAdd(a.hdr + 1, 1u) == gridDim.x - 1u;
+        if (last) {
+            a.hdr[1] = 0u;
+            a.hdr[0] = s_tag;
+        }
+        gmisc[2] = last;
+    }
+    if constexpr (kGather) {
+        __syncthreads();
+        if (gmisc[2]) gather_finish<kT>(a, gmisc);
     }
 }
 
@@ -613,7 +682,7 @@ __global__ void __launch_bounds__(kStatThreads, 1)
     load_x_async<kStatThreads>(x, n8, xs);
     cp_async_wait_all();
     __syncthreads();
-    const GpStats st = gp_stats_smem<kStatThreads>(xs, d_in / kGroup, d_in, k, inv_n, inv_n1, red);
+    const XStats st = x_stats<kStatThreads>(xs, n8, d_in, k, inv_n, inv_n1, red);
     const int n = x_mask_list<kStatThreads>(xs, d_in, st.mean, st.thresh, reinterpret_cast<uint32_t*>(mask), list,
                                             reinterpret_cast<int*>(red) + 2 * (kStatThreads / 32));
     __syncthreads();
@@ -863,13 +932,13 @@ dq_status_t check_launch() {
 }
 
 
-template <bool kSplit, bool kNative, int kOut, int kW, int kR>
+template <bool kSplit, bool kNative, int kOut, int kW, int kR, bool kGather = false>
 dq_status_t launch_b1(const B1Args& a, int grid, cudaStream_t stream) {
     constexpr int wi = kW == kB1Warps ? 0 : 1;
     constexpr int ri = kR == 1 ? 0 : kR == 2 ? 1 : kR == 4 ? 2 : 3;
-    constexpr int id = 4 + 16 * (4 * wi + ri) + (kSplit ? 8 : 0) + (kNative ? 4 : 0) + kOut;
+    constexpr int id = 4 + 16 * (4 * wi + ri) + (kSplit ? 8 : 0) + (kNative ? 4 : 0) + kOut + (kGather ? 128 : 0);
     static_assert(id < kNumKernels, "kernel attribute slot");
-    const dq_status_t st = ensure_smem(b1_kernel<kSplit, kNative, kOut, kW, kR>, id, a.S.total);
+    const dq_status_t st = ensure_smem(b1_kernel<kSplit, kNative, kOut, kW, kR, kGather>, id, a.S.total);
     if (st != DQ_OK) return st;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -881,7 +950,7 @@ dq_status_t launch_b1(const B1Args& a, int grid, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, b1_kernel<kSplit, kNative, kOut, kW, kR>, a);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, b1_kernel<kSplit, kNative, kOut, kW, kR, kGather>, a);
     if (e != cudaSuccess) { set_cuda_error(e); return DQ_ERR_CUDA; }
     return check_launch();
 }
@@ -901,13 +970,24 @@ dq_status_t launch_b1_native(const B1Args& a, int out_mode, int rounds, int grid
     if (rounds <= 1) return launch_b1_out<true, kW, 1>(a, out_mode, grid, stream);
     if (rounds <= 2) return launch_b1_out<true, kW, 2>(a, out_mode, grid, stream);
     if (rounds <= 4) return launch_b1_out<true, kW, 4>(a, out_mode, grid, stream);
-    return launch_b1_out<true, kW, kPlanRounds>(a, out_mode, grid, stream);
+    return launch_b1_out<true, kW, plan_rounds_max<kW>()>(a, out_mode, grid, stream);
+}
+
+// The gathering split GEMV: native layout, staged outlier columns (the
+// slices are whole row blocks, so d_out is a multiple of 16).
+template <int kW>
+dq_status_t launch_b1_gather(const B1Args& a, int rounds, int grid, cudaStream_t stream) {
+    if (rounds <= 1) return launch_b1<true, true, kOutStaged, kW, 1, true>(a, grid, stream);
+    if (rounds <= 2) return launch_b1<true, true, kOutStaged, kW, 2, true>(a, grid, stream);
+    if (rounds <= 4) return launch_b1<true, true, kOutStaged, kW, 4, true>(a, grid, stream);
+    return launch_b1<true, true, kOutStaged, kW, plan_rounds_max<kW>(), true>(a, grid, stream);
 }
 
 dq_status_t launch_b1_warps(const B1Args& a, int warps, int out_mode, int rounds, int grid, cudaStream_t stream) {
     if (!a.native)
-        return warps == kB1Warps ? launch_b1_out<false, kB1Warps, kPlanRounds>(a, out_mode, grid, stream)
-                                 : launch_b1_out<false, kB1WarpsSmall, kPlanRounds>(a, out_mode, grid, stream);
+        return warps == kB1Warps
+                   ? launch_b1_out<false, kB1Warps, plan_rounds_max<kB1Warps>()>(a, out_mode, grid, stream)
+                   : launch_b1_out<false, kB1WarpsSmall, plan_rounds_max<kB1WarpsSmall>()>(a, out_mode, grid, stream);
     return warps == kB1Warps ? launch_b1_native<kB1Warps>(a, out_mode, rounds, grid, stream)
                              : launch_b1_native<kB1WarpsSmall>(a, out_mode, rounds, grid, stream);
 }
@@ -956,7 +1036,6 @@ dq_status_t b1_setup(const dq_weights_t& w, const uint16_t* x, uint16_t* y, floa
     }
     a.nrb_max = nrb_max;
     p.grid = grid;
-    p.rounds = (NC + 7) / 8;  // plan rounds of x per virtual thread
     p.out_mode = kOutNone;
     if (split) p.out_mode = w.fp16_cm ? ((w.d_out % 8) == 0 ? kOutStaged : kOutColDirect) : kOutRowDirect;
     if (w.native) {
@@ -971,6 +1050,7 @@ dq_status_t b1_setup(const dq_weights_t& w, const uint16_t* x, uint16_t* y, floa
                 if (a.S.total > di.smem_optin) continue;
                 a.depth = depth;
                 p.warps = warps;
+                p.rounds = (64 * NC + 32 * warps - 1) / (32 * warps);  // plan rounds: pieces per thread
                 return DQ_OK;
             }
         }
@@ -986,6 +1066,7 @@ dq_status_t b1_setup(const dq_weights_t& w, const uint16_t* x, uint16_t* y, floa
         a.S = b1_smem(w.d_in, nrb_max, split, p.warps, p.warps * kB1Stages);
     }
     if (a.S.total > di.smem_optin) return DQ_ERR_UNSUPPORTED;
+    p.rounds = (64 * NC + 32 * p.warps - 1) / (32 * p.warps);
     return DQ_OK;
 }
 
@@ -998,6 +1079,24 @@ dq_status_t launch_gemv_b1(const dq_weights_t& w, const uint16_t* x, uint16_t* y
     const dq_status_t st = b1_setup(w, x, y, k, split, workspace, a, p);
     if (st != DQ_OK) return st;
     return launch_b1_warps(a, p.warps, p.out_mode, p.rounds, p.grid, stream);
+}
+
+dq_status_t launch_gemv_b1_gather(const dq_weights_t& w, const uint16_t* x, uint16_t* y, float k, void* workspace,
+                                  const dq_gather_t& g, cudaStream_t stream) {
+    B1Args a;
+    B1Plan p;
+    const dq_status_t st = b1_setup(w, x, y, k, true, workspace, a, p);
+    if (st != DQ_OK) return st;
+    if (!a.native || p.out_mode != kOutStaged) return DQ_ERR_UNSUPPORTED;
+    a.g_rank = g.rank;
+    a.g_world = g.world;
+    a.g_rows_per = g.rows_per;
+    a.g_total = g.d_total;
+    for (int q = 0; q < kMaxGatherRanks; ++q)
+        a.g_region[q] = q < g.world ? static_cast<uint8_t*>(g.region[q]) : nullptr;
+    a.g_lay = gather_layout(g.rows_per);
+    return p.warps == kB1Warps ? launch_b1_gather<kB1Warps>(a, p.rounds, p.grid, stream)
+                               : launch_b1_gather<kB1WarpsSmall>(a, p.rounds, p.grid, stream);
 }
 
 dq_status_t launch_build_native(const uint8_t* packed, const uint16_t* scales, const uint16_t* zeros,

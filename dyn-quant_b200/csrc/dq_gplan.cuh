@@ -1,19 +1,17 @@
-// dq_gplan.cuh -- the activation plan in the group partition: the statistics
-// of x, the outlier mask with the reference's capacity rule
+// dq_gplan.cuh -- the activation plan of the streaming kernel in the group
+// partition: the outlier mask with the reference's capacity rule
 // (src/outlier_detect.cuh:104-205), the MMA B fragments of the masked
 // activation x', its per-group sums and the outlier list, computed by up to
-// kPlanThreads threads from registers.
+// kPlanThreads threads from registers.  (The statistics themselves come from
+// x_stats_bar of dq_plan.cuh, the partition every kernel shares, so that all
+// kernels derive the same mask bit for bit.)
 //
 // Partition.  x (d_in = 128 G columns) is G groups of 16 pieces (a piece is 8
 // consecutive columns, 16 bytes).  Plan thread tau = TPG j + h (TPG threads per
 // group, the largest of 16, 8, 4, 2, 1 with G TPG <= kPlanThreads) holds the
 // PPT = 16 / TPG consecutive pieces 16 j + PPT h .. 16 j + PPT h + PPT - 1 of
-// group j.  Sums run in a fixed order: per thread over its pieces (word by
-// word, low half then high half), a xor butterfly within each warp, then a
-// fixed tree over the 16 warp totals (threads past G TPG, and warps past the
-// plan threads, add exact zeros).  The statistics therefore depend on d_in and
-// x only, not on the kernel or its thread count: the split GEMV, the
-// standalone detector and the batched plan derive the same mask bit for bit.
+// group j.  The per-group sums of x' run in a fixed order (per thread over its
+// pieces, then a xor butterfly over the group's TPG lanes).
 #pragma once
 
 #include "dq_common.cuh"
@@ -65,115 +63,6 @@ __device__ __forceinline__ void gp_load_smem(const uint4* xs, int G, int tau, Gp
 #pragma unroll
         for (int i = 0; i < kPPT; ++i) r.v[i] = xs[16 * j + kPPT * h + i];
     }
-}
-
-// Sum of the 16 floats at red (16-byte aligned shared memory), fixed tree.
-__device__ __forceinline__ float gp_tree16(const float* red) {
-    const uint32_t a = smem_u32(red);
-    const uint4 q0 = lds_v4(a), q1 = lds_v4(a + 16), q2 = lds_v4(a + 32), q3 = lds_v4(a + 48);
-    auto f = [](uint32_t u) { return __uint_as_float(u); };
-    const float s0 = (f(q0.x) + f(q0.y)) + (f(q0.z) + f(q0.w));
-    const float s1 = (f(q1.x) + f(q1.y)) + (f(q1.z) + f(q1.w));
-    const float s2 = (f(q2.x) + f(q2.y)) + (f(q2.z) + f(q2.w));
-    const float s3 = (f(q3.x) + f(q3.y)) + (f(q3.z) + f(q3.w));
-    return (s0 + s1) + (s2 + s3);
-}
-
-struct GpStats {
-    float mean, thresh, var, m2;
-};
-
-// Mean, unbiased variance and threshold k sqrt(max(var, 1e-8)) of x.  Called
-// by every thread of warps 0 .. NW-1 (NW >= kPlanWarps; plan thread tau =
-// threadIdx.x); bar() synchronises exactly those threads.  red: 32 floats of
-// shared memory, 16-byte aligned, not in use; red[NW..15] must hold zeros
-// when NW < 16 (the caller zeroes them once).
-template <int kPPT, class Bar>
-__device__ __forceinline__ GpStats gp_stats(const GpRegs<kPPT>& r, int d_in, float k, float inv_n, float inv_n1,
-                                            float* red, Bar bar) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    float s = 0.f;
-#pragma unroll
-    for (int i = 0; i < kPPT; ++i)
-#pragma unroll
-        for (int w = 0; w < 4; ++w) {
-            const uint32_t u = gp_word(r.v[i], w);
-            s = add_f16_f32(hi16(u), add_f16_f32(lo16(u), s));
-        }
-    s = warp_sum(s);
-    if (lane == 0) red[warp] = s;
-    bar();
-    GpStats st;
-    st.mean = __fmul_rn(gp_tree16(red), inv_n);
-    float q = 0.f;
-#pragma unroll
-    for (int i = 0; i < kPPT; ++i)
-#pragma unroll
-        for (int w = 0; w < 4; ++w) {
-            const uint32_t u = gp_word(r.v[i], w);
-            const float d0 = sub_f16_f32(lo16(u), st.mean);
-            const float d1 = sub_f16_f32(hi16(u), st.mean);
-            q = __fmaf_rn(d1, d1, __fmaf_rn(d0, d0, q));
-        }
-    q = warp_sum(q);
-    if (lane == 0) red[16 + warp] = q;
-    bar();
-    st.m2 = gp_tree16(red + 16);
-    st.var = d_in > 1 ? __fmul_rn(st.m2, inv_n1) : 0.f;
-    st.thresh = __fmul_rn(k, __fsqrt_rn(fmaxf(st.var, 1e-8f)));
-    return st;
-}
-
-// gp_stats from x in shared memory (natural order), by the NT >= kPlanThreads
-// threads of a block (plan thread tau = threadIdx.x; threads past the
-// partition add zeros): the same partition, order and tree, so the same bits
-// as gp_stats over registers.  red: 32 floats, 16-byte aligned, not in use;
-// two __syncthreads().
-template <int NT>
-__device__ __forceinline__ GpStats gp_stats_smem(const uint4* xs, int G, int d_in, float k, float inv_n,
-                                                 float inv_n1, float* red) {
-    static_assert(NT >= kPlanThreads && NT <= 512 && NT % 32 == 0, "plan partition");
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int TPG = gp_tpg(G), PPT = 16 / TPG;
-    const int tau = threadIdx.x;
-    const bool mine = tau < G * TPG;
-    const uint4* src = xs + 16 * (tau / TPG) + PPT * (tau % TPG);
-    float s = 0.f;
-    if (mine)
-        for (int i = 0; i < PPT; ++i) {
-            const uint4 v = src[i];
-#pragma unroll
-            for (int w = 0; w < 4; ++w) {
-                const uint32_t u = gp_word(v, w);
-                s = add_f16_f32(hi16(u), add_f16_f32(lo16(u), s));
-            }
-        }
-    s = warp_sum(s);
-    if (lane == 0) red[warp] = s;
-    if (NT < 512 && threadIdx.x < 16 - NT / 32) red[NT / 32 + threadIdx.x] = 0.f;
-    __syncthreads();
-    GpStats st;
-    st.mean = __fmul_rn(gp_tree16(red), inv_n);
-    float q = 0.f;
-    if (mine)
-        for (int i = 0; i < PPT; ++i) {
-            const uint4 v = src[i];
-#pragma unroll
-            for (int w = 0; w < 4; ++w) {
-                const uint32_t u = gp_word(v, w);
-                const float d0 = sub_f16_f32(lo16(u), st.mean);
-                const float d1 = sub_f16_f32(hi16(u), st.mean);
-                q = __fmaf_rn(d1, d1, __fmaf_rn(d0, d0, q));
-            }
-        }
-    q = warp_sum(q);
-    if (lane == 0) red[16 + warp] = q;
-    if (NT < 512 && threadIdx.x < 16 - NT / 32) red[16 + NT / 32 + threadIdx.x] = 0.f;
-    __syncthreads();
-    st.m2 = gp_tree16(red + 16);
-    st.var = d_in > 1 ? __fmul_rn(st.m2, inv_n1) : 0.f;
-    st.thresh = __fmul_rn(k, __fsqrt_rn(fmaxf(st.var, 1e-8f)));
-    return st;
 }
 
 // Outlier bits of one piece: bit 2i (2i + 1) for the low (high) half of word i.

@@ -307,6 +307,10 @@ void set_cuda_error(cudaError_t e);
 // Kernel launchers (arguments already validated by the C ABI layer).
 dq_status_t launch_gemv_b1(const dq_weights_t& w, const uint16_t* x, uint16_t* y, float k,
                            bool split, void* workspace, cudaStream_t stream);
+// The split GEMV with the row-sharded gather fused (native layout and mirror,
+// d_out a multiple of 16): y holds g.d_total rows.
+dq_status_t launch_gemv_b1_gather(const dq_weights_t& w, const uint16_t* x, uint16_t* y, float k, void* workspace,
+                                  const dq_gather_t& g, cudaStream_t stream);
 dq_status_t launch_build_native(const uint8_t* packed, const uint16_t* scales, const uint16_t* zeros,
                                 int d_out, int d_in, uint8_t* out, cudaStream_t stream);
 dq_status_t read_device_error(uint32_t* word, bool clear);

@@ -94,7 +94,8 @@ __device__ __forceinline__ float sum16_tree(const float* p) {
 }
 
 // Mean and unbiased variance of x (in xs), threshold k * sqrt(max(var, 1e-8)),
-// reading x from shared memory (detector, batched plan kernel).  The same
+// reading x from shared memory (detector, batched plan kernel, streaming
+// kernel).  The same
 // partition and summation order as x_stats_regs: bit-identical statistics.
 // Two passes (sum, then sum of squared deviations) over a fixed partition of
 // kStatThreads virtual threads (virtual thread v: pieces v, v + 512, ...;
@@ -103,9 +104,10 @@ __device__ __forceinline__ float sum16_tree(const float* p) {
 // count, and the standalone detector get bit-identical statistics.
 // inv_n = 1/d_in and inv_n1 = 1/(d_in - 1) come from the host.
 // red: >= 32 floats, 16-byte aligned, not in use; two barriers.
-template <int NT>
-__device__ __forceinline__ XStats x_stats(const uint4* xs, int n8, int d_in, float k, float inv_n, float inv_n1,
-                                          float* red) {
+// bar() synchronises the NT threads (warps 0 .. NT/32 - 1) running it.
+template <int NT, class Bar>
+__device__ __forceinline__ XStats x_stats_bar(const uint4* xs, int n8, int d_in, float k, float inv_n, float inv_n1,
+                                              float* red, Bar bar) {
     constexpr int NW = NT / 32;
     constexpr int NWV = kStatThreads / 32;
     static_assert(NT <= kStatThreads && NT % 32 == 0, "statistics partition");
@@ -124,7 +126,7 @@ __device__ __forceinline__ XStats x_stats(const uint4* xs, int n8, int d_in, flo
         const float ws = warp_sum((s[0] + s[1]) + (s[2] + s[3]));
         if (lane == 0) red[vw] = ws;
     }
-    __syncthreads();
+    bar();
     const float total = sum16_tree(red);
     XStats r;
     r.mean = __fmul_rn(total, inv_n);
@@ -144,12 +146,18 @@ __device__ __forceinline__ XStats x_stats(const uint4* xs, int n8, int d_in, flo
         const float wq = warp_sum((m[0] + m[1]) + (m[2] + m[3]));
         if (lane == 0) red[NWV + vw] = wq;
     }
-    __syncthreads();
+    bar();
     const float m2 = sum16_tree(red + NWV);
     r.m2 = m2;
     r.var = (d_in > 1) ? __fmul_rn(m2, inv_n1) : 0.f;
     r.thresh = __fmul_rn(k, __fsqrt_rn(fmaxf(r.var, 1e-8f)));
     return r;
+}
+
+template <int NT>
+__device__ __forceinline__ XStats x_stats(const uint4* xs, int n8, int d_in, float k, float inv_n, float inv_n1,
+                                          float* red) {
+    return x_stats_bar<NT>(xs, n8, d_in, k, inv_n, inv_n1, red, []() { __syncthreads(); });
 }
 
 // Outlier mask with the reference's capacity rule, and the ascending outlier
@@ -246,110 +254,17 @@ __device__ int x_mask_list(const uint4* xs, int d_in, float mean, float thresh, 
 }
 
 // ---------------------------------------------------------------------------
-// The activation plan from registers (batch-1 kernel).
+// The rest of the batch-1 kernel's plan, in a balanced partition.
 //
-// x is read once, straight into registers: each thread holds the 16-byte
-// pieces (8 columns) of its virtual threads v (v = tid, and v = tid + NT when
-// NT < kStatThreads), pieces p = v + kStatThreads r.  The statistics reduce
-// in the fixed order of x_stats (per virtual thread in piece order, xor
-// butterfly per virtual warp, a fixed tree over the 16 virtual warps), so the
-// batch-1 kernel, the detector and the batched plan kernel derive the same
-// statistics; the mask, the masked MMA B fragments, the per-group sums and
-// the outlier list all come from the same registers.
+// x sits in natural order in xb (shared memory; the statistics came from
+// x_stats over it).  Thread tid takes pieces p = tid + NT r (r < R), so every
+// thread holds at most one piece more than any other, and the 16 pieces of a
+// group are the 16 lanes of one half-warp in one round.  From its pieces each
+// thread derives the outlier bits; a ballot prefix within each warp and the
+// warp totals give the list positions.  After one barrier (every piece of x
+// is in registers) xb is overwritten with the MMA B fragments of x', the
+// per-group sums go to xp4 and the list is written.
 // ---------------------------------------------------------------------------
-constexpr int kPlanRounds = (kMaxDIn / 8 + kStatThreads - 1) / kStatThreads;
-
-// R: rounds held, ceil(d_in / (8 kStatThreads)) or more (fewer registers for
-// the kernels of short rows).
-template <int NT, int R = kPlanRounds>
-struct XRegs {
-    static constexpr int VPT = (kStatThreads + NT - 1) / NT;  // virtual threads per thread
-    static constexpr int RND = R;
-    uint4 v[VPT][R];
-};
-
-// Virtual thread q of this thread (kStatThreads or more: none).
-template <int NT>
-__device__ __forceinline__ int plan_vthread(int q) {
-    return static_cast<int>(threadIdx.x) + q * NT;
-}
-
-// Whether this warp has virtual thread q (uniform over the warp).
-template <int NT>
-__device__ __forceinline__ bool plan_warp_has(int q) {
-    return q == 0 || static_cast<int>(threadIdx.x & ~31u) + q * NT < kStatThreads;
-}
-
-template <int NT, int R>
-__device__ __forceinline__ void x_regs_load_global(const uint16_t* __restrict__ x, int n8, XRegs<NT, R>& r) {
-#pragma unroll
-    for (int q = 0; q < XRegs<NT, R>::VPT; ++q)
-#pragma unroll
-        for (int rr = 0; rr < R; ++rr) {
-            const int v = plan_vthread<NT>(q), p = v + kStatThreads * rr;
-            uint4 val = make_uint4(0, 0, 0, 0);
-            if (v < kStatThreads && p < n8) val = ldcg_v4(x + 8 * static_cast<size_t>(p));
-            r.v[q][rr] = val;
-        }
-}
-
-// x_stats over the registers (pieces past d_in hold zeros).  red: 2
-// kStatThreads/32 floats, 16-byte aligned, not in use; two barriers.
-template <int NT, int R>
-__device__ __forceinline__ XStats x_stats_regs(const XRegs<NT, R>& r, int n8, int d_in, float k, float inv_n,
-                                               float inv_n1, float* red) {
-    constexpr int NWV = kStatThreads / 32;
-    const int lane = threadIdx.x & 31;
-#pragma unroll
-    for (int q = 0; q < XRegs<NT, R>::VPT; ++q) {
-        if (!plan_warp_has<NT>(q)) break;
-        const int v = plan_vthread<NT>(q);
-        float s[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int rr = 0; rr < R; ++rr) {
-            if (kStatThreads * rr >= n8) break;  // uniform
-            if (v + kStatThreads * rr < n8) {
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const uint32_t w = word_of(r.v[q][rr], i);
-                    s[i] = add_f16_f32(hi16(w), add_f16_f32(lo16(w), s[i]));
-                }
-            }
-        }
-        const float ws = warp_sum((s[0] + s[1]) + (s[2] + s[3]));
-        if (lane == 0) red[v >> 5] = ws;
-    }
-    __syncthreads();
-    XStats st;
-    st.mean = __fmul_rn(sum16_tree(red), inv_n);
-#pragma unroll
-    for (int q = 0; q < XRegs<NT, R>::VPT; ++q) {
-        if (!plan_warp_has<NT>(q)) break;
-        const int v = plan_vthread<NT>(q);
-        float m[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int rr = 0; rr < R; ++rr) {
-            if (kStatThreads * rr >= n8) break;
-            if (v + kStatThreads * rr < n8) {
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const uint32_t w = word_of(r.v[q][rr], i);
-                    const float d0 = sub_f16_f32(lo16(w), st.mean);
-                    const float d1 = sub_f16_f32(hi16(w), st.mean);
-                    m[i] = __fmaf_rn(d1, d1, __fmaf_rn(d0, d0, m[i]));
-                }
-            }
-        }
-        const float wq = warp_sum((m[0] + m[1]) + (m[2] + m[3]));
-        if (lane == 0) red[NWV + (v >> 5)] = wq;
-    }
-    __syncthreads();
-    const float m2 = sum16_tree(red + NWV);
-    st.m2 = m2;
-    st.var = (d_in > 1) ? __fmul_rn(m2, inv_n1) : 0.f;
-    st.thresh = __fmul_rn(k, __fsqrt_rn(fmaxf(st.var, 1e-8f)));
-    return st;
-}
 
 // Outlier bits of one piece: bit 2i (2i + 1) for the low (high) half of word i.
 __device__ __forceinline__ uint32_t piece_bits(const uint4& v, float mean, float thresh) {
@@ -363,80 +278,13 @@ __device__ __forceinline__ uint32_t piece_bits(const uint4& v, float mean, float
     return b;
 }
 
-// The MMA B fragments of x' (x with the outliers zeroed), the per-group sums
-// and the outlier list, from the registers.
-//   xb   [NC][64] 16-byte pieces in MMA B order [word wi][slice sl][group jj]:
-//        the f16 pairs (x0,x4), (x2,x6), (x1,x5), (x3,x7) of each piece;
-//        pieces past d_in (to the end of the last chunk) are zero
-//   xp4  [NC * 4] per group (1024 sum x' even columns, 1024 sum x' odd
-//        columns, sum x', 0)
-//   list the outliers, column | FP16 bits of x << 16, in (warp, lane,
-//        column) order (a fixed order; any order serves the GEMV)
-// kMask: false for the INT4 path (no mask, no list).  mask32: null to
-// derive the mask from (mean, thresh), else the mask words to apply.  wcnt:
-// NT/32 ints of shared memory not in use, 16-byte aligned.  One barrier;
-// returns the outlier count (every thread); the list is complete after the
-// caller's next barrier.  When the count exceeds cap the list is not written
-// (the caller applies the reference's capacity rule with x_mask_list).
-template <int NT, bool kMask, int R>
-__device__ __forceinline__ int x_frags_regs(const XRegs<NT, R>& r, int n8, int NC, float mean, float thresh,
-                                            const uint32_t* mask32, int cap, uint4* xb, float4* xp4,
-                                            uint32_t* list, int* wcnt) {
+// Exclusive prefix of this thread's cnt over the block in (warp, lane) order
+// and the block total (cnt < 2^8).  wcnt: NT/32 ints, 16-byte aligned, not in
+// use; one barrier.
+template <int NT>
+__device__ __forceinline__ int plan_prefix(int cnt, int* wcnt, int& total) {
     constexpr int NW = NT / 32;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int npc = 64 * NC;  // pieces of all chunks
-    uint32_t bits[XRegs<NT, R>::VPT][R];
-    int cnt = 0;
-#pragma unroll
-    for (int q = 0; q < XRegs<NT, R>::VPT; ++q) {
-#pragma unroll
-        for (int rr = 0; rr < R; ++rr) bits[q][rr] = 0;
-        if (!plan_warp_has<NT>(q)) continue;
-        const int v = plan_vthread<NT>(q);
-#pragma unroll
-        for (int rr = 0; rr < R; ++rr) {
-            if (kStatThreads * rr >= npc) break;  // uniform: no piece of this round in any chunk
-            const int p = v + kStatThreads * rr;
-            uint4 w = r.v[q][rr];
-            if (kMask && p < n8) {
-                const uint32_t b = mask32 ? (lds_u32(smem_u32(mask32 + (p >> 2))) >> (8 * (p & 3))) & 0xFFu
-                                          : piece_bits(w, mean, thresh);
-                bits[q][rr] = b;
-                cnt += __popc(b);
-                if (b) {
-                    uint32_t keep[4];
-#pragma unroll
-                    for (int i = 0; i < 4; ++i)
-                        keep[i] = ((b >> (2 * i)) & 1u ? 0u : 0x0000FFFFu) | ((b >> (2 * i + 1)) & 1u ? 0u : 0xFFFF0000u);
-                    w.x &= keep[0];
-                    w.y &= keep[1];
-                    w.z &= keep[2];
-                    w.w &= keep[3];
-                }
-            }
-            float pe = add_f16_f32(lo16(w.w), add_f16_f32(lo16(w.z), add_f16_f32(lo16(w.y), add_f16_f32(lo16(w.x), 0.f))));
-            float po = add_f16_f32(hi16(w.w), add_f16_f32(hi16(w.z), add_f16_f32(hi16(w.y), add_f16_f32(hi16(w.x), 0.f))));
-            if (p < npc) {
-                const int c = p >> 6, i = p & 63;
-                const int jj = i >> 4, sl = (i >> 2) & 3, wi = i & 3;
-                xb[64 * c + (wi * 4 + sl) * 4 + jj] =
-                    make_uint4((w.x & 0xFFFFu) | (w.z << 16), (w.y & 0xFFFFu) | (w.w << 16),
-                               (w.x >> 16) | (w.z & 0xFFFF0000u), (w.y >> 16) | (w.w & 0xFFFF0000u));
-            }
-            // the 16 pieces of a group are the 16 lanes of one half-warp in one round
-#pragma unroll
-            for (int o = 8; o >= 1; o >>= 1) {
-                pe += __shfl_xor_sync(0xffffffffu, pe, o);
-                po += __shfl_xor_sync(0xffffffffu, po, o);
-            }
-            if ((p & 15) == 0 && p < npc) xp4[p >> 4] = make_float4(1024.f * pe, 1024.f * po, pe + po, 0.f);
-        }
-    }
-    if (!kMask) {
-        __syncthreads();
-        return 0;
-    }
-    // list positions: per-warp prefix of the counts (< 2^8) from their bits' ballots
     const unsigned lt = (1u << lane) - 1u;
     int before = 0, wtot = 0;
 #pragma unroll
@@ -447,7 +295,8 @@ __device__ __forceinline__ int x_frags_regs(const XRegs<NT, R>& r, int n8, int N
     }
     if (lane == 0) wcnt[warp] = wtot;
     __syncthreads();
-    int base = 0, total = 0;
+    int base = 0;
+    total = 0;
     const uint32_t wa = smem_u32(wcnt);
 #pragma unroll
     for (int w4 = 0; w4 < NW / 4; ++w4) {
@@ -459,23 +308,104 @@ __device__ __forceinline__ int x_frags_regs(const XRegs<NT, R>& r, int n8, int N
             total += c[i];
         }
     }
-    if (total > cap) return total;
-    int pos = base + before;
+    return base + before;
+}
+
+// The plan after the statistics (kMask) or the fragments of x alone (INT4
+// GEMV).  R: rounds, at least ceil(64 NC / NT).
+//   xb   in: x in natural order (n8 pieces); out: [NC][64] 16-byte pieces in
+//        MMA B order [word wi][slice sl][group jj], the f16 pairs (x0,x4),
+//        (x2,x6), (x1,x5), (x3,x7) of each piece of x'; pieces past d_in (to
+//        the end of the last chunk) are zero
+//   xp4  [4 NC] per group (1024 sum x' even columns, 1024 sum x' odd columns,
+//        sum x', 0); groups past d_in are zero
+//   list the outliers (column | FP16 bits of x << 16): in (warp, lane, round)
+//        order, or ascending when the reference's capacity rule applies
+//        (more than d_in/16 outliers: x_mask_list, mask32 its mask)
+// red: kB1RedBytes of shared memory not in use.  Returns the outlier count
+// (every thread); everything is complete on return (ends with a barrier).
+template <int NT, int R, bool kMask>
+__device__ __forceinline__ int plan_balanced(uint4* xb, int n8, int NC, int d_in, float mean, float thresh,
+                                             float4* xp4, uint32_t* list, uint32_t* mask32, int* red) {
+    static_assert(NT % 32 == 0 && NT <= 512, "plan threads");
+    const int tid = threadIdx.x;
+    const int npc = 64 * NC;
+    uint4 v[R];
+    uint32_t bits[R];
+    int cnt = 0;
 #pragma unroll
-    for (int q = 0; q < XRegs<NT, R>::VPT; ++q) {
-        const int v = plan_vthread<NT>(q);
+    for (int rr = 0; rr < R; ++rr) {
+        const int p = tid + NT * rr;
+        v[rr] = p < n8 ? xb[p] : make_uint4(0, 0, 0, 0);
+        bits[rr] = (kMask && p < n8) ? piece_bits(v[rr], mean, thresh) : 0u;
+        cnt += __popc(bits[rr]);
+    }
+    int total = 0, pos = 0;
+    bool capacity = false;
+    if (kMask) {
+        pos = plan_prefix<NT>(cnt, red, total);
+        if (total > d_in / 16) {
+            // No stripe class can exceed its capacity ((d_in/4)/4) below this
+            // total; above it the reference's rule may drop outliers.
+            capacity = true;
+            total = x_mask_list<NT>(xb, d_in, mean, thresh, mask32, list, red + 16);
+            __syncthreads();
+#pragma unroll
+            for (int rr = 0; rr < R; ++rr) {
+                const int p = tid + NT * rr;
+                if (p < n8) bits[rr] = (mask32[p >> 2] >> (8 * (p & 3))) & 0xFFu;
+            }
+        }
+    }
+    __syncthreads();  // every piece of x is in registers: xb may be overwritten
+#pragma unroll
+    for (int rr = 0; rr < R; ++rr) {
+        if (NT * rr >= npc) break;  // uniform
+        const int p = tid + NT * rr;
+        uint4 w = v[rr];
+        const uint32_t b = bits[rr];
+        if (b) {
+            uint32_t keep[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                keep[i] = ((b >> (2 * i)) & 1u ? 0u : 0x0000FFFFu) | ((b >> (2 * i + 1)) & 1u ? 0u : 0xFFFF0000u);
+            w.x &= keep[0];
+            w.y &= keep[1];
+            w.z &= keep[2];
+            w.w &= keep[3];
+        }
+        float pe = add_f16_f32(lo16(w.w), add_f16_f32(lo16(w.z), add_f16_f32(lo16(w.y), add_f16_f32(lo16(w.x), 0.f))));
+        float po = add_f16_f32(hi16(w.w), add_f16_f32(hi16(w.z), add_f16_f32(hi16(w.y), add_f16_f32(hi16(w.x), 0.f))));
+        if (p < npc) {
+            const int c = p >> 6, i = p & 63;
+            const int jj = i >> 4, sl = (i >> 2) & 3, wi = i & 3;
+            xb[64 * c + (wi * 4 + sl) * 4 + jj] =
+                make_uint4((w.x & 0xFFFFu) | (w.z << 16), (w.y & 0xFFFFu) | (w.w << 16),
+                           (w.x >> 16) | (w.z & 0xFFFF0000u), (w.y >> 16) | (w.w & 0xFFFF0000u));
+        }
+        // the 16 pieces of a group are the 16 lanes of one half-warp
+#pragma unroll
+        for (int o = 8; o >= 1; o >>= 1) {
+            pe += __shfl_xor_sync(0xffffffffu, pe, o);
+            po += __shfl_xor_sync(0xffffffffu, po, o);
+        }
+        if ((p & 15) == 0 && p < npc) xp4[p >> 4] = make_float4(1024.f * pe, 1024.f * po, pe + po, 0.f);
+    }
+    if (kMask && !capacity) {
 #pragma unroll
         for (int rr = 0; rr < R; ++rr) {
-            uint32_t b = bits[q][rr];
+            uint32_t b = bits[rr];
+            const int p = tid + NT * rr;
             while (b) {
                 const int e = __ffs(b) - 1;
-                const uint32_t word = word_of(r.v[q][rr], e >> 1);
+                const uint32_t word = word_of(v[rr], e >> 1);
                 const uint32_t h = (e & 1) ? (word >> 16) : (word & 0xFFFFu);
-                list[pos++] = static_cast<uint32_t>(8 * (v + kStatThreads * rr) + e) | (h << 16);
+                list[pos++] = static_cast<uint32_t>(8 * p + e) | (h << 16);
                 b &= b - 1u;
             }
         }
     }
+    __syncthreads();
     return total;
 }
 

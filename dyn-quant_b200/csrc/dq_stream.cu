@@ -43,6 +43,7 @@
 
 #include "dq_common.cuh"
 #include "dq_gplan.cuh"
+#include "dq_plan.cuh"
 #include "dq_internal.h"
 
 namespace dq {
@@ -331,7 +332,21 @@ __global__ void __launch_bounds__(kST, 1) stream_kernel(const SArgs a) {
         gp_load<kPPT>(a.x, a.G, tid, xr);
         int n_out = 0;
         if (kSplit) {
-            const GpStats st = gp_stats<kPPT>(xr, a.d_in, a.k, a.inv_n, a.inv_n1, red, bar);
+            // The statistics in the partition of dq_plan.cuh (that of the block
+            // kernel, the detector and the batched plan: the same bits), from
+            // x in natural order in xb (overwritten by the fragments below).
+            {
+                const int TPG = 16 / kPPT;
+                if (tid < a.G * TPG) {
+                    const int j = tid / TPG, h = tid % TPG;
+#pragma unroll
+                    for (int i = 0; i < kPPT; ++i) xb[16 * j + kPPT * h + i] = xr.v[i];
+                }
+            }
+            bar();
+            const XStats st = x_stats_bar<kSCons * 32>(xb, a.d_in / 8, a.d_in, a.k, a.inv_n, a.inv_n1, red, bar);
+            bar();  // every thread is done with xb
+            zero_pad(tid, kSCons * 32);
             const int cap = a.d_in / 16;  // no stripe class can exceed its capacity below this total
             n_out = gp_frags<kPPT, kSCons, true>(xr, a.G, st.mean, st.thresh, nullptr, cap, xb, xp4, list, scratch, bar);
             if (n_out > cap) {

@@ -8,10 +8,12 @@ rank from the same x, with a reduction order that does not depend on the
 slice, so every rank applies the same mask.  The exchange is either
 
   "nccl": one NCCL all-gather over NVLink after the GEMV, or
-  "peer": fused into the GEMV kernel (dq_split_gemv_gather): every CTA
-          publishes its rows in its rank's gather region, raises a flag in
-          the other ranks' regions and copies their rows over NVLink once
-          their flags are up (bounded waits), so a call is one kernel.
+  "peer": fused into the GEMV kernel (dq_split_gemv_gather): every output
+          row also goes straight into every other rank's gather region
+          (peer stores over NVLink); the last CTA of the call adds an
+          arrival to every other rank's region, waits (bounded) for the
+          other ranks' arrivals in its own and copies their rows into y,
+          so a call is one kernel and no rank reads another's memory.
 
 One process per GPU (torch.distributed for the plumbing).  The partition and
 the NCCL gather are plain functions so that their logic can be exercised on
