@@ -313,6 +313,11 @@ def run_reference(args, rank: int, world: int) -> None:
     if rank != 0:
         return
     import oracle as O
+    if args.sweep:
+        if world > 1:
+            raise SystemExit("--sweep runs on one GPU")
+        run_sweep(args, dev)
+        return
     wl = WL.from_args(args)
     if wl.name in MOE_WORKLOADS:
         return run_moe_reference(args, rank, world)
@@ -983,6 +988,102 @@ def run_moe_reference(args, rank: int, world: int) -> None:
 
 
 # ---------------------------------------------------------------------------
+SWEEP_M = (1, 4, 8, 16)
+SWEEP_FRAC = (0.0, 0.01, 0.05, 0.10)
+SWEEP_DIST = ("normal", "t3")
+SWEEP_K = (2.0, 3.0, 4.0, 6.0)
+
+
+def run_sweep(args, dev) -> None:
+    """The outlier / batch sweep on one 8192 x 8192 GEMV: every point of
+    M x outlier fraction x distribution x k, timed as a graph of back-to-back
+    split GEMV calls over rotating weight copies (the batch-1 kernel at M = 1,
+    the batched kernels above).  One JSON line per point; with --sweep-md the
+    table is also written as markdown."""
+    import torch
+
+    import dyn_quant
+    from dyn_quant import _lib
+
+    L = _lib.lib()
+    d_out = d_in = 8192
+    n_sets = max(2, math.ceil(3 * L2_BYTES / gemv_bytes(d_out, d_in, 0, 1)))
+    w0 = torch.from_numpy(weights_np(d_out, d_in, 0)).to(dev)
+    mods = []
+    for s in range(n_sets):
+        lin = dyn_quant.DynQuantLinear(d_in, d_out, 3.0)
+        lin.load_weight(w0 if s == 0 else torch.roll(w0, shifts=s * 97, dims=0).contiguous())
+        mods.append(lin)
+    w32 = mods[0].fp16_w.float()
+    structs = [_lib.weights(m.packed.data_ptr(), m.scales.data_ptr(), m.zeros.data_ptr(), None, m.fp16_w.data_ptr(),
+                            d_out, d_in, m._native.data_ptr()) for m in mods]
+    ws_bytes = max(L.dq_workspace_bytes(d_out, d_in), L.dq_workspace_bytes_batched(d_out, d_in, max(SWEEP_M)))
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
+    y = torch.empty(max(SWEEP_M) * d_out, dtype=torch.float16, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    peak, peak_note = measured_peak_gbs()
+    n_launch = 20
+    rows = []
+    for dist_ in SWEEP_DIST:
+        for frac in SWEEP_FRAC:
+            for M in SWEEP_M:
+                S = synth()
+                xh = S.activation(d_in, frac, seed=1, dist=dist_) if M == 1 else \
+                    S.activations(M, d_in, frac, seed=1, dist=dist_)
+                x = torch.from_numpy(np.ascontiguousarray(xh)).to(dev)
+                for k in SWEEP_K:
+                    def launch(i, st):
+                        w = structs[i % n_sets]
+                        if M == 1:
+                            r = L.dq_split_gemv(C.byref(w), C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr()), k,
+                                                C.c_void_p(ws.data_ptr()), ws_bytes, C.c_void_p(st.cuda_stream))
+                        else:
+                            r = L.dq_split_gemv_batched(C.byref(w), C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr()),
+                                                        M, k, C.c_void_p(ws.data_ptr()), ws_bytes,
+                                                        C.c_void_p(st.cuda_stream))
+                        if r != 0:
+                            raise RuntimeError(f"sweep GEMV: {_lib.status_string(r)}")
+                    with torch.cuda.stream(stream):
+                        launch(0, stream)
+                    stream.synchronize()
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g, stream=stream):
+                        cur = torch.cuda.current_stream()
+                        for i in range(n_launch):
+                            launch(i, cur)
+                    us = statistics.median(graph_time_us(stream, g, n_launch) for _ in range(3))
+                    del g
+                    xr = x.reshape(M, d_in)
+                    masks = [dyn_quant.detect_outliers(r, k)[0] for r in xr]
+                    n_union = int(torch.stack(masks).any(0).sum().item())
+                    n_mean = float(torch.stack(masks).sum(1).float().mean().item())
+                    yk = mods[0](xr.squeeze(0) if M == 1 else xr).float().reshape(M, d_out)
+                    y32 = xr.float() @ w32.t()
+                    rl2 = float((torch.linalg.vector_norm(yk - y32) / torch.linalg.vector_norm(y32)).item())
+                    b = gemv_bytes(d_out, d_in, n_union, M)
+                    row = {"M": M, "frac": frac, "dist": dist_, "k": k, "outliers_per_vector": round(n_mean, 1),
+                           "outliers_union": n_union, "us": round(us, 2), "gb_s": round(b / (us * 1e-6) / 1e9, 1),
+                           "frac_of_peak": round(b / (us * 1e-6) / 1e9 / peak, 3), "rel_l2_vs_fp32": float(f"{rl2:.3e}")}
+                    rows.append(row)
+                    print(json.dumps(row), flush=True)
+    if args.sweep_md:
+        with open(args.sweep_md, "w") as f:
+            f.write("# Outlier / batch sweep: one 8192 x 8192 split GEMV on one B200\n\n")
+            f.write("Command: `python bench.py --sweep --sweep-md " + args.sweep_md + "`\n\n")
+            f.write(f"Weights synth.weights(8192, 8192, seed=100) and {n_sets - 1} row rotations (every call reads "
+                    "its weights from HBM); activations synth.activation(s) seed 1 (vector t: seed 1 + t); "
+                    f"graph of {n_launch} back-to-back calls, median of 3 replays. Batch 1: the batch-1 kernel; "
+                    "M > 1: the batched kernels (plan, INT4 part, FP16 part). Bytes: INT4 codes + FP16 scale/zero + "
+                    "the FP16 columns of the union of the vectors' outliers + x + y. Peak: "
+                    f"{peak:.1f} GB/s ({peak_note}). rel-L2 against an FP32 dense GEMV on the original FP16 weights.\n\n")
+            f.write("| dist | frac | M | k | outliers / vector | union | µs | GB/s | of peak | rel-L2 vs FP32 |\n")
+            f.write("|---|---|---|---|---|---|---|---|---|---|\n")
+            for r in rows:
+                f.write(f"| {r['dist']} | {r['frac']:.2f} | {r['M']} | {r['k']:g} | {r['outliers_per_vector']} | "
+                        f"{r['outliers_union']} | {r['us']} | {r['gb_s']} | {r['frac_of_peak']} | "
+                        f"{r['rel_l2_vs_fp32']:.3e} |\n")
+
+
 def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     import torch
     import torch.distributed as dist
@@ -1053,6 +1154,9 @@ def main(argv=None) -> None:
     ap.add_argument("--shard", choices=["auto", "rows", "replicas"], default="auto",
                     help="N > 1: row sharding with a gather, or independent replicas; auto follows the "
                          "deployment of each shape: rows for the 70B workloads, replicas for the 7B and sweep ones")
+    ap.add_argument("--sweep", action="store_true",
+                    help="the outlier / batch sweep of one 8192x8192 GEMV (M x frac x dist x k), one JSON line per point")
+    ap.add_argument("--sweep-md", default=None, help="with --sweep: also write the table as markdown to this path")
     ap.add_argument("--max-sets", type=int, default=0,
                     help="cap on rotating weight copies (profiling runs only; the default rotates through >= 3x L2)")
     args = ap.parse_args(argv)

@@ -129,11 +129,13 @@ DQ_API dq_status_t dq_build_native(const uint8_t* packed, const uint16_t* scales
 
 /*
  * Workspace of the batch-1 GEMVs: device memory of at least
- * dq_workspace_bytes(d_out, d_in) bytes (a fixed 256 + 128 KiB, whatever the
- * shape), 256-byte aligned, ZERO-FILLED before its first use.  It holds a call
- * counter, an arrival counter and, per CTA, the partial row sums of the
- * 16-row block that CTA shares with the one before it, each tagged with the
- * call's number so that a sum left by an earlier call is never taken.  Every
+ * dq_workspace_bytes(d_out, d_in) bytes, 256-byte aligned, ZERO-FILLED before
+ * its first use.  Its first 256 + 128 KiB hold a call counter, an arrival
+ * counter and, per CTA, the partial row sums of the 16-row block that CTA
+ * shares with the one before it, each tagged with the call's number so that a
+ * sum left by an earlier call is never taken (the block kernel needs no
+ * more); the rest, which grows with the shape, serves the streaming kernel
+ * (task queue and per-row-block partial sums, DQ_STREAM=1).  Every
  * call leaves it ready for the next one, so one zero-filled workspace serves
  * any number of stream-ordered calls of any shape; after a call that reported
  * a device error (dq_read_device_error), reset it with dq_reset_workspace.
@@ -290,14 +292,19 @@ DQ_API size_t dq_gather_region_bytes(int32_t rows_per);
  * Row-sharded split GEMV with the all-gather fused into the kernel: this
  * rank's rows of y = the split GEMV of x (w->d_out == g->rows_per, native
  * layout and column-major mirror required), then the full y[d_total] on every
- * rank.  Each CTA publishes its rows in this rank's region, raises its flag
- * in every other rank's region (system-scope release), waits for the same
- * CTA of every other rank (bounded, about a second: on timeout bit 4 of the
- * device error word is set and that rank's rows are left unwritten) and
- * copies their rows from the peers' regions over NVLink.  All ranks call it
- * with the same shapes; y is this process's own buffer.  Replaces
- * launch_split_gemv (src/split_gemv.cu:160-198) on a slice of the rows plus
- * the collective that would follow it.
+ * rank.  Every output row is stored in y and, over NVLink, in every other
+ * rank's region (the copy of the call's parity: two copies of the full
+ * output follow a 256-byte header of u32 [calls completed, arrivals for
+ * calls of parity 0, of parity 1]).  The last CTA of the call adds one
+ * arrival (system-scope release) to every other rank's header, waits until
+ * every other rank's arrival is in this rank's header (bounded, about a
+ * second: on timeout bit 4 of the device error word is set and those ranks'
+ * rows are left unwritten), copies their rows from this rank's own region
+ * into y and counts the call completed.  No rank reads another's memory.
+ * All ranks call it with the same shapes, in the same order; y is this
+ * process's own buffer.  Replaces launch_split_gemv
+ * (src/split_gemv.cu:160-198) on a slice of the rows plus the collective
+ * that would follow it.
  */
 DQ_API dq_status_t dq_split_gemv_gather(const dq_weights_t* w, const uint16_t* x, uint16_t* y, float outlier_k,
                                         void* workspace, size_t workspace_bytes, const dq_gather_t* g,

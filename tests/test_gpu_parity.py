@@ -160,6 +160,37 @@ def test_capacity_rule_many_outliers():
     check_y(y, y16m, y32m, what="split(capacity)")
 
 
+def _concentrated(d_in, first, n, mag, seed):
+    """x ~ N(0, 1) with n channels of magnitude mag (random signs) among the
+    first `first` columns: the outliers pile up in one or a few 512-column
+    chunks (more than the outlier segments a weight stage carries)."""
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal(d_in).astype(np.float32)
+    idx = rng.choice(first, n, replace=False)
+    x[idx] = mag * np.sign(rng.standard_normal(n))
+    return x.astype(np.float16)
+
+
+@pytest.mark.parametrize("d_out,d_in,first,n", [
+    (4096, 4096, 512, 20),     # one chunk, two 16-column batches
+    (4096, 4096, 512, 40),     # one chunk, past the staged segments
+    (4096, 4096, 204, 150),    # the reference test's layout: the first channels
+    (2048, 28672, 512, 24),    # longest rows (fewer staged segments per stage)
+    (1000, 8192, 1024, 70),    # ragged last row block, two chunks
+])
+def test_split_gemv_concentrated_outliers(d_out, d_in, first, n):
+    w = synth.weights(d_out, d_in, seed=5)
+    x = _concentrated(d_in, first, n, 50.0, seed=6)
+    packed, scales, zeros = O.quantize(w)
+    p_t, s_t, z_t = dev(packed), dev(scales), dev(zeros)
+    for native in (True, False):
+        wts = abi_weights(p_t, s_t, z_t, w_cm=abi_colmajor(dev(w)),
+                          native=abi_build_native(p_t, s_t, z_t) if native else None)
+        y = host(abi_split_gemv(wts, dev(x), 3.0))
+        y16, y32, _ = O.split_gemv(packed, scales, zeros, w, x, 3.0)
+        check_y(y, y16, y32, what=f"split {d_out}x{d_in} {n} outliers in the first {first} (native={native})")
+
+
 def test_constant_activation_has_no_outliers():
     x = np.full(1024, 0.75, np.float16)
     mask, idx, stats = abi_detect(dev(x), 3.0)
