@@ -313,11 +313,6 @@ def run_reference(args, rank: int, world: int) -> None:
     if rank != 0:
         return
     import oracle as O
-    if args.sweep:
-        if world > 1:
-            raise SystemExit("--sweep runs on one GPU")
-        run_sweep(args, dev)
-        return
     wl = WL.from_args(args)
     if wl.name in MOE_WORKLOADS:
         return run_moe_reference(args, rank, world)
@@ -1092,6 +1087,11 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     dev = torch.device("cuda", local_rank)
     if world > 1:
         init_nccl(dev)
+    if args.sweep:
+        if world > 1:
+            raise SystemExit("--sweep runs on one GPU")
+        run_sweep(args, dev)
+        return
     wl = WL.from_args(args)
     if wl.name in MOE_WORKLOADS:
         main = moe_block(args, wl, rank, world, dev, True)

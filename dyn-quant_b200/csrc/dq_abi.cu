@@ -394,6 +394,16 @@ dq_status_t static_scratch(void** out, cudaStream_t stream) {
 
 }  // namespace
 
+extern "C" dq_status_t dq_reset_noalloc_workspace(void* stream) {
+    void* ws = nullptr;
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    dq_status_t st = static_scratch(&ws, s);  // (a first call clears the whole array already)
+    if (st != DQ_OK) return st;
+    const cudaError_t e = cudaMemsetAsync(ws, 0, kStaticScratchBytes, s);
+    if (e != cudaSuccess) { set_cuda_error(e); return DQ_ERR_CUDA; }
+    return DQ_OK;
+}
+
 extern "C" dq_status_t dq_split_gemv_noalloc(const dq_weights_t* w, const uint16_t* x, uint16_t* y,
                                              float outlier_k, void* stream) {
     if (w && w->d_out == 0 && check_dims(w->d_out, w->d_in) == DQ_OK) return DQ_OK;

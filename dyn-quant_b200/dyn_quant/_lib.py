@@ -31,6 +31,7 @@ EXPORTED_SYMBOLS = (
     "dq_build_colmajor",
     "dq_split_gemv",
     "dq_split_gemv_noalloc",
+    "dq_reset_noalloc_workspace",
     "dq_split_gemv_batched",
     "dq_workspace_bytes_batched",
     "dq_silu_mul",
@@ -119,6 +120,8 @@ def lib() -> C.CDLL:
         L.dq_split_gemv.argtypes = [C.POINTER(DqWeights), P, P, f32, P, C.c_size_t, P]
         L.dq_split_gemv_noalloc.restype = st
         L.dq_split_gemv_noalloc.argtypes = [C.POINTER(DqWeights), P, P, f32, P]
+        L.dq_reset_noalloc_workspace.restype = st
+        L.dq_reset_noalloc_workspace.argtypes = [P]
         L.dq_split_gemv_batched.restype = st
         L.dq_split_gemv_batched.argtypes = [C.POINTER(DqWeights), P, P, i32, f32, P, C.c_size_t, P]
         L.dq_workspace_bytes_batched.restype = C.c_size_t

@@ -48,15 +48,18 @@ def shard_rows(d_out: int, world: int, rank: int) -> Tuple[int, int, int]:
 
 
 def gather_rows(y_local: torch.Tensor, d_out: int, rows_per: int, group=None,
-                out: torch.Tensor | None = None) -> torch.Tensor:
+                out: torch.Tensor | None = None, pad: torch.Tensor | None = None) -> torch.Tensor:
     """All-gather the ranks' output slices into y [d_out] (y_local: this rank's
-    rows, at most rows_per of them)."""
+    rows, at most rows_per of them).  out ([world * rows_per]) and pad
+    ([rows_per], for a slice shorter than rows_per; its tail must be zero)
+    are preallocated buffers; without them the call allocates its own."""
     world = dist.get_world_size(group)
     if y_local.numel() > rows_per:
         raise ValueError("local slice taller than the padded slice")
     if y_local.numel() < rows_per:
-        pad = torch.zeros(rows_per, dtype=y_local.dtype, device=y_local.device)
-        pad[: y_local.numel()] = y_local
+        if pad is None or pad.numel() != rows_per:
+            pad = torch.zeros(rows_per, dtype=y_local.dtype, device=y_local.device)
+        pad[: y_local.numel()].copy_(y_local.reshape(-1))
         y_local = pad
     full = out if out is not None and out.numel() == world * rows_per else torch.empty(
         world * rows_per, dtype=y_local.dtype, device=y_local.device)
@@ -157,6 +160,7 @@ class ShardedDynQuantLinear(torch.nn.Module):
             self.local = DynQuantLinear(d_in, max(self.r1 - self.r0, 0), outlier_k) if self.r1 > self.r0 else None
         self._local_gemv = local_gemv  # test hook: a local GEMV other than the kernel
         self._gather_buf = None
+        self._pad_buf = None
         self._peer: PeerGather | None = None
         self._ws = None
 
@@ -205,4 +209,6 @@ class ShardedDynQuantLinear(torch.nn.Module):
             y_local = torch.empty(0, dtype=torch.float16, device=x.device)
         if self._gather_buf is None or self._gather_buf.device != x.device:
             self._gather_buf = torch.empty(self.world * self.rows_per, dtype=torch.float16, device=x.device)
-        return gather_rows(y_local.to(torch.float16), self.d_out, self.rows_per, self.group, self._gather_buf)
+            self._pad_buf = torch.zeros(self.rows_per, dtype=torch.float16, device=x.device)
+        return gather_rows(y_local.to(torch.float16), self.d_out, self.rows_per, self.group, self._gather_buf,
+                           self._pad_buf)

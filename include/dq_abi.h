@@ -193,6 +193,18 @@ DQ_API dq_status_t dq_split_gemv_noalloc(const dq_weights_t* w, const uint16_t* 
                                          float outlier_k, void* stream);
 
 /*
+ * Zero-fill dq_split_gemv_noalloc's static array on the current device, on
+ * `stream` (an asynchronous memset, no allocation).  After a call that
+ * reported a device error (dq_read_device_error: a bounded wait gave up) the
+ * array holds that call's tagged partial sums and a completed-call count that
+ * later calls still use correctly, so nothing needs resetting; a caller that
+ * wants the array back in its first-call state (after a CUDA error it has
+ * recovered from, say) calls this, ordered before the next no-alloc call.  No
+ * counterpart in the reference.
+ */
+DQ_API dq_status_t dq_reset_noalloc_workspace(void* stream);
+
+/*
  * Workspace of dq_split_gemv_batched for m vectors: at least
  * dq_workspace_bytes_batched(d_out, d_in, m) bytes, 256-byte aligned and
  * ZERO-FILLED before its first use.  It begins with the batch-1 region (so one

@@ -84,6 +84,21 @@ def test_noalloc_allocates_no_device_memory():
     assert np.array_equal(host(y).view(np.uint16), first.view(np.uint16))  # bit-reproducible
 
 
+def test_noalloc_reset_keeps_results():
+    """dq_reset_noalloc_workspace zeroes the static array on a stream; calls
+    before and after it give the same bits."""
+    torch.cuda.set_device(0)
+    d_out, d_in = 1024, 8192
+    w = synth.weights(d_out, d_in, seed=7)
+    wts, _, _, _ = _weights(w, "colmajor+native")
+    x_t = dev(synth.activation(d_in, 0.03, seed=8))
+    y0 = host(noalloc_split_gemv(wts, x_t, 3.0)).copy()
+    _lib = abi()
+    _lib.check(_lib.lib().dq_reset_noalloc_workspace(stream_ptr()), "dq_reset_noalloc_workspace")
+    y1 = host(noalloc_split_gemv(wts, x_t, 3.0))
+    assert np.array_equal(y0.view(np.uint16), y1.view(np.uint16))
+
+
 def test_noalloc_rejects_bad_arguments():
     _lib = abi()
     L = _lib.lib()
