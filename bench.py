@@ -26,8 +26,9 @@ both arms; the GPU arm's extra rotating copies are row rotations of it.
 One process per GPU.  Under torchrun (N > 1) the 70B workloads are
 row-sharded, as a 70B model is deployed: each rank holds whole 16-row blocks
 of the weights, runs the split GEMV on its slice with the same x, and the
-output slices are gathered after every GEMV ("scaling": "strong": the total
-work is the workload's, whatever N).  The 7B and sweep workloads fit one GPU
+output slices are gathered inside every GEMV kernel over NVLink peer memory
+(--gather nccl: an NCCL all-gather after every GEMV instead) ("scaling":
+"strong": the total work is the workload's, whatever N).  The 7B and sweep workloads fit one GPU
 and run as N independent replicas ("scaling": "weak"); --shard overrides
 either choice.  The time is the max over ranks.  At N = 1 the line also
 carries extra blocks (7B MLP, 7B q_proj, the Mixtral MoE step and one point
@@ -1148,9 +1149,9 @@ def main(argv=None) -> None:
     ap.add_argument("--frac", type=float, default=None, help="injected outlier fraction (default: the workload's)")
     ap.add_argument("--k", type=float, default=K_OUTLIER, help="outlier threshold in standard deviations")
     ap.add_argument("--dist", choices=["normal", "t3"], default="normal", help="activation distribution")
-    ap.add_argument("--gather", choices=["peer", "nccl"], default="nccl",
-                    help="row-sharded runs: the output slices gathered by an NCCL all-gather after each GEMV, "
-                         "or inside the GEMV kernel over NVLink peer memory")
+    ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
+                    help="row-sharded runs: the output slices gathered inside the GEMV kernel over NVLink peer "
+                         "memory (the default), or by an NCCL all-gather after each GEMV")
     ap.add_argument("--shard", choices=["auto", "rows", "replicas"], default="auto",
                     help="N > 1: row sharding with a gather, or independent replicas; auto follows the "
                          "deployment of each shape: rows for the 70B workloads, replicas for the 7B and sweep ones")

@@ -147,8 +147,8 @@ dq_status_t dq_read_device_error(uint32_t* word, int clear) {
     if (st != DQ_OK) return st;
     st = read_stream_error(&bs, clear != 0);
     if (st != DQ_OK) return st;
-    // streaming kernel: bit 0 of its word (own copies) -> bit 5, bit 1 (another rank's rows) -> bit 4
-    *word = b1 | (bg << 8) | ((bs & 1u) ? (1u << 5) : 0u) | ((bs & 2u) ? (1u << 4) : 0u);
+    // streaming kernel: bit 0 of its word (its own copies) -> bit 5
+    *word = b1 | (bg << 8) | ((bs & 1u) ? (1u << 5) : 0u);
     return DQ_OK;
 }
 
@@ -209,10 +209,10 @@ dq_status_t dq_reset_workspace(void* workspace, size_t workspace_bytes, void* st
     return DQ_OK;
 }
 
-// The split / INT4 GEMV (plain or with the fused gather) runs the batch-1
-// kernel of dq_gemv.cu, which is the faster of the two on B200 at every
-// Llama-2 shape measured.  With DQ_STREAM=1 in the environment (read once)
-// the streaming kernel (dq_stream.cu) serves the calls it supports instead
+// The split / INT4 GEMV runs the batch-1 kernel of dq_gemv.cu, which is the
+// faster of the two on B200 at every Llama-2 shape measured (the fused
+// gather always does).  With DQ_STREAM=1 in the environment (read once) the
+// streaming kernel (dq_stream.cu) serves the plain calls it supports instead
 // (native layout, column-major mirror for the split GEMV), for timing the
 // two against each other.
 static bool stream_requested() {
@@ -234,7 +234,7 @@ dq_status_t dq_split_gemv(const dq_weights_t* w, const uint16_t* x, uint16_t* y,
     dq_status_t st = check_weights(w, x, y, true, workspace, workspace_bytes);
     if (st != DQ_OK) return st;
     if (use_stream(*w, true, workspace_bytes))
-        return launch_gemv_stream(*w, x, y, outlier_k, true, workspace, nullptr, static_cast<cudaStream_t>(stream));
+        return launch_gemv_stream(*w, x, y, outlier_k, true, workspace, static_cast<cudaStream_t>(stream));
     return launch_gemv_b1(*w, x, y, outlier_k, true, workspace, static_cast<cudaStream_t>(stream));
 }
 
@@ -260,8 +260,6 @@ dq_status_t dq_split_gemv_gather(const dq_weights_t* w, const uint16_t* x, uint1
     if (!w->native || !w->fp16_cm || !stream_supported(*w, true)) return DQ_ERR_INVALID_ARGUMENT;
     if (stream_geom(w->d_out, w->d_in).n_rb > kStreamMaxRb) return DQ_ERR_UNSUPPORTED;
     if (workspace_bytes < stream_ws(w->d_out, w->d_in).total) return DQ_ERR_WORKSPACE;
-    if (stream_requested())
-        return launch_gemv_stream(*w, x, y, outlier_k, true, workspace, g, static_cast<cudaStream_t>(stream));
     return launch_gemv_b1_gather(*w, x, y, outlier_k, workspace, *g, static_cast<cudaStream_t>(stream));
 }
 
@@ -311,7 +309,7 @@ dq_status_t dq_int4_gemv(const dq_weights_t* w, const uint16_t* x, uint16_t* y, 
     dq_status_t st = check_weights(w, x, y, false, workspace, workspace_bytes);
     if (st != DQ_OK) return st;
     if (use_stream(*w, false, workspace_bytes))
-        return launch_gemv_stream(*w, x, y, 0.f, false, workspace, nullptr, static_cast<cudaStream_t>(stream));
+        return launch_gemv_stream(*w, x, y, 0.f, false, workspace, static_cast<cudaStream_t>(stream));
     return launch_gemv_b1(*w, x, y, 0.f, false, workspace, static_cast<cudaStream_t>(stream));
 }
 

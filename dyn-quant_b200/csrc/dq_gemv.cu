@@ -101,49 +101,40 @@ __host__ __device__ inline int unit_owner(long long u, int P, long long U) {
     return static_cast<int>((u * P + P - 1) / U);
 }
 
-// The fused gather's last step, by the last CTA of this rank's call (every
-// CTA's rows are in the other ranks' regions: each fenced before it counted
-// itself done).  Tell every other rank that this rank's rows of the call are
-// in its region, wait (bounded, about a second: on timeout bit 4 of the error
-// word, the other ranks' rows left unwritten) until every other rank's rows
-// are in this one, copy them into y, and count the call completed.
+// The fused gather, after this CTA stored its rows (in y and, as tagged
+// words, in every other rank's region): the same rows of every other rank's
+// slice (rows [r0, r1) of the slice, which that rank's CTA of the same index
+// stores, the partition being the same on every rank) are read from this
+// rank's own region once their words carry this call's tag, and written
+// into y.  Each word is waited for (bounded, about a second in all: on
+// timeout bit 4 of the error word is set and the row is left unwritten).
 template <int kT>
-__device__ void gather_finish(const B1Args& a, uint32_t* gmisc) {
-    const int tid = threadIdx.x;
-    const uint32_t call = gmisc[1], par = call & 1u;
-    uint8_t* own = a.g_region[a.g_rank];
-    unsigned int* arrived = reinterpret_cast<unsigned int*>(own + a.g_lay.hdr) + 1 + par;
-    if (tid == 0) {
-        __threadfence_system();
-        for (int q = 0; q < a.g_world; ++q)
-            if (q != a.g_rank)
-                red_release_sys_add_u32(reinterpret_cast<unsigned int*>(a.g_region[q] + a.g_lay.hdr) + 1 + par, 1u);
-        const unsigned int want = static_cast<unsigned int>(a.g_world - 1);
-        uint32_t v = ld_acquire_sys_u32(arrived);
-        const long long t0 = clock64();
-        while (v < want && clock64() - t0 < (1ll << 31)) v = ld_acquire_sys_u32(arrived);
-        gmisc[3] = v >= want;
-        if (v < want) atomicOr(&g_error_word, 16u);
-    }
-    __syncthreads();
-    if (gmisc[3]) {
-        // The rows came over NVLink into this GPU's memory: read them at L2.
-        const uint16_t* src = reinterpret_cast<const uint16_t*>(own + a.g_lay.yfull + par * a.g_lay.ybytes);
-        const bool vec = (reinterpret_cast<uintptr_t>(a.y) & 15u) == 0;
-        for (int q = 0; q < a.g_world; ++q) {
-            if (q == a.g_rank) continue;
-            const int r0 = q * a.g_rows_per, r1 = min(r0 + a.g_rows_per, a.g_total);
-            const int nv = vec ? (r1 - r0) / 8 : 0;  // r0 is a multiple of 16 rows: 32-byte aligned
-            for (int i = tid; i < nv; i += kT)
-                reinterpret_cast<uint4*>(a.y + r0)[i] = ldcg_v4(reinterpret_cast<const uint4*>(src + r0) + i);
-            for (int r = r0 + 8 * nv + tid; r < r1; r += kT) a.y[r] = ldcg_u16(src + r);
+__device__ void gather_rows(const B1Args& a, uint32_t call, int r0, int r1) {
+    const uint32_t tag = call & 0xFFFFu, par = call & 1u;
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(a.g_region[a.g_rank] + a.g_lay.yfull + par * a.g_lay.ybytes);
+    const int n = r1 - r0;
+    const long long t_end = clock64() + (1ll << 31);
+    bool ok = true;
+    for (int q = 0; q < a.g_world; ++q) {
+        if (q == a.g_rank) continue;
+        const int base = q * a.g_rows_per + r0;
+        for (int i = threadIdx.x; i < n; i += kT) {
+            const int grow = base + i;
+            if (grow >= a.g_total) break;
+            uint32_t w = ld_relaxed_sys_u32(src + grow);
+            while ((w >> 16) != tag && ok) {
+                if (clock64() > t_end) {
+                    ok = false;
+                    break;
+                }
+                __nanosleep(64);
+                w = ld_relaxed_sys_u32(src + grow);
+            }
+            if (!ok) break;
+            a.y[grow] = static_cast<uint16_t>(w & 0xFFFFu);
         }
     }
-    __syncthreads();
-    if (tid == 0) {
-        *arrived = 0u;  // every other rank's arrival for this call is in
-        reinterpret_cast<unsigned int*>(own + a.g_lay.hdr)[0] = call;
-    }
+    if (!ok) atomicOr(&g_error_word, 16u);
 }
 
 // Rounds of the balanced plan partition (pieces of x per thread) for the
@@ -268,8 +259,8 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
     // advances it, so all CTAs of a call see the same tag.
     uint32_t& s_tag = *reinterpret_cast<uint32_t*>(smem + a.S.misc);
     // Gather: misc[1] this call's number (calls this rank completed + 1; its
-    // parity picks the copy written in the ranks' regions), misc[2] last CTA,
-    // misc[3] the other ranks' rows are in.
+    // parity picks the copy written in the ranks' regions, its low 16 bits
+    // tag the words), misc[2] last CTA.
     uint32_t* gmisc = reinterpret_cast<uint32_t*>(smem + a.S.misc);
     if (tid == 0) {
         const uint32_t e = ldcg_u32(a.hdr) + 1u;
@@ -287,9 +278,11 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
         const int grow = a.g_rank * a.g_rows_per + row;
         if (grow >= a.g_total) return;
         a.y[grow] = h;
-        const size_t off = a.g_lay.yfull + static_cast<size_t>(gmisc[1] & 1u) * a.g_lay.ybytes + 2 * static_cast<size_t>(grow);
+        const uint32_t call = gmisc[1];
+        const size_t off = a.g_lay.yfull + static_cast<size_t>(call & 1u) * a.g_lay.ybytes + 4 * static_cast<size_t>(grow);
+        const uint32_t word = static_cast<uint32_t>(h) | ((call & 0xFFFFu) << 16);
         for (int q = 0; q < a.g_world; ++q)
-            if (q != a.g_rank) *reinterpret_cast<uint16_t*>(a.g_region[q] + off) = h;
+            if (q != a.g_rank) st_relaxed_sys_u32(reinterpret_cast<uint32_t*>(a.g_region[q] + off), word);
     };
     // x into xb in natural order (requested before the weight copies, so that
     // it does not queue behind them on the SM's return path).
@@ -592,19 +585,23 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
 
     // This CTA is done with the workspace (its tag read, its words published,
     // its finaliser wait over): the last CTA of the call advances the tag.
+    if constexpr (kGather) {
+        // The rows this CTA stores: its row blocks from rbf (rbf + 1 when a
+        // contributor) to rbz, below d_out.
+        const int rs = (contrib ? rbf + 1 : rbf) * kRowBlock;
+        const int re = min((rbz + 1) * kRowBlock, a.d_out);
+        __syncthreads();  // (every thread has the call number)
+        if (re > rs) gather_rows<kT>(a, gmisc[1], rs, re);
+    }
     __syncthreads();
     if (tid == 0) {
-        if (kGather) __threadfence_system();  // this CTA's rows are in the other ranks' regions
         const bool last = atomicAdd(a.hdr + 1, 1u) == gridDim.x - 1u;
         if (last) {
             a.hdr[1] = 0u;
             a.hdr[0] = s_tag;
+            // every CTA has read this call's number: count the call completed
+            if (kGather) reinterpret_cast<unsigned int*>(a.g_region[a.g_rank] + a.g_lay.hdr)[0] = gmisc[1];
         }
-        gmisc[2] = last;
-    }
-    if constexpr (kGather) {
-        __syncthreads();
-        if (gmisc[2]) gather_finish<kT>(a, gmisc);
     }
 }
 

@@ -87,12 +87,15 @@ struct WsLayout {
 inline size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
 // Gather region of one rank (row-sharded split GEMV with the gather fused):
-//   hdr    u32 [0] calls this rank has completed, [1] / [2] the other ranks'
-//          arrivals for the running call of parity 0 / 1 (every other rank
-//          adds 1 once its rows are in this region)
-//   yfull  two FP16 copies of the full output (kMaxGatherRanks x rows_per
-//          rows), for calls of parity 0 and 1: rank q stores its rows of a
-//          call straight into every other rank's copy of that parity
+//   hdr    u32 [0] calls this rank has completed (the running call's number
+//          is that + 1)
+//   yfull  two copies of the full output (kMaxGatherRanks x rows_per rows),
+//          for calls of parity 0 and 1, one 32-bit word per row: the FP16
+//          value in the low half, the low 16 bits of the call's number in
+//          the high half.  Rank q stores its rows of a call straight into
+//          every other rank's copy of that parity; a word is this call's
+//          once it carries this call's tag (one 32-bit store: value and tag
+//          arrive together), so no fence or flag is needed.
 // Zero-filled once; every rank makes the same calls in the same order.  A
 // rank is at most one call ahead of another (it waits for every other
 // rank's rows of each call), so the copy it writes is never the one read.
@@ -104,7 +107,7 @@ inline GatherLayout gather_layout(int rows_per) {
     GatherLayout L;
     L.hdr = 0;
     L.yfull = 256;
-    L.ybytes = align256(static_cast<size_t>(kMaxGatherRanks) * rows_per * 2);
+    L.ybytes = align256(static_cast<size_t>(kMaxGatherRanks) * rows_per * 4);
     L.total = L.yfull + 2 * L.ybytes;
     return L;
 }
@@ -340,9 +343,8 @@ inline BgWs bg_ws(const BgGeom& g, int d_out, int d_in) {
 }
 
 bool stream_supported(const dq_weights_t& w, bool split);
-// g: the row-sharded gather (null: none; y then holds d_out rows, else g->d_total).
 dq_status_t launch_gemv_stream(const dq_weights_t& w, const uint16_t* x, uint16_t* y, float k, bool split,
-                               void* workspace, const dq_gather_t* g, cudaStream_t stream);
+                               void* workspace, cudaStream_t stream);
 dq_status_t read_stream_error(uint32_t* word, bool clear);
 
 dq_status_t launch_gemv_batched(const dq_weights_t& w, const uint16_t* x, uint16_t* y, int M, float k,

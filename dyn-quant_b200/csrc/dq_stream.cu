@@ -82,11 +82,6 @@ struct SArgs {
     float k, inv_n, inv_n1;
     int d_out, d_in, G, NC, n_rb, tpr, m, n_tasks, n_static, R;
     SSmem S;
-    // fused gather (kGather): this rank, the ranks, slice height, output rows,
-    // every rank's gather region as mapped here
-    int g_rank, g_world, g_rows_per, g_total;
-    uint8_t* g_region[kMaxGatherRanks];
-    GatherLayout g_lay;
 };
 
 __device__ __forceinline__ void task_range(const SArgs& a, int t, int& ub, int& ue) {
@@ -113,7 +108,7 @@ __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, bool
     return true;
 }
 
-template <bool kSplit, int kPPT, bool kGather>
+template <bool kSplit, int kPPT>
 __global__ void __launch_bounds__(kST, 1) stream_kernel(const SArgs a) {
     extern __shared__ __align__(128) char smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -184,10 +179,6 @@ __global__ void __launch_bounds__(kST, 1) stream_kernel(const SArgs a) {
     pdl_launch_dependents();
     pdl_wait();  // x, y and the workspace may belong to the preceding kernel until here
 
-    // Gather: this call's number (calls this rank completed + 1) picks the
-    // parity of the copies written in the ranks' regions.
-    int* g_call_s = tgen + kTS + 1;
-    if (kGather && tid == 0) *g_call_s = static_cast<int>(ldcg_u32(a.g_region[a.g_rank] + a.g_lay.hdr) + 1u);
     bool ok = true;
     if (warp == kSCons) {
         // ------------------------------------------------------------ producer
@@ -510,21 +501,7 @@ __global__ void __launch_bounds__(kST, 1) stream_kernel(const SArgs a) {
                     v += (lane & 8) ? o2 : o0;
                 }
                 const int row = rb * kRowBlock + lane;
-                // Row `row` of this call's output: y, and with the gather also the
-                // other ranks' copies (peer stores over NVLink).
-                auto store_row = [&](float value) {
-                    const uint16_t h = __half_as_ushort(__float2half_rn(value));
-                    if (!kGather) {
-                        a.y[row] = h;
-                        return;
-                    }
-                    const int grow = a.g_rank * a.g_rows_per + row;
-                    if (grow >= a.g_total) return;
-                    a.y[grow] = h;
-                    const size_t off = a.g_lay.yfull + static_cast<size_t>(*g_call_s & 1) * a.g_lay.ybytes + 2 * grow;
-                    for (int q = 0; q < a.g_world; ++q)
-                        if (q != a.g_rank) *reinterpret_cast<uint16_t*>(a.g_region[q] + off) = h;
-                };
+                auto store_row = [&](float value) { a.y[row] = __half_as_ushort(__float2half_rn(value)); };
                 if (a.tpr == 1) {
                     if (lane < 16 && row < a.d_out) store_row(v);
                 } else {
@@ -563,53 +540,15 @@ __global__ void __launch_bounds__(kST, 1) stream_kernel(const SArgs a) {
 
     // Every CTA done: the last one resets the queue for the next call.
     __syncthreads();
-    int* last_s = g_call_s + 1;
-    if (tid == 0) {
-        if (kGather) __threadfence_system();  // this CTA's rows are in the other ranks' regions
-        const bool last = atomicAdd(a.ctr + 1, 1u) == gridDim.x - 1u;
-        if (last) {
-            a.ctr[0] = 0u;
-            a.ctr[1] = 0u;
-        }
-        *last_s = last;
-    }
-    if (!kGather) return;
-    __syncthreads();
-    if (!*last_s) return;
-    // The gather, by the last CTA of this rank: tell every other rank that this
-    // rank's rows of the call are in its region, wait (bounded) until every
-    // other rank's rows are in this one, then copy them into y.
-    const int call = *g_call_s, par = call & 1;
-    uint8_t* own = a.g_region[a.g_rank];
-    unsigned int* arrived = reinterpret_cast<unsigned int*>(own + a.g_lay.hdr) + 1 + par;
-    int& s_gok = last_s[1];
-    if (tid == 0) {
-        for (int q = 0; q < a.g_world; ++q)
-            if (q != a.g_rank) red_release_sys_add_u32(reinterpret_cast<unsigned int*>(a.g_region[q] + a.g_lay.hdr) + 1 + par, 1u);
-        const unsigned int want = static_cast<unsigned int>(a.g_world - 1);
-        uint32_t v = ld_acquire_sys_u32(arrived);
-        const long long t0 = clock64();
-        while (v < want && clock64() - t0 < kWaitCycles) v = ld_acquire_sys_u32(arrived);
-        s_gok = v >= want;
-        if (!s_gok) atomicOr(&g_stream_error, 2u);
-    }
-    __syncthreads();
-    if (s_gok) {
-        const uint16_t* src = reinterpret_cast<const uint16_t*>(own + a.g_lay.yfull + static_cast<size_t>(par) * a.g_lay.ybytes);
-        const int mine0 = a.g_rank * a.g_rows_per, mine1 = mine0 + a.g_rows_per;
-        for (int r = tid; r < a.g_total; r += kST)
-            if (r < mine0 || r >= mine1) a.y[r] = ld_relaxed_sys_u16(src + r);
-    }
-    __syncthreads();
-    if (tid == 0) {
-        *arrived = 0u;  // every other rank's arrival for this call is in
-        reinterpret_cast<unsigned int*>(own + a.g_lay.hdr)[0] = static_cast<unsigned int>(call);
+    if (tid == 0 && atomicAdd(a.ctr + 1, 1u) == gridDim.x - 1u) {
+        a.ctr[0] = 0u;
+        a.ctr[1] = 0u;
     }
 }
 
 // Per-device, per-kernel "max dynamic shared memory" opt-in, done once.
 constexpr int kMaxDevices = 64;
-constexpr int kNumKernels = 16;  // (gather, split, plan pieces per thread)
+constexpr int kNumKernels = 8;  // (split, plan pieces per thread)
 int g_smem_set[kMaxDevices][kNumKernels];
 
 template <class K>
@@ -633,10 +572,10 @@ dq_status_t ensure_smem_s(K kernel, int id, int bytes) {
     return DQ_OK;
 }
 
-template <bool kSplit, int kPPT, bool kGather>
+template <bool kSplit, int kPPT>
 dq_status_t launch_stream_t(const SArgs& a, int grid, cudaStream_t stream) {
-    constexpr int id = (kGather ? 8 : 0) + (kSplit ? 4 : 0) + (kPPT == 1 ? 0 : kPPT == 2 ? 1 : kPPT == 4 ? 2 : 3);
-    const dq_status_t st = ensure_smem_s(stream_kernel<kSplit, kPPT, kGather>, id, a.S.total);
+    constexpr int id = (kSplit ? 4 : 0) + (kPPT == 1 ? 0 : kPPT == 2 ? 1 : kPPT == 4 ? 2 : 3);
+    const dq_status_t st = ensure_smem_s(stream_kernel<kSplit, kPPT>, id, a.S.total);
     if (st != DQ_OK) return st;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -648,20 +587,20 @@ dq_status_t launch_stream_t(const SArgs& a, int grid, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, stream_kernel<kSplit, kPPT, kGather>, a);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, stream_kernel<kSplit, kPPT>, a);
     if (e != cudaSuccess) { set_cuda_error(e); return DQ_ERR_CUDA; }
     e = cudaGetLastError();
     if (e != cudaSuccess) { set_cuda_error(e); return DQ_ERR_CUDA; }
     return DQ_OK;
 }
 
-template <bool kSplit, bool kGather>
+template <bool kSplit>
 dq_status_t launch_stream_p(const SArgs& a, int ppt, int grid, cudaStream_t stream) {
     switch (ppt) {
-        case 1: return launch_stream_t<kSplit, 1, kGather>(a, grid, stream);
-        case 2: return launch_stream_t<kSplit, 2, kGather>(a, grid, stream);
-        case 4: return launch_stream_t<kSplit, 4, kGather>(a, grid, stream);
-        default: return launch_stream_t<kSplit, 8, kGather>(a, grid, stream);
+        case 1: return launch_stream_t<kSplit, 1>(a, grid, stream);
+        case 2: return launch_stream_t<kSplit, 2>(a, grid, stream);
+        case 4: return launch_stream_t<kSplit, 4>(a, grid, stream);
+        default: return launch_stream_t<kSplit, 8>(a, grid, stream);
     }
 }
 
@@ -683,7 +622,7 @@ bool stream_supported(const dq_weights_t& w, bool split) {
 }
 
 dq_status_t launch_gemv_stream(const dq_weights_t& w, const uint16_t* x, uint16_t* y, float k, bool split,
-                               void* workspace, const dq_gather_t* g, cudaStream_t stream) {
+                               void* workspace, cudaStream_t stream) {
     DeviceInfo di;
     const dq_status_t st = device_info(&di);
     if (st != DQ_OK) return st;
@@ -729,17 +668,7 @@ dq_status_t launch_gemv_stream(const dq_weights_t& w, const uint16_t* x, uint16_
     if (R < kSCons) return DQ_ERR_UNSUPPORTED;
     a.R = R;
     const int ppt = 16 / gp_tpg(a.G);
-    if (g) {
-        a.g_rank = g->rank;
-        a.g_world = g->world;
-        a.g_rows_per = g->rows_per;
-        a.g_total = g->d_total;
-        for (int q = 0; q < kMaxGatherRanks; ++q)
-            a.g_region[q] = static_cast<uint8_t*>(q < g->world ? g->region[q] : nullptr);
-        a.g_lay = gather_layout(g->rows_per);
-        return launch_stream_p<true, true>(a, ppt, grid, stream);
-    }
-    return split ? launch_stream_p<true, false>(a, ppt, grid, stream) : launch_stream_p<false, false>(a, ppt, grid, stream);
+    return split ? launch_stream_p<true>(a, ppt, grid, stream) : launch_stream_p<false>(a, ppt, grid, stream);
 }
 
 dq_status_t read_stream_error(uint32_t* word, bool clear) {

@@ -9,11 +9,12 @@ slice, so every rank applies the same mask.  The exchange is either
 
   "nccl": one NCCL all-gather over NVLink after the GEMV, or
   "peer": fused into the GEMV kernel (dq_split_gemv_gather): every output
-          row also goes straight into every other rank's gather region
-          (peer stores over NVLink); the last CTA of the call adds an
-          arrival to every other rank's region, waits (bounded) for the
-          other ranks' arrivals in its own and copies their rows into y,
-          so a call is one kernel and no rank reads another's memory.
+          row also goes straight into every other rank's gather region as
+          one 32-bit word (the FP16 value and the call's 16-bit tag), and
+          each CTA copies the same rows of the other ranks' slices from its
+          own region into y once their words carry the call's tag (bounded
+          waits): one kernel per call, no fences, and no rank reads another's
+          memory.
 
 One process per GPU (torch.distributed for the plumbing).  The partition and
 the NCCL gather are plain functions so that their logic can be exercised on

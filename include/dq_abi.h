@@ -305,16 +305,16 @@ DQ_API size_t dq_gather_region_bytes(int32_t rows_per);
  * rank's rows of y = the split GEMV of x (w->d_out == g->rows_per, native
  * layout and column-major mirror required), then the full y[d_total] on every
  * rank.  Every output row is stored in y and, over NVLink, in every other
- * rank's region (the copy of the call's parity: two copies of the full
- * output follow a 256-byte header of u32 [calls completed, arrivals for
- * calls of parity 0, of parity 1]).  The last CTA of the call adds one
- * arrival (system-scope release) to every other rank's header, waits until
- * every other rank's arrival is in this rank's header (bounded, about a
- * second: on timeout bit 4 of the device error word is set and those ranks'
- * rows are left unwritten), copies their rows from this rank's own region
- * into y and counts the call completed.  No rank reads another's memory.
- * All ranks call it with the same shapes, in the same order; y is this
- * process's own buffer.  Replaces launch_split_gemv
+ * rank's region, as one 32-bit word: the FP16 value in the low half and the
+ * low 16 bits of the call's number in the high half (the region: a 256-byte
+ * header holding u32 [calls completed], then two copies of the full output,
+ * 8 x rows_per words each, for calls of parity 0 and 1).  Each CTA then reads
+ * the same rows of every other rank's slice from this rank's own region as
+ * soon as their words carry this call's tag (bounded wait, about a second:
+ * on timeout bit 4 of the device error word is set and those rows are left
+ * unwritten) and writes them into y.  No fences, flags or reads of another
+ * rank's memory.  All ranks call it with the same shapes, in the same order;
+ * y is this process's own buffer.  Replaces launch_split_gemv
  * (src/split_gemv.cu:160-198) on a slice of the rows plus the collective
  * that would follow it.
  */
@@ -342,8 +342,8 @@ DQ_API dq_status_t dq_ipc_close(void* ptr);
  * output is not valid), bit 1 by a batch-1 kernel whose bounded wait for a
  * neighbouring CTA's partial sums gave up, bit 4 by a gathering kernel whose
  * bounded wait for another rank's rows gave up, bit 5 by the streaming kernel
- * (the gathering kernel, or DQ_STREAM=1) whose bounded wait for its own bulk
- * copies gave up (it carries on; its output is not valid), bit 8 by a batched kernel
+ * (DQ_STREAM=1) whose bounded wait for its own bulk copies gave up (it
+ * carries on; its output is not valid), bit 8 by a batched kernel
  * whose bounded wait for its own bulk copies gave up.  Synchronous; clear != 0
  * resets the word.  No reference counterpart.
  */

@@ -2,22 +2,21 @@
 one GPU.
 
 * world 1: the gathered call agrees with the plain split GEMV and the
-  oracle (the parity tolerance; the two kernels sum in different orders),
-  and repeats itself bit for bit.
+  oracle, and repeats itself bit for bit.
 * rank 0 of 2: the other rank is emulated from the host, which plants that
-  rank's rows in rank 0's region (the copy of the call's parity) and its
-  arrival in rank 0's header before each call.  Rank 0's kernel must return
-  its own rows and the planted rows in the other rank's place, store its own
-  rows in the other region's copy and add its arrival there.  No second
-  kernel runs: nothing on this GPU waits for another kernel.
-* the bounded wait running out: no arrival planted, so the wait gives up
+  rank's rows in rank 0's region (the copy of the call's parity) as tagged
+  words before each call.  Rank 0's kernel must return its own rows and the
+  planted rows in the other rank's place, and store its own rows, tagged,
+  in the other region's copy.  No second kernel runs: nothing on this GPU
+  waits for another kernel.
+* the bounded wait running out: nothing planted, so the waits give up
   after about a second; the kernel reports bit 4 of the device error word,
   writes its own rows and leaves the other rank's rows untouched.
 
-Region layout (include/dq_abi.h, dq_gather_t): a 256-byte header (u32 calls
-completed, arrivals for calls of parity 0 and 1), then two copies of the
-full output (8 x rows_per FP16 rows, padded to 256 bytes) for calls of parity
-0 and 1.
+Region layout (include/dq_abi.h, dq_split_gemv_gather): a 256-byte header
+(u32 calls completed), then two copies of the full output (8 x rows_per
+32-bit words, padded to 256 bytes) for calls of parity 0 and 1; a word is
+the FP16 value | the low 16 bits of the call's number << 16.
 """
 import ctypes as C
 
@@ -34,7 +33,7 @@ MAX_RANKS = 8
 
 
 def _layout(rows_per):
-    ybytes = (MAX_RANKS * rows_per * 2 + 255) // 256 * 256
+    ybytes = (MAX_RANKS * rows_per * 4 + 255) // 256 * 256
     return 256, ybytes, 256 + 2 * ybytes  # copies start, bytes per copy, total
 
 
@@ -59,12 +58,17 @@ def _desc(rank, world, rows_per, d_total, regions):
 
 
 def _hdr(region):
-    return host(region[:12].view(torch.int32))
+    return host(region[:4].view(torch.int32))
 
 
-def _copy(region, rows_per, par, n):
+def _words(region, rows_per, par, n):
+    """The first n words of the region's copy of parity par (int32 view)."""
     start, ybytes, _ = _layout(rows_per)
-    return region[start + par * ybytes:start + par * ybytes + 2 * n].view(torch.float16)
+    return region[start + par * ybytes:start + par * ybytes + 4 * n].view(torch.int32)
+
+
+def _tagged(vals_f16: np.ndarray, call: int) -> np.ndarray:
+    return (vals_f16.view(np.uint16).astype(np.uint32) | np.uint32((call & 0xFFFF) << 16)).view(np.int32)
 
 
 def test_region_bytes():
@@ -99,7 +103,7 @@ def test_world_one_is_the_split_gemv():
         assert _gather(wts, x, y, g) == 0
         torch.cuda.synchronize()
         first = host(y).copy()
-        assert list(_hdr(region)) == [2 * call - 1, 0, 0]
+        assert list(_hdr(region)) == [2 * call - 1]
         assert _gather(wts, x, y, g) == 0
         ref = abi_split_gemv(wts, x, 3.0)
         torch.cuda.synchronize()
@@ -107,7 +111,7 @@ def test_world_one_is_the_split_gemv():
         check_y(first, host(ref), what=f"call {call} vs dq_split_gemv")
         y16, _, _ = O.split_gemv(packed, scales, zeros, w, xh, 3.0)
         check_y(first, y16, what=f"call {call} vs the oracle")
-        assert list(_hdr(region)) == [2 * call, 0, 0]
+        assert list(_hdr(region)) == [2 * call]
 
 
 @pytest.mark.parametrize("rows_per,d_in,tail", [(1024, 4096, 5), (3584, 8192, 0), (512, 11008, 16)])
@@ -120,34 +124,29 @@ def test_rank0_of_two_with_planted_peer(rows_per, d_in, tail):
     r1 = torch.zeros(total, dtype=torch.uint8, device="cuda")
     g = _desc(0, 2, rows_per, d_total, [r0, r1])
     rng = np.random.default_rng(5)
-    sent = [0, 0]  # arrivals rank 0 has added to rank 1's header, per parity
     for call in range(1, 4):
         par = call & 1
         x = dev(synth.activation(d_in, 0.02, seed=40 + call))
-        # rank 1 has stored its rows of this call in rank 0's copy and arrived
+        # rank 1 has stored its rows of this call in rank 0's copy, tagged
         peer_rows = rng.standard_normal(d_total - rows_per).astype(np.float16)
-        _copy(r0, rows_per, par, d_total)[rows_per:].copy_(dev(peer_rows))
-        r0[4 + 4 * par:8 + 4 * par].view(torch.int32).fill_(1)
+        _words(r0, rows_per, par, d_total)[rows_per:].copy_(dev(_tagged(peer_rows, call)))
         y = torch.full((d_total,), float("nan"), dtype=torch.float16, device="cuda")
         assert _gather(wts, x, y, g) == 0
         own = _own_rows(wts, x)
         torch.cuda.synchronize()
-        sent[par] += 1
         yh = host(y)
         assert np.array_equal(yh[:rows_per].view(np.int16), host(own).view(np.int16)), f"call {call}: own rows"
         assert np.array_equal(yh[rows_per:].view(np.int16), peer_rows.view(np.int16)), f"call {call}: peer rows"
-        # rank 0 stored its rows in rank 1's copy of this parity and arrived there
-        theirs = host(_copy(r1, rows_per, par, rows_per))
-        assert np.array_equal(theirs.view(np.int16), host(own).view(np.int16)), f"call {call}: rows sent"
-        h0, h1 = _hdr(r0), _hdr(r1)
-        assert h0[0] == call and h0[1 + par] == 0, f"call {call}: own header {h0}"
-        assert h1[1 + par] == sent[par], f"call {call}: arrivals sent {h1}"
+        # rank 0 stored its rows, tagged with this call, in rank 1's copy of this parity
+        theirs = host(_words(r1, rows_per, par, rows_per))
+        assert np.array_equal(theirs, _tagged(host(own), call)), f"call {call}: rows sent"
+        assert list(_hdr(r0)) == [call], f"call {call}: calls completed"
     err = C.c_uint32(0)
     assert abi().lib().dq_read_device_error(C.byref(err), 0) == 0 and err.value & 16 == 0
 
 
 def test_wait_runs_out():
-    """No arrival from the other rank: the bounded wait gives up (about a second)."""
+    """Nothing from the other rank: the bounded waits give up (about a second)."""
     from dyn_quant import synth
     _lib = abi()
     rows_per, d_in = 256, 4096
