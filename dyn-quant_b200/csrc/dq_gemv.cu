@@ -112,27 +112,25 @@ template <int kT>
 __device__ void gather_rows(const B1Args& a, uint32_t call, int r0, int r1) {
     const uint32_t tag = call & 0xFFFFu, par = call & 1u;
     const uint32_t* src = reinterpret_cast<const uint32_t*>(a.g_region[a.g_rank] + a.g_lay.yfull + par * a.g_lay.ybytes);
-    const int n = r1 - r0;
+    const int n = r1 - r0, total = (a.g_world - 1) * n;
     const long long t_end = clock64() + (1ll << 31);
     bool ok = true;
-    for (int q = 0; q < a.g_world; ++q) {
-        if (q == a.g_rank) continue;
-        const int base = q * a.g_rows_per + r0;
-        for (int i = threadIdx.x; i < n; i += kT) {
-            const int grow = base + i;
-            if (grow >= a.g_total) break;
-            uint32_t w = ld_relaxed_sys_u32(src + grow);
-            while ((w >> 16) != tag && ok) {
-                if (clock64() > t_end) {
-                    ok = false;
-                    break;
-                }
-                __nanosleep(64);
-                w = ld_relaxed_sys_u32(src + grow);
+    // (other rank, row) pairs spread over all threads, so that every word is
+    // waited for at the same time
+    for (int i = threadIdx.x; i < total && ok; i += kT) {
+        const int qi = i / n, q = qi + (qi >= a.g_rank ? 1 : 0);
+        const int grow = q * a.g_rows_per + r0 + (i - qi * n);
+        if (grow >= a.g_total) continue;
+        uint32_t w = ld_relaxed_sys_u32(src + grow);
+        while ((w >> 16) != tag) {
+            if (clock64() > t_end) {
+                ok = false;
+                break;
             }
-            if (!ok) break;
-            a.y[grow] = static_cast<uint16_t>(w & 0xFFFFu);
+            __nanosleep(64);
+            w = ld_relaxed_sys_u32(src + grow);
         }
+        if (ok) a.y[grow] = static_cast<uint16_t>(w & 0xFFFFu);
     }
     if (!ok) atomicOr(&g_error_word, 16u);
 }
