@@ -197,14 +197,15 @@ dq_status_t dq_split_gemv_batched(const dq_weights_t* w, const uint16_t* x, uint
 
 size_t dq_workspace_bytes(int32_t d_out, int32_t d_in) {
     if (check_dims(d_out, d_in) != DQ_OK) return 0;
-    return stream_ws(d_out, d_in).total;
+    const size_t a = stream_ws(d_out, d_in).total, b = b1_workspace_bytes(d_out, d_in);
+    return a > b ? a : b;
 }
 
 dq_status_t dq_reset_workspace(void* workspace, size_t workspace_bytes, void* stream) {
     if (!workspace) return DQ_ERR_INVALID_ARGUMENT;
-    const size_t head = ws_header().total;
-    const cudaError_t e = cudaMemsetAsync(workspace, 0, workspace_bytes < head ? workspace_bytes : head,
-                                          static_cast<cudaStream_t>(stream));
+    // All of it: the counters at the head and the tagged words behind them
+    // (a reset restarts the call tags, so no word of an earlier call may stay).
+    const cudaError_t e = cudaMemsetAsync(workspace, 0, workspace_bytes, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) { set_cuda_error(e); return DQ_ERR_CUDA; }
     return DQ_OK;
 }
@@ -235,7 +236,7 @@ dq_status_t dq_split_gemv(const dq_weights_t* w, const uint16_t* x, uint16_t* y,
     if (st != DQ_OK) return st;
     if (use_stream(*w, true, workspace_bytes))
         return launch_gemv_stream(*w, x, y, outlier_k, true, workspace, static_cast<cudaStream_t>(stream));
-    return launch_gemv_b1(*w, x, y, outlier_k, true, workspace, static_cast<cudaStream_t>(stream));
+    return launch_gemv_b1(*w, x, y, outlier_k, true, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 size_t dq_gather_region_bytes(int32_t rows_per) {
@@ -260,7 +261,7 @@ dq_status_t dq_split_gemv_gather(const dq_weights_t* w, const uint16_t* x, uint1
     if (!w->native || !w->fp16_cm || !stream_supported(*w, true)) return DQ_ERR_INVALID_ARGUMENT;
     if (stream_geom(w->d_out, w->d_in).n_rb > kStreamMaxRb) return DQ_ERR_UNSUPPORTED;
     if (workspace_bytes < stream_ws(w->d_out, w->d_in).total) return DQ_ERR_WORKSPACE;
-    return launch_gemv_b1_gather(*w, x, y, outlier_k, workspace, *g, static_cast<cudaStream_t>(stream));
+    return launch_gemv_b1_gather(*w, x, y, outlier_k, workspace, workspace_bytes, *g, static_cast<cudaStream_t>(stream));
 }
 
 dq_status_t dq_device_alloc(size_t bytes, void** ptr) {
@@ -310,7 +311,7 @@ dq_status_t dq_int4_gemv(const dq_weights_t* w, const uint16_t* x, uint16_t* y, 
     if (st != DQ_OK) return st;
     if (use_stream(*w, false, workspace_bytes))
         return launch_gemv_stream(*w, x, y, 0.f, false, workspace, static_cast<cudaStream_t>(stream));
-    return launch_gemv_b1(*w, x, y, 0.f, false, workspace, static_cast<cudaStream_t>(stream));
+    return launch_gemv_b1(*w, x, y, 0.f, false, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 dq_status_t dq_reference_gemv(const uint16_t* w16, const uint16_t* x, uint16_t* y, int32_t d_out,
@@ -417,5 +418,5 @@ extern "C" dq_status_t dq_split_gemv_noalloc(const dq_weights_t* w, const uint16
     void* ws = nullptr;
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     if ((st = static_scratch(&ws, s)) != DQ_OK) return st;
-    return launch_gemv_b1(*w, x, y, outlier_k, true, ws, s);
+    return launch_gemv_b1(*w, x, y, outlier_k, true, ws, kStaticScratchBytes, s);
 }

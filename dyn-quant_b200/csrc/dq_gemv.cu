@@ -74,9 +74,11 @@ struct B1Args {
     uint16_t* y;
     unsigned int* hdr;        // workspace: [0] tag of the last completed call, [1] CTAs done in this call
     unsigned long long* fix;  // workspace: per CTA, the published partial sums of its first row block
+    unsigned long long* xsl;  // workspace: per row block and slab 1 .. nslab-1, its partial sums
     float k;
     float inv_n, inv_n1;      // 1/d_in, 1/(d_in - 1) for the statistics of x
     int d_out, d_in, NC, U, nrb_max;
+    int nslab, NCs;           // column slabs (1: none) and chunks per slab; U = row blocks x NCs
     int depth;                // ring stages per warp (reference layout: kB1Stages)
     B1Smem S;
     // fused gather (kGather): this rank, the ranks, slice height, output rows,
@@ -146,22 +148,38 @@ constexpr int plan_rounds_max() { return (kMaxDIn / 8 + 32 * kW - 1) / (32 * kW)
 // partition (at least ceil(64 NC / threads)).  kGather: the row-sharded gather is fused
 // (each output row also goes to every other rank's gather region; the last
 // CTA exchanges the arrivals and copies the other ranks' rows into y).
-template <bool kSplit, bool kNative, int kOut, int kW, int kR, bool kGather>
+template <bool kSplit, bool kNative, int kOut, int kW, int kR, bool kGather, bool kSlab>
 __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
     constexpr int kT = kW * 32;
     extern __shared__ __align__(128) char smem[];
     const int G = a.d_in / kGroup;
-    const int NC = a.NC;
     const int n8 = a.d_in >> 3;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t = lane & 3;
-    const int P = gridDim.x, c = blockIdx.x;
-    const long long U = a.U;
+    const int c = blockIdx.x;
+    // Column slabs (kSlab, long rows): CTAs [cs0, cs0 + P) work on slab sl,
+    // the NCs chunks sl NCs .. (sl + 1) NCs - 1 of every row block.  The unit
+    // indices below are the slab's, (row block, chunk of the slab), and a
+    // row's slab sums meet in the CTA of slab 0 that stores it.
+    const int nslab = kSlab ? a.nslab : 1;
+    const int grid = static_cast<int>(gridDim.x);
+    const int sl = nslab > 1 ? ((c + 1) * nslab - 1) / grid : 0;
+    const int cs0 = sl * grid / nslab;
+    const int P = (sl + 1) * grid / nslab - cs0;
+    const int cl = c - cs0;         // this CTA's index within its slab
+    const int NC = a.NCs;           // chunks per row block in this CTA's unit sequence
+    const int chunk0 = sl * a.NCs;  // first chunk of the slab
+    const long long U = a.U;        // units of the slab: row blocks x NC
+    auto gunit = [&](int u) -> long long {  // a unit of the slab as a unit of the weights
+        if (nslab == 1) return u;
+        const int rb = u / NC;
+        return static_cast<long long>(rb) * a.NC + chunk0 + (u - rb * NC);
+    };
 
     // This CTA's units [cu0, cu1) in (row block, chunk) order.  Warp w takes
     // cu0 + w, cu0 + w + kW, ..., so all warps work through the first row block
     // together at the start and through the last one at the end.
-    const int cu0 = unit_start(U, c, P), cu1 = unit_start(U, c + 1, P);
+    const int cu0 = unit_start(U, cl, P), cu1 = unit_start(U, cl + 1, P);
     const int rbf = cu0 / NC;                 // first row block touched by this CTA
     const int rbz = (cu1 - 1) / NC;           // last
     const int nrb = rbz - rbf + 1;
@@ -212,7 +230,7 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
         if (kNative) {
             if (lane == 0) {
                 mbar_arrive_expect_tx(bar, kB1UnitBytes);
-                bulk_g2s(dst, a.native + static_cast<size_t>(u) * kB1UnitBytes, kB1UnitBytes, bar);
+                bulk_g2s(dst, a.native + static_cast<size_t>(gunit(u)) * kB1UnitBytes, kB1UnitBytes, bar);
             }
         } else {
             const int rbase = rb * kRowBlock;
@@ -249,7 +267,7 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
     uint32_t armed = 0;  // stages with a copy in flight
     if (kNative && lane == 0)
         for (int k = 0; k < fill && k < kB1Stages; ++k)
-            prefetch_l2_bulk(a.native + static_cast<size_t>(cu0 + warp + kW * k) * kB1UnitBytes, kB1UnitBytes);
+            prefetch_l2_bulk(a.native + static_cast<size_t>(gunit(cu0 + warp + kW * k)) * kB1UnitBytes, kB1UnitBytes);
     pdl_launch_dependents();
     pdl_wait();  // x, y and the workspace may belong to the preceding kernel until here
     // This call's tag: one more than the last completed call's (never zero).
@@ -282,9 +300,44 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
         for (int q = 0; q < a.g_world; ++q)
             if (q != a.g_rank) st_relaxed_sys_u32(reinterpret_cast<uint32_t*>(a.g_region[q] + off), word);
     };
+    // Output row `row` of this call with this CTA's sum v: with column slabs
+    // a CTA of slab sl > 0 publishes v as a tagged word (this call's tag in the
+    // high half) for the row's slab-0 CTA, which waits for the nslab - 1
+    // words (bounded), adds them in slab order and stores the row.
+    bool slab_ok = true;
+    auto emit_row = [&](int row, float v) {
+        if (nslab == 1) {
+            store_row(row, v);
+            return;
+        }
+        unsigned long long* w = a.xsl + static_cast<size_t>(row >> 4) * (nslab - 1) * 16 + (row & 15);
+        const uint32_t tag = s_tag;
+        if (sl > 0) {
+            st_relaxed_gpu_u64(w + (sl - 1) * 16, (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v));
+            return;
+        }
+        const long long t0 = clock64();
+        for (int q = 1; q < nslab; ++q) {
+            unsigned long long u = ld_relaxed_gpu_u64(w + (q - 1) * 16);
+            while (static_cast<uint32_t>(u >> 32) != tag && clock64() - t0 < (1ll << 31))
+                u = ld_relaxed_gpu_u64(w + (q - 1) * 16);
+            slab_ok = slab_ok && static_cast<uint32_t>(u >> 32) == tag;
+            v += __uint_as_float(static_cast<uint32_t>(u));
+        }
+        store_row(row, v);
+    };
     // x into xb in natural order (requested before the weight copies, so that
-    // it does not queue behind them on the SM's return path).
-    load_x_async<kT>(a.x, n8, xb);
+    // it does not queue behind them on the SM's return path): with column
+    // slabs only the slab's pieces, and for the split GEMV all of x once more
+    // into the staging area (the statistics and the outlier count are over
+    // all of x).  The staging area is the row sums, the outlier list and the
+    // outlier buffers, none of which is used before the plan ends.
+    const int piece0 = 64 * chunk0;
+    const int n8s = nslab > 1 ? min(64 * NC, n8 - piece0) : n8;
+    const bool stage_x = kSplit && nslab > 1;
+    uint4* xstage = reinterpret_cast<uint4*>(smem + a.S.part);
+    load_x_async<kT>(a.x + 8 * static_cast<size_t>(piece0), n8s, xb);
+    if (stage_x) load_x_async<kT>(a.x, n8, xstage);
     if (kNative) {
         for (int k = 0; k < fill; ++k) {
             issue(k, cu0 + warp + kW * k);
@@ -306,11 +359,24 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
     int n_out = 0;
     int* pscratch = reinterpret_cast<int*>(red) + 32;  // after the statistics' 32 floats
     if (kSplit) {
-        const XStats st = x_stats<kT>(xb, n8, a.d_in, a.k, a.inv_n, a.inv_n1, red);
-        n_out = plan_balanced<kT, kR, true>(xb, n8, NC, a.d_in, st.mean, st.thresh, xp4, list,
-                                            reinterpret_cast<uint32_t*>(mask), pscratch);
+        const uint4* xs = stage_x ? xstage : xb;  // all of x
+        const XStats st = x_stats<kT>(xs, n8, a.d_in, a.k, a.inv_n, a.inv_n1, red);
+        int total_all = -1;
+        if (stage_x) {
+            int cnt = 0;
+            for (int p = tid; p < n8; p += kT) cnt += __popc(piece_bits(xs[p], st.mean, st.thresh));
+            total_all = block_count<kT>(cnt, pscratch + 128);
+        }
+        n_out = plan_balanced<kT, kR, true>(xb, n8s, NC, a.d_in, st.mean, st.thresh, xp4, list,
+                                            reinterpret_cast<uint32_t*>(mask), pscratch, xs, piece0, total_all);
+        if (stage_x) {  // the staging area becomes the row sums again
+            for (int i = tid; i < nrb * kW * 16; i += kT) part[i] = 0.f;
+            if (kOut != kOutNone)
+                for (int i = tid; i < kW * a.nrb_max * 16; i += kT) opart[i] = 0.f;
+            __syncthreads();
+        }
     } else {
-        plan_balanced<kT, kR, false>(xb, n8, NC, a.d_in, 0.f, 0.f, xp4, nullptr, nullptr, pscratch);
+        plan_balanced<kT, kR, false>(xb, n8s, NC, a.d_in, 0.f, 0.f, xp4, nullptr, nullptr, pscratch, xb, piece0);
     }
 
     // ---- outlier columns: y[r] += W16[r][c] * x[c] for the rows of row blocks orb0 .. rbz ----
@@ -412,7 +478,7 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
     // The finaliser's warp 0 (lanes 0-15 = rows of rbz) adds the contributors'
     // sums in CTA order.  With one contributor its word is loaded in the middle
     // of the unit loop and only inspected at the end.
-    const int c_hi = finaliser ? unit_owner(static_cast<long long>(rbz + 1) * NC - 1, P, U) : c;
+    const int c_hi = finaliser ? cs0 + unit_owner(static_cast<long long>(rbz + 1) * NC - 1, P, U) : c;
     unsigned long long early = 0ull;
 
     // ---- units ----
@@ -552,7 +618,7 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
 #pragma unroll
             for (int w = 0; w < kW; ++w) sum += opart[(w * a.nrb_max + rbl) * 16 + rr];
         const int row = rb * kRowBlock + rr;
-        if (row < a.d_out) store_row(row, sum);
+        if (row < a.d_out) emit_row(row, sum);
     }
     if (finaliser && warp == 0) {
         const int rbl = rbz - rbf;
@@ -578,8 +644,9 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
             sum += __uint_as_float(static_cast<uint32_t>(v));
         }
         if (!__all_sync(0xffffffffu, ok_all) && lane == 0) atomicOr(&g_error_word, 2u);
-        if (lane < 16 && row < a.d_out) store_row(row, sum);
+        if (lane < 16 && row < a.d_out) emit_row(row, sum);
     }
+    if (!slab_ok) atomicOr(&g_error_word, 2u);
 
     // This CTA is done with the workspace (its tag read, its words published,
     // its finaliser wait over): the last CTA of the call advances the tag.
@@ -587,7 +654,7 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
         // The rows this CTA stores: its row blocks from rbf (rbf + 1 when a
         // contributor) to rbz, below d_out.
         const int rs = (contrib ? rbf + 1 : rbf) * kRowBlock;
-        const int re = min((rbz + 1) * kRowBlock, a.d_out);
+        const int re = sl > 0 ? rs : min((rbz + 1) * kRowBlock, a.d_out);  // slab 0 stores the rows
         __syncthreads();  // (every thread has the call number)
         if (re > rs) gather_rows<kT>(a, gmisc[1], rs, re);
     }
@@ -895,7 +962,7 @@ __global__ void colmajor_kernel(const uint16_t* __restrict__ w, int d_out, int d
 
 // Per-device, per-kernel "max dynamic shared memory" opt-in, done once.
 constexpr int kMaxDevices = 64;
-constexpr int kNumKernels = 272;
+constexpr int kNumKernels = 528;
 int g_smem_set[kMaxDevices][kNumKernels];  // bytes already opted in (0 = none)
 
 template <class K>
@@ -927,13 +994,14 @@ dq_status_t check_launch() {
 }
 
 
-template <bool kSplit, bool kNative, int kOut, int kW, int kR, bool kGather = false>
+template <bool kSplit, bool kNative, int kOut, int kW, int kR, bool kGather = false, bool kSlab = false>
 dq_status_t launch_b1(const B1Args& a, int grid, cudaStream_t stream) {
     constexpr int wi = kW == kB1Warps ? 0 : 1;
     constexpr int ri = kR == 1 ? 0 : kR == 2 ? 1 : kR == 4 ? 2 : 3;
-    constexpr int id = 4 + 16 * (4 * wi + ri) + (kSplit ? 8 : 0) + (kNative ? 4 : 0) + kOut + (kGather ? 128 : 0);
+    constexpr int id = 4 + 16 * (4 * wi + ri) + (kSplit ? 8 : 0) + (kNative ? 4 : 0) + kOut + (kGather ? 128 : 0) +
+                       (kSlab ? 256 : 0);
     static_assert(id < kNumKernels, "kernel attribute slot");
-    const dq_status_t st = ensure_smem(b1_kernel<kSplit, kNative, kOut, kW, kR, kGather>, id, a.S.total);
+    const dq_status_t st = ensure_smem(b1_kernel<kSplit, kNative, kOut, kW, kR, kGather, kSlab>, id, a.S.total);
     if (st != DQ_OK) return st;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -945,23 +1013,26 @@ dq_status_t launch_b1(const B1Args& a, int grid, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, b1_kernel<kSplit, kNative, kOut, kW, kR, kGather>, a);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, b1_kernel<kSplit, kNative, kOut, kW, kR, kGather, kSlab>, a);
     if (e != cudaSuccess) { set_cuda_error(e); return DQ_ERR_CUDA; }
     return check_launch();
 }
 
-template <bool kNative, int kW, int kR>
+template <bool kNative, int kW, int kR, bool kSlab = false>
 dq_status_t launch_b1_out(const B1Args& a, int out_mode, int grid, cudaStream_t stream) {
     switch (out_mode) {
-        case kOutStaged: return launch_b1<true, kNative, kOutStaged, kW, kR>(a, grid, stream);
-        case kOutColDirect: return launch_b1<true, kNative, kOutColDirect, kW, kR>(a, grid, stream);
-        case kOutRowDirect: return launch_b1<true, kNative, kOutRowDirect, kW, kR>(a, grid, stream);
-        default: return launch_b1<false, kNative, kOutNone, kW, kR>(a, grid, stream);
+        case kOutStaged: return launch_b1<true, kNative, kOutStaged, kW, kR, false, kSlab>(a, grid, stream);
+        case kOutColDirect: return launch_b1<true, kNative, kOutColDirect, kW, kR, false, kSlab>(a, grid, stream);
+        case kOutRowDirect: return launch_b1<true, kNative, kOutRowDirect, kW, kR, false, kSlab>(a, grid, stream);
+        default: return launch_b1<false, kNative, kOutNone, kW, kR, false, kSlab>(a, grid, stream);
     }
 }
 
 template <int kW>
 dq_status_t launch_b1_native(const B1Args& a, int out_mode, int rounds, int grid, cudaStream_t stream) {
+    if (a.nslab > 1)  // column slabs: at most 4 rounds (b1_setup)
+        return rounds <= 2 ? launch_b1_out<true, kW, 2, true>(a, out_mode, grid, stream)
+                           : launch_b1_out<true, kW, 4, true>(a, out_mode, grid, stream);
     if (rounds <= 1) return launch_b1_out<true, kW, 1>(a, out_mode, grid, stream);
     if (rounds <= 2) return launch_b1_out<true, kW, 2>(a, out_mode, grid, stream);
     if (rounds <= 4) return launch_b1_out<true, kW, 4>(a, out_mode, grid, stream);
@@ -972,6 +1043,9 @@ dq_status_t launch_b1_native(const B1Args& a, int out_mode, int rounds, int grid
 // slices are whole row blocks, so d_out is a multiple of 16).
 template <int kW>
 dq_status_t launch_b1_gather(const B1Args& a, int rounds, int grid, cudaStream_t stream) {
+    if (a.nslab > 1)
+        return rounds <= 2 ? launch_b1<true, true, kOutStaged, kW, 2, true, true>(a, grid, stream)
+                           : launch_b1<true, true, kOutStaged, kW, 4, true, true>(a, grid, stream);
     if (rounds <= 1) return launch_b1<true, true, kOutStaged, kW, 1, true>(a, grid, stream);
     if (rounds <= 2) return launch_b1<true, true, kOutStaged, kW, 2, true>(a, grid, stream);
     if (rounds <= 4) return launch_b1<true, true, kOutStaged, kW, 4, true>(a, grid, stream);
@@ -993,7 +1067,7 @@ struct B1Plan {
 };
 
 dq_status_t b1_setup(const dq_weights_t& w, const uint16_t* x, uint16_t* y, float k, bool split, void* workspace,
-                     B1Args& a, B1Plan& p) {
+                     size_t workspace_bytes, B1Args& a, B1Plan& p) {
     DeviceInfo di;
     const dq_status_t st = device_info(&di);
     if (st != DQ_OK) return st;
@@ -1016,36 +1090,59 @@ dq_status_t b1_setup(const dq_weights_t& w, const uint16_t* x, uint16_t* y, floa
     a.d_out = w.d_out;
     a.d_in = w.d_in;
     a.NC = NC;
-    a.U = static_cast<int>(n_rb * NC);
     const WsLayout W = ws_layout(w.d_out, w.d_in);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     a.hdr = reinterpret_cast<unsigned int*>(ws + W.hdr);
     a.fix = reinterpret_cast<unsigned long long*>(ws + W.fix);
-    int grid = di.sm_count < a.U ? di.sm_count : a.U;
+    a.xsl = reinterpret_cast<unsigned long long*>(ws + ws_slab_offset());
+    int grid = di.sm_count < n_rb * NC ? di.sm_count : static_cast<int>(n_rb * NC);
     if (grid > kMaxCtas) grid = kMaxCtas;
+    // Column slabs for long rows (native layout): every slab's CTAs then
+    // cover all row blocks over fewer chunks, so a CTA's plan converts only
+    // its slab of x.  Not when the workspace has no room for the slab words,
+    // a slab would get fewer than two CTAs, a slab's plan would take more
+    // than 4 rounds, or a CTA's share is long (the plan is then a small part
+    // of it).
+    int nslab = w.native ? b1_slabs(NC) : 1;
+    if (nslab > 1) {
+        const int ncs = NC / nslab;
+        const long long per_cta = (n_rb * NC + grid - 1) / grid;
+        if (grid < 2 * nslab || 64 * ncs > 4 * 32 * kB1WarpsSmall || per_cta > kB1SlabMaxUnits ||
+            workspace_bytes < ws_slab_offset() + b1_slab_bytes(w.d_out, nslab))
+            nslab = 1;
+    }
+    a.nslab = nslab;
+    a.NCs = NC / nslab;
+    a.U = static_cast<int>(n_rb * a.NCs);
     int nrb_max = 1;
-    for (int c = 0; c < grid; ++c) {
-        const int u0 = unit_start(a.U, c, grid), u1 = unit_start(a.U, c + 1, grid);
-        const int n = (u1 - 1) / NC - u0 / NC + 1;
-        if (n > nrb_max) nrb_max = n;
+    for (int sl = 0; sl < nslab; ++sl) {
+        const int c0 = sl * grid / nslab, P = (sl + 1) * grid / nslab - c0;
+        for (int c = 0; c < P; ++c) {
+            const int u0 = unit_start(a.U, c, P), u1 = unit_start(a.U, c + 1, P);
+            if (u1 <= u0) continue;
+            const int n = (u1 - 1) / a.NCs - u0 / a.NCs + 1;
+            if (n > nrb_max) nrb_max = n;
+        }
     }
     a.nrb_max = nrb_max;
+    const int slab_nc = nslab > 1 ? a.NCs : 0;
     p.grid = grid;
     p.out_mode = kOutNone;
     if (split) p.out_mode = w.fp16_cm ? ((w.d_out % 8) == 0 ? kOutStaged : kOutColDirect) : kOutRowDirect;
     if (w.native) {
         // A ring of as many stages per warp as fit (at least kB1Stages, no more
         // than a warp has units), 16 warps or 12.
-        const int u_warp = ((a.U + grid - 1) / grid + kB1WarpsSmall - 1) / kB1WarpsSmall;
+        const int per_cta = nslab > 1 ? (a.U + grid / nslab - 1) / (grid / nslab) : (a.U + grid - 1) / grid;
+        const int u_warp = (per_cta + kB1WarpsSmall - 1) / kB1WarpsSmall;
         const int ring_warps[2] = {kB1Warps, kB1WarpsSmall};
         for (int warps : ring_warps) {
             for (int depth = kB1MaxDepth; depth >= kB1Stages; --depth) {
                 if (depth > kB1Stages && depth > u_warp) continue;
-                a.S = b1_smem(w.d_in, nrb_max, split, warps, warps * depth);
+                a.S = b1_smem(w.d_in, nrb_max, split, warps, warps * depth, slab_nc);
                 if (a.S.total > di.smem_optin) continue;
                 a.depth = depth;
                 p.warps = warps;
-                p.rounds = (64 * NC + 32 * warps - 1) / (32 * warps);  // plan rounds: pieces per thread
+                p.rounds = (64 * a.NCs + 32 * warps - 1) / (32 * warps);  // plan rounds: pieces per thread
                 return DQ_OK;
             }
         }
@@ -1067,20 +1164,26 @@ dq_status_t b1_setup(const dq_weights_t& w, const uint16_t* x, uint16_t* y, floa
 
 }  // namespace
 
+size_t b1_workspace_bytes(int d_out, int d_in) {
+    const int NC = (d_in / kGroup + kCG - 1) / kCG;
+    const int S = b1_slabs(NC);
+    return S > 1 ? ws_slab_offset() + b1_slab_bytes(d_out, S) : ws_layout(d_out, d_in).total;
+}
+
 dq_status_t launch_gemv_b1(const dq_weights_t& w, const uint16_t* x, uint16_t* y, float k,
-                           bool split, void* workspace, cudaStream_t stream) {
+                           bool split, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
     B1Args a;
     B1Plan p;
-    const dq_status_t st = b1_setup(w, x, y, k, split, workspace, a, p);
+    const dq_status_t st = b1_setup(w, x, y, k, split, workspace, workspace_bytes, a, p);
     if (st != DQ_OK) return st;
     return launch_b1_warps(a, p.warps, p.out_mode, p.rounds, p.grid, stream);
 }
 
 dq_status_t launch_gemv_b1_gather(const dq_weights_t& w, const uint16_t* x, uint16_t* y, float k, void* workspace,
-                                  const dq_gather_t& g, cudaStream_t stream) {
+                                  size_t workspace_bytes, const dq_gather_t& g, cudaStream_t stream) {
     B1Args a;
     B1Plan p;
-    const dq_status_t st = b1_setup(w, x, y, k, true, workspace, a, p);
+    const dq_status_t st = b1_setup(w, x, y, k, true, workspace, workspace_bytes, a, p);
     if (st != DQ_OK) return st;
     if (!a.native || p.out_mode != kOutStaged) return DQ_ERR_UNSUPPORTED;
     a.g_rank = g.rank;

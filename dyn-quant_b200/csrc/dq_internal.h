@@ -49,9 +49,14 @@ struct B1Smem {
     int ring, bars, misc, zero, bsm, xp, mask, red, part, opart, list, obuf, total;
 };
 
-// slots: ring slots of kB1StageBytes, each with its mbarrier.
-inline B1Smem b1_smem(int d_in, int nrb_max, bool split, int warps, int slots) {
-    const int NC = (d_in / 128 + kB1ChunkGroups - 1) / kB1ChunkGroups;
+// slots: ring slots of kB1StageBytes, each with its mbarrier.  slab_nc: the
+// chunks of a column slab (0: no slabs); bsm and xp then hold the slab's
+// fragments only, while the mask and the list stay sized for all of x, and
+// part .. obuf (unused until the plan is done) first hold all of x for the
+// statistics.
+inline B1Smem b1_smem(int d_in, int nrb_max, bool split, int warps, int slots, int slab_nc = 0) {
+    const int NCall = (d_in / 128 + kB1ChunkGroups - 1) / kB1ChunkGroups;
+    const int NC = slab_nc > 0 ? slab_nc : NCall;
     B1Smem S;
     int off = 0;
     S.ring = off;  off += slots * kB1StageBytes;
@@ -60,12 +65,15 @@ inline B1Smem b1_smem(int d_in, int nrb_max, bool split, int warps, int slots) {
     S.zero = off;  off += kB1ChunkB;
     S.bsm = off;   off += NC * kB1ChunkB;
     S.xp = off;    off += NC * kB1ChunkGroups * 16;
-    S.mask = off;  off += split ? NC * 64 : 0;
+    S.mask = off;  off += split ? NCall * 64 : 0;
     S.red = off;   off += kB1RedBytes;
     S.part = off;  off += nrb_max * warps * 16 * 4;
     S.opart = off; off += split ? warps * nrb_max * 16 * 4 : 0;
     S.list = off;  off += split ? align16(d_in) : 0;
     S.obuf = off;  off += split ? warps * kB1OutBufs * kB1OutBufBytes : 0;
+    // Column slabs of the split GEMV stage all of x from part on while the
+    // plan runs (the statistics are over all of x).
+    if (slab_nc > 0 && split && off < S.part + align16(2 * d_in)) off = S.part + align16(2 * d_in);
     S.total = off;
     return S;
 }
@@ -79,12 +87,30 @@ inline B1Smem b1_smem(int d_in, int nrb_max, bool split, int warps, int slots) {
 //        (tag << 32 | FP32 bits): a word is this call's only if it carries
 //        this call's tag, so words left by an earlier call are never taken.
 // Zero before first use; every call leaves it ready for the next one (also a
-// call whose bounded waits gave up).
+// call whose bounded waits gave up).  Long rows cut into column slabs also
+// use the slab region after the fixed header (ws_slab_offset).
 struct WsLayout {
     size_t hdr, fix, total;
 };
 
 inline size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+
+constexpr int kB1SlabMinNC = 32;          // chunks per row (d_in / 512) from which rows are cut into slabs
+constexpr int kB1SlabMaxUnits = 64;       // ... when a CTA's share is at most this many units
+// Column slabs of a batch-1 call with NC chunks per row: the largest divisor
+// of NC not above ceil(NC / 16) (so a slab holds about 16 chunks), or 1.
+inline int b1_slabs(int NC) {
+    if (NC < kB1SlabMinNC) return 1;
+    for (int S = (NC + 15) / 16; S > 1; --S)
+        if (NC % S == 0) return S;
+    return 1;
+}
+// Slab region: per row block and slab 1 .. S-1, 16 tagged partial row sums
+// (tag << 32 | FP32 bits), 8 bytes each.
+inline size_t b1_slab_bytes(int d_out, int S) {
+    const size_t n_rb = (static_cast<size_t>(d_out) + 15) / 16;
+    return align256(n_rb * static_cast<size_t>(S - 1) * 16 * sizeof(unsigned long long));
+}
 
 // Gather region of one rank (row-sharded split GEMV with the gather fused):
 //   hdr    u32 [0] calls this rank has completed (the running call's number
@@ -173,6 +199,14 @@ inline WsHeader ws_header() {
     H.total = off;
     return H;
 }
+// The slab region of the batch-1 kernel follows the fixed header; per-shape
+// scratch of the other kernels follows the slab region of the shape.
+inline size_t ws_slab_offset() { return ws_header().total; }
+inline size_t ws_scratch_base(int d_out, int d_in) {
+    const int NC = (d_in / 128 + kB1ChunkGroups - 1) / kB1ChunkGroups;
+    const int S = b1_slabs(NC);
+    return ws_header().total + (S > 1 ? b1_slab_bytes(d_out, S) : 0);
+}
 
 struct StreamWs {
     size_t ctr, rbcnt, part, total;
@@ -183,8 +217,9 @@ inline StreamWs stream_ws(int d_out, int d_in) {
     StreamWs L;
     L.ctr = H.stream_ctr;
     L.rbcnt = H.stream_rbcnt;
-    L.part = H.total;
-    L.total = H.total + (g.tpr > 1 ? align256(static_cast<size_t>(g.n_rb) * g.tpr * 64) : 0);
+    const size_t base = ws_scratch_base(d_out, d_in);
+    L.part = base;
+    L.total = base + (g.tpr > 1 ? align256(static_cast<size_t>(g.n_rb) * g.tpr * 64) : 0);
     return L;
 }
 
@@ -309,11 +344,13 @@ void set_cuda_error(cudaError_t e);
 
 // Kernel launchers (arguments already validated by the C ABI layer).
 dq_status_t launch_gemv_b1(const dq_weights_t& w, const uint16_t* x, uint16_t* y, float k,
-                           bool split, void* workspace, cudaStream_t stream);
+                           bool split, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+// Workspace bytes the batch-1 kernel uses for a shape (its slab region included).
+size_t b1_workspace_bytes(int d_out, int d_in);
 // The split GEMV with the row-sharded gather fused (native layout and mirror,
 // d_out a multiple of 16): y holds g.d_total rows.
 dq_status_t launch_gemv_b1_gather(const dq_weights_t& w, const uint16_t* x, uint16_t* y, float k, void* workspace,
-                                  const dq_gather_t& g, cudaStream_t stream);
+                                  size_t workspace_bytes, const dq_gather_t& g, cudaStream_t stream);
 dq_status_t launch_build_native(const uint8_t* packed, const uint16_t* scales, const uint16_t* zeros,
                                 int d_out, int d_in, uint8_t* out, cudaStream_t stream);
 dq_status_t read_device_error(uint32_t* word, bool clear);
@@ -327,12 +364,10 @@ dq_status_t launch_colmajor(const uint16_t* w16, int d_out, int d_in, uint16_t* 
                             cudaStream_t stream);
 
 inline BgWs bg_ws(const BgGeom& g, int d_out, int d_in) {
-    (void)d_out;
-    (void)d_in;
     BgWs L;
     const WsHeader H = ws_header();
     L.ctr = H.batched_ctr;
-    size_t off = H.total;
+    size_t off = ws_scratch_base(d_out, d_in);
     L.masks = off; off += align256(static_cast<size_t>(kBgMaxM) * g.W * 4);
     L.ulist = off; off += align256(static_cast<size_t>(d_in) * 4);
     L.xrow = off;  off += align256(static_cast<size_t>(d_in) * g.MP * 2);

@@ -168,7 +168,7 @@ __device__ __forceinline__ XStats x_stats(const uint4* xs, int n8, int d_in, flo
 // (d_in/4)/4 of each class in column order.  Writes mask32 and list; returns
 // the outlier count.  Barrier-synchronised; the list and mask are complete
 // after the caller's next barrier.  scratch: >= NW * 5 ints used by nothing
-// else.
+// else.  list may be null (the mask only).
 template <int NT>
 __device__ int x_mask_list(const uint4* xs, int d_in, float mean, float thresh, uint32_t* mask32, uint32_t* list,
                            int* scratch) {
@@ -242,7 +242,7 @@ __device__ int x_mask_list(const uint4* xs, int d_in, float mean, float thresh, 
         const int wj = w0 + q;
         if (wj < w1) {
             mask32[wj] = bits[q];
-            uint32_t m = bits[q];
+            uint32_t m = list ? bits[q] : 0u;
             while (m) {
                 const int col = 32 * wj + (__ffs(m) - 1);
                 list[pos++] = static_cast<uint32_t>(col) | (static_cast<uint32_t>(xh[col]) << 16);
@@ -276,6 +276,20 @@ __device__ __forceinline__ uint32_t piece_bits(const uint4& v, float mean, float
         b |= (fabsf(sub_f16_f32(hi16(w), mean)) > thresh ? 1u : 0u) << (2 * i + 1);
     }
     return b;
+}
+
+// Block total of a per-thread count (every thread gets it).  wcnt: NT/32 ints
+// not in use until the caller's next barrier; one barrier.
+template <int NT>
+__device__ __forceinline__ int block_count(int cnt, int* wcnt) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    cnt = static_cast<int>(__reduce_add_sync(0xffffffffu, static_cast<unsigned>(cnt)));
+    if (lane == 0) wcnt[warp] = cnt;
+    __syncthreads();
+    int total = 0;
+#pragma unroll
+    for (int w = 0; w < NT / 32; ++w) total += wcnt[w];
+    return total;
 }
 
 // Exclusive prefix of this thread's cnt over the block in (warp, lane) order
@@ -319,14 +333,21 @@ __device__ __forceinline__ int plan_prefix(int cnt, int* wcnt, int& total) {
 //        the end of the last chunk) are zero
 //   xp4  [4 NC] per group (1024 sum x' even columns, 1024 sum x' odd columns,
 //        sum x', 0); groups past d_in are zero
-//   list the outliers (column | FP16 bits of x << 16): in (warp, lane, round)
-//        order, or ascending when the reference's capacity rule applies
-//        (more than d_in/16 outliers: x_mask_list, mask32 its mask)
+//   list the outliers (column | FP16 bits of x << 16) in (warp, lane, round)
+//        order; with more than d_in/16 outliers the reference's capacity
+//        rule decides the mask (x_mask_list over all of x; mask32 receives
+//        it)
 // red: kB1RedBytes of shared memory not in use.  Returns the outlier count
 // (every thread); everything is complete on return (ends with a barrier).
+// Column slabs: xb may hold only the pieces [piece0, piece0 + n8) of x (a
+// slab of NC chunks); xfull is all of x in natural order in shared memory
+// (xb itself when it holds all of x) and total_all the outlier count over
+// all of x (-1: xb holds all of x, count it here).  The list then holds the
+// slab's outliers (columns of x) and the return value is their number.
 template <int NT, int R, bool kMask>
 __device__ __forceinline__ int plan_balanced(uint4* xb, int n8, int NC, int d_in, float mean, float thresh,
-                                             float4* xp4, uint32_t* list, uint32_t* mask32, int* red) {
+                                             float4* xp4, uint32_t* list, uint32_t* mask32, int* red,
+                                             const uint4* xfull, int piece0 = 0, int total_all = -1) {
     static_assert(NT % 32 == 0 && NT <= 512, "plan threads");
     const int tid = threadIdx.x;
     const int npc = 64 * NC;
@@ -341,20 +362,24 @@ __device__ __forceinline__ int plan_balanced(uint4* xb, int n8, int NC, int d_in
         cnt += __popc(bits[rr]);
     }
     int total = 0, pos = 0;
-    bool capacity = false;
     if (kMask) {
         pos = plan_prefix<NT>(cnt, red, total);
-        if (total > d_in / 16) {
+        if ((total_all >= 0 ? total_all : total) > d_in / 16) {
             // No stripe class can exceed its capacity ((d_in/4)/4) below this
-            // total; above it the reference's rule may drop outliers.
-            capacity = true;
-            total = x_mask_list<NT>(xb, d_in, mean, thresh, mask32, list, red + 16);
+            // total; above it the reference's rule may drop outliers: the
+            // mask from all of x in column order, then this thread's bits
+            // from it and the list positions again.
+            __syncthreads();  // every thread has read the warp counts (x_mask_list's scratch follows them)
+            x_mask_list<NT>(xfull, d_in, mean, thresh, mask32, nullptr, red + 16);
             __syncthreads();
+            cnt = 0;
 #pragma unroll
             for (int rr = 0; rr < R; ++rr) {
-                const int p = tid + NT * rr;
-                if (p < n8) bits[rr] = (mask32[p >> 2] >> (8 * (p & 3))) & 0xFFu;
+                const int p = tid + NT * rr, pg = piece0 + p;
+                bits[rr] = p < n8 ? (mask32[pg >> 2] >> (8 * (pg & 3))) & 0xFFu : 0u;
+                cnt += __popc(bits[rr]);
             }
+            pos = plan_prefix<NT>(cnt, red, total);
         }
     }
     __syncthreads();  // every piece of x is in registers: xb may be overwritten
@@ -391,11 +416,11 @@ __device__ __forceinline__ int plan_balanced(uint4* xb, int n8, int NC, int d_in
         }
         if ((p & 15) == 0 && p < npc) xp4[p >> 4] = make_float4(1024.f * pe, 1024.f * po, pe + po, 0.f);
     }
-    if (kMask && !capacity) {
+    if (kMask) {
 #pragma unroll
         for (int rr = 0; rr < R; ++rr) {
             uint32_t b = bits[rr];
-            const int p = tid + NT * rr;
+            const int p = piece0 + tid + NT * rr;
             while (b) {
                 const int e = __ffs(b) - 1;
                 const uint32_t word = word_of(v[rr], e >> 1);

@@ -44,7 +44,7 @@ torch::Tensor workspace_for(const torch::Device& dev, void* stream, size_t bytes
     return it->second;
 }
 
-// Zero-fill the counters of every cached workspace on its own stream (after
+// Zero-fill every cached workspace on its own stream (after
 // dq_read_device_error reported an error; see include/dq_abi.h).
 void reset_workspaces() {
     std::lock_guard<std::mutex> lock(workspace_mu());
@@ -368,7 +368,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("build_colmajor", &build_colmajor, "Column-major FP16 mirror of a weight matrix");
     m.def("detect_outliers", &detect_outliers, "Standalone outlier detector");
     m.def("version", []() { return dq_version(); });
-    m.def("reset_workspaces", &reset_workspaces, "Zero the counters of the cached GEMV workspaces");
+    m.def("reset_workspaces", &reset_workspaces, "Zero the cached GEMV workspaces");
     m.def("read_device_error", [](bool clear) {
         uint32_t w = 0;
         check_status(dq_read_device_error(&w, clear ? 1 : 0), "read_device_error");

@@ -133,9 +133,12 @@ DQ_API dq_status_t dq_build_native(const uint8_t* packed, const uint16_t* scales
  * its first use.  Its first 256 + 128 KiB hold a call counter, an arrival
  * counter and, per CTA, the partial row sums of the 16-row block that CTA
  * shares with the one before it, each tagged with the call's number so that a
- * sum left by an earlier call is never taken (the block kernel needs no
- * more); the rest, which grows with the shape, serves the streaming kernel
- * (task queue and per-row-block partial sums, DQ_STREAM=1).  Every
+ * sum left by an earlier call is never taken; then the counters of the other
+ * kernels and, for rows of 16384 columns or more cut into column slabs, the
+ * slabs' tagged partial row sums (8 bytes per row and slab after the first;
+ * a smaller workspace runs such a call without slabs); the rest, which grows
+ * with the shape, serves the streaming kernel (task queue and per-row-block
+ * partial sums, DQ_STREAM=1) and the batched kernels.  Every
  * call leaves it ready for the next one, so one zero-filled workspace serves
  * any number of stream-ordered calls of any shape; after a call that reported
  * a device error (dq_read_device_error), reset it with dq_reset_workspace.
@@ -144,8 +147,8 @@ DQ_API dq_status_t dq_build_native(const uint8_t* packed, const uint16_t* scales
 DQ_API size_t dq_workspace_bytes(int32_t d_out, int32_t d_in);
 
 /*
- * Zero-fill the counters at the head of a workspace on `stream` (an
- * asynchronous memset of its first bytes, no allocation).  Needed only after
+ * Zero-fill a workspace on `stream` (an asynchronous memset of its
+ * workspace_bytes, no allocation).  Needed only after
  * dq_read_device_error reported an error of a call that used the workspace:
  * such a call may leave a row block's arrival counter short.  No reference
  * counterpart.

@@ -114,7 +114,8 @@ def test_world_one_is_the_split_gemv():
         assert list(_hdr(region)) == [2 * call]
 
 
-@pytest.mark.parametrize("rows_per,d_in,tail", [(1024, 4096, 5), (3584, 8192, 0), (512, 11008, 16)])
+@pytest.mark.parametrize("rows_per,d_in,tail", [(1024, 4096, 5), (3584, 8192, 0), (512, 11008, 16),
+                                              (1024, 28672, 3)])
 def test_rank0_of_two_with_planted_peer(rows_per, d_in, tail):
     from dyn_quant import synth
     d_total = 2 * rows_per - tail

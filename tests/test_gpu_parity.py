@@ -22,7 +22,8 @@ CASES = [
     (4096, 4096, 0.02, 3.0, "normal"),    # Llama-2-7B q_proj, 2 % outliers
     (1024, 11008, 0.01, 3.0, "normal"),   # 7B down-proj input width
     (2048, 8192, 0.03, 3.0, "normal"),    # 70B q_proj input width
-    (512, 28672, 0.03, 3.0, "normal"),    # 70B down-proj input width
+    (512, 28672, 0.03, 3.0, "normal"),    # 70B down-proj input width (four column slabs)
+    (1000, 16384, 0.03, 3.0, "normal"),   # two column slabs, ragged last row block
     (100, 256, 0.05, 3.0, "normal"),      # ragged d_out
     (17, 128, 0.05, 2.0, "normal"),       # smallest d_in
     (1, 4096, 0.02, 3.0, "normal"),       # one row
@@ -124,7 +125,7 @@ def test_split_gemv_matches_oracle(d_out, d_in, frac, k, dist, layout):
 
 
 @pytest.mark.parametrize("native", [True, False])
-@pytest.mark.parametrize("d_out,d_in,frac,k,dist", CASES[:7], ids=IDS[:7])
+@pytest.mark.parametrize("d_out,d_in,frac,k,dist", CASES[:8], ids=IDS[:8])
 def test_int4_gemv_matches_oracle(d_out, d_in, frac, k, dist, native):
     w, x, packed, scales, zeros = make_case(d_out, d_in, frac, dist)
     p_t, s_t, z_t = dev(packed), dev(scales), dev(zeros)
@@ -135,7 +136,7 @@ def test_int4_gemv_matches_oracle(d_out, d_in, frac, k, dist, native):
     check_y(y, y16, y32, what="int4")
 
 
-@pytest.mark.parametrize("d_out,d_in,frac,k,dist", CASES[:7], ids=IDS[:7])
+@pytest.mark.parametrize("d_out,d_in,frac,k,dist", CASES[:8], ids=IDS[:8])
 def test_reference_gemv_matches_oracle(d_out, d_in, frac, k, dist):
     w, x, *_ = make_case(d_out, d_in, frac, dist)
     y = host(abi_reference_gemv(dev(w), dev(x)))
@@ -143,9 +144,10 @@ def test_reference_gemv_matches_oracle(d_out, d_in, frac, k, dist):
     check_y(y, y16, y32, what="fp16 gemv")
 
 
-def test_capacity_rule_many_outliers():
-    # k = 0.05 flags most channels; the per-stripe capacity (d_in/16) must trim them
-    d_in = 2048
+@pytest.mark.parametrize("d_in", [2048, 16384, 28672])
+def test_capacity_rule_many_outliers(d_in):
+    # k = 0.05 flags most channels; the per-stripe capacity (d_in/16) must trim
+    # them (16384 and 28672: rows cut into column slabs, the mask from all of x)
     x = synth.activation(d_in, 0.0, seed=11)
     mask, idx, stats = abi_detect(dev(x), 0.05)
     rmask, ridx, rstats = O.detect(x, 0.05)
@@ -163,7 +165,7 @@ def test_capacity_rule_many_outliers():
 def _concentrated(d_in, first, n, mag, seed):
     """x ~ N(0, 1) with n channels of magnitude mag (random signs) among the
     first `first` columns: the outliers pile up in one or a few 512-column
-    chunks (more than the outlier segments a weight stage carries)."""
+    chunks."""
     rng = np.random.default_rng(seed)
     x = rng.standard_normal(d_in).astype(np.float32)
     idx = rng.choice(first, n, replace=False)
@@ -173,9 +175,9 @@ def _concentrated(d_in, first, n, mag, seed):
 
 @pytest.mark.parametrize("d_out,d_in,first,n", [
     (4096, 4096, 512, 20),     # one chunk, two 16-column batches
-    (4096, 4096, 512, 40),     # one chunk, past the staged segments
+    (4096, 4096, 512, 40),     # one chunk, three 16-column batches
     (4096, 4096, 204, 150),    # the reference test's layout: the first channels
-    (2048, 28672, 512, 24),    # longest rows (fewer staged segments per stage)
+    (2048, 28672, 512, 24),    # longest rows: all outliers in the first column slab
     (1000, 8192, 1024, 70),    # ragged last row block, two chunks
 ])
 def test_split_gemv_concentrated_outliers(d_out, d_in, first, n):
