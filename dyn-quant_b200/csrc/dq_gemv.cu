@@ -361,14 +361,14 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
     if (kSplit) {
         const uint4* xs = stage_x ? xstage : xb;  // all of x
         const XStats st = x_stats<kT>(xs, n8, a.d_in, a.k, a.inv_n, a.inv_n1, red);
-        int total_all = -1;
+        int total_all = 0;
         if (stage_x) {
             int cnt = 0;
             for (int p = tid; p < n8; p += kT) cnt += __popc(piece_bits(xs[p], st.mean, st.thresh));
             total_all = block_count<kT>(cnt, pscratch + 128);
         }
-        n_out = plan_balanced<kT, kR, true>(xb, n8s, NC, a.d_in, st.mean, st.thresh, xp4, list,
-                                            reinterpret_cast<uint32_t*>(mask), pscratch, xs, piece0, total_all);
+        n_out = plan_balanced<kT, kR, true, kSlab>(xb, n8s, NC, a.d_in, st.mean, st.thresh, xp4, list,
+                                                   reinterpret_cast<uint32_t*>(mask), pscratch, xs, piece0, total_all);
         if (stage_x) {  // the staging area becomes the row sums again
             for (int i = tid; i < nrb * kW * 16; i += kT) part[i] = 0.f;
             if (kOut != kOutNone)
@@ -376,7 +376,7 @@ __global__ void __launch_bounds__(kW * 32, 1) b1_kernel(const B1Args a) {
             __syncthreads();
         }
     } else {
-        plan_balanced<kT, kR, false>(xb, n8s, NC, a.d_in, 0.f, 0.f, xp4, nullptr, nullptr, pscratch, xb, piece0);
+        plan_balanced<kT, kR, false>(xb, n8s, NC, a.d_in, 0.f, 0.f, xp4, nullptr, nullptr, pscratch);
     }
 
     // ---- outlier columns: y[r] += W16[r][c] * x[c] for the rows of row blocks orb0 .. rbz ----

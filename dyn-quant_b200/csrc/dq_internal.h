@@ -95,8 +95,8 @@ struct WsLayout {
 
 inline size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
-constexpr int kB1SlabMinNC = 32;          // chunks per row (d_in / 512) from which rows are cut into slabs
-constexpr int kB1SlabMaxUnits = 64;       // ... when a CTA's share is at most this many units
+constexpr int kB1SlabMinNC = 48;          // chunks per row (d_in / 512) from which rows are cut into slabs
+constexpr int kB1SlabMaxUnits = 128;      // ... when a CTA's share is at most this many units
 // Column slabs of a batch-1 call with NC chunks per row: the largest divisor
 // of NC not above ceil(NC / 16) (so a slab holds about 16 chunks), or 1.
 inline int b1_slabs(int NC) {

@@ -339,15 +339,15 @@ __device__ __forceinline__ int plan_prefix(int cnt, int* wcnt, int& total) {
 //        it)
 // red: kB1RedBytes of shared memory not in use.  Returns the outlier count
 // (every thread); everything is complete on return (ends with a barrier).
-// Column slabs: xb may hold only the pieces [piece0, piece0 + n8) of x (a
-// slab of NC chunks); xfull is all of x in natural order in shared memory
-// (xb itself when it holds all of x) and total_all the outlier count over
-// all of x (-1: xb holds all of x, count it here).  The list then holds the
-// slab's outliers (columns of x) and the return value is their number.
-template <int NT, int R, bool kMask>
+// Column slabs (kSlab): xb holds only the pieces [piece0, piece0 + n8) of x
+// (a slab of NC chunks); xfull is all of x in natural order in shared memory
+// and total_all the outlier count over all of x.  The list then holds the
+// slab's outliers (columns of x) in (warp, lane, round) order also under the
+// capacity rule, and the return value is their number.
+template <int NT, int R, bool kMask, bool kSlab = false>
 __device__ __forceinline__ int plan_balanced(uint4* xb, int n8, int NC, int d_in, float mean, float thresh,
                                              float4* xp4, uint32_t* list, uint32_t* mask32, int* red,
-                                             const uint4* xfull, int piece0 = 0, int total_all = -1) {
+                                             const uint4* xfull = nullptr, int piece0 = 0, int total_all = 0) {
     static_assert(NT % 32 == 0 && NT <= 512, "plan threads");
     const int tid = threadIdx.x;
     const int npc = 64 * NC;
@@ -362,13 +362,28 @@ __device__ __forceinline__ int plan_balanced(uint4* xb, int n8, int NC, int d_in
         cnt += __popc(bits[rr]);
     }
     int total = 0, pos = 0;
-    if (kMask) {
+    bool capacity = false;
+    if (kMask && !kSlab) {
         pos = plan_prefix<NT>(cnt, red, total);
-        if ((total_all >= 0 ? total_all : total) > d_in / 16) {
+        if (total > d_in / 16) {
             // No stripe class can exceed its capacity ((d_in/4)/4) below this
-            // total; above it the reference's rule may drop outliers: the
-            // mask from all of x in column order, then this thread's bits
-            // from it and the list positions again.
+            // total; above it the reference's rule may drop outliers.
+            capacity = true;
+            total = x_mask_list<NT>(xb, d_in, mean, thresh, mask32, list, red + 16);
+            __syncthreads();
+#pragma unroll
+            for (int rr = 0; rr < R; ++rr) {
+                const int p = tid + NT * rr;
+                if (p < n8) bits[rr] = (mask32[p >> 2] >> (8 * (p & 3))) & 0xFFu;
+            }
+        }
+    }
+    if (kMask && kSlab) {
+        pos = plan_prefix<NT>(cnt, red, total);
+        if (total_all > d_in / 16) {
+            // Under the capacity rule: the mask from all of x in column
+            // order, then this thread's bits from it and the list positions
+            // again.
             __syncthreads();  // every thread has read the warp counts (x_mask_list's scratch follows them)
             x_mask_list<NT>(xfull, d_in, mean, thresh, mask32, nullptr, red + 16);
             __syncthreads();
@@ -416,11 +431,11 @@ __device__ __forceinline__ int plan_balanced(uint4* xb, int n8, int NC, int d_in
         }
         if ((p & 15) == 0 && p < npc) xp4[p >> 4] = make_float4(1024.f * pe, 1024.f * po, pe + po, 0.f);
     }
-    if (kMask) {
+    if (kMask && !capacity) {
 #pragma unroll
         for (int rr = 0; rr < R; ++rr) {
             uint32_t b = bits[rr];
-            const int p = piece0 + tid + NT * rr;
+            const int p = (kSlab ? piece0 : 0) + tid + NT * rr;
             while (b) {
                 const int e = __ffs(b) - 1;
                 const uint32_t word = word_of(v[rr], e >> 1);

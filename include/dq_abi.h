@@ -134,7 +134,7 @@ DQ_API dq_status_t dq_build_native(const uint8_t* packed, const uint16_t* scales
  * counter and, per CTA, the partial row sums of the 16-row block that CTA
  * shares with the one before it, each tagged with the call's number so that a
  * sum left by an earlier call is never taken; then the counters of the other
- * kernels and, for rows of 16384 columns or more cut into column slabs, the
+ * kernels and, for rows of 24576 columns or more cut into column slabs, the
  * slabs' tagged partial row sums (8 bytes per row and slab after the first;
  * a smaller workspace runs such a call without slabs); the rest, which grows
  * with the shape, serves the streaming kernel (task queue and per-row-block
