@@ -1053,6 +1053,7 @@ def run_sweep(args, dev) -> None:
                     masks = [dyn_quant.detect_outliers(r, k)[0] for r in xr]
                     n_union = int(torch.stack(masks).any(0).sum().item())
                     n_mean = float(torch.stack(masks).sum(1).float().mean().item())
+                    mods[0].outlier_k = k  # the sweep point's k for the accuracy check too
                     yk = mods[0](xr.squeeze(0) if M == 1 else xr).float().reshape(M, d_out)
                     y32 = xr.float() @ w32.t()
                     rl2 = float((torch.linalg.vector_norm(yk - y32) / torch.linalg.vector_norm(y32)).item())
