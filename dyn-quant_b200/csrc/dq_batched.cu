@@ -4,18 +4,22 @@
 // applied to each vector with its own statistics and outlier mask, while the
 // weights stream from HBM once for all vectors.
 //
-// Three kernels, chained on the stream by programmatic dependent launch:
+// Four kernels, chained on the stream by programmatic dependent launch:
 //  1. bplan_kernel, one CTA per vector: the statistics and the outlier mask
 //     of x[m], with the code and the fixed partition of the batch-1 kernel
 //     (dq_plan.cuh), so each vector gets exactly the batch-1 mask; the CTA
 //     writes its vector's outlier-only row (x[m][c] where c is an outlier of
-//     m, else 0).  The last CTA to finish builds the union of the M masks
-//     (ascending columns) and gathers the union's columns of those rows into
-//     x_o[u][m], one union column's vectors contiguous.
-//  2. bdense_kernel: the INT4 part over x' (each vector's outliers zeroed),
-//     split over K: CTA (cx, slab) streams chunks [slab S, slab S + S) of the
-//     row blocks [rb0, rb1) through per-warp cp.async.bulk rings.  Each warp
-//     owns whole row blocks and writes its slab's partial sums.
+//     m, else 0) and its share of the x' tables (the MMA B operands of every
+//     chunk, outliers zeroed, and the per-group sums).
+//  1b. bunion_kernel, 128 CTAs: each derives the union of the M masks
+//     (ascending columns) and gathers its share of the union's columns of
+//     the outlier-only rows into x_o[u][m], one union column's vectors
+//     contiguous.
+//  2. bdense_kernel: the INT4 part over x', split over K: CTA (cx, slab)
+//     copies its slab's x' tables in with two bulk copies and streams chunks
+//     [slab S, slab S + S) of the row blocks [rb0, rb1) through per-warp
+//     cp.async.bulk rings.  Each warp owns whole row blocks and writes its
+//     slab's partial sums.
 //  3. bout_kernel, one CTA per 16-row block: the FP16 part,
 //     Y_o = W16[:, union] x_o, on the tensor cores, then y = the slabs'
 //     partial sums + Y_o, in a fixed order (results do not depend on timing).
@@ -74,10 +78,10 @@ __device__ __forceinline__ float4 lds_f4(uint32_t addr) {
 }
 
 // ---------------------------------------------------------------------------
-// 1. Plan: statistics, masks, union
+// 1. Plan: statistics, masks, x' tables
 // ---------------------------------------------------------------------------
 struct BPSmem {
-    int xs, mask, list, red, flag, total;
+    int xs, mask, red, total;
 };
 
 inline BPSmem bp_smem(int d_in) {
@@ -85,9 +89,7 @@ inline BPSmem bp_smem(int d_in) {
     int off = 0;
     S.xs = off;   off += align16(2 * d_in);
     S.mask = off; off += align16(d_in / 8);
-    S.list = off; off += align16(d_in);
     S.red = off;  off += kB1RedBytes;
-    S.flag = off; off += 16;
     S.total = off;
     return S;
 }
@@ -95,115 +97,157 @@ inline BPSmem bp_smem(int d_in) {
 struct BPArgs {
     const uint16_t* x;   // [M][d_in]
     uint32_t* masks;     // [kBgMaxM][W]
-    uint32_t* ulist;     // [d_in]
-    uint16_t* xrow;      // [MP][d_in] outlier-only rows
-    uint16_t* xo;        // [d_in][MP] by union position
-    unsigned int* ctr;   // [0] arrival counter, [1] union size
+    uint16_t* xrow;      // [MP][d_in] outlier-only rows (rows m < M)
+    uint4* xtab;         // [NC][4 groups][4 slices][MP][4] the INT4 part's B operands
+    float4* xsum;        // [NC][4 groups][MP] per-group sums of x'
     float k, inv_n, inv_n1;
-    int M, MP, d_in, W, NRB;
+    int M, MP, d_in, W, NC;
     BPSmem S;
 };
 
+// One CTA per vector slot m < MP.  For m < M: the statistics and the outlier
+// mask of x[m] with the code and the fixed partition of the batch-1 kernel
+// (dq_plan.cuh), so each vector gets exactly the batch-1 mask; the vector's
+// outlier-only row (x[m][c] where c is an outlier of m, else 0); and the
+// vector's share of the x' tables that every INT4-part CTA copies in whole:
+// piece p (8 columns) of chunk cc goes to xtab[cc][group][slice][m][p & 3] as
+// the f16 pairs (x0,x4), (x2,x6), (x1,x5), (x3,x7) of x' (x with m's outliers
+// zeroed), and xsum[cc][group][m] = (1024 sum x' even columns, 1024 sum x' odd
+// columns, sum x', 0).  For M <= m < MP (padding of the last 8-vector tile):
+// zeros in the tables.
 __global__ void __launch_bounds__(kStatThreads, 1) bplan_kernel(const BPArgs a) {
     constexpr int NT = kStatThreads;
     extern __shared__ __align__(128) char smem[];
     uint4* xs = reinterpret_cast<uint4*>(smem + a.S.xs);
     uint32_t* mask32 = reinterpret_cast<uint32_t*>(smem + a.S.mask);
-    uint32_t* list = reinterpret_cast<uint32_t*>(smem + a.S.list);
     float* red = reinterpret_cast<float*>(smem + a.S.red);
-    int* flag = reinterpret_cast<int*>(smem + a.S.flag);
     const int m = blockIdx.x, tid = threadIdx.x;
     const int n8 = a.d_in >> 3;
+    const int npc = a.NC * 64;  // pieces of the tables: whole 512-column chunks
+    auto tab = [&](int p) -> uint4* {
+        const int cc = p >> 6, q = p & 63;
+        return a.xtab + ((((cc * 4 + (q >> 4)) * 4 + ((q >> 2) & 3)) * a.MP + m) * 4 + (q & 3));
+    };
+    auto sum_of = [&](int p) -> float4* { return a.xsum + ((p >> 4) * a.MP + m); };
 
     pdl_launch_dependents();
     pdl_wait();  // x and the workspace may belong to the preceding kernel until here
+    if (m >= a.M) {
+        for (int p = tid; p < npc; p += NT) {
+            *tab(p) = make_uint4(0, 0, 0, 0);
+            if ((p & 15) == 0) *sum_of(p) = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        return;
+    }
     load_x_async<NT>(a.x + static_cast<size_t>(m) * a.d_in, n8, xs);
     cp_async_wait_all();
     __syncthreads();
     const XStats st = x_stats<NT>(xs, n8, a.d_in, a.k, a.inv_n, a.inv_n1, red);
-    x_mask_list<NT>(xs, a.d_in, st.mean, st.thresh, mask32, list,
+    x_mask_list<NT>(xs, a.d_in, st.mean, st.thresh, mask32, nullptr,
                     reinterpret_cast<int*>(red) + 2 * (kStatThreads / 32));
     __syncthreads();
     for (int i = tid; i < a.W; i += NT) a.masks[static_cast<size_t>(m) * a.W + i] = mask32[i];
-    // Row m of the outlier-only rows (16-byte stores), and the all-zero rows of
-    // the padding vectors M .. MP-1.
-    {
-        const uint8_t* mb = reinterpret_cast<const uint8_t*>(mask32);
-        for (int p = tid; p < n8; p += NT) {
-            const uint32_t b = mb[p];
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (b) {
-                const uint4 w = xs[p];
-                uint32_t keep[4];
+    // npc is a multiple of 64 and NT of 32: a warp's 32 pieces are all below
+    // npc or all above, and a half-warp holds the 16 pieces of one group.
+    const uint8_t* mb = reinterpret_cast<const uint8_t*>(mask32);
+    for (int p = tid; p < npc; p += NT) {
+        const uint4 w = p < n8 ? xs[p] : make_uint4(0, 0, 0, 0);
+        const uint32_t b = p < n8 ? mb[p] : 0u;
+        uint32_t keep[4];
 #pragma unroll
-                for (int i = 0; i < 4; ++i)
-                    keep[i] = ((b >> (2 * i)) & 1u ? 0x0000FFFFu : 0u) | ((b >> (2 * i + 1)) & 1u ? 0xFFFF0000u : 0u);
-                v = make_uint4(w.x & keep[0], w.y & keep[1], w.z & keep[2], w.w & keep[3]);
-            }
-            *reinterpret_cast<uint4*>(a.xrow + static_cast<size_t>(m) * a.d_in + 8 * p) = v;
-            for (int mm = a.M + m; mm < a.MP; mm += a.M)
-                *reinterpret_cast<uint4*>(a.xrow + static_cast<size_t>(mm) * a.d_in + 8 * p) = make_uint4(0, 0, 0, 0);
+        for (int i = 0; i < 4; ++i)
+            keep[i] = ((b >> (2 * i)) & 1u ? 0x0000FFFFu : 0u) | ((b >> (2 * i + 1)) & 1u ? 0xFFFF0000u : 0u);
+        if (p < n8)
+            *reinterpret_cast<uint4*>(a.xrow + static_cast<size_t>(m) * a.d_in + 8 * p) =
+                make_uint4(w.x & keep[0], w.y & keep[1], w.z & keep[2], w.w & keep[3]);
+        const uint4 v = make_uint4(w.x & ~keep[0], w.y & ~keep[1], w.z & ~keep[2], w.w & ~keep[3]);
+        float pe = add_f16_f32(lo16(v.w), add_f16_f32(lo16(v.z), add_f16_f32(lo16(v.y), add_f16_f32(lo16(v.x), 0.f))));
+        float po = add_f16_f32(hi16(v.w), add_f16_f32(hi16(v.z), add_f16_f32(hi16(v.y), add_f16_f32(hi16(v.x), 0.f))));
+        *tab(p) = make_uint4((v.x & 0xFFFFu) | (v.z << 16), (v.y & 0xFFFFu) | (v.w << 16),
+                             (v.x >> 16) | (v.z & 0xFFFF0000u), (v.y >> 16) | (v.w & 0xFFFF0000u));
+#pragma unroll
+        for (int o = 8; o >= 1; o >>= 1) {
+            pe += __shfl_xor_sync(0xffffffffu, pe, o);
+            po += __shfl_xor_sync(0xffffffffu, po, o);
         }
+        if ((p & 15) == 0) *sum_of(p) = make_float4(1024.f * pe, 1024.f * po, pe + po, 0.f);
     }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) *flag = atomicAdd(a.ctr, 1u) == static_cast<unsigned>(a.M - 1);
-    __syncthreads();
-    if (!*flag) return;
-    __threadfence();
+}
 
-    // The last CTA: union of the M masks, ascending.  Thread tid owns the
-    // words [w0, w1), at most two (W <= kMaxDIn / 32 <= 2 NT).
-    static_assert(kMaxDIn / 32 <= 2 * NT, "union words per thread");
+// ---------------------------------------------------------------------------
+// 1b. Union of the masks and the outlier columns' x
+// ---------------------------------------------------------------------------
+struct BUArgs {
+    const uint32_t* masks;  // [kBgMaxM][W]
+    const uint16_t* xrow;   // [MP][d_in] outlier-only rows (rows m < M)
+    uint16_t* ulist;        // [d_in] union columns, ascending
+    uint16_t* xo;           // [d_in rounded up to 16][MP] by union position
+    unsigned int* ctr;      // [1] union size
+    int M, MP, d_in, W;
+};
+
+// kBuCtas CTAs.  Every CTA derives the union of the M masks and its prefix
+// (ascending columns) itself, then takes the union positions
+// [U b / kBuCtas, U (b + 1) / kBuCtas): their columns into ulist and
+// xo[u][m] = xrow[m][column] (zero for the padding vectors m >= M); the last
+// CTA also zeroes the positions U .. (U rounded up to 16) - 1.
+__global__ void __launch_bounds__(kBuThreads) bunion_kernel(const BUArgs a) {
+    constexpr int NT = kBuThreads;
+    static_assert(kMaxDIn / 32 <= 4 * NT, "union words per thread");
+    static_assert(kMaxDIn <= kBuCtas * kBuMaxPos, "union positions per CTA");
+    __shared__ int scratch[NT / 32];
+    __shared__ uint16_t pcol[kBuMaxPos];
+    const int tid = threadIdx.x, b = blockIdx.x;
+
+    pdl_launch_dependents();
+    pdl_wait();  // the masks and rows of the plan kernel
     const int w0 = static_cast<int>(static_cast<long long>(tid) * a.W / NT);
     const int w1 = static_cast<int>(static_cast<long long>(tid + 1) * a.W / NT);
-    uint32_t u[2] = {0u, 0u};
+    uint32_t u[4] = {0u, 0u, 0u, 0u};
     int cnt[1] = {0};
 #pragma unroll
-    for (int q = 0; q < 2; ++q) {
+    for (int q = 0; q < 4; ++q) {
         const int wj = w0 + q;
         if (wj < w1) {
-            for (int mm = 0; mm < a.M; ++mm) u[q] |= ldcg_u32(a.masks + static_cast<size_t>(mm) * a.W + wj);
+            uint32_t v[kBgMaxM];  // every vector's word in flight at once
+#pragma unroll
+            for (int mm = 0; mm < kBgMaxM; ++mm)
+                v[mm] = mm < a.M ? ldcg_u32(a.masks + static_cast<size_t>(mm) * a.W + wj) : 0u;
+#pragma unroll
+            for (int mm = 0; mm < kBgMaxM; ++mm) u[q] |= v[mm];
             cnt[0] += __popc(u[q]);
         }
     }
     int pre[1], tot[1];
-    block_scan<NT, 1>(cnt, pre, tot, reinterpret_cast<int*>(red));
+    block_scan<NT, 1>(cnt, pre, tot, scratch);
+    const int U = tot[0];
+    const int lo = static_cast<int>(static_cast<long long>(U) * b / kBuCtas);
+    const int hi = static_cast<int>(static_cast<long long>(U) * (b + 1) / kBuCtas);
+    if (b == 0 && tid == 0) a.ctr[1] = static_cast<unsigned>(U);
     int pos = pre[0];
-    uint16_t* ucols = reinterpret_cast<uint16_t*>(xs);  // x of this CTA is no longer needed
 #pragma unroll
-    for (int q = 0; q < 2; ++q) {
-        const int wj = w0 + q;
-        if (wj < w1) {
-            uint32_t rest = u[q];
-            while (rest) {
-                const int col = 32 * wj + __ffs(rest) - 1;
-                a.ulist[pos] = static_cast<uint32_t>(col);
-                ucols[pos++] = static_cast<uint16_t>(col);
-                rest &= rest - 1u;
+    for (int q = 0; q < 4; ++q) {
+        uint32_t rest = u[q];
+        while (rest && pos < hi) {
+            const int col = 32 * (w0 + q) + __ffs(rest) - 1;
+            if (pos >= lo) {
+                pcol[pos - lo] = static_cast<uint16_t>(col);
+                a.ulist[pos] = static_cast<uint16_t>(col);
             }
+            ++pos;
+            rest &= rest - 1u;
         }
     }
     __syncthreads();
-    // x_o[u][:] = the outlier-only rows at union column u, all loads of a
-    // thread in flight together; the last batch of 16 is padded with zeros.
-    const int U = tot[0];
-    const int upad = (U + 15) & ~15;
-    for (int u0 = tid; u0 < upad; u0 += NT) {
-        uint16_t v[kBgMaxM];
-        const int col = u0 < U ? ucols[u0] : 0;
-#pragma unroll
-        for (int mm = 0; mm < kBgMaxM; ++mm)
-            v[mm] = (u0 < U && mm < a.MP) ? ldcg_u16(a.xrow + static_cast<size_t>(mm) * a.d_in + col)
-                                          : static_cast<uint16_t>(0);
-        uint4* dst = reinterpret_cast<uint4*>(a.xo + static_cast<size_t>(u0) * a.MP);
-        dst[0] = make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], v[3]), pack_h2(v[4], v[5]), pack_h2(v[6], v[7]));
-        if (a.MP == 16)
-            dst[1] = make_uint4(pack_h2(v[8], v[9]), pack_h2(v[10], v[11]), pack_h2(v[12], v[13]), pack_h2(v[14], v[15]));
+    const int n = hi - lo;
+    for (int i = tid; i < n * a.MP; i += NT) {
+        const int p = i / a.MP, mm = i - p * a.MP;
+        const uint16_t v = mm < a.M ? ldcg_u16(a.xrow + static_cast<size_t>(mm) * a.d_in + pcol[p]) : uint16_t{0};
+        a.xo[static_cast<size_t>(lo + p) * a.MP + mm] = v;
     }
-    if (tid == 0) {
-        a.ctr[1] = static_cast<unsigned>(tot[0]);
-        a.ctr[0] = 0u;  // ready for the next call
+    if (b == kBuCtas - 1) {
+        const int upad = (U + 15) & ~15;
+        for (int i = tid; i < (upad - U) * a.MP; i += NT) a.xo[static_cast<size_t>(U) * a.MP + i] = 0;
     }
 }
 
@@ -220,7 +264,7 @@ enum : int {
 struct BOArgs {
     const uint16_t* w16;     // row-major FP16 [d_out][d_in]
     const uint16_t* w16_cm;  // column-major mirror [d_in][d_out]
-    const uint32_t* ulist;
+    const uint16_t* ulist;   // [d_in] union columns, ascending
     const uint16_t* xo;      // [d_in][MP] by union position
     const unsigned int* ctr;
     const float* dpart;      // [nslab][MP][d_out] the INT4 part's partial sums
@@ -228,20 +272,26 @@ struct BOArgs {
     int d_out, d_in, MP, M, nslab;
 };
 
-// One CTA per 16-row block.
+// One CTA per 16-row block.  Dynamic shared memory: the union's columns
+// (2 bytes each, room for d_in), copied in at the start, so that no copy of a
+// column segment waits on a load of its column index.
 template <int kOut, int NT>
 __global__ void __launch_bounds__(kBgOutWarps * 32) bout_kernel(const BOArgs a) {
     constexpr int MP = 8 * NT;
     __shared__ __align__(128) unsigned char abuf[kBgOutWarps][kBgOutBufs][512];  // 16 columns x 16 rows
     __shared__ __align__(128) unsigned char bbuf[kBgOutWarps][kBgOutBufs][512];  // 16 columns x 16 vectors
     __shared__ float red[kBgOutWarps][NT][4][32];
+    extern __shared__ __align__(16) uint16_t ucol[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int rb = blockIdx.x;
 
-    // The plan kernel has completed (the dense kernel let this grid launch
-    // only after its own wait for it): the union and x_o can be read now.
+    // The plan kernels have completed (the dense kernel let this grid launch
+    // only after its own wait for them): the union and x_o can be read now.
     pdl_launch_dependents();
     const int U = static_cast<int>(ldcg_u32(a.ctr + 1));
+    for (int i = threadIdx.x; 8 * i < U; i += kBgOutWarps * 32)
+        reinterpret_cast<uint4*>(ucol)[i] = ldcg_v4(a.ulist + 8 * i);
+    __syncthreads();
     const int nbat = (U + 15) / 16;
     const int nb = warp < nbat ? (nbat - warp + kBgOutWarps - 1) / kBgOutWarps : 0;  // batches warp, warp + 8, ...
     const uint32_t wa = smem_u32(&abuf[warp][0][0]), wb = smem_u32(&bbuf[warp][0][0]);
@@ -255,7 +305,7 @@ __global__ void __launch_bounds__(kBgOutWarps * 32) bout_kernel(const BOArgs a) 
         const uint32_t da = wa + (k % kBgOutBufs) * 512 + 16 * lane;
         const uint32_t db = wb + (k % kBgOutBufs) * 512 + 16 * lane;
         const bool valid = kc < U;
-        const int col = valid ? static_cast<int>(ldcg_u32(a.ulist + kc)) : 0;
+        const int col = valid ? static_cast<int>(ucol[kc]) : 0;
         if (kc < ((U + 15) & ~15) && (MP == 16 || half == 0))
             cp_async16(db, a.xo + static_cast<size_t>(kc) * MP + 8 * half);
         else sts_v4(db, make_uint4(0, 0, 0, 0));
@@ -332,10 +382,10 @@ __global__ void __launch_bounds__(kBgOutWarps * 32) bout_kernel(const BOArgs a) 
 // ---------------------------------------------------------------------------
 struct BDArgs {
     const uint8_t* native;   // unit layout
-    const uint16_t* x;       // [M][d_in]
-    const uint32_t* masks;   // [kBgMaxM][W]
+    const uint4* xtab;       // [NC][4][4][MP][4] x' tables of the plan kernel
+    const float4* xsum;      // [NC][4][MP]
     float* dpart;            // [nslab][MP][d_out]
-    int M, d_out, d_in, NC, NRB, S, nslab, cps, W;
+    int M, d_out, d_in, NC, NRB, S, nslab, cps;
     int pf_rb;               // row blocks per warp (from its first) pulled into L2 before the plan is ready
     int sm_ring, sm_bars, sm_xtab, sm_xsum;
 };
@@ -348,7 +398,7 @@ inline BDSmem bd_smem(int S, int MP) {
     BDSmem L;
     int off = 0;
     L.ring = off; off += kBgWarps * kBgStages * kUnit;
-    L.bars = off; off += (kBgWarps * kBgStages * 8 + 127) / 128 * 128;
+    L.bars = off; off += (kBgWarps * kBgStages * 8 + 8 + 127) / 128 * 128;  // + the tables' mbarrier
     L.xtab = off; off += S * MP * 1024;
     L.xsum = off; off += S * kB1ChunkGroups * MP * 16;
     L.total = off;
@@ -358,7 +408,6 @@ inline BDSmem bd_smem(int S, int MP) {
 template <int NT>
 __global__ void __launch_bounds__(kBgWarps * 32, 1) bdense_kernel(const BDArgs a) {
     constexpr int MP = 8 * NT;
-    constexpr int kT = kBgWarps * 32;
     extern __shared__ __align__(128) char smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t = lane & 3;
@@ -384,12 +433,14 @@ __global__ void __launch_bounds__(kBgWarps * 32, 1) bdense_kernel(const BDArgs a
         mbar_arrive_expect_tx(bar, kUnit);
         bulk_g2s(ring + s * kUnit, a.native + unit_of(j) * kUnit, kUnit, bar);
     };
+    const uint32_t xbar = smem_u32(smem + a.sm_bars) + kBgWarps * kBgStages * 8;  // the x' tables
 
     // The weights do not depend on the preceding kernels: the first stages go
     // out before griddepcontrol.wait, and the warp's first pf_rb row blocks
     // (each one contiguous run of nch units) are pulled into L2 meanwhile, so
-    // the stream runs while the plan kernel works.
+    // the stream runs while the plan kernels work.
     uint32_t armed = 0;
+    if (tid == 0) mbar_init(xbar, 1);
     if (lane == 0) {
 #pragma unroll
         for (int s = 0; s < kBgStages; ++s) mbar_init(bars + 8 * s, 1);
@@ -403,68 +454,21 @@ __global__ void __launch_bounds__(kBgWarps * 32, 1) bdense_kernel(const BDArgs a
 #pragma unroll
     for (int s = 0; s < kBgStages; ++s)
         if (s < wn) armed |= 1u << s;
-    __syncwarp();
+    __syncthreads();  // the tables' mbarrier is initialised
 
-    pdl_wait();  // x and the masks come from the plan kernel
+    pdl_wait();  // the x' tables come from the plan kernel
     pdl_launch_dependents();  // only now: the FP16-part kernel reads the plan before its own wait
     if (rb1 <= rb0) return;  // no row blocks (no copies were issued)
 
-    // x' of this slab's chunks for every vector, in MMA B order: piece p
-    // (8 columns) of chunk cc, vector tok goes to [cc][group p >> 4][slice
-    // (p >> 2) & 3][tok][p & 3] as the f16 pairs (x0,x4), (x2,x6), (x1,x5),
-    // (x3,x7), outliers of tok zeroed; xsum[cc][group][tok] = (1024 sum x'
-    // even columns, 1024 sum x' odd columns, sum x', 0).  16 consecutive
-    // threads hold the 16 pieces of one (chunk, group, vector).
-    // All of a thread's loads go out first (at most kMaxXP pieces), then the
-    // pieces are processed.
-    constexpr int kMaxXP = 4096 / kT;  // S * MP <= 64
-    static_assert(kMaxXP * kT == 4096, "x' pieces per thread");
-    const int npc = nch * MP * 64;
-    uint4 xv[kMaxXP];
-    uint32_t xm[kMaxXP];
-#pragma unroll
-    for (int k = 0; k < kMaxXP; ++k) {
-        const int i = tid + k * kT;
-        const int p = i & 63, tok = (i >> 6) % MP, cc = i / (64 * MP);
-        const int col = (c0 + cc) * 512 + 8 * p;
-        xv[k] = make_uint4(0, 0, 0, 0);
-        xm[k] = 0;
-        if (i < npc && tok < a.M && col < a.d_in) {
-            xv[k] = ldcg_v4(a.x + static_cast<size_t>(tok) * a.d_in + col);
-            xm[k] = ldcg_u32(a.masks + static_cast<size_t>(tok) * a.W + (col >> 5));
-        }
+    // This slab's x' tables (chunks c0 .. c0 + nch - 1 of every vector), built
+    // once by the plan kernel: two bulk copies.
+    if (tid == 0) {
+        const uint32_t tb = static_cast<uint32_t>(nch) * MP * 1024, sb2 = static_cast<uint32_t>(nch) * 4 * MP * 16;
+        mbar_arrive_expect_tx(xbar, tb + sb2);
+        bulk_g2s(smem_u32(xtab), a.xtab + static_cast<size_t>(c0) * MP * 64, tb, xbar);
+        bulk_g2s(smem_u32(xsum), a.xsum + static_cast<size_t>(c0) * 4 * MP, sb2, xbar);
     }
-#pragma unroll
-    for (int k = 0; k < kMaxXP; ++k) {
-        const int i = tid + k * kT;
-        if (k * kT >= npc) break;  // uniform
-        const int p = i & 63, tok = (i >> 6) % MP, cc = i / (64 * MP);
-        const int col = (c0 + cc) * 512 + 8 * p;
-        uint4 w = xv[k];
-        const uint32_t mb = (xm[k] >> (col & 31)) & 0xFFu;
-        if (mb) {
-            uint32_t keep[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-                keep[q] = ((mb >> (2 * q)) & 1u ? 0u : 0x0000FFFFu) | ((mb >> (2 * q + 1)) & 1u ? 0u : 0xFFFF0000u);
-            w.x &= keep[0];
-            w.y &= keep[1];
-            w.z &= keep[2];
-            w.w &= keep[3];
-        }
-        float pe = add_f16_f32(lo16(w.w), add_f16_f32(lo16(w.z), add_f16_f32(lo16(w.y), add_f16_f32(lo16(w.x), 0.f))));
-        float po = add_f16_f32(hi16(w.w), add_f16_f32(hi16(w.z), add_f16_f32(hi16(w.y), add_f16_f32(hi16(w.x), 0.f))));
-        xtab[(((cc * 4 + (p >> 4)) * 4 + ((p >> 2) & 3)) * MP + tok) * 4 + (p & 3)] =
-            make_uint4((w.x & 0xFFFFu) | (w.z << 16), (w.y & 0xFFFFu) | (w.w << 16), (w.x >> 16) | (w.z & 0xFFFF0000u),
-                       (w.y >> 16) | (w.w & 0xFFFF0000u));
-#pragma unroll
-        for (int o = 8; o >= 1; o >>= 1) {
-            pe += __shfl_xor_sync(0xffffffffu, pe, o);
-            po += __shfl_xor_sync(0xffffffffu, po, o);
-        }
-        if ((i & 15) == 0) xsum[(cc * 4 + (p >> 4)) * MP + tok] = make_float4(1024.f * pe, 1024.f * po, pe + po, 0.f);
-    }
-    __syncthreads();
+    const bool xok = mbar_wait_bounded(xbar, 0u);
 
     const uint32_t xtab_a = smem_u32(xtab);
     const uint32_t xsum_a = smem_u32(xsum);
@@ -488,9 +492,10 @@ __global__ void __launch_bounds__(kBgWarps * 32, 1) bdense_kernel(const BDArgs a
             }
     };
 
-    bool ok = true;
+    bool ok = __all_sync(0xffffffffu, xok);
+    if (!ok && lane == 0) atomicOr(&g_berror_word, 1u);
     uint32_t phase = 0;
-    for (int j = 0; j < wn; ++j) {
+    for (int j = 0; ok && j < wn; ++j) {
         const int s = j % kBgStages;
         const bool got = mbar_wait_bounded(bars + 8 * s, (phase >> s) & 1u);
         if (!__all_sync(0xffffffffu, got)) {
@@ -552,6 +557,7 @@ __global__ void __launch_bounds__(kBgWarps * 32, 1) bdense_kernel(const BDArgs a
     }
     if (!ok) {
         // Do not leave copies in flight into shared memory this CTA is about to release.
+        if (!xok) mbar_wait_bounded(xbar, 0u);
 #pragma unroll
         for (int s = 0; s < kBgStages; ++s)
             if (armed & (1u << s)) mbar_wait_bounded(bars + 8 * s, (phase >> s) & 1u);
@@ -605,17 +611,22 @@ dq_status_t launch_pdl(K kernel, dim3 grid, int threads, int smem, cudaStream_t 
 
 template <int kOut, int NT>
 dq_status_t launch_bout(const BOArgs& a, int grid, cudaStream_t stream) {
-    return launch_pdl(bout_kernel<kOut, NT>, dim3(grid), kBgOutWarps * 32, 0, stream, a);
+    const int smem = align16(2 * a.d_in) + 16;  // the union's columns
+    const dq_status_t st = ensure_smem(bout_kernel<kOut, NT>, 3 + 2 * kOut + (NT - 1), smem);
+    if (st != DQ_OK) return st;
+    return launch_pdl(bout_kernel<kOut, NT>, dim3(grid), kBgOutWarps * 32, smem, stream, a);
 }
 
 template <int NT>
-dq_status_t launch_batched_nt(const BgGeom& G, const BPArgs& pa, const BOArgs& oa, int out_mode, int ogrid,
-                              const BDArgs& da, int dsmem, cudaStream_t stream) {
+dq_status_t launch_batched_nt(const BgGeom& G, const BPArgs& pa, const BUArgs& ua, const BOArgs& oa, int out_mode,
+                              int ogrid, const BDArgs& da, int dsmem, cudaStream_t stream) {
     dq_status_t st = ensure_smem(bplan_kernel, 0, pa.S.total);
     if (st != DQ_OK) return st;
     st = ensure_smem(bdense_kernel<NT>, NT, dsmem);
     if (st != DQ_OK) return st;
-    st = launch_pdl(bplan_kernel, dim3(G.M), kStatThreads, pa.S.total, stream, pa);
+    st = launch_pdl(bplan_kernel, dim3(G.MP), kStatThreads, pa.S.total, stream, pa);
+    if (st != DQ_OK) return st;
+    st = launch_pdl(bunion_kernel, dim3(kBuCtas), kBuThreads, 0, stream, ua);
     if (st != DQ_OK) return st;
     st = launch_pdl(bdense_kernel<NT>, dim3(da.cps, G.nslab), kBgWarps * 32, dsmem, stream, da);
     if (st != DQ_OK) return st;
@@ -642,10 +653,9 @@ dq_status_t launch_gemv_batched(const dq_weights_t& w, const uint16_t* x, uint16
     BPArgs pa;
     pa.x = x;
     pa.masks = reinterpret_cast<uint32_t*>(ws + L.masks);
-    pa.ulist = reinterpret_cast<uint32_t*>(ws + L.ulist);
-    pa.xo = reinterpret_cast<uint16_t*>(ws + L.xo);
     pa.xrow = reinterpret_cast<uint16_t*>(ws + L.xrow);
-    pa.ctr = reinterpret_cast<unsigned int*>(ws + L.ctr);
+    pa.xtab = reinterpret_cast<uint4*>(ws + L.xtab);
+    pa.xsum = reinterpret_cast<float4*>(ws + L.xsum);
     pa.k = k;
     pa.inv_n = 1.0f / static_cast<float>(w.d_in);
     pa.inv_n1 = w.d_in > 1 ? 1.0f / static_cast<float>(w.d_in - 1) : 0.f;
@@ -653,16 +663,27 @@ dq_status_t launch_gemv_batched(const dq_weights_t& w, const uint16_t* x, uint16
     pa.MP = G.MP;
     pa.d_in = w.d_in;
     pa.W = G.W;
-    pa.NRB = G.NRB;
+    pa.NC = G.NC;
     pa.S = bp_smem(w.d_in);
     if (pa.S.total > di.smem_optin) return DQ_ERR_UNSUPPORTED;
+
+    BUArgs ua;
+    ua.masks = pa.masks;
+    ua.xrow = pa.xrow;
+    ua.ulist = reinterpret_cast<uint16_t*>(ws + L.ulist);
+    ua.xo = reinterpret_cast<uint16_t*>(ws + L.xo);
+    ua.ctr = reinterpret_cast<unsigned int*>(ws + L.ctr);
+    ua.M = M;
+    ua.MP = G.MP;
+    ua.d_in = w.d_in;
+    ua.W = G.W;
 
     BOArgs oa;
     oa.w16 = w.fp16;
     oa.w16_cm = w.fp16_cm;
-    oa.ulist = pa.ulist;
-    oa.xo = pa.xo;
-    oa.ctr = pa.ctr;
+    oa.ulist = ua.ulist;
+    oa.xo = ua.xo;
+    oa.ctr = ua.ctr;
     oa.dpart = reinterpret_cast<float*>(ws + L.dpart);
     oa.y = y;
     oa.d_out = w.d_out;
@@ -675,8 +696,8 @@ dq_status_t launch_gemv_batched(const dq_weights_t& w, const uint16_t* x, uint16
 
     BDArgs da;
     da.native = w.native;
-    da.x = x;
-    da.masks = pa.masks;
+    da.xtab = pa.xtab;
+    da.xsum = pa.xsum;
     da.dpart = reinterpret_cast<float*>(ws + L.dpart);
     da.M = M;
     da.d_out = w.d_out;
@@ -686,7 +707,6 @@ dq_status_t launch_gemv_batched(const dq_weights_t& w, const uint16_t* x, uint16
     da.S = G.S;
     da.nslab = G.nslab;
     da.cps = std::max(1, std::min(G.NRB, di.sm_count / G.nslab));
-    da.W = G.W;
     {
         // L2 prefetch of the weights during the plan: all of them when they
         // take at most kBgPrefetchBytes, else that share of each warp's rows.
@@ -700,8 +720,8 @@ dq_status_t launch_gemv_batched(const dq_weights_t& w, const uint16_t* x, uint16
     da.sm_xtab = DS.xtab;
     da.sm_xsum = DS.xsum;
 
-    return G.NT == 1 ? launch_batched_nt<1>(G, pa, oa, out_mode, ogrid, da, DS.total, stream)
-                     : launch_batched_nt<2>(G, pa, oa, out_mode, ogrid, da, DS.total, stream);
+    return G.NT == 1 ? launch_batched_nt<1>(G, pa, ua, oa, out_mode, ogrid, da, DS.total, stream)
+                     : launch_batched_nt<2>(G, pa, ua, oa, out_mode, ogrid, da, DS.total, stream);
 }
 
 dq_status_t read_batched_error(uint32_t* word, bool clear) {

@@ -292,6 +292,9 @@ constexpr int kBgWarps = 16;      // warps of a dense CTA (one CTA per SM)
 constexpr int kBgStages = 2;      // bulk-copy ring stages per warp
 constexpr int kBgOutWarps = 8;    // warps of an FP16-part CTA
 constexpr int kBgOutBufs = 3;     // per-warp outlier segment buffers in flight
+constexpr int kBuCtas = 128;      // CTAs of the union kernel
+constexpr int kBuThreads = 256;   // threads of a union CTA
+constexpr int kBuMaxPos = 256;    // union positions per union CTA at most (kMaxDIn / kBuCtas, rounded up)
 constexpr double kBgPrefetchBytes = 64.0 * 1024 * 1024;  // L2 the batched INT4 part claims ahead of the plan
 constexpr int kBgRefSMs = 148;    // SM count the slab width is chosen for (keeps the workspace device-independent)
 
@@ -319,16 +322,18 @@ inline BgGeom bg_geom(int d_out, int d_in, int M) {
 }
 
 // Workspace of a batched call, after the batch-1 region (ws_layout): byte
-// offsets from the start of the workspace.  Only ctr[0] must be zero on entry
-// (at a fixed offset; every call leaves it zero); the rest is scratch.
-//   ctr    [0] plan arrival counter, [1] union size
+// offsets from the start of the workspace.  All of it is scratch that a call
+// writes before it reads it.
+//   ctr    [0] unused (zero), [1] union size
 //   masks  [kBgMaxM][W] outlier bits of each vector
-//   ulist  [d_in] the union of the masks, ascending columns
+//   ulist  [d_in] u16: the union of the masks, ascending columns
 //   xrow   [MP][d_in] FP16: x[m][c] where column c is an outlier of vector m, else 0
 //   xo     [d_in][MP] FP16: xrow[m][ulist[u]] at [u][m], u < U rounded up to 16
+//   xtab   [NC][4][4][MP][4] 16-byte MMA B pieces of x' (each vector's outliers zeroed)
+//   xsum   [NC][4][MP] float4 per-group sums of x'
 //   dpart  [nslab][MP][d_out] FP32 per-slab partial sums of the INT4 part
 struct BgWs {
-    size_t ctr, masks, ulist, xrow, xo, dpart, total;
+    size_t ctr, masks, ulist, xrow, xo, xtab, xsum, dpart, total;
 };
 
 inline BgWs bg_ws(const BgGeom& g, int d_out, int d_in);
@@ -371,7 +376,9 @@ inline BgWs bg_ws(const BgGeom& g, int d_out, int d_in) {
     L.masks = off; off += align256(static_cast<size_t>(kBgMaxM) * g.W * 4);
     L.ulist = off; off += align256(static_cast<size_t>(d_in) * 4);
     L.xrow = off;  off += align256(static_cast<size_t>(d_in) * g.MP * 2);
-    L.xo = off;    off += align256(static_cast<size_t>(d_in) * g.MP * 2);
+    L.xo = off;    off += align256(static_cast<size_t>(d_in + 16) * g.MP * 2);
+    L.xtab = off;  off += align256(static_cast<size_t>(g.NC) * g.MP * 1024);
+    L.xsum = off;  off += align256(static_cast<size_t>(g.NC) * 4 * g.MP * 16);
     L.dpart = off; off += align256(static_cast<size_t>(g.nslab) * g.MP * d_out * 4);
     L.total = off;
     return L;
