@@ -4,22 +4,21 @@
 // applied to each vector with its own statistics and outlier mask, while the
 // weights stream from HBM once for all vectors.
 //
-// Four kernels, chained on the stream by programmatic dependent launch:
+// Three kernels, chained on the stream by programmatic dependent launch:
 //  1. bplan_kernel, one CTA per vector: the statistics and the outlier mask
 //     of x[m], with the code and the fixed partition of the batch-1 kernel
 //     (dq_plan.cuh), so each vector gets exactly the batch-1 mask; the CTA
 //     writes its vector's outlier-only row (x[m][c] where c is an outlier of
 //     m, else 0) and its share of the x' tables (the MMA B operands of every
 //     chunk, outliers zeroed, and the per-group sums).
-//  1b. bunion_kernel, 128 CTAs: each derives the union of the M masks
-//     (ascending columns) and gathers its share of the union's columns of
-//     the outlier-only rows into x_o[u][m], one union column's vectors
-//     contiguous.
 //  2. bdense_kernel: the INT4 part over x', split over K: CTA (cx, slab)
 //     copies its slab's x' tables in with two bulk copies and streams chunks
 //     [slab S, slab S + S) of the row blocks [rb0, rb1) through per-warp
 //     cp.async.bulk rings.  Each warp owns whole row blocks and writes its
-//     slab's partial sums.
+//     slab's partial sums.  While the tables arrive, every CTA derives the
+//     union of the M masks (ascending columns) and gathers its share of the
+//     union's columns of the outlier-only rows into x_o[u][m], one union
+//     column's vectors contiguous.
 //  3. bout_kernel, one CTA per 16-row block: the FP16 part,
 //     Y_o = W16[:, union] x_o, on the tensor cores, then y = the slabs'
 //     partial sums + Y_o, in a fixed order (results do not depend on timing).
@@ -27,8 +26,8 @@
 //     segments (16 rows of a column, contiguous in the column-major mirror)
 //     and the B segments (the column's x_o values) come in by 16-byte cp.async
 //     and ldmatrix.trans; the eight warps' sums are added in a fixed order.
-//     It depends on the plan only until the INT4 part is needed, so its
-//     tensor-core work starts as the dense kernel's CTAs drain.
+//     Its CTAs start as the dense kernel's CTAs drain (those hold all of an
+//     SM's registers), after the dense kernel has completed.
 //
 // Tensor-core formulation of the INT4 part (mma.sync.m16n8k16, f16 x f16 ->
 // f32; 16 weight rows x 8 vectors x 16 columns of one 128-column group).
@@ -175,7 +174,7 @@ __global__ void __launch_bounds__(kStatThreads, 1) bplan_kernel(const BPArgs a) 
 }
 
 // ---------------------------------------------------------------------------
-// 1b. Union of the masks and the outlier columns' x
+// 1b. Union of the masks and the outlier columns' x (run by the INT4-part CTAs)
 // ---------------------------------------------------------------------------
 struct BUArgs {
     const uint32_t* masks;  // [kBgMaxM][W]
@@ -186,28 +185,24 @@ struct BUArgs {
     int M, MP, d_in, W;
 };
 
-// kBuCtas CTAs.  Every CTA derives the union of the M masks and its prefix
-// (ascending columns) itself, then takes the union positions
-// [U b / kBuCtas, U (b + 1) / kBuCtas): their columns into ulist and
-// xo[u][m] = xrow[m][column] (zero for the padding vectors m >= M); the last
-// CTA also zeroes the positions U .. (U rounded up to 16) - 1.
-__global__ void __launch_bounds__(kBuThreads) bunion_kernel(const BUArgs a) {
-    constexpr int NT = kBuThreads;
-    static_assert(kMaxDIn / 32 <= 4 * NT, "union words per thread");
-    static_assert(kMaxDIn <= kBuCtas * kBuMaxPos, "union positions per CTA");
-    __shared__ int scratch[NT / 32];
-    __shared__ uint16_t pcol[kBuMaxPos];
-    const int tid = threadIdx.x, b = blockIdx.x;
-
-    pdl_launch_dependents();
-    pdl_wait();  // the masks and rows of the plan kernel
+// CTA b of G: derives the union of the M masks and its prefix (ascending
+// columns) itself, then takes the union positions [U b / G, U (b + 1) / G):
+// their columns into ulist and xo[u][m] = xrow[m][column] (zero for the
+// padding vectors m >= M); CTA G - 1 also zeroes the positions
+// U .. (U rounded up to 16) - 1, and CTA 0 stores U.  NT threads, all of them
+// calling; barrier-synchronised.  scratch: NT / 32 ints; pcol: kBuMaxPos u16.
+template <int NT>
+__device__ void union_share(const BUArgs& a, int b, int G, int* scratch, uint16_t* pcol) {
+    constexpr int kWq = (kMaxDIn / 32 + NT - 1) / NT;  // mask words per thread at most
+    const int tid = threadIdx.x;
     const int w0 = static_cast<int>(static_cast<long long>(tid) * a.W / NT);
     const int w1 = static_cast<int>(static_cast<long long>(tid + 1) * a.W / NT);
-    uint32_t u[4] = {0u, 0u, 0u, 0u};
+    uint32_t u[kWq];
     int cnt[1] = {0};
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < kWq; ++q) {
         const int wj = w0 + q;
+        u[q] = 0u;
         if (wj < w1) {
             uint32_t v[kBgMaxM];  // every vector's word in flight at once
 #pragma unroll
@@ -221,31 +216,37 @@ __global__ void __launch_bounds__(kBuThreads) bunion_kernel(const BUArgs a) {
     int pre[1], tot[1];
     block_scan<NT, 1>(cnt, pre, tot, scratch);
     const int U = tot[0];
-    const int lo = static_cast<int>(static_cast<long long>(U) * b / kBuCtas);
-    const int hi = static_cast<int>(static_cast<long long>(U) * (b + 1) / kBuCtas);
+    const int lo = static_cast<int>(static_cast<long long>(U) * b / G);
+    const int hi = static_cast<int>(static_cast<long long>(U) * (b + 1) / G);
     if (b == 0 && tid == 0) a.ctr[1] = static_cast<unsigned>(U);
-    int pos = pre[0];
+    // The share in windows of kBuMaxPos positions: their columns into pcol
+    // (by the threads owning their mask words), then the gather by all.
+    for (int wlo = lo; wlo < hi; wlo += kBuMaxPos) {
+        const int whi = min(hi, wlo + kBuMaxPos);
+        int pos = pre[0];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        uint32_t rest = u[q];
-        while (rest && pos < hi) {
-            const int col = 32 * (w0 + q) + __ffs(rest) - 1;
-            if (pos >= lo) {
-                pcol[pos - lo] = static_cast<uint16_t>(col);
-                a.ulist[pos] = static_cast<uint16_t>(col);
+        for (int q = 0; q < kWq; ++q) {
+            uint32_t rest = u[q];
+            while (rest && pos < whi) {
+                const int col = 32 * (w0 + q) + __ffs(rest) - 1;
+                if (pos >= wlo) {
+                    pcol[pos - wlo] = static_cast<uint16_t>(col);
+                    a.ulist[pos] = static_cast<uint16_t>(col);
+                }
+                ++pos;
+                rest &= rest - 1u;
             }
-            ++pos;
-            rest &= rest - 1u;
         }
+        __syncthreads();
+        const int n = whi - wlo;
+        for (int i = tid; i < n * a.MP; i += NT) {
+            const int p = i / a.MP, mm = i - p * a.MP;
+            const uint16_t v = mm < a.M ? ldcg_u16(a.xrow + static_cast<size_t>(mm) * a.d_in + pcol[p]) : uint16_t{0};
+            a.xo[static_cast<size_t>(wlo + p) * a.MP + mm] = v;
+        }
+        __syncthreads();  // pcol is rewritten by the next window
     }
-    __syncthreads();
-    const int n = hi - lo;
-    for (int i = tid; i < n * a.MP; i += NT) {
-        const int p = i / a.MP, mm = i - p * a.MP;
-        const uint16_t v = mm < a.M ? ldcg_u16(a.xrow + static_cast<size_t>(mm) * a.d_in + pcol[p]) : uint16_t{0};
-        a.xo[static_cast<size_t>(lo + p) * a.MP + mm] = v;
-    }
-    if (b == kBuCtas - 1) {
+    if (b == G - 1) {
         const int upad = (U + 15) & ~15;
         for (int i = tid; i < (upad - U) * a.MP; i += NT) a.xo[static_cast<size_t>(U) * a.MP + i] = 0;
     }
@@ -285,9 +286,10 @@ __global__ void __launch_bounds__(kBgOutWarps * 32) bout_kernel(const BOArgs a) 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int rb = blockIdx.x;
 
-    // The plan kernels have completed (the dense kernel let this grid launch
-    // only after its own wait for them): the union and x_o can be read now.
+    // The union and x_o come from the INT4-part kernel's CTAs (which hold all
+    // of the SMs' registers, so this grid's CTAs start as they drain).
     pdl_launch_dependents();
+    pdl_wait();
     const int U = static_cast<int>(ldcg_u32(a.ctr + 1));
     for (int i = threadIdx.x; 8 * i < U; i += kBgOutWarps * 32)
         reinterpret_cast<uint4*>(ucol)[i] = ldcg_v4(a.ulist + 8 * i);
@@ -354,7 +356,6 @@ __global__ void __launch_bounds__(kBgOutWarps * 32) bout_kernel(const BOArgs a) 
 #pragma unroll
         for (int e = 0; e < 4; ++e) red[warp][nt][e][lane] = d[nt][e];
     __syncthreads();
-    pdl_wait();  // the dense kernel's partial sums
     for (int i = threadIdx.x; i < NT * 4 * 32; i += kBgOutWarps * 32) {
         const int nt = i >> 7, e = (i >> 5) & 3, ln = i & 31;
         const int row = rb * kRowBlock + (ln >> 2) + 8 * (e >> 1);
@@ -385,6 +386,7 @@ struct BDArgs {
     const uint4* xtab;       // [NC][4][4][MP][4] x' tables of the plan kernel
     const float4* xsum;      // [NC][4][MP]
     float* dpart;            // [nslab][MP][d_out]
+    BUArgs un;               // the union and x_o, a share per CTA
     int M, d_out, d_in, NC, NRB, S, nslab, cps;
     int pf_rb;               // row blocks per warp (from its first) pulled into L2 before the plan is ready
     int sm_ring, sm_bars, sm_xtab, sm_xsum;
@@ -456,18 +458,24 @@ __global__ void __launch_bounds__(kBgWarps * 32, 1) bdense_kernel(const BDArgs a
         if (s < wn) armed |= 1u << s;
     __syncthreads();  // the tables' mbarrier is initialised
 
-    pdl_wait();  // the x' tables come from the plan kernel
-    pdl_launch_dependents();  // only now: the FP16-part kernel reads the plan before its own wait
-    if (rb1 <= rb0) return;  // no row blocks (no copies were issued)
+    pdl_wait();  // the x' tables, masks and rows come from the plan kernel
+    pdl_launch_dependents();
 
     // This slab's x' tables (chunks c0 .. c0 + nch - 1 of every vector), built
-    // once by the plan kernel: two bulk copies.
-    if (tid == 0) {
+    // once by the plan kernel: two bulk copies, in flight while the CTA does
+    // its share of the union and x_o for the FP16-part kernel.
+    if (tid == 0 && rb1 > rb0) {
         const uint32_t tb = static_cast<uint32_t>(nch) * MP * 1024, sb2 = static_cast<uint32_t>(nch) * 4 * MP * 16;
         mbar_arrive_expect_tx(xbar, tb + sb2);
         bulk_g2s(smem_u32(xtab), a.xtab + static_cast<size_t>(c0) * MP * 64, tb, xbar);
         bulk_g2s(smem_u32(xsum), a.xsum + static_cast<size_t>(c0) * 4 * MP, sb2, xbar);
     }
+    {
+        __shared__ int uscratch[kBgWarps];
+        __shared__ uint16_t pcol[kBuMaxPos];
+        union_share<kBgWarps * 32>(a.un, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y, uscratch, pcol);
+    }
+    if (rb1 <= rb0) return;  // no row blocks (no copies were issued)
     const bool xok = mbar_wait_bounded(xbar, 0u);
 
     const uint32_t xtab_a = smem_u32(xtab);
@@ -626,8 +634,6 @@ dq_status_t launch_batched_nt(const BgGeom& G, const BPArgs& pa, const BUArgs& u
     if (st != DQ_OK) return st;
     st = launch_pdl(bplan_kernel, dim3(G.MP), kStatThreads, pa.S.total, stream, pa);
     if (st != DQ_OK) return st;
-    st = launch_pdl(bunion_kernel, dim3(kBuCtas), kBuThreads, 0, stream, ua);
-    if (st != DQ_OK) return st;
     st = launch_pdl(bdense_kernel<NT>, dim3(da.cps, G.nslab), kBgWarps * 32, dsmem, stream, da);
     if (st != DQ_OK) return st;
     switch (out_mode) {
@@ -698,6 +704,7 @@ dq_status_t launch_gemv_batched(const dq_weights_t& w, const uint16_t* x, uint16
     da.native = w.native;
     da.xtab = pa.xtab;
     da.xsum = pa.xsum;
+    da.un = ua;
     da.dpart = reinterpret_cast<float*>(ws + L.dpart);
     da.M = M;
     da.d_out = w.d_out;

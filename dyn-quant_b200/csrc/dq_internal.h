@@ -292,9 +292,7 @@ constexpr int kBgWarps = 16;      // warps of a dense CTA (one CTA per SM)
 constexpr int kBgStages = 2;      // bulk-copy ring stages per warp
 constexpr int kBgOutWarps = 8;    // warps of an FP16-part CTA
 constexpr int kBgOutBufs = 3;     // per-warp outlier segment buffers in flight
-constexpr int kBuCtas = 128;      // CTAs of the union kernel
-constexpr int kBuThreads = 256;   // threads of a union CTA
-constexpr int kBuMaxPos = 256;    // union positions per union CTA at most (kMaxDIn / kBuCtas, rounded up)
+constexpr int kBuMaxPos = 256;    // union positions an INT4-part CTA gathers per window
 constexpr double kBgPrefetchBytes = 64.0 * 1024 * 1024;  // L2 the batched INT4 part claims ahead of the plan
 constexpr int kBgRefSMs = 148;    // SM count the slab width is chosen for (keeps the workspace device-independent)
 
