@@ -273,18 +273,28 @@ struct BOArgs {
     int d_out, d_in, MP, M, nslab;
 };
 
-// One CTA per 16-row block.  Dynamic shared memory: the union's columns
-// (2 bytes each, room for d_in), copied in at the start, so that no copy of a
-// column segment waits on a load of its column index.
-template <int kOut, int NT>
+// One CTA per RB consecutive 16-row blocks (RB = 1, 2 or 4: column segments
+// of 32 RB contiguous bytes in the column-major mirror).  Dynamic shared
+// memory: per warp kBgOutBufs buffers of [16 columns x 16 RB rows of W16 |
+// 16 columns x 16 vectors of x_o], then the union's columns (2 bytes each,
+// room for d_in), copied in at the start, so that no copy of a column segment
+// waits on a load of its column index.  After the loop the buffers hold the
+// warps' sums.
+template <int RB>
+__host__ __device__ constexpr int bout_buf_bytes() { return RB * 512 + 512; }
+template <int RB>
+inline int bout_smem(int d_in) { return kBgOutWarps * kBgOutBufs * bout_buf_bytes<RB>() + align16(2 * d_in) + 16; }
+
+template <int kOut, int NT, int RB>
 __global__ void __launch_bounds__(kBgOutWarps * 32) bout_kernel(const BOArgs a) {
     constexpr int MP = 8 * NT;
-    __shared__ __align__(128) unsigned char abuf[kBgOutWarps][kBgOutBufs][512];  // 16 columns x 16 rows
-    __shared__ __align__(128) unsigned char bbuf[kBgOutWarps][kBgOutBufs][512];  // 16 columns x 16 vectors
-    __shared__ float red[kBgOutWarps][NT][4][32];
-    extern __shared__ __align__(16) uint16_t ucol[];
+    constexpr int kBuf = bout_buf_bytes<RB>();
+    constexpr int kA = RB * 512;  // A part of a buffer: column ci's RB * 16 rows at ci * 32 RB
+    static_assert(kBgOutWarps * RB * NT * 4 * 32 * 4 <= kBgOutWarps * kBgOutBufs * kBuf, "warp sums in the buffers");
+    extern __shared__ __align__(128) unsigned char osm[];
+    uint16_t* ucol = reinterpret_cast<uint16_t*>(osm + kBgOutWarps * kBgOutBufs * kBuf);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int rb = blockIdx.x;
+    const int rb0 = blockIdx.x * RB;
 
     // The union and x_o come from the INT4-part kernel's CTAs (which hold all
     // of the SMs' registers, so this grid's CTAs start as they drain).
@@ -296,69 +306,92 @@ __global__ void __launch_bounds__(kBgOutWarps * 32) bout_kernel(const BOArgs a) 
     __syncthreads();
     const int nbat = (U + 15) / 16;
     const int nb = warp < nbat ? (nbat - warp + kBgOutWarps - 1) / kBgOutWarps : 0;  // batches warp, warp + 8, ...
-    const uint32_t wa = smem_u32(&abuf[warp][0][0]), wb = smem_u32(&bbuf[warp][0][0]);
+    const uint32_t wbase = smem_u32(osm) + warp * kBgOutBufs * kBuf;
 
-    // Batch k of this warp into buffer k % kBgOutBufs: lane = (column lane >> 1
-    // of the batch, half lane & 1): 8 rows of W16 and 8 vectors of x_o.
+    // Batch k of this warp into buffer k % kBgOutBufs.  A: 16 columns x 2 RB
+    // pieces of 8 rows, piece i = lane + 32 j -> column i / (2 RB), rows
+    // 8 (i % (2 RB)) ..; B: lane = (column lane >> 1, half lane & 1), 8
+    // vectors of x_o.
     auto issue = [&](int k) {
-        const int kc = 16 * (warp + kBgOutWarps * k) + (lane >> 1);
-        const int half = lane & 1;
-        const int row0 = rb * kRowBlock + 8 * half;
-        const uint32_t da = wa + (k % kBgOutBufs) * 512 + 16 * lane;
-        const uint32_t db = wb + (k % kBgOutBufs) * 512 + 16 * lane;
-        const bool valid = kc < U;
-        const int col = valid ? static_cast<int>(ucol[kc]) : 0;
-        if (kc < ((U + 15) & ~15) && (MP == 16 || half == 0))
-            cp_async16(db, a.xo + static_cast<size_t>(kc) * MP + 8 * half);
-        else sts_v4(db, make_uint4(0, 0, 0, 0));
-        if (kOut == kBoStaged) {
-            if (valid && row0 < a.d_out) cp_async16(da, a.w16_cm + static_cast<size_t>(col) * a.d_out + row0);
-            else sts_v4(da, make_uint4(0, 0, 0, 0));
-        } else {
-            uint16_t h[8];
+        const int kb = 16 * (warp + kBgOutWarps * k);
+        const uint32_t buf = wbase + (k % kBgOutBufs) * kBuf;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int r = row0 + i;
-                h[i] = (valid && r < a.d_out)
-                           ? (kOut == kBoColDirect ? ldg_u16(a.w16_cm + static_cast<size_t>(col) * a.d_out + r)
-                                                   : ldg_u16(a.w16 + static_cast<size_t>(r) * a.d_in + col))
-                           : static_cast<uint16_t>(0);
+        for (int j = 0; j < RB; ++j) {
+            const int i = lane + 32 * j;
+            const int ci = i / (2 * RB), pi = i % (2 * RB);
+            const int kc = kb + ci;
+            const int row0 = rb0 * kRowBlock + 8 * pi;
+            const uint32_t da = buf + ci * (32 * RB) + 16 * pi;
+            const bool valid = kc < U;
+            const int col = valid ? static_cast<int>(ucol[kc]) : 0;
+            if (kOut == kBoStaged) {
+                if (valid && row0 < a.d_out) cp_async16(da, a.w16_cm + static_cast<size_t>(col) * a.d_out + row0);
+                else sts_v4(da, make_uint4(0, 0, 0, 0));
+            } else {
+                uint16_t h[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const int r = row0 + e;
+                    h[e] = (valid && r < a.d_out)
+                               ? (kOut == kBoColDirect ? ldg_u16(a.w16_cm + static_cast<size_t>(col) * a.d_out + r)
+                                                       : ldg_u16(a.w16 + static_cast<size_t>(r) * a.d_in + col))
+                               : static_cast<uint16_t>(0);
+                }
+                sts_v4(da, make_uint4(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]), pack_h2(h[4], h[5]),
+                                      pack_h2(h[6], h[7])));
             }
-            sts_v4(da, make_uint4(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]), pack_h2(h[4], h[5]),
-                                  pack_h2(h[6], h[7])));
+        }
+        {
+            const int kc = kb + (lane >> 1), half = lane & 1;
+            const uint32_t db = buf + kA + 16 * lane;
+            if (kc < ((U + 15) & ~15) && (MP == 16 || half == 0))
+                cp_async16(db, a.xo + static_cast<size_t>(kc) * MP + 8 * half);
+            else sts_v4(db, make_uint4(0, 0, 0, 0));
         }
         cp_async_commit();
     };
-    float d[NT][4];
+    float d[RB][NT][4];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) d[nt][0] = d[nt][1] = d[nt][2] = d[nt][3] = 0.f;
+    for (int r = 0; r < RB; ++r)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) d[r][nt][0] = d[r][nt][1] = d[r][nt][2] = d[r][nt][3] = 0.f;
     for (int k = 0; k < kBgOutBufs && k < nb; ++k) issue(k);
     for (int k = 0; k < nb; ++k) {
         if (k + 2 < nb) cp_async_wait_group<2>();
         else if (k + 1 < nb) cp_async_wait_group<1>();
         else cp_async_wait_group<0>();
         __syncwarp();
-        const uint32_t ab = wa + (k % kBgOutBufs) * 512, bb = wb + (k % kBgOutBufs) * 512;
-        uint32_t a0, a1, a2, a3;
-        // A: matrix j = (column half j >> 1, row half j & 1); lane 8j + i gives column (j >> 1) * 8 + i
-        ldmatrix_x4_trans(ab + (((lane >> 4) * 8 + (lane & 7)) * 32) + ((lane >> 3) & 1) * 16, a0, a1, a2, a3);
+        const uint32_t ab = wbase + (k % kBgOutBufs) * kBuf, bb = ab + kA;
         // B: matrix j = (column half j & 1, vector half j >> 1); rows are columns (32 bytes each)
         uint32_t b0, b1, b2, b3;
         ldmatrix_x4_trans(bb + ((((lane >> 3) & 1) * 8 + (lane & 7)) * 32) + (lane >> 4) * 16, b0, b1, b2, b3);
-        mma_16816(d[0], a0, a1, a2, a3, b0, b1);
-        if (NT == 2) mma_16816(d[NT - 1], a0, a1, a2, a3, b2, b3);
+#pragma unroll
+        for (int r = 0; r < RB; ++r) {
+            // A of row block r: matrix j = (column half j >> 1, row half j & 1);
+            // lane 8j + i gives column (j >> 1) * 8 + i
+            uint32_t a0, a1, a2, a3;
+            ldmatrix_x4_trans(ab + ((lane >> 4) * 8 + (lane & 7)) * (32 * RB) + 32 * r + ((lane >> 3) & 1) * 16,
+                              a0, a1, a2, a3);
+            mma_16816(d[r][0], a0, a1, a2, a3, b0, b1);
+            if (NT == 2) mma_16816(d[r][NT - 1], a0, a1, a2, a3, b2, b3);
+        }
         __syncwarp();  // every lane is done with the buffers before they are refilled
         if (k + kBgOutBufs < nb) issue(k + kBgOutBufs);
     }
-    // The warps' sums in warp order, then the INT4 part's slabs in order.
+    cp_async_wait_group<0>();
+    __syncthreads();  // every warp is done with its buffers: they take the warps' sums
+    float* red = reinterpret_cast<float*>(osm);  // [warp][r][nt][4][32]
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+    for (int r = 0; r < RB; ++r)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) red[warp][nt][e][lane] = d[nt][e];
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) red[(((warp * RB + r) * NT + nt) * 4 + e) * 32 + lane] = d[r][nt][e];
     __syncthreads();
-    for (int i = threadIdx.x; i < NT * 4 * 32; i += kBgOutWarps * 32) {
-        const int nt = i >> 7, e = (i >> 5) & 3, ln = i & 31;
-        const int row = rb * kRowBlock + (ln >> 2) + 8 * (e >> 1);
+    // The warps' sums in warp order, then the INT4 part's slabs in order.
+    for (int i = threadIdx.x; i < RB * NT * 4 * 32; i += kBgOutWarps * 32) {
+        const int r = i / (NT * 128), nt = (i >> 7) % NT, e = (i >> 5) & 3, ln = i & 31;
+        const int row = (rb0 + r) * kRowBlock + (ln >> 2) + 8 * (e >> 1);
         const int tok = nt * 8 + 2 * (ln & 3) + (e & 1);
         if (row >= a.d_out || tok >= a.M) continue;
         float v = 0.f;
@@ -373,7 +406,7 @@ __global__ void __launch_bounds__(kBgOutWarps * 32) bout_kernel(const BOArgs a) 
         }
         float o = 0.f;
 #pragma unroll
-        for (int w = 0; w < kBgOutWarps; ++w) o += red[w][nt][e][ln];
+        for (int w = 0; w < kBgOutWarps; ++w) o += red[(((w * RB + r) * NT + nt) * 4 + e) * 32 + ln];
         a.y[static_cast<size_t>(tok) * a.d_out + row] = __half_as_ushort(__float2half_rn(v + o));
     }
 }
@@ -576,7 +609,7 @@ __global__ void __launch_bounds__(kBgWarps * 32, 1) bdense_kernel(const BDArgs a
 // Host side
 // ---------------------------------------------------------------------------
 constexpr int kMaxDevices = 64;
-constexpr int kNumKernels = 16;
+constexpr int kNumKernels = 32;
 int g_smem_set[kMaxDevices][kNumKernels];
 
 template <class K>
@@ -617,17 +650,34 @@ dq_status_t launch_pdl(K kernel, dim3 grid, int threads, int smem, cudaStream_t 
     return DQ_OK;
 }
 
-template <int kOut, int NT>
-dq_status_t launch_bout(const BOArgs& a, int grid, cudaStream_t stream) {
-    const int smem = align16(2 * a.d_in) + 16;  // the union's columns
-    const dq_status_t st = ensure_smem(bout_kernel<kOut, NT>, 3 + 2 * kOut + (NT - 1), smem);
+template <int kOut, int NT, int RB>
+dq_status_t launch_bout_rb(const BOArgs& a, cudaStream_t stream) {
+    constexpr int rbi = RB == 1 ? 0 : RB == 2 ? 1 : 2;
+    const int smem = bout_smem<RB>(a.d_in);
+    const dq_status_t st = ensure_smem(bout_kernel<kOut, NT, RB>, 3 + (2 * kOut + NT - 1) * 3 + rbi, smem);
     if (st != DQ_OK) return st;
-    return launch_pdl(bout_kernel<kOut, NT>, dim3(grid), kBgOutWarps * 32, smem, stream, a);
+    const int nrb = (a.d_out + kRowBlock - 1) / kRowBlock;
+    return launch_pdl(bout_kernel<kOut, NT, RB>, dim3((nrb + RB - 1) / RB), kBgOutWarps * 32, smem, stream, a);
+}
+
+// Row blocks per FP16-part CTA.  One 8-vector tile: as many as keep at least
+// one CTA per SM (8192 x 8192 at M = 8: 35.8 -> 33.9 us per call with two;
+// the MoE step 0.80 -> 0.72 ms).  Two tiles: one (at M = 16 two row blocks
+// per CTA took the call from 36 to 45 us in back-to-back calls, though the
+// kernel alone ran as fast).
+template <int kOut, int NT>
+dq_status_t launch_bout(const BOArgs& a, int sm_count, cudaStream_t stream) {
+    const int nrb = (a.d_out + kRowBlock - 1) / kRowBlock;
+    if constexpr (NT == 1) {
+        if (nrb >= 4 * sm_count) return launch_bout_rb<kOut, NT, 4>(a, stream);
+        if (nrb >= 2 * sm_count) return launch_bout_rb<kOut, NT, 2>(a, stream);
+    }
+    return launch_bout_rb<kOut, NT, 1>(a, stream);
 }
 
 template <int NT>
 dq_status_t launch_batched_nt(const BgGeom& G, const BPArgs& pa, const BUArgs& ua, const BOArgs& oa, int out_mode,
-                              int ogrid, const BDArgs& da, int dsmem, cudaStream_t stream) {
+                              int sm_count, const BDArgs& da, int dsmem, cudaStream_t stream) {
     dq_status_t st = ensure_smem(bplan_kernel, 0, pa.S.total);
     if (st != DQ_OK) return st;
     st = ensure_smem(bdense_kernel<NT>, NT, dsmem);
@@ -637,9 +687,9 @@ dq_status_t launch_batched_nt(const BgGeom& G, const BPArgs& pa, const BUArgs& u
     st = launch_pdl(bdense_kernel<NT>, dim3(da.cps, G.nslab), kBgWarps * 32, dsmem, stream, da);
     if (st != DQ_OK) return st;
     switch (out_mode) {
-        case kBoStaged: return launch_bout<kBoStaged, NT>(oa, ogrid, stream);
-        case kBoColDirect: return launch_bout<kBoColDirect, NT>(oa, ogrid, stream);
-        default: return launch_bout<kBoRowDirect, NT>(oa, ogrid, stream);
+        case kBoStaged: return launch_bout<kBoStaged, NT>(oa, sm_count, stream);
+        case kBoColDirect: return launch_bout<kBoColDirect, NT>(oa, sm_count, stream);
+        default: return launch_bout<kBoRowDirect, NT>(oa, sm_count, stream);
     }
 }
 
@@ -698,7 +748,6 @@ dq_status_t launch_gemv_batched(const dq_weights_t& w, const uint16_t* x, uint16
     oa.M = M;
     oa.nslab = G.nslab;
     const int out_mode = w.fp16_cm ? ((w.d_out % 8) == 0 ? kBoStaged : kBoColDirect) : kBoRowDirect;
-    const int ogrid = G.NRB;
 
     BDArgs da;
     da.native = w.native;
@@ -727,8 +776,8 @@ dq_status_t launch_gemv_batched(const dq_weights_t& w, const uint16_t* x, uint16
     da.sm_xtab = DS.xtab;
     da.sm_xsum = DS.xsum;
 
-    return G.NT == 1 ? launch_batched_nt<1>(G, pa, ua, oa, out_mode, ogrid, da, DS.total, stream)
-                     : launch_batched_nt<2>(G, pa, ua, oa, out_mode, ogrid, da, DS.total, stream);
+    return G.NT == 1 ? launch_batched_nt<1>(G, pa, ua, oa, out_mode, di.sm_count, da, DS.total, stream)
+                     : launch_batched_nt<2>(G, pa, ua, oa, out_mode, di.sm_count, da, DS.total, stream);
 }
 
 dq_status_t read_batched_error(uint32_t* word, bool clear) {
