@@ -195,6 +195,35 @@ dq_status_t dq_split_gemv_batched(const dq_weights_t* w, const uint16_t* x, uint
     return launch_gemv_batched(*w, x, y, m, outlier_k, workspace, static_cast<cudaStream_t>(stream));
 }
 
+size_t dq_workspace_bytes_batched_grouped(int32_t d_out, int32_t d_in, int32_t m_max, int32_t groups) {
+    if (check_dims(d_out, d_in) != DQ_OK || m_max < 1 || m_max > kBgMaxM || groups < 1 || groups > kBgMaxGroups)
+        return 0;
+    return batched_grouped_region(d_out, d_in, m_max) * static_cast<size_t>(groups);
+}
+
+dq_status_t dq_split_gemv_batched_grouped(const dq_weights_t* w, const uint16_t* const* x, uint16_t* const* y,
+                                          const int32_t* m, int32_t groups, float outlier_k, void* workspace,
+                                          size_t workspace_bytes, void* stream) {
+    if (!w || !x || !y || !m) return DQ_ERR_INVALID_ARGUMENT;
+    if (groups < 1 || groups > kBgMaxGroups) return DQ_ERR_SHAPE;
+    int m_max = 0;
+    for (int e = 0; e < groups; ++e) {
+        if (m[e] < 1 || m[e] > kBgMaxM) return DQ_ERR_SHAPE;
+        if (w[e].d_out != w[0].d_out || w[e].d_in != w[0].d_in) return DQ_ERR_SHAPE;
+        if ((w[e].fp16_cm == nullptr) != (w[0].fp16_cm == nullptr)) return DQ_ERR_INVALID_ARGUMENT;
+        if (m[e] > m_max) m_max = m[e];
+    }
+    if (w[0].d_out == 0 && check_dims(w[0].d_out, w[0].d_in) == DQ_OK) return DQ_OK;
+    const size_t need = dq_workspace_bytes_batched_grouped(w[0].d_out, w[0].d_in, m_max, groups);
+    for (int e = 0; e < groups; ++e) {
+        const dq_status_t st = check_weights(&w[e], x[e], y[e], true, workspace, workspace_bytes);
+        if (st != DQ_OK) return st;
+        if (!w[e].native) return DQ_ERR_INVALID_ARGUMENT;
+    }
+    if (need == 0 || workspace_bytes < need) return DQ_ERR_WORKSPACE;
+    return launch_gemv_batched_grouped(w, x, y, m, groups, outlier_k, workspace, static_cast<cudaStream_t>(stream));
+}
+
 size_t dq_workspace_bytes(int32_t d_out, int32_t d_in) {
     if (check_dims(d_out, d_in) != DQ_OK) return 0;
     const size_t a = stream_ws(d_out, d_in).total, b = b1_workspace_bytes(d_out, d_in);

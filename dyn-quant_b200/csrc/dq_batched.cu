@@ -55,6 +55,14 @@ __device__ unsigned int g_berror_word;
 
 constexpr int kUnit = kB1UnitBytes;
 
+// The arguments of NG problems of one launch (NG = 1: a plain batched call;
+// NG > 1: a grouped call, problem g in blockIdx.y (plan, FP16 part) or
+// blockIdx.z (INT4 part)).
+template <class A, int NG>
+struct Group {
+    A p[NG];
+};
+
 // The codes of a word as exact FP16 integers: q for the even columns, 16 q for
 // the odd ones (the exponent-biased values with the bias 1024 taken off, one
 // exact HSUB2 per register).  Without the bias the MMA sums q x' directly:
@@ -114,7 +122,9 @@ struct BPArgs {
 // zeroed), and xsum[cc][group][m] = (1024 sum x' even columns, 1024 sum x' odd
 // columns, sum x', 0).  For M <= m < MP (padding of the last 8-vector tile):
 // zeros in the tables.
-__global__ void __launch_bounds__(kStatThreads, 1) bplan_kernel(const BPArgs a) {
+template <int NG>
+__global__ void __launch_bounds__(kStatThreads, 1) bplan_kernel(const Group<BPArgs, NG> grp) {
+    const BPArgs& a = grp.p[NG == 1 ? 0 : blockIdx.y];
     constexpr int NT = kStatThreads;
     extern __shared__ __align__(128) char smem[];
     uint4* xs = reinterpret_cast<uint4*>(smem + a.S.xs);
@@ -285,8 +295,9 @@ __host__ __device__ constexpr int bout_buf_bytes() { return RB * 512 + 512; }
 template <int RB>
 inline int bout_smem(int d_in) { return kBgOutWarps * kBgOutBufs * bout_buf_bytes<RB>() + align16(2 * d_in) + 16; }
 
-template <int kOut, int NT, int RB>
-__global__ void __launch_bounds__(kBgOutWarps * 32) bout_kernel(const BOArgs a) {
+template <int kOut, int NT, int RB, int NG>
+__global__ void __launch_bounds__(kBgOutWarps * 32) bout_kernel(const Group<BOArgs, NG> grp) {
+    const BOArgs& a = grp.p[NG == 1 ? 0 : blockIdx.y];
     constexpr int MP = 8 * NT;
     constexpr int kBuf = bout_buf_bytes<RB>();
     constexpr int kA = RB * 512;  // A part of a buffer: column ci's RB * 16 rows at ci * 32 RB
@@ -440,8 +451,9 @@ inline BDSmem bd_smem(int S, int MP) {
     return L;
 }
 
-template <int NT>
-__global__ void __launch_bounds__(kBgWarps * 32, 1) bdense_kernel(const BDArgs a) {
+template <int NT, int NG>
+__global__ void __launch_bounds__(kBgWarps * 32, 1) bdense_kernel(const Group<BDArgs, NG> grp) {
+    const BDArgs& a = grp.p[NG == 1 ? 0 : blockIdx.z];
     constexpr int MP = 8 * NT;
     extern __shared__ __align__(128) char smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -609,7 +621,7 @@ __global__ void __launch_bounds__(kBgWarps * 32, 1) bdense_kernel(const BDArgs a
 // Host side
 // ---------------------------------------------------------------------------
 constexpr int kMaxDevices = 64;
-constexpr int kNumKernels = 32;
+constexpr int kNumKernels = 48;
 int g_smem_set[kMaxDevices][kNumKernels];
 
 template <class K>
@@ -650,14 +662,18 @@ dq_status_t launch_pdl(K kernel, dim3 grid, int threads, int smem, cudaStream_t 
     return DQ_OK;
 }
 
-template <int kOut, int NT, int RB>
-dq_status_t launch_bout_rb(const BOArgs& a, cudaStream_t stream) {
+template <int kOut, int NT, int RB, int NG>
+dq_status_t launch_bout_rb(const Group<BOArgs, NG>& g, int ng, cudaStream_t stream) {
     constexpr int rbi = RB == 1 ? 0 : RB == 2 ? 1 : 2;
+    constexpr int id = 6 + ((2 * kOut + NT - 1) * 3 + rbi) * 2 + (NG == 1 ? 0 : 1);
+    static_assert(id < kNumKernels, "kernel attribute slot");
+    const BOArgs& a = g.p[0];
     const int smem = bout_smem<RB>(a.d_in);
-    const dq_status_t st = ensure_smem(bout_kernel<kOut, NT, RB>, 3 + (2 * kOut + NT - 1) * 3 + rbi, smem);
+    const dq_status_t st = ensure_smem(bout_kernel<kOut, NT, RB, NG>, id, smem);
     if (st != DQ_OK) return st;
     const int nrb = (a.d_out + kRowBlock - 1) / kRowBlock;
-    return launch_pdl(bout_kernel<kOut, NT, RB>, dim3((nrb + RB - 1) / RB), kBgOutWarps * 32, smem, stream, a);
+    return launch_pdl(bout_kernel<kOut, NT, RB, NG>, dim3((nrb + RB - 1) / RB, ng), kBgOutWarps * 32, smem, stream,
+                      g);
 }
 
 // Row blocks per FP16-part CTA.  One 8-vector tile: as many as keep at least
@@ -665,48 +681,43 @@ dq_status_t launch_bout_rb(const BOArgs& a, cudaStream_t stream) {
 // the MoE step 0.80 -> 0.72 ms).  Two tiles: one (at M = 16 two row blocks
 // per CTA took the call from 36 to 45 us in back-to-back calls, though the
 // kernel alone ran as fast).
-template <int kOut, int NT>
-dq_status_t launch_bout(const BOArgs& a, int sm_count, cudaStream_t stream) {
-    const int nrb = (a.d_out + kRowBlock - 1) / kRowBlock;
+template <int kOut, int NT, int NG>
+dq_status_t launch_bout(const Group<BOArgs, NG>& g, int ng, int sm_count, cudaStream_t stream) {
+    const long long ctas = static_cast<long long>((g.p[0].d_out + kRowBlock - 1) / kRowBlock) * ng;
     if constexpr (NT == 1) {
-        if (nrb >= 4 * sm_count) return launch_bout_rb<kOut, NT, 4>(a, stream);
-        if (nrb >= 2 * sm_count) return launch_bout_rb<kOut, NT, 2>(a, stream);
+        if (ctas >= 4LL * sm_count) return launch_bout_rb<kOut, NT, 4, NG>(g, ng, stream);
+        if (ctas >= 2LL * sm_count) return launch_bout_rb<kOut, NT, 2, NG>(g, ng, stream);
     }
-    return launch_bout_rb<kOut, NT, 1>(a, stream);
+    return launch_bout_rb<kOut, NT, 1, NG>(g, ng, stream);
 }
 
-template <int NT>
-dq_status_t launch_batched_nt(const BgGeom& G, const BPArgs& pa, const BUArgs& ua, const BOArgs& oa, int out_mode,
-                              int sm_count, const BDArgs& da, int dsmem, cudaStream_t stream) {
-    dq_status_t st = ensure_smem(bplan_kernel, 0, pa.S.total);
+template <int NT, int NG>
+dq_status_t launch_batched_group(const BgGeom& G, int ng, const Group<BPArgs, NG>& pg, const Group<BDArgs, NG>& dg,
+                                 const Group<BOArgs, NG>& og, int out_mode, int sm_count, int dsmem,
+                                 cudaStream_t stream) {
+    dq_status_t st = ensure_smem(bplan_kernel<NG>, NG == 1 ? 0 : 1, pg.p[0].S.total);
     if (st != DQ_OK) return st;
-    st = ensure_smem(bdense_kernel<NT>, NT, dsmem);
+    st = ensure_smem(bdense_kernel<NT, NG>, 2 + (NT - 1) * 2 + (NG == 1 ? 0 : 1), dsmem);
     if (st != DQ_OK) return st;
-    st = launch_pdl(bplan_kernel, dim3(G.MP), kStatThreads, pa.S.total, stream, pa);
+    st = launch_pdl(bplan_kernel<NG>, dim3(G.MP, ng), kStatThreads, pg.p[0].S.total, stream, pg);
     if (st != DQ_OK) return st;
-    st = launch_pdl(bdense_kernel<NT>, dim3(da.cps, G.nslab), kBgWarps * 32, dsmem, stream, da);
+    st = launch_pdl(bdense_kernel<NT, NG>, dim3(dg.p[0].cps, G.nslab, ng), kBgWarps * 32, dsmem, stream, dg);
     if (st != DQ_OK) return st;
     switch (out_mode) {
-        case kBoStaged: return launch_bout<kBoStaged, NT>(oa, sm_count, stream);
-        case kBoColDirect: return launch_bout<kBoColDirect, NT>(oa, sm_count, stream);
-        default: return launch_bout<kBoRowDirect, NT>(oa, sm_count, stream);
+        case kBoStaged: return launch_bout<kBoStaged, NT, NG>(og, ng, sm_count, stream);
+        case kBoColDirect: return launch_bout<kBoColDirect, NT, NG>(og, ng, sm_count, stream);
+        default: return launch_bout<kBoRowDirect, NT, NG>(og, ng, sm_count, stream);
     }
 }
 
-}  // namespace
-
-dq_status_t launch_gemv_batched(const dq_weights_t& w, const uint16_t* x, uint16_t* y, int M, float k,
-                                void* workspace, cudaStream_t stream) {
-    DeviceInfo di;
-    dq_status_t st = device_info(&di);
-    if (st != DQ_OK) return st;
-    const BgGeom G = bg_geom(w.d_out, w.d_in, M);
+// The kernels' arguments for one problem (weights w, M vectors x, outputs y)
+// with its workspace region ws, in the call's geometry G; cps CTAs per slab,
+// and the share pf_share of each warp's row blocks that the INT4 part pulls
+// into L2 before its dependency wait (1 or more: all).
+void problem_args(const dq_weights_t& w, const uint16_t* x, uint16_t* y, int M, float k, char* ws, const BgGeom& G,
+                  int cps, double pf_share, BPArgs& pa, BDArgs& da, BOArgs& oa) {
     const BgWs L = bg_ws(G, w.d_out, w.d_in);
-    char* ws = static_cast<char*>(workspace);
     const BDSmem DS = bd_smem(G.S, G.MP);
-    if (DS.total > di.smem_optin) return DQ_ERR_UNSUPPORTED;
-
-    BPArgs pa;
     pa.x = x;
     pa.masks = reinterpret_cast<uint32_t*>(ws + L.masks);
     pa.xrow = reinterpret_cast<uint16_t*>(ws + L.xrow);
@@ -721,7 +732,6 @@ dq_status_t launch_gemv_batched(const dq_weights_t& w, const uint16_t* x, uint16
     pa.W = G.W;
     pa.NC = G.NC;
     pa.S = bp_smem(w.d_in);
-    if (pa.S.total > di.smem_optin) return DQ_ERR_UNSUPPORTED;
 
     BUArgs ua;
     ua.masks = pa.masks;
@@ -734,7 +744,6 @@ dq_status_t launch_gemv_batched(const dq_weights_t& w, const uint16_t* x, uint16
     ua.d_in = w.d_in;
     ua.W = G.W;
 
-    BOArgs oa;
     oa.w16 = w.fp16;
     oa.w16_cm = w.fp16_cm;
     oa.ulist = ua.ulist;
@@ -747,9 +756,7 @@ dq_status_t launch_gemv_batched(const dq_weights_t& w, const uint16_t* x, uint16
     oa.MP = G.MP;
     oa.M = M;
     oa.nslab = G.nslab;
-    const int out_mode = w.fp16_cm ? ((w.d_out % 8) == 0 ? kBoStaged : kBoColDirect) : kBoRowDirect;
 
-    BDArgs da;
     da.native = w.native;
     da.xtab = pa.xtab;
     da.xsum = pa.xsum;
@@ -762,22 +769,73 @@ dq_status_t launch_gemv_batched(const dq_weights_t& w, const uint16_t* x, uint16
     da.NRB = G.NRB;
     da.S = G.S;
     da.nslab = G.nslab;
-    da.cps = std::max(1, std::min(G.NRB, di.sm_count / G.nslab));
+    da.cps = cps;
     {
-        // L2 prefetch of the weights during the plan: all of them when they
-        // take at most kBgPrefetchBytes, else that share of each warp's rows.
-        const double total = static_cast<double>(G.NRB) * G.NC * kUnit;
-        const int nrw_max = (G.NRB / da.cps + 1 + kBgWarps - 1) / kBgWarps + 1;
-        da.pf_rb = total <= kBgPrefetchBytes ? nrw_max
-                                             : static_cast<int>(nrw_max * (kBgPrefetchBytes / total));
+        // L2 prefetch of the weights during the plan: each warp's first row
+        // blocks, pf_share of them (1: all).
+        const int nrw_max = (G.NRB / cps + 1 + kBgWarps - 1) / kBgWarps + 1;
+        da.pf_rb = pf_share >= 1.0 ? nrw_max : static_cast<int>(nrw_max * pf_share);
     }
     da.sm_ring = DS.ring;
     da.sm_bars = DS.bars;
     da.sm_xtab = DS.xtab;
     da.sm_xsum = DS.xsum;
+}
 
-    return G.NT == 1 ? launch_batched_nt<1>(G, pa, ua, oa, out_mode, di.sm_count, da, DS.total, stream)
-                     : launch_batched_nt<2>(G, pa, ua, oa, out_mode, di.sm_count, da, DS.total, stream);
+int out_mode_of(const dq_weights_t& w) {
+    return w.fp16_cm ? ((w.d_out % 8) == 0 ? kBoStaged : kBoColDirect) : kBoRowDirect;
+}
+
+}  // namespace
+
+dq_status_t launch_gemv_batched(const dq_weights_t& w, const uint16_t* x, uint16_t* y, int M, float k,
+                                void* workspace, cudaStream_t stream) {
+    DeviceInfo di;
+    dq_status_t st = device_info(&di);
+    if (st != DQ_OK) return st;
+    const BgGeom G = bg_geom(w.d_out, w.d_in, M);
+    const BDSmem DS = bd_smem(G.S, G.MP);
+    if (DS.total > di.smem_optin || bp_smem(w.d_in).total > di.smem_optin) return DQ_ERR_UNSUPPORTED;
+    const int cps = std::max(1, std::min(G.NRB, di.sm_count / G.nslab));
+    const double total = static_cast<double>(G.NRB) * G.NC * kUnit;
+    Group<BPArgs, 1> pg;
+    Group<BDArgs, 1> dg;
+    Group<BOArgs, 1> og;
+    problem_args(w, x, y, M, k, static_cast<char*>(workspace), G, cps, kBgPrefetchBytes / total, pg.p[0], dg.p[0],
+                 og.p[0]);
+    const int om = out_mode_of(w);
+    return G.NT == 1 ? launch_batched_group<1, 1>(G, 1, pg, dg, og, om, di.sm_count, DS.total, stream)
+                     : launch_batched_group<2, 1>(G, 1, pg, dg, og, om, di.sm_count, DS.total, stream);
+}
+
+size_t batched_grouped_region(int d_out, int d_in, int m_max) {
+    return align256(bg_ws(bg_geom(d_out, d_in, m_max), d_out, d_in).total);
+}
+
+dq_status_t launch_gemv_batched_grouped(const dq_weights_t* w, const uint16_t* const* x, uint16_t* const* y,
+                                        const int32_t* m, int ng, float k, void* workspace, cudaStream_t stream) {
+    DeviceInfo di;
+    dq_status_t st = device_info(&di);
+    if (st != DQ_OK) return st;
+    int m_max = 1;
+    for (int e = 0; e < ng; ++e) m_max = std::max(m_max, static_cast<int>(m[e]));
+    const int d_out = w[0].d_out, d_in = w[0].d_in;
+    const BgGeom G = bg_geom(d_out, d_in, m_max);
+    const BDSmem DS = bd_smem(G.S, G.MP);
+    if (DS.total > di.smem_optin || bp_smem(d_in).total > di.smem_optin) return DQ_ERR_UNSUPPORTED;
+    const size_t region = batched_grouped_region(d_out, d_in, m_max);
+    // The INT4 part's CTAs: about one per SM over all problems.
+    const int cps = std::max(1, std::min(G.NRB, di.sm_count / (G.nslab * ng)));
+    const double total = static_cast<double>(G.NRB) * G.NC * kUnit * ng;
+    Group<BPArgs, kBgMaxGroups> pg;
+    Group<BDArgs, kBgMaxGroups> dg;
+    Group<BOArgs, kBgMaxGroups> og;
+    for (int e = 0; e < ng; ++e)
+        problem_args(w[e], x[e], y[e], m[e], k, static_cast<char*>(workspace) + e * region, G, cps,
+                     kBgPrefetchBytes / total, pg.p[e], dg.p[e], og.p[e]);
+    const int om = out_mode_of(w[0]);
+    return G.NT == 1 ? launch_batched_group<1, kBgMaxGroups>(G, ng, pg, dg, og, om, di.sm_count, DS.total, stream)
+                     : launch_batched_group<2, kBgMaxGroups>(G, ng, pg, dg, og, om, di.sm_count, DS.total, stream);
 }
 
 dq_status_t read_batched_error(uint32_t* word, bool clear) {

@@ -288,6 +288,7 @@ inline size_t native_bytes(int d_out, int d_in) {
 // Batched split GEMV (1 <= M <= 16 activation vectors, dq_batched.cu)
 // ---------------------------------------------------------------------------
 constexpr int kBgMaxM = 16;       // vectors per call
+constexpr int kBgMaxGroups = 16;  // problems of one grouped batched call
 constexpr int kBgWarps = 16;      // warps of a dense CTA (one CTA per SM)
 constexpr int kBgStages = 2;      // bulk-copy ring stages per warp
 constexpr int kBgOutWarps = 8;    // warps of an FP16-part CTA
@@ -389,6 +390,12 @@ dq_status_t read_stream_error(uint32_t* word, bool clear);
 
 dq_status_t launch_gemv_batched(const dq_weights_t& w, const uint16_t* x, uint16_t* y, int M, float k,
                                 void* workspace, cudaStream_t stream);
+// Grouped batched call: ng problems of one shape (weights w[e], m[e] vectors
+// x[e] -> y[e]), problem e in the workspace region e of
+// batched_grouped_region(d_out, d_in, max m) bytes.
+dq_status_t launch_gemv_batched_grouped(const dq_weights_t* w, const uint16_t* const* x, uint16_t* const* y,
+                                        const int32_t* m, int ng, float k, void* workspace, cudaStream_t stream);
+size_t batched_grouped_region(int d_out, int d_in, int m_max);
 dq_status_t read_batched_error(uint32_t* word, bool clear);
 // h[r][:d] = fp16(silu(a[r][:d]) * b[r][:d]) for r < rows, a and b rows ld apart (d, ld multiples of 8).
 dq_status_t launch_silu_mul(const uint16_t* a, const uint16_t* b, uint16_t* h, long long rows, long long d,

@@ -34,6 +34,8 @@ EXPORTED_SYMBOLS = (
     "dq_reset_noalloc_workspace",
     "dq_split_gemv_batched",
     "dq_workspace_bytes_batched",
+    "dq_split_gemv_batched_grouped",
+    "dq_workspace_bytes_batched_grouped",
     "dq_silu_mul",
     "dq_silu_mul_pairs",
     "dq_moe_combine",
@@ -55,6 +57,8 @@ EXPORTED_SYMBOLS = (
 )
 
 MAX_GATHER_RANKS = 8  # DQ_MAX_GATHER_RANKS
+MAX_BATCH = 16        # vectors of one batched split GEMV call
+MAX_GROUPS = 16       # problems of one grouped batched call
 
 
 class DqWeights(C.Structure):
@@ -126,6 +130,11 @@ def lib() -> C.CDLL:
         L.dq_split_gemv_batched.argtypes = [C.POINTER(DqWeights), P, P, i32, f32, P, C.c_size_t, P]
         L.dq_workspace_bytes_batched.restype = C.c_size_t
         L.dq_workspace_bytes_batched.argtypes = [i32, i32, i32]
+        L.dq_split_gemv_batched_grouped.restype = st
+        L.dq_split_gemv_batched_grouped.argtypes = [C.POINTER(DqWeights), C.POINTER(P), C.POINTER(P),
+                                                    C.POINTER(i32), i32, f32, P, C.c_size_t, P]
+        L.dq_workspace_bytes_batched_grouped.restype = C.c_size_t
+        L.dq_workspace_bytes_batched_grouped.argtypes = [i32, i32, i32, i32]
         L.dq_silu_mul.restype = st
         L.dq_silu_mul.argtypes = [P, P, P, C.c_int64, P]
         L.dq_silu_mul_pairs.restype = st
@@ -173,6 +182,18 @@ def status_string(status: int) -> str:
 def check(status: int, what: str) -> None:
     if status != DQ_OK:
         raise DqError(status, what, lib().dq_last_cuda_error() if status == DQ_ERR_CUDA else 0)
+
+
+def batched_grouped(w_list, x_ptrs, y_ptrs, ms, k: float, ws_ptr: int, ws_bytes: int, stream: int) -> int:
+    """dq_split_gemv_batched_grouped over len(w_list) problems (DqWeights,
+    device addresses of x[e] and y[e], vector counts m[e]); returns the status."""
+    n = len(w_list)
+    w_arr = (DqWeights * n)(*w_list)
+    x_arr = (C.c_void_p * n)(*x_ptrs)
+    y_arr = (C.c_void_p * n)(*y_ptrs)
+    m_arr = (C.c_int32 * n)(*ms)
+    return lib().dq_split_gemv_batched_grouped(w_arr, x_arr, y_arr, m_arr, n, float(k), C.c_void_p(ws_ptr), ws_bytes,
+                                               C.c_void_p(stream))
 
 
 def weights(packed: int, scales: int, zeros: int, fp16: int | None, fp16_cm: int | None,

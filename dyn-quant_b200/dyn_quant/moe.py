@@ -63,6 +63,18 @@ class MoERouting:
         t = self.tokens.get(e)
         return 0 if t is None else int(t.numel())
 
+    def stacked(self, experts: Sequence[int]):
+        """The rows routed to the given experts, one expert after another:
+        (token indices int64 on the device, per-expert counts).  Cached per
+        expert list, so a CUDA graph captured after the first call reuses it."""
+        key = tuple(experts)
+        hit = self.__dict__.setdefault("_stacked", {}).get(key)
+        if hit is None:
+            rows = torch.cat([self.tokens64[e] for e in experts]) if experts else None
+            hit = (rows, [self.count(e) for e in experts])
+            self._stacked[key] = hit
+        return hit
+
 
 def silu_mul(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     """fp16(silu(a) * b), silu(v) = v / (1 + exp(-v)) in FP32 (dq_silu_mul)."""
@@ -142,7 +154,67 @@ class MoEFFN(torch.nn.Module):
         else:
             out.zero_()
         reduce = len(self.local) < self.n_experts
+        if x.is_cuda and self._grouped(x, routing, out):
+            if reduce:
+                dist.all_reduce(out, group=group)
+            return out.to(torch.float16)
         return moe_forward(x, routing, self.local, self.expert, out, reduce, group).to(torch.float16)
+
+    def _grouped(self, x: torch.Tensor, routing: MoERouting, out: torch.Tensor) -> bool:
+        """The local experts' step with grouped batched calls: one call for
+        every expert's w13 on its tokens, one gated activation over all rows,
+        one call for every w2, then the combine expert by expert (the order of
+        moe_forward, so out gets the same additions in the same order).
+        Returns False (nothing done) where the grouped call does not apply:
+        more than 16 experts here, or more than 16 tokens on one expert."""
+        es = [e for e in self.local if routing.count(e) > 0]
+        if not es or len(es) > _lib.MAX_GROUPS or any(routing.count(e) > _lib.MAX_BATCH for e in es):
+            return len(es) == 0
+        if x.dtype != torch.float16:
+            x = x.to(torch.float16)
+        rows, counts = routing.stacked(es)
+        xg = x.index_select(0, rows).contiguous()
+        n = xg.shape[0]
+        D, F = self.d_model, self.d_ff
+        h13 = torch.empty(n, 2 * F, dtype=torch.float16, device=x.device)
+        y2 = torch.empty(n, D, dtype=torch.float16, device=x.device)
+        ws = self._workspace(x.device, max(counts), len(es))
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        offs = [0]
+        for c in counts:
+            offs.append(offs[-1] + c)
+        for layers, src, dst, d_src, d_dst in ((self.w13, xg, h13, D, 2 * F), (self.w2, None, y2, F, D)):
+            if src is None:
+                src = silu_mul_pairs(h13)
+            st = _lib.batched_grouped([_weights_of(layers[str(e)]) for e in es],
+                                      [src.data_ptr() + 2 * d_src * o for o in offs[:-1]],
+                                      [dst.data_ptr() + 2 * d_dst * o for o in offs[:-1]], counts,
+                                      self.outlier_k, ws.data_ptr(), ws.numel(), stream)
+            _lib.check(st, "dq_split_gemv_batched_grouped")
+        for i, e in enumerate(es):
+            combine_(out, y2[offs[i]:offs[i + 1]], routing.tokens[e], routing.weight[e])
+        return True
+
+    def _workspace(self, device: torch.device, m_max: int, groups: int) -> torch.Tensor:
+        L = _lib.lib()
+        need = max(L.dq_workspace_bytes_batched_grouped(2 * self.d_ff, self.d_model, m_max, groups),
+                   L.dq_workspace_bytes_batched_grouped(self.d_model, self.d_ff, m_max, groups))
+        ws = self.__dict__.get("_ws")
+        if ws is None or ws.device != device or ws.numel() < need:
+            ws = torch.zeros(need, dtype=torch.uint8, device=device)
+            self.__dict__["_ws"] = ws
+        return ws
+
+
+def _weights_of(lin: DynQuantLinear):
+    """The dq_weights_t of a loaded DynQuantLinear (its FP16 weights are the
+    row-major matrix or the transpose of the column-major mirror)."""
+    f = lin.fp16_w
+    d_out, d_in = f.shape
+    cm = d_out > 1 and f.stride() == (1, d_out)
+    return _lib.weights(lin.packed.data_ptr(), lin.scales.data_ptr(), lin.zeros.data_ptr(),
+                        None if cm else f.data_ptr(), f.data_ptr() if cm else None, d_out, d_in,
+                        lin._native.data_ptr())
 
 
 def moe_forward(x: torch.Tensor, routing: MoERouting, local: Sequence[int],

@@ -212,9 +212,9 @@ DQ_API dq_status_t dq_reset_noalloc_workspace(void* stream);
  * dq_workspace_bytes_batched(d_out, d_in, m) bytes, 256-byte aligned and
  * ZERO-FILLED before its first use.  It begins with the batch-1 region (so one
  * workspace serves both entry points and every shape it is large enough for),
- * then one arrival counter that every call leaves at zero again, then scratch
- * that each call overwrites (masks, the outlier-only rows, the outlier union
- * and its activation table, per-slab partial sums).  Calls that share a
+ * then scratch that each call overwrites (masks, the outlier-only rows, the
+ * x' tables, the outlier union and its activation table, per-slab partial
+ * sums).  Calls that share a
  * workspace must not overlap on the GPU.  Every call leaves it ready for the
  * next one (after a device error: dq_reset_workspace).  0 on invalid shapes.
  */
@@ -237,6 +237,34 @@ DQ_API size_t dq_workspace_bytes_batched(int32_t d_out, int32_t d_in, int32_t m)
 DQ_API dq_status_t dq_split_gemv_batched(const dq_weights_t* w, const uint16_t* x, uint16_t* y, int32_t m,
                                          float outlier_k, void* workspace, size_t workspace_bytes,
                                          void* stream);
+
+/*
+ * Workspace of dq_split_gemv_batched_grouped: one region per problem, each
+ * sized for m_max vectors (the largest m of the call).  0 on invalid
+ * arguments (1 <= m_max <= 16, 1 <= groups <= 16).
+ */
+DQ_API size_t dq_workspace_bytes_batched_grouped(int32_t d_out, int32_t d_in, int32_t m_max, int32_t groups);
+
+/*
+ * `groups` batched split GEMVs of one shape in one set of launches: for every
+ * problem e, y[e] = dq_split_gemv_batched(&w[e], x[e], m[e]).  Built for the
+ * experts of a mixture-of-experts layer, each with the few tokens routed to
+ * it: one launch streams every expert's weights, so the per-call latency of
+ * the plan and of a short weight stream is paid once instead of per expert.
+ * Each problem's results are bit-identical to its own dq_split_gemv_batched
+ * call when m[e] and the call's largest m are both at most 8 or both above
+ * 8; otherwise they agree within FP32 rounding (the call runs every problem
+ * with the two-tile geometry, which cuts the INT4 sums into other slabs).
+ * w: host array of `groups` weight descriptors of one shape, all with
+ * native, and all with or all without fp16_cm; x, y: host arrays of device
+ * pointers ([m[e]][d_in] and [m[e]][d_out] f16, 16-byte aligned); m: host
+ * array, 1 <= m[e] <= 16; 1 <= groups <= 16.  No counterpart in the reference
+ * (its entry point is batch 1).  Enqueues three kernels.
+ */
+DQ_API dq_status_t dq_split_gemv_batched_grouped(const dq_weights_t* w, const uint16_t* const* x,
+                                                 uint16_t* const* y, const int32_t* m, int32_t groups,
+                                                 float outlier_k, void* workspace, size_t workspace_bytes,
+                                                 void* stream);
 
 /*
  * Gated activation of a mixture-of-experts FFN (Mixtral-style

@@ -84,3 +84,27 @@ def test_moe_ffn_matches_oracle(E, D, F, T, K):
                       torch.zeros(T, D), False).numpy().astype(np.float64)
     rel = np.linalg.norm(out - ref) / np.linalg.norm(ref)
     assert rel <= 5e-3, rel
+
+
+def test_moe_grouped_step_equals_the_expert_loop():
+    """MoEFFN.forward runs the local experts through grouped batched calls
+    (one for every w13, one for every w2); with at most 8 tokens on every
+    expert those run the same kernels in the same geometry as the per-expert
+    calls of moe_forward, so the step is bit-identical to the expert loop.
+    (Between 2 and 8 tokens on every expert: a single token goes through the
+    batch-1 kernel in the loop.)"""
+    E, D, F, T, K = 8, 1024, 2048, 16, 2
+    rng = np.random.default_rng(12)
+    ex = np.stack([rng.choice(E, K, replace=False) for _ in range(T)])
+    w = rng.random((T, K)).astype(np.float32)
+    layer = MoEFFN(E, D, F)
+    for e in range(E):
+        layer.load_expert(e, dev(synth.weights(F, D, seed=40 + e)), dev(synth.weights(F, D, seed=50 + e)),
+                          dev(synth.weights(D, F, seed=60 + e)))
+    r = MoERouting(torch.from_numpy(ex), torch.from_numpy(w), E, device="cuda")
+    assert all(2 <= r.count(e) <= 8 for e in range(E))
+    x = dev(synth.activations(T, D, 0.02, seed=4))
+    grouped = layer(x, r)
+    loop = moe_forward(x, r, layer.local, layer.expert, torch.zeros(T, D, device="cuda"), False).to(torch.float16)
+    torch.cuda.synchronize()
+    assert torch.equal(grouped.view(torch.int16), loop.view(torch.int16))
