@@ -192,8 +192,10 @@ def batched_grouped(w_list, x_ptrs, y_ptrs, ms, k: float, ws_ptr: int, ws_bytes:
     x_arr = (C.c_void_p * n)(*x_ptrs)
     y_arr = (C.c_void_p * n)(*y_ptrs)
     m_arr = (C.c_int32 * n)(*ms)
-    return lib().dq_split_gemv_batched_grouped(w_arr, x_arr, y_arr, m_arr, n, float(k), C.c_void_p(ws_ptr), ws_bytes,
-                                               C.c_void_p(stream))
+    def vp(v):
+        return v if isinstance(v, C.c_void_p) else C.c_void_p(v)
+    return lib().dq_split_gemv_batched_grouped(w_arr, x_arr, y_arr, m_arr, n, float(k), vp(ws_ptr), ws_bytes,
+                                               vp(stream))
 
 
 def weights(packed: int, scales: int, zeros: int, fp16: int | None, fp16_cm: int | None,

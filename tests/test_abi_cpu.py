@@ -76,6 +76,27 @@ def test_validation_happens_before_any_cuda_call():
     assert L.dq_build_colmajor(C.c_void_p(16), 4, 100, C.c_void_p(16), None) == _lib.DQ_ERR_SHAPE
 
 
+def test_grouped_validation_happens_before_any_cuda_call():
+    L = _lib.lib()
+    w = _lib.weights(16, 16, 16, None, 16, 256, 1024, 16)
+    ws = 1 << 30
+    need = L.dq_workspace_bytes_batched_grouped(256, 1024, 4, 2)
+    assert need > 0 and L.dq_workspace_bytes_batched_grouped(256, 1024, 4, 17) == 0
+    assert L.dq_workspace_bytes_batched_grouped(256, 100, 4, 2) == 0
+
+    def call(ws_list, xs, ms, wsb=ws, ws_ptr=256):
+        return _lib.batched_grouped(ws_list, xs, [16] * len(xs), ms, 3.0, ws_ptr, wsb, None)
+    assert call([w, w], [16, 16], [2, 0]) == _lib.DQ_ERR_SHAPE
+    assert call([w, w], [16, 16], [2, 17]) == _lib.DQ_ERR_SHAPE
+    assert call([], [], []) == _lib.DQ_ERR_SHAPE
+    other = _lib.weights(16, 16, 16, None, 16, 256, 2048, 16)
+    assert call([w, other], [16, 16], [2, 2]) == _lib.DQ_ERR_SHAPE
+    assert call([w, w], [16, 18], [2, 2]) == _lib.DQ_ERR_ALIGNMENT
+    assert call([w, w], [16, 16], [2, 4], wsb=need - 256) == _lib.DQ_ERR_WORKSPACE
+    no_native = _lib.weights(16, 16, 16, None, 16, 256, 1024, None)
+    assert call([w, no_native], [16, 16], [2, 2]) == _lib.DQ_ERR_INVALID_ARGUMENT
+
+
 def test_check_raises_dqerror():
     with pytest.raises(_lib.DqError) as e:
         _lib.check(_lib.DQ_ERR_SHAPE, "dq_split_gemv")
