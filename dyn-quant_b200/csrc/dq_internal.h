@@ -185,7 +185,7 @@ inline StreamGeom stream_geom(int d_out, int d_in) {
 //   [0, ws_layout().total)   the b1 kernel's tag, arrivals and tagged partial sums
 //   stream_ctr               [0] tasks taken from the queue, [1] CTAs done
 //   stream_rbcnt             [kStreamMaxRb] tasks of each row block done
-//   batched_ctr              the batched plan's arrival counter and union size
+//   batched_ctr              [1] the batched call's union size (written every call)
 // After the header, per-shape scratch that each call overwrites.
 struct WsHeader {
     size_t stream_ctr, stream_rbcnt, batched_ctr, total;
