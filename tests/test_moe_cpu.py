@@ -63,6 +63,19 @@ def test_routing_lists():
         MoERouting(torch.tensor([[0, E]]), torch.ones(1, 2), E, device="cpu")
 
 
+def test_stacked_rows_follow_the_expert_order():
+    """The grouped step's row gather: the experts' token lists one after
+    another, in the order asked for, with their counts; cached per order."""
+    ex, w = _routing()
+    r = MoERouting(ex, w, E, device="cpu")
+    order = [e for e in (2, 0, 3, 1) if r.count(e)]
+    rows, counts = r.stacked(order)
+    assert counts == [r.count(e) for e in order]
+    assert rows.tolist() == sum((r.tokens64[e].tolist() for e in order), [])
+    assert r.stacked(order)[0] is rows
+    assert r.stacked(list(reversed(order)))[0] is not rows
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
