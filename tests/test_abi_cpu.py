@@ -76,6 +76,24 @@ def test_validation_happens_before_any_cuda_call():
     assert L.dq_build_colmajor(C.c_void_p(16), 4, 100, C.c_void_p(16), None) == _lib.DQ_ERR_SHAPE
 
 
+def test_workspace_sizes_cover_the_column_slabs():
+    """Rows of 24576 columns or more may run in column slabs, whose tagged
+    partial sums (8 bytes per row and slab after the first) follow the
+    workspace's fixed 197376-byte head; a workspace of dq_workspace_bytes
+    always has room for them."""
+    L = _lib.lib()
+    head = 197376
+    for d_out in (1024, 4096, 8192):
+        n_rb = (d_out + 15) // 16
+        assert L.dq_workspace_bytes(d_out, 28672) >= head + n_rb * 3 * 16 * 8  # 4 slabs of 14 chunks
+        assert L.dq_workspace_bytes(d_out, 30720) >= head + n_rb * 3 * 16 * 8  # 4 slabs of 15 chunks
+    assert L.dq_workspace_bytes(8192, 8192) >= head
+    # the grouped batched workspace is one region per problem
+    one = L.dq_workspace_bytes_batched_grouped(4096, 14336, 8, 1)
+    assert one > 0 and L.dq_workspace_bytes_batched_grouped(4096, 14336, 8, 8) == 8 * one
+    assert one % 256 == 0
+
+
 def test_grouped_validation_happens_before_any_cuda_call():
     L = _lib.lib()
     w = _lib.weights(16, 16, 16, None, 16, 256, 1024, 16)
